@@ -1,0 +1,344 @@
+"""AFT-full fwd+bwd benchmark (tokens/s) on 1..N B200s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2|c1|c4]
+    python bench.py --impl reference ...      # CPU oracle on the host cores
+
+One step = forward + backward of the causal AFT-full operator over one batch
+of synthetic sequences (seeded N(0,1) Q, K, V, dZ; w ~ N(0, 0.02)), the
+backward reusing the forward's operand panels.  Default workload: B=32, T=512,
+d=512, bf16 tensors, fp32 accumulation, per GPU (weak scaling); with N > 1
+GPUs every rank runs its own batch shard and the shared bias gradient dW is
+summed across ranks with one NCCL all-reduce inside the step.
+
+`value`  : tokens/s of the whole job, inputs resident in HBM, device-timed
+           with CUDA events, L2 flushed between steps (outside the events).
+`e2e`    : the same through the C ABI with host (pinned) buffers: each step
+           copies Q, K, V, dZ host->device and Z, dQ, dK, dV, dW back.
+`roofline`: the dominant kernel's achieved bytes or FLOPs per launch over its
+           CUDA-event time, against the measured peaks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+CONFIGS = {
+    # name: (B, T, d, dtype, description)
+    "c1": (4, 64, 128, "f32", "AFT-full causal fwd+bwd fp32 B=4 T=64 d=128"),
+    "c2": (32, 512, 512, "bf16", "AFT-full causal fwd+bwd bf16 B=32 T=512 d=512"),
+    "c4": (8, 4096, 1024, "bf16", "AFT-full causal fwd+bwd bf16 B=8 T=4096 d=1024"),
+}
+METRIC = "AFT fwd+bwd tokens/s"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
+                "source": "measured"}
+    return dict(FALLBACK_PEAKS, bf16_tflops_sustained=1400.0, source="fallback")
+
+
+def causal_flops(B, T, d):
+    """Algorithmic tensor-core FLOPs of one fwd+bwd: three [num|den]-shaped
+    contractions, each 2*B*d*T*(T+1) with the causal half skipped."""
+    return 6.0 * B * d * T * (T + 1)
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi sampled every 200 ms while the timed region runs."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.rows = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                      "--format=csv,noheader,nounits"], capture_output=True,
+                                     text=True, timeout=5).stdout.strip()
+                if out:
+                    self.rows.append([c.strip() for c in out.split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        self._t.join(timeout=10)
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in self.rows for n, v in zip(names, r[5:9]) if v.strip().lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+# ------------------------------------------------------------------ CPU
+def cpu_baseline(B, T, d, dtype_name, budget_s=10.0):
+    """Oracle port (fp32 C restatement, OpenMP over query rows) on the host
+    cores, on a bounded sample of the workload: as many of the B sequences as
+    fit the time budget.  Returns (tokens/s, cores, sample description)."""
+    import oracle
+
+    cores = os.cpu_count() or 1
+    oracle.set_threads(cores)
+    rng = np.random.default_rng(0)
+    W = (0.02 * rng.standard_normal((T, T))).astype(np.float32)
+
+    def one(nseq):
+        Q, K, V, dZ = (rng.standard_normal((nseq, T, d)).astype(np.float32) for _ in range(4))
+        t0 = time.perf_counter()
+        oracle.aft_full_fwd(Q, K, V, W, True)
+        oracle.aft_full_bwd(Q, K, V, W, dZ, True)
+        return time.perf_counter() - t0
+
+    t1 = one(1)
+    n = int(max(1, min(B, budget_s / max(t1, 1e-6))))
+    tn = one(n) if n > 1 else t1
+    return n * T / tn, cores, f"{n} of {B} sequences (T={T}, d={d}) fwd+bwd, fp32, {cores} threads, {tn:.2f} s"
+
+
+# ------------------------------------------------------------------ main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-budget", type=float, default=10.0)
+    args = ap.parse_args()
+
+    B, T, d, dt, desc = CONFIGS[args.config]
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    config = {"workload": desc, "B_per_gpu": B, "T": T, "d": d, "causal": True,
+              "global_batch": B * world, "seq_len": T, "parallelism": f"batch-shard x{world}",
+              "l2": "flushed between steps (256 MiB write)"}
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        K = max(1, args.steps)
+        vals = []
+        for _ in range(max(0, args.warmup)):
+            pass  # the oracle has no warm-up state; W is honoured by not timing it
+        tok_s, cores, sample = cpu_baseline(B, T, d, dt, budget_s=min(args.cpu_budget, 60.0 / K))
+        vals.append(tok_s)
+        line = {"metric": METRIC, "value": tok_s, "unit": "tokens/s", "impl": "reference", "n_gpus": args.gpus,
+                "steps": K, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+                "dtype": "f32", "data": "synthetic", "config": config, "vs_baseline": None,
+                "ms_per_step": 1e3 * B * T / tok_s,
+                "cpu_baseline": {"value": tok_s, "unit": "tokens/s", "cores": cores, "kind": "port",
+                                 "sample": sample},
+                "e2e": {"value": tok_s, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+
+    import torch
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+
+    from dart_cuda_b200 import ops
+
+    tdt = torch.bfloat16 if dt == "bf16" else torch.float32
+    esz = 2 if dt == "bf16" else 4
+    g = torch.Generator(device=dev)
+    g.manual_seed(1000 + rank)
+    Q, K_, V, dZ = (torch.randn(B, T, d, device=dev, generator=g).to(tdt) for _ in range(4))
+    g0 = torch.Generator(device=dev)
+    g0.manual_seed(999)  # w is shared: the same on every rank
+    w = 0.02 * torch.randn(T, T, device=dev, generator=g0)
+    Z = torch.empty_like(Q)
+    dQ, dK, dV = torch.empty_like(Q), torch.empty_like(K_), torch.empty_like(V)
+    dW = torch.empty(T, T, device=dev)
+    ws = ops.AftWorkspace(B, T, T, d, tdt, flags=1, device=dev)
+    flush = torch.empty(256 * 1024 * 1024 // 4, device=dev)
+
+    def step():
+        ops.aft_fwd(Q, K_, V, w, causal=True, out=Z, workspace=ws)
+        ops.aft_bwd(Q, K_, V, w, dZ, causal=True, grads=(dQ, dK, dV, dW), workspace=ws, ws_valid=True)
+        if dist is not None:
+            dist.all_reduce(dW)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    barrier()
+    stream = torch.cuda.current_stream()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    sampler = ClockSampler(local)
+    with sampler:
+        barrier()
+        for i in range(args.steps):
+            flush.zero_()
+            starts[i].record(stream)
+            step()
+            ends[i].record(stream)
+        barrier()
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    total_ms = sum(step_ms)
+    if dist is not None:
+        t = torch.tensor([total_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t)
+    ms_per_step = total_ms / args.steps
+    value = B * T * world / (ms_per_step / 1e3)
+
+    # ---- per-kernel timing pass (same steps, events around every launch)
+    ops.profile_enable(True)
+    for i in range(args.steps):
+        flush.zero_()
+        step()
+    torch.cuda.synchronize()
+    prof = ops.profile_read()
+    ops.profile_enable(False)
+    launches = sum(c for _, c in prof.values()) / args.steps
+
+    # ---- end to end through the C ABI with pinned host buffers
+    hQ, hK, hV, hdZ = (x.cpu().pin_memory() for x in (Q, K_, V, dZ))
+    hZ, hdQ, hdK, hdV = (torch.empty(x.shape, dtype=x.dtype).pin_memory() for x in (Z, dQ, dK, dV))
+    hdW = torch.empty(T, T).pin_memory()
+
+    def e2e_step():
+        Q.copy_(hQ, non_blocking=True)
+        K_.copy_(hK, non_blocking=True)
+        V.copy_(hV, non_blocking=True)
+        dZ.copy_(hdZ, non_blocking=True)
+        step()
+        hZ.copy_(Z, non_blocking=True)
+        hdQ.copy_(dQ, non_blocking=True)
+        hdK.copy_(dK, non_blocking=True)
+        hdV.copy_(dV, non_blocking=True)
+        hdW.copy_(dW, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+    if dist is not None:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t)
+    e2e_val = B * T * world / (e2e_ms / args.steps / 1e3)
+    h2d = 4 * B * T * d * esz
+    d2h = 4 * B * T * d * esz + T * T * 4
+
+    # ---- roofline of the dominant kernel
+    P = peaks()
+    Tp = (T + 127) // 128 * 128
+    dp_ = (d + 127) // 128 * 128
+    io = B * T * d * esz           # one user tensor
+    pan = B * Tp * dp_ * esz        # one operand panel (E'V, E', g or n)
+    ap_ = Tp * Tp * esz
+    bytes_per = {
+        "aft_prep_w": T * T * 4 + ap_,
+        "aft_prep_colmax": io,
+        "aft_prep_p": 2 * io + 2 * pan,
+        "aft_tc_fwd": 2 * pan + ap_ + 2 * io,
+        "aft_tc_bwd_recompute": 2 * pan + ap_ + 3 * io + 2 * pan,
+        "aft_tc_dkdv": 2 * pan + ap_ + 4 * io,
+        "aft_tc_dw": 4 * pan + 2 * T * T * 4,
+    }
+    gemm = 2.0 * B * d * T * (T + 1)  # one [num|den] contraction, causal half
+    flops_per = {"aft_tc_fwd": gemm, "aft_tc_bwd_recompute": gemm, "aft_tc_dkdv": gemm, "aft_tc_dw": gemm}
+    kern = {}
+    for name, (ms, cnt) in prof.items():
+        per_ms = ms / max(cnt, 1)
+        gbs = bytes_per.get(name, 0) / (per_ms / 1e3) / 1e9
+        tfs = flops_per.get(name, 0) / (per_ms / 1e3) / 1e12
+        kern[name] = {"ms_per_launch": per_ms, "launches": cnt, "share": ms / max(sum(m for m, _ in prof.values()), 1e-9),
+                      "GB/s": gbs, "TFLOP/s": tfs,
+                      "hbm_frac": gbs / P["hbm_gbs"], "tensor_frac": tfs / P["bf16_tflops"]}
+    dom = max(prof, key=lambda k: prof[k][0]) if prof else None
+    roof = None
+    if dom:
+        k = kern[dom]
+        bound = "tensor" if k["tensor_frac"] > k["hbm_frac"] else "hbm"
+        if bound == "tensor":
+            roof = {"bound": "tensor", "achieved": k["TFLOP/s"], "peak": P["bf16_tflops"], "unit": "TFLOP/s",
+                    "frac": k["tensor_frac"], "traffic": None, "kernel": dom,
+                    "peak_source": P["source"] + " bf16 burst"}
+        else:
+            roof = {"bound": "hbm", "achieved": k["GB/s"], "peak": P["hbm_gbs"], "unit": "GB/s",
+                    "frac": k["hbm_frac"], "traffic": None, "kernel": dom, "peak_source": P["source"]}
+
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": max(3, args.warmup), "ms_per_step": ms_per_step, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": dt, "data": "synthetic", "config": config,
+        "tflops": causal_flops(B, T, d) * world / (ms_per_step / 1e3) / 1e12,
+        "e2e": {"value": e2e_val, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "roofline": roof, "kernels": kern, "gpu_launches": launches * args.steps,
+        "clocks": sampler.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        tok_s, cores, sample = cpu_baseline(B, T, d, dt, budget_s=args.cpu_budget)
+        line["cpu_baseline"] = {"value": tok_s, "unit": "tokens/s", "cores": cores, "kind": "port",
+                                "sample": sample}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    del ws
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

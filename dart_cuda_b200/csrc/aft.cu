@@ -1,0 +1,921 @@
+// AFT-full forward and backward on sm_100a.
+//
+// The reference computes, per (t, d), a joint-max-stabilised softmax-like
+// weighted sum over i <= t with one CUDA thread per query row
+// (native/src/kernels/attention.cuh:6-40, native/src/engine.cu:522-590).
+// Here the same operator is factorised into dense contractions that run on
+// the 5th-generation tensor cores:
+//
+//   m_t  = max_{i in S(t)} w[t,i]            c_{b,d} = max_i K[b,i,d]
+//   A'   = [i in S(t)] * exp(w - m)  (Tq x Tk, shared by the batch)
+//   E'   = exp(K - c);  PV = E' * V;  PE = E'          ([B, Tk, D] each)
+//   num' = A' PV, den' = A' PE,  r = num'/den',  Z = sigmoid(Q) * r
+//
+// The scale factors e^{m_t} and e^{c_{b,d}} cancel exactly in r and in every
+// gradient, so the result equals the reference's up to rounding.  Backward:
+//
+//   g = dZ*sigmoid(Q)/den',  n = -g*r,  dQ = dZ*r*sigmoid(Q)*(1-sigmoid(Q))
+//   H1 = A'^T g, H2 = A'^T n          ->  dV = E'*H1,  dK = E'*(V*H1 + H2)
+//   dW = A' (.) sum_b (g_b PV_b^T + n_b PE_b^T)
+//
+// Four tcgen05 contraction modes share one warp-specialised kernel:
+//   FWD   : acc[d, t] = sum_i PV[i,d] A'[t,i]  (+ PE)   -> Z
+//   BWD1  : same contraction                            -> dQ, g, n
+//   HGRAD : acc[d, i] = sum_t G[t,d] A'[t,i]            -> dK, dV
+//   WGRAD : acc[t, i] = sum_{b,d} G[b,t,d] P[b,i,d]     -> dW (split-K, atomics)
+// Operands are staged by TMA into 128-byte-swizzled shared memory; one thread
+// issues the MMAs into TMEM; four warps read TMEM back in the epilogue.
+#include <cuda_bf16.h>
+#include <math.h>
+
+#include <algorithm>
+
+#include "dc_internal.h"
+#include "dc_ptx.cuh"
+
+namespace dc {
+namespace aft {
+
+constexpr int BM = 128;        // accumulator rows = TMEM lanes
+constexpr int BN = 128;        // accumulator columns (one accumulator)
+constexpr int T_ALIGN = 128;   // workspace padding of Tq and Tk
+constexpr int D_ALIGN = 128;   // workspace padding of D
+constexpr int kThreads = 192;  // warps 0-3 epilogue, warp 4 TMA, warp 5 MMA
+
+enum Mode { FWD = 0, BWD1 = 1, HGRAD = 2, WGRAD = 3 };
+
+// ------------------------------------------------------------ element I/O
+__device__ __forceinline__ float ld_io(const float *p, size_t i) { return p[i]; }
+__device__ __forceinline__ float ld_io(const __nv_bfloat16 *p, size_t i)
+{
+    return __bfloat162float(p[i]);
+}
+__device__ __forceinline__ void st_io(float *p, size_t i, float v) { p[i] = v; }
+__device__ __forceinline__ void st_io(__nv_bfloat16 *p, size_t i, float v)
+{
+    p[i] = __float2bfloat16_rn(v);
+}
+
+// operand precision: bf16, or fp32 rounded to tf32 (round-to-nearest-away)
+template <class E> __device__ __forceinline__ E to_op(float v);
+template <> __device__ __forceinline__ __nv_bfloat16 to_op<__nv_bfloat16>(float v)
+{
+    return __float2bfloat16_rn(v);
+}
+template <> __device__ __forceinline__ float to_op<float>(float v)
+{
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(v));
+    return __uint_as_float(r);
+}
+__device__ __forceinline__ float from_op(float v) { return v; }
+__device__ __forceinline__ float from_op(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+__device__ __forceinline__ float sigmoidf_(float q) { return 1.0f / (1.0f + __expf(-q)); }
+
+// ------------------------------------------------------------ parameters
+struct Params {
+    int B, Tq, Tk, D, Tqp, Tkp, dp;
+    int causal, accumulate;
+    int n_tiles;      // tiles along t (FWD/BWD1) or i (HGRAD, WGRAD)
+    int kpb;          // WGRAD: K steps per batch element (dp / BKe)
+    int splits;       // WGRAD: split-K factor
+    const void *Q, *K, *V, *dZ;
+    void *Z, *dQ, *dK, *dV;
+    float *dW;
+    const float *w;
+    int ldw;
+    const float *m;   // [Tqp]
+    const float *c;   // [B][dp]
+    void *G1, *G2;    // [B][Tqp][dp] operand precision
+    int *status;
+};
+
+// ------------------------------------------------------------ epilogues
+// Shared by the tensor-core and CUDA-core paths so both apply identical
+// element-wise maths to the contraction results.
+template <class IO>
+__device__ __forceinline__ void epi_fwd(const Params &p, int b, int t, int d, float num,
+                                        float den)
+{
+    if (t < p.Tq && d < p.D) {
+        size_t o = ((size_t)b * p.Tq + t) * p.D + d;
+        float s = sigmoidf_(ld_io((const IO *)p.Q, o));
+        st_io((IO *)p.Z, o, s * (num / den));
+    }
+}
+
+template <class IO, class E>
+__device__ __forceinline__ void epi_bwd1(const Params &p, int b, int t, int d, float num,
+                                         float den)
+{
+    float g = 0.f, n = 0.f;
+    if (t < p.Tq && d < p.D) {
+        size_t o = ((size_t)b * p.Tq + t) * p.D + d;
+        float s = sigmoidf_(ld_io((const IO *)p.Q, o));
+        float dz = ld_io((const IO *)p.dZ, o);
+        float r = num / den;
+        float dq = dz * r * s * (1.0f - s);
+        if (p.accumulate) dq += ld_io((const IO *)p.dQ, o);
+        st_io((IO *)p.dQ, o, dq);
+        g = dz * s / den;
+        n = -g * r;
+    }
+    size_t go = ((size_t)b * p.Tqp + t) * p.dp + d;
+    ((E *)p.G1)[go] = to_op<E>(g);
+    ((E *)p.G2)[go] = to_op<E>(n);
+}
+
+template <class IO>
+__device__ __forceinline__ void epi_hgrad(const Params &p, int b, int i, int d, float h1,
+                                          float h2)
+{
+    if (i < p.Tk && d < p.D) {
+        size_t o = ((size_t)b * p.Tk + i) * p.D + d;
+        float e = __expf(ld_io((const IO *)p.K, o) - p.c[(size_t)b * p.dp + d]);
+        float v = ld_io((const IO *)p.V, o);
+        float dv = e * h1;
+        float dk = e * (v * h1 + h2);
+        if (p.accumulate) {
+            dv += ld_io((const IO *)p.dV, o);
+            dk += ld_io((const IO *)p.dK, o);
+        }
+        st_io((IO *)p.dV, o, dv);
+        st_io((IO *)p.dK, o, dk);
+    }
+}
+
+__device__ __forceinline__ void epi_wgrad(const Params &p, int t, int i, float acc)
+{
+    if (t < p.Tq && i < p.Tk && (!p.causal || i <= t)) {
+        size_t o = (size_t)t * p.ldw + i;
+        float a = __expf(p.w[o] - p.m[t]);
+        atomicAdd(p.dW + o, a * acc);
+    }
+}
+
+// ------------------------------------------------------------ reductions
+__device__ __forceinline__ float warp_max(float v)
+{
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+__device__ __forceinline__ float block_max(float v, float *red)
+{
+    int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    v = warp_max(v);
+    if (lane == 0) red[wid] = v;
+    __syncthreads();
+    int nw = (blockDim.x + 31) >> 5;
+    v = (threadIdx.x < (unsigned)nw) ? red[threadIdx.x] : -INFINITY;
+    if (wid == 0) v = warp_max(v);
+    if (threadIdx.x == 0) red[0] = v;
+    __syncthreads();
+    v = red[0];
+    __syncthreads();
+    return v;
+}
+
+// ------------------------------------------------------------ prep kernels
+// Row maxima m_t over the visible set and A' = exp(w - m) (0 outside the
+// set and in the padding), one block per padded row.
+template <class E>
+__global__ void prep_w_kernel(const float *__restrict__ w, int ldw, int Tq, int Tk, int Tkp,
+                              int causal, float *__restrict__ m, E *__restrict__ Ap)
+{
+    __shared__ float red[32];
+    const int t = blockIdx.x;
+    E *row = Ap + (size_t)t * Tkp;
+    if (t >= Tq) {
+        for (int i = threadIdx.x; i < Tkp; i += blockDim.x) row[i] = to_op<E>(0.f);
+        if (threadIdx.x == 0) m[t] = 0.f;
+        return;
+    }
+    const int lim = causal ? min(t + 1, Tk) : Tk;
+    const float *wr = w + (size_t)t * ldw;
+    float mx = -INFINITY;
+    for (int i = threadIdx.x; i < lim; i += blockDim.x) mx = fmaxf(mx, wr[i]);
+    mx = block_max(mx, red);
+    if (threadIdx.x == 0) m[t] = mx;
+    for (int i = threadIdx.x; i < Tkp; i += blockDim.x)
+        row[i] = to_op<E>(i < lim ? __expf(wr[i] - mx) : 0.f);
+}
+
+// Partial column maxima of K over row slices: cpart[s][b][d].
+template <class IO>
+__global__ void prep_colmax_kernel(const IO *__restrict__ K, int B, int Tk, int D, int dp,
+                                   int rows_per_split, float *__restrict__ cpart)
+{
+    const int d = blockIdx.x * blockDim.x + threadIdx.x;
+    const int s = blockIdx.y, b = blockIdx.z;
+    if (d >= D) return;
+    const int i0 = s * rows_per_split, i1 = min(Tk, i0 + rows_per_split);
+    const IO *Kb = K + (size_t)b * Tk * D;
+    float mx = -INFINITY;
+    for (int i = i0; i < i1; ++i) mx = fmaxf(mx, ld_io(Kb, (size_t)i * D + d));
+    cpart[((size_t)s * B + b) * dp + d] = mx;
+}
+
+__global__ void prep_colmax_final_kernel(const float *__restrict__ cpart, int nsplit, int B,
+                                         int D, int dp, float *__restrict__ c)
+{
+    const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= B * dp) return;
+    const int d = idx % dp;
+    float mx = 0.f;
+    if (d < D) {
+        mx = -INFINITY;
+        for (int s = 0; s < nsplit; ++s) mx = fmaxf(mx, cpart[(size_t)s * B * dp + idx]);
+    }
+    c[idx] = mx;
+}
+
+// PV = exp(K - c) * V and PE = exp(K - c) over the padded [B, Tkp, dp] space.
+template <class IO, class E>
+__global__ void prep_p_kernel(const IO *__restrict__ K, const IO *__restrict__ V,
+                              const float *__restrict__ c, int B, int Tk, int D, int Tkp,
+                              int dp, E *__restrict__ PV, E *__restrict__ PE)
+{
+    const size_t total = (size_t)B * Tkp * dp;
+    for (size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+         idx += (size_t)gridDim.x * blockDim.x) {
+        const int d = (int)(idx % dp);
+        const size_t r = idx / dp;
+        const int i = (int)(r % Tkp);
+        const int b = (int)(r / Tkp);
+        float pv = 0.f, pe = 0.f;
+        if (i < Tk && d < D) {
+            const size_t src = ((size_t)b * Tk + i) * D + d;
+            const float e = __expf(ld_io(K, src) - c[(size_t)b * dp + d]);
+            pe = e;
+            pv = e * ld_io(V, src);
+        }
+        PV[idx] = to_op<E>(pv);
+        PE[idx] = to_op<E>(pe);
+    }
+}
+
+// ------------------------------------------------------------ CUDA-core path
+// Same contractions on CUDA cores in fp32 (cross-check of the tensor-core
+// path and of the prep kernels; not the product's fast path).
+template <int MODE, class E, class IO>
+__global__ void aft_simt_kernel(const Params p, const E *__restrict__ Ap,
+                                const E *__restrict__ PV, const E *__restrict__ PE)
+{
+    const E *G1 = (const E *)p.G1;
+    const E *G2 = (const E *)p.G2;
+    if (MODE == FWD || MODE == BWD1) {
+        const size_t total = (size_t)p.B * p.Tqp * p.dp;
+        const size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+        if (idx >= total) return;
+        const int d = (int)(idx % p.dp);
+        const int t = (int)((idx / p.dp) % p.Tqp);
+        const int b = (int)(idx / ((size_t)p.dp * p.Tqp));
+        float num = 0.f, den = 0.f;
+        const int lim = p.causal ? min(t + 1, p.Tkp) : p.Tkp;
+        for (int i = 0; i < lim; ++i) {
+            const float a = from_op(Ap[(size_t)t * p.Tkp + i]);
+            const size_t o = ((size_t)b * p.Tkp + i) * p.dp + d;
+            num += a * from_op(PV[o]);
+            den += a * from_op(PE[o]);
+        }
+        if (MODE == FWD)
+            epi_fwd<IO>(p, b, t, d, num, den);
+        else
+            epi_bwd1<IO, E>(p, b, t, d, num, den);
+    } else if (MODE == HGRAD) {
+        const size_t total = (size_t)p.B * p.Tkp * p.dp;
+        const size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+        if (idx >= total) return;
+        const int d = (int)(idx % p.dp);
+        const int i = (int)((idx / p.dp) % p.Tkp);
+        const int b = (int)(idx / ((size_t)p.dp * p.Tkp));
+        float h1 = 0.f, h2 = 0.f;
+        for (int t = p.causal ? i : 0; t < p.Tqp; ++t) {
+            const float a = from_op(Ap[(size_t)t * p.Tkp + i]);
+            const size_t o = ((size_t)b * p.Tqp + t) * p.dp + d;
+            h1 += a * from_op(G1[o]);
+            h2 += a * from_op(G2[o]);
+        }
+        epi_hgrad<IO>(p, b, i, d, h1, h2);
+    } else {
+        const size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+        if (idx >= (size_t)p.Tq * p.Tk) return;
+        const int t = (int)(idx / p.Tk), i = (int)(idx % p.Tk);
+        if (p.causal && i > t) return;
+        float acc = 0.f;
+        for (int b = 0; b < p.B; ++b)
+            for (int d = 0; d < p.dp; ++d) {
+                const size_t og = ((size_t)b * p.Tqp + t) * p.dp + d;
+                const size_t op = ((size_t)b * p.Tkp + i) * p.dp + d;
+                acc += from_op(G1[og]) * from_op(PV[op]) + from_op(G2[og]) * from_op(PE[op]);
+            }
+        epi_wgrad(p, t, i, acc);
+    }
+}
+
+// ------------------------------------------------------------ tensor-core path
+template <int MODE, class E>
+struct TcCfg {
+    static constexpr bool TF32 = sizeof(E) == 4;
+    static constexpr bool W = MODE == WGRAD;
+    static constexpr int BKe = 128 / (int)sizeof(E);   // K elements per stage
+    static constexpr int UK = TF32 ? 8 : 16;           // K per MMA instruction
+    static constexpr int NSUB = BKe / UK;              // MMAs per stage and accumulator
+    static constexpr int BOX_MN = 128 / (int)sizeof(E);// elements in one 128 B MN block
+    static constexpr int A_BYTES = BM * 128;
+    static constexpr int B_BYTES = BN * 128;
+    static constexpr int STAGE_BYTES = 2 * A_BYTES + (W ? 2 : 1) * B_BYTES;
+    static constexpr int STAGES = W ? 3 : 4;
+    static constexpr uint32_t TMEM_COLS = W ? 128 : 256;
+    static constexpr uint32_t A_MN = W ? 0 : 1;
+    static constexpr uint32_t B_MN = MODE == HGRAD ? 1 : 0;
+    static constexpr uint32_t IDESC = umma_idesc(TF32 ? 2u : 1u, BM, BN, A_MN, B_MN);
+    static constexpr uint32_t MN_LBO = BKe * 128;      // bytes between MN blocks
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+};
+
+// Decode the WGRAD tile index into (mt, nt): causal tiles are the lower
+// triangle nt <= mt listed row by row.
+__device__ __forceinline__ void wgrad_tile(int L, int causal, int n_tiles, int &mt, int &nt)
+{
+    if (!causal) {
+        mt = L / n_tiles;
+        nt = L % n_tiles;
+        return;
+    }
+    int r = (int)((sqrtf(8.0f * (float)L + 1.0f) - 1.0f) * 0.5f);
+    while ((r + 1) * (r + 2) / 2 <= L) ++r;
+    while (r * (r + 1) / 2 > L) --r;
+    mt = r;
+    nt = L - r * (r + 1) / 2;
+}
+
+template <int MODE, class E, class IO>
+__global__ void __launch_bounds__(kThreads, 1)
+    aft_tc_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtensorMap mapA1,
+                  const __grid_constant__ CUtensorMap mapA2,
+                  const __grid_constant__ CUtensorMap mapB1,
+                  const __grid_constant__ CUtensorMap mapB2)
+{
+    using C = TcCfg<MODE, E>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::STAGES * C::STAGE_BYTES);
+    uint64_t *full = bars;                  // [STAGES]
+    uint64_t *empty = bars + C::STAGES;     // [STAGES]
+    uint64_t *accf = bars + 2 * C::STAGES;  // [1]
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * C::STAGES + 1);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    // ---- tile coordinates and K range
+    int b = 0, mchunk = 0, nt = 0, k0 = 0, k1 = 0;
+    if (MODE == FWD || MODE == BWD1) {
+        nt = p.n_tiles - 1 - (int)blockIdx.x;  // long (late-t) tiles first
+        mchunk = blockIdx.y;
+        b = blockIdx.z;
+        k1 = (p.causal ? min(p.Tkp, (nt + 1) * BN) : p.Tkp) / C::BKe;
+    } else if (MODE == HGRAD) {
+        nt = blockIdx.x;
+        mchunk = blockIdx.y;
+        b = blockIdx.z;
+        k0 = p.causal ? (nt * BN) / C::BKe : 0;
+        k1 = p.Tqp / C::BKe;
+    } else {
+        wgrad_tile(blockIdx.x, p.causal, p.n_tiles, mchunk, nt);
+        const int total = p.B * p.kpb;
+        k0 = (int)(((long long)blockIdx.y * total) / p.splits);
+        k1 = (int)(((long long)(blockIdx.y + 1) * total) / p.splits);
+    }
+    const int nk = k1 - k0;
+
+    if (threadIdx.x == 0) {
+        *abort_flag = 0;
+        for (int s = 0; s < C::STAGES; ++s) {
+            mbar_init(smem_u32(&full[s]), 1);
+            mbar_init(smem_u32(&empty[s]), 1);
+        }
+        mbar_init(smem_u32(accf), 1);
+        fence_mbar_init();
+    }
+    if (warp == 4 && lane == 0) {
+        tma_prefetch(&mapA1);
+        tma_prefetch(&mapA2);
+        tma_prefetch(&mapB1);
+        if (C::W) tma_prefetch(&mapB2);
+    }
+    if (warp == 5) {
+        tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 4) {
+        // ------------------------------------------------ TMA producer
+        if (lane == 0) {
+            int issued = 0;
+            for (int k = 0; k < nk; ++k) {
+                const int s = k % C::STAGES;
+                const uint32_t ph = (k / C::STAGES) & 1;
+                if (!mbar_wait(smem_u32(&empty[s]), ph ^ 1, abort_flag, p.status,
+                               DC_DEVERR_TIMEOUT_EMPTY))
+                    break;
+                const uint32_t fb = smem_u32(&full[s]);
+                mbar_arrive_expect_tx(fb, C::STAGE_BYTES);
+                const uint32_t st = smem_u32(smem + s * C::STAGE_BYTES);
+                const int kk = k0 + k;
+                if (MODE == FWD || MODE == BWD1 || MODE == HGRAD) {
+                    // A1/A2: [BKe rows of K] x [128 of d], MN-major boxes
+#pragma unroll
+                    for (int j = 0; j < BM / C::BOX_MN; ++j) {
+                        const int x = mchunk * BM + j * C::BOX_MN;
+                        tma_load_3d(st + j * C::MN_LBO, &mapA1, fb, x, kk * C::BKe, b);
+                        tma_load_3d(st + C::A_BYTES + j * C::MN_LBO, &mapA2, fb, x,
+                                    kk * C::BKe, b);
+                    }
+                    if (MODE == HGRAD) {
+                        // B: A'[t rows (K), i cols (N)], MN-major boxes
+#pragma unroll
+                        for (int j = 0; j < BN / C::BOX_MN; ++j)
+                            tma_load_2d(st + 2 * C::A_BYTES + j * C::MN_LBO, &mapB1, fb,
+                                        nt * BN + j * C::BOX_MN, kk * C::BKe);
+                    } else {
+                        // B: A'[t rows (N), i cols (K)], K-major box
+                        tma_load_2d(st + 2 * C::A_BYTES, &mapB1, fb, kk * C::BKe, nt * BN);
+                    }
+                } else {
+                    const int bb = kk / p.kpb, kd = kk % p.kpb;
+                    tma_load_3d(st, &mapA1, fb, kd * C::BKe, mchunk * BM, bb);
+                    tma_load_3d(st + C::A_BYTES, &mapA2, fb, kd * C::BKe, mchunk * BM, bb);
+                    tma_load_3d(st + 2 * C::A_BYTES, &mapB1, fb, kd * C::BKe, nt * BN, bb);
+                    tma_load_3d(st + 2 * C::A_BYTES + C::B_BYTES, &mapB2, fb, kd * C::BKe,
+                                nt * BN, bb);
+                }
+                ++issued;
+            }
+            if (*abort_flag) {
+                // let the copies already in flight land before the CTA exits
+                for (int k = max(0, issued - C::STAGES); k < issued; ++k)
+                    mbar_wait(smem_u32(&full[k % C::STAGES]), (k / C::STAGES) & 1, nullptr,
+                              p.status, DC_DEVERR_TIMEOUT_DRAIN);
+            }
+        }
+    } else if (warp == 5) {
+        // ------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            for (int k = 0; k < nk; ++k) {
+                const int s = k % C::STAGES;
+                const uint32_t ph = (k / C::STAGES) & 1;
+                if (!mbar_wait(smem_u32(&full[s]), ph, abort_flag, p.status,
+                               DC_DEVERR_TIMEOUT_FULL))
+                    break;
+                tc_fence_after();
+                const uint32_t a1 = smem_u32(smem + s * C::STAGE_BYTES);
+                const uint32_t a2 = a1 + C::A_BYTES;
+                const uint32_t b1 = a1 + 2 * C::A_BYTES;
+                const uint32_t b2 = b1 + C::B_BYTES;
+#pragma unroll
+                for (int u = 0; u < C::NSUB; ++u) {
+                    const uint32_t accum = (k > 0 || u > 0) ? 1u : 0u;
+                    uint64_t da1, da2, db1, db2;
+                    if (C::A_MN) {
+                        da1 = sw128_desc(a1 + u * C::UK * 128, C::MN_LBO, 1024);
+                        da2 = sw128_desc(a2 + u * C::UK * 128, C::MN_LBO, 1024);
+                    } else {
+                        da1 = sw128_desc(a1 + u * C::UK * (int)sizeof(E), 16, 1024);
+                        da2 = sw128_desc(a2 + u * C::UK * (int)sizeof(E), 16, 1024);
+                    }
+                    if (C::B_MN) {
+                        db1 = sw128_desc(b1 + u * C::UK * 128, C::MN_LBO, 1024);
+                        db2 = db1;
+                    } else {
+                        db1 = sw128_desc(b1 + u * C::UK * (int)sizeof(E), 16, 1024);
+                        db2 = sw128_desc(b2 + u * C::UK * (int)sizeof(E), 16, 1024);
+                    }
+                    if (C::W) {
+                        umma<C::TF32>(tmem, da1, db1, C::IDESC, accum);
+                        umma<C::TF32>(tmem, da2, db2, C::IDESC, 1u);
+                    } else {
+                        umma<C::TF32>(tmem, da1, db1, C::IDESC, accum);
+                        umma<C::TF32>(tmem + BN, da2, db1, C::IDESC, accum);
+                    }
+                }
+                umma_commit(smem_u32(&empty[s]));
+            }
+            umma_commit(smem_u32(accf));
+            if (*abort_flag)  // MMAs must finish before TMEM is released
+                mbar_wait(smem_u32(accf), 0, nullptr, p.status, DC_DEVERR_TIMEOUT_DRAIN);
+        }
+    } else {
+        // ------------------------------------------------ epilogue (warps 0-3)
+        // warp-uniform, because the TMEM loads below are warp-collective
+        const bool ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(accf), 0, abort_flag, p.status,
+                                                          DC_DEVERR_TIMEOUT_ACC));
+        tc_fence_after();
+        if (ok && nk > 0) {
+            const int row = warp * 32 + lane;
+            const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
+#pragma unroll 1
+            for (int cb = 0; cb < BN / 32; ++cb) {
+                float v1[32], v2[32];
+                tmem_ld32(lane_addr + cb * 32, v1);
+                if (!C::W) tmem_ld32(lane_addr + BN + cb * 32, v2);
+                const int col0 = nt * BN + cb * 32;
+                if (MODE == FWD) {
+                    const int d = mchunk * BM + row;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) epi_fwd<IO>(p, b, col0 + j, d, v1[j], v2[j]);
+                } else if (MODE == BWD1) {
+                    const int d = mchunk * BM + row;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        epi_bwd1<IO, E>(p, b, col0 + j, d, v1[j], v2[j]);
+                } else if (MODE == HGRAD) {
+                    const int d = mchunk * BM + row;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) epi_hgrad<IO>(p, b, col0 + j, d, v1[j], v2[j]);
+                } else {
+                    const int t = mchunk * BM + row;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) epi_wgrad(p, t, col0 + j, v1[j]);
+                }
+            }
+        }
+        tc_fence_before();
+    }
+    __syncthreads();
+    if (warp == 5) {
+        tc_fence_after();
+        tmem_dealloc(tmem, C::TMEM_COLS);
+    }
+}
+
+// ------------------------------------------------------------ host side
+struct Layout {
+    int B, Tq, Tk, D, Tqp, Tkp, dp, esz, nsplit, rows_per_split;
+    size_t off_m, off_c, off_cpart, off_ap, off_pv, off_pe, off_g1, off_g2, total;
+};
+
+static int operand_size(int dtype, int flags)
+{
+    return (dtype == DC_F32 && !(flags & DC_AFT_COMPUTE_BF16)) ? 4 : 2;
+}
+
+static Layout make_layout(int B, int Tq, int Tk, int D, int dtype, int flags)
+{
+    Layout L{};
+    L.B = B;
+    L.Tq = Tq;
+    L.Tk = Tk;
+    L.D = D;
+    L.Tqp = (int)round_up(std::max(Tq, 1), T_ALIGN);
+    L.Tkp = (int)round_up(std::max(Tk, 1), T_ALIGN);
+    L.dp = (int)round_up(std::max(D, 1), D_ALIGN);
+    L.esz = operand_size(dtype, flags);
+    const int dblocks = (D + 255) / 256;
+    int want = (4 * 148 + dblocks * B - 1) / std::max(1, dblocks * B);
+    L.nsplit = std::max(1, std::min(want, (Tk + 31) / 32));
+    L.rows_per_split = (Tk + L.nsplit - 1) / L.nsplit;
+    L.nsplit = std::max(1, (Tk + L.rows_per_split - 1) / L.rows_per_split);
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        size_t o = off;
+        off += round_up((int64_t)bytes, 1024);
+        return o;
+    };
+    L.off_m = take((size_t)L.Tqp * 4);
+    L.off_c = take((size_t)B * L.dp * 4);
+    L.off_cpart = take((size_t)L.nsplit * B * L.dp * 4);
+    L.off_ap = take((size_t)L.Tqp * L.Tkp * L.esz);
+    L.off_pv = take((size_t)B * L.Tkp * L.dp * L.esz);
+    L.off_pe = take((size_t)B * L.Tkp * L.dp * L.esz);
+    L.off_g1 = take((size_t)B * L.Tqp * L.dp * L.esz);
+    L.off_g2 = take((size_t)B * L.Tqp * L.dp * L.esz);
+    L.total = off;
+    return L;
+}
+
+static int validate(const void *Q, const void *K, const void *V, const float *w, int ldw,
+                    int B, int Tq, int Tk, int D, int dtype, int flags)
+{
+    if (B < 0 || Tq < 0 || Tk < 0 || D < 0)
+        return fail(DC_ERR_INVALID, "negative shape B=%d Tq=%d Tk=%d D=%d", B, Tq, Tk, D);
+    if (dtype != DC_F32 && dtype != DC_BF16) return fail(DC_ERR_INVALID, "dtype %d", dtype);
+    if ((flags & DC_AFT_CAUSAL) && Tq != Tk)
+        return fail(DC_ERR_INVALID, "causal AFT needs Tq == Tk (got %d, %d)", Tq, Tk);
+    if ((long long)B * Tq * D == 0) return DC_OK;
+    if (Tk == 0) return fail(DC_ERR_INVALID, "Tk must be positive when Tq*D*B > 0");
+    if (ldw < Tk) return fail(DC_ERR_INVALID, "ldw (%d) < Tk (%d)", ldw, Tk);
+    if (!Q || !K || !V || !w) return fail(DC_ERR_INVALID, "null input pointer");
+    if ((long long)B * std::max(Tq, Tk) * (long long)D >= (1ll << 40))
+        return fail(DC_ERR_INVALID, "tensor too large");
+    return DC_OK;
+}
+
+// Workspace handed in or allocated on the stream.
+struct Workspace {
+    char *base = nullptr;
+    bool owned = false;
+    cudaStream_t stream = nullptr;
+    ~Workspace()
+    {
+        if (owned && base) cudaFreeAsync(base, stream);
+    }
+};
+
+static int get_workspace(Workspace &ws, const Layout &L, void *workspace, size_t bytes,
+                         cudaStream_t stream)
+{
+    ws.stream = stream;
+    if (workspace) {
+        if (bytes < L.total)
+            return fail(DC_ERR_NOMEM, "workspace of %zu bytes < %zu needed", bytes, L.total);
+        if ((reinterpret_cast<uintptr_t>(workspace) & 1023) != 0)
+            return fail(DC_ERR_INVALID, "workspace must be 1024-byte aligned");
+        ws.base = static_cast<char *>(workspace);
+        return DC_OK;
+    }
+    void *p = nullptr;
+    DC_CUDA_TRY(cudaMallocAsync(&p, L.total, stream));
+    ws.base = static_cast<char *>(p);
+    ws.owned = true;
+    return DC_OK;
+}
+
+template <class IO, class E>
+static int run_prep(const Layout &L, const IO *K, const IO *V, const float *w, int ldw,
+                    int causal, char *ws, cudaStream_t st)
+{
+    float *m = reinterpret_cast<float *>(ws + L.off_m);
+    float *c = reinterpret_cast<float *>(ws + L.off_c);
+    float *cpart = reinterpret_cast<float *>(ws + L.off_cpart);
+    E *Ap = reinterpret_cast<E *>(ws + L.off_ap);
+    E *PV = reinterpret_cast<E *>(ws + L.off_pv);
+    E *PE = reinterpret_cast<E *>(ws + L.off_pe);
+    {
+        KernelTimer kt("aft_prep_w", st);
+        prep_w_kernel<E><<<L.Tqp, 256, 0, st>>>(w, ldw, L.Tq, L.Tk, L.Tkp, causal, m, Ap);
+    }
+    {
+        KernelTimer kt("aft_prep_colmax", st);
+        dim3 g1((L.D + 255) / 256, L.nsplit, L.B);
+        prep_colmax_kernel<IO><<<g1, 256, 0, st>>>(K, L.B, L.Tk, L.D, L.dp, L.rows_per_split,
+                                                   cpart);
+        const int nbd = L.B * L.dp;
+        prep_colmax_final_kernel<<<(nbd + 255) / 256, 256, 0, st>>>(cpart, L.nsplit, L.B, L.D,
+                                                                      L.dp, c);
+    }
+    {
+        KernelTimer kt("aft_prep_p", st);
+        const size_t total = (size_t)L.B * L.Tkp * L.dp;
+        const int blocks = (int)std::min<size_t>((total + 255) / 256, (size_t)sm_count() * 16);
+        prep_p_kernel<IO, E><<<blocks, 256, 0, st>>>(K, V, c, L.B, L.Tk, L.D, L.Tkp, L.dp, PV, PE);
+    }
+    DC_CUDA_TRY(cudaGetLastError());
+    return DC_OK;
+}
+
+static CUtensorMapDataType tmap_type(int esz)
+{
+    return esz == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+}
+
+// [B][rows][dp] operand buffer; box of `bx` (inner, d) x `by` rows.
+static int map_3d(CUtensorMap *m, const void *base, const Layout &L, int rows, uint32_t bx,
+                  uint32_t by)
+{
+    uint64_t dims[3] = {(uint64_t)L.dp, (uint64_t)rows, (uint64_t)L.B};
+    uint64_t strides[2] = {(uint64_t)L.dp * L.esz, (uint64_t)rows * L.dp * L.esz};
+    uint32_t box[3] = {bx, by, 1};
+    return encode_tmap(m, tmap_type(L.esz), 3, base, dims, strides, box);
+}
+
+// A' [Tqp][Tkp]; box of `bx` (inner, i) x `by` rows (t).
+static int map_ap(CUtensorMap *m, const void *base, const Layout &L, uint32_t bx, uint32_t by)
+{
+    uint64_t dims[2] = {(uint64_t)L.Tkp, (uint64_t)L.Tqp};
+    uint64_t strides[1] = {(uint64_t)L.Tkp * L.esz};
+    uint32_t box[2] = {bx, by};
+    return encode_tmap(m, tmap_type(L.esz), 2, base, dims, strides, box);
+}
+
+template <int MODE, class E, class IO>
+static int launch_tc(const Params &p, const Layout &L, char *ws, cudaStream_t st)
+{
+    using C = TcCfg<MODE, E>;
+    static bool attr_set[64] = {false};  // per instantiation and device
+    int dev = 0;
+    DC_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return fail(DC_ERR_UNSUPPORTED, "device ordinal %d", dev);
+    if (!attr_set[dev]) {
+        DC_CUDA_TRY(cudaFuncSetAttribute(aft_tc_kernel<MODE, E, IO>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         C::SMEM_BYTES));
+        attr_set[dev] = true;
+    }
+    CUtensorMap mA1, mA2, mB1, mB2;
+    const uint32_t BK = C::BKe, BOX = C::BOX_MN;
+    if (MODE == FWD || MODE == BWD1) {
+        DC_TRY(map_3d(&mA1, ws + L.off_pv, L, L.Tkp, BOX, BK));
+        DC_TRY(map_3d(&mA2, ws + L.off_pe, L, L.Tkp, BOX, BK));
+        DC_TRY(map_ap(&mB1, ws + L.off_ap, L, BK, BN));
+        mB2 = mB1;
+    } else if (MODE == HGRAD) {
+        DC_TRY(map_3d(&mA1, ws + L.off_g1, L, L.Tqp, BOX, BK));
+        DC_TRY(map_3d(&mA2, ws + L.off_g2, L, L.Tqp, BOX, BK));
+        DC_TRY(map_ap(&mB1, ws + L.off_ap, L, BOX, BK));
+        mB2 = mB1;
+    } else {
+        DC_TRY(map_3d(&mA1, ws + L.off_g1, L, L.Tqp, BK, BM));
+        DC_TRY(map_3d(&mA2, ws + L.off_g2, L, L.Tqp, BK, BM));
+        DC_TRY(map_3d(&mB1, ws + L.off_pv, L, L.Tkp, BK, BN));
+        DC_TRY(map_3d(&mB2, ws + L.off_pe, L, L.Tkp, BK, BN));
+    }
+    dim3 grid;
+    if (MODE == FWD || MODE == BWD1)
+        grid = dim3(L.Tqp / BN, L.dp / BM, L.B);
+    else if (MODE == HGRAD)
+        grid = dim3(L.Tkp / BN, L.dp / BM, L.B);
+    else {
+        const int mt = L.Tqp / BM, nt = L.Tkp / BN;
+        const int tiles = p.causal ? mt * (mt + 1) / 2 : mt * nt;
+        grid = dim3(tiles, p.splits, 1);
+    }
+    static const char *names[4] = {"aft_tc_fwd", "aft_tc_bwd_recompute", "aft_tc_dkdv",
+                                   "aft_tc_dw"};
+    {
+        KernelTimer kt(names[MODE], st);
+        aft_tc_kernel<MODE, E, IO><<<grid, kThreads, C::SMEM_BYTES, st>>>(p, mA1, mA2, mB1, mB2);
+    }
+    DC_CUDA_TRY(cudaGetLastError());
+    return DC_OK;
+}
+
+template <int MODE, class E, class IO>
+static int launch_simt(const Params &p, const Layout &L, char *ws, cudaStream_t st)
+{
+    size_t n;
+    if (MODE == FWD || MODE == BWD1)
+        n = (size_t)L.B * L.Tqp * L.dp;
+    else if (MODE == HGRAD)
+        n = (size_t)L.B * L.Tkp * L.dp;
+    else
+        n = (size_t)L.Tq * L.Tk;
+    KernelTimer kt("aft_simt", st);
+    aft_simt_kernel<MODE, E, IO><<<(unsigned)((n + 255) / 256), 256, 0, st>>>(
+        p, reinterpret_cast<const E *>(ws + L.off_ap), reinterpret_cast<const E *>(ws + L.off_pv),
+        reinterpret_cast<const E *>(ws + L.off_pe));
+    DC_CUDA_TRY(cudaGetLastError());
+    return DC_OK;
+}
+
+template <int MODE, class E, class IO>
+static int launch(const Params &p, const Layout &L, char *ws, cudaStream_t st, int flags)
+{
+    if (flags & DC_AFT_SIMT) return launch_simt<MODE, E, IO>(p, L, ws, st);
+    return launch_tc<MODE, E, IO>(p, L, ws, st);
+}
+
+static Params make_params(const Layout &L, char *ws, int flags)
+{
+    Params p{};
+    p.B = L.B;
+    p.Tq = L.Tq;
+    p.Tk = L.Tk;
+    p.D = L.D;
+    p.Tqp = L.Tqp;
+    p.Tkp = L.Tkp;
+    p.dp = L.dp;
+    p.causal = (flags & DC_AFT_CAUSAL) ? 1 : 0;
+    p.accumulate = (flags & DC_AFT_ACCUMULATE) ? 1 : 0;
+    p.m = reinterpret_cast<const float *>(ws + L.off_m);
+    p.c = reinterpret_cast<const float *>(ws + L.off_c);
+    p.G1 = ws + L.off_g1;
+    p.G2 = ws + L.off_g2;
+    p.status = device_status_word();
+    return p;
+}
+
+template <class IO, class E>
+static int fwd_impl(const void *Q, const void *K, const void *V, const float *w, int ldw,
+                    void *Z, const Layout &L, int flags, char *ws, cudaStream_t st)
+{
+    if (!(flags & DC_AFT_WS_VALID))
+        DC_TRY(run_prep<IO, E>(L, (const IO *)K, (const IO *)V, w, ldw,
+                               (flags & DC_AFT_CAUSAL) ? 1 : 0, ws, st));
+    Params p = make_params(L, ws, flags);
+    p.Q = Q;
+    p.K = K;
+    p.V = V;
+    p.Z = Z;
+    p.w = w;
+    p.ldw = ldw;
+    p.n_tiles = L.Tqp / BN;
+    return launch<FWD, E, IO>(p, L, ws, st, flags);
+}
+
+template <class IO, class E>
+static int bwd_impl(const void *Q, const void *K, const void *V, const float *w, int ldw,
+                    const void *dZ, void *dQ, void *dK, void *dV, float *dW, const Layout &L,
+                    int flags, char *ws, cudaStream_t st)
+{
+    const int causal = (flags & DC_AFT_CAUSAL) ? 1 : 0;
+    if (!(flags & DC_AFT_WS_VALID))
+        DC_TRY(run_prep<IO, E>(L, (const IO *)K, (const IO *)V, w, ldw, causal, ws, st));
+    if (!(flags & DC_AFT_ACCUMULATE))
+        DC_CUDA_TRY(cudaMemset2DAsync(dW, (size_t)ldw * 4, 0, (size_t)L.Tk * 4, L.Tq, st));
+    Params p = make_params(L, ws, flags);
+    p.Q = Q;
+    p.K = K;
+    p.V = V;
+    p.dZ = dZ;
+    p.dQ = dQ;
+    p.dK = dK;
+    p.dV = dV;
+    p.dW = dW;
+    p.w = w;
+    p.ldw = ldw;
+    p.n_tiles = L.Tqp / BN;
+    DC_TRY((launch<BWD1, E, IO>(p, L, ws, st, flags)));
+    p.n_tiles = L.Tkp / BN;
+    DC_TRY((launch<HGRAD, E, IO>(p, L, ws, st, flags)));
+    // split-K factor for dW: enough CTAs to cover the SMs, >= 4 K steps each
+    p.kpb = L.dp / TcCfg<WGRAD, E>::BKe;
+    const int mt = L.Tqp / BM;
+    const int tiles = causal ? mt * (mt + 1) / 2 : mt * (L.Tkp / BN);
+    const int ktot = L.B * p.kpb;
+    int splits = (sm_count() + tiles - 1) / tiles;
+    splits = std::max(1, std::min(splits, ktot / 4));
+    p.splits = std::max(1, std::min(splits, ktot));
+    p.n_tiles = L.Tkp / BN;
+    return launch<WGRAD, E, IO>(p, L, ws, st, flags);
+}
+
+}  // namespace aft
+}  // namespace dc
+
+using namespace dc;
+using namespace dc::aft;
+
+extern "C" {
+
+int dc_aft_workspace_size(int B, int Tq, int Tk, int D, int dtype, int flags, size_t *bytes)
+{
+    clear_error();
+    if (!bytes) return fail(DC_ERR_INVALID, "bytes is NULL");
+    if (B < 0 || Tq < 0 || Tk < 0 || D < 0) return fail(DC_ERR_INVALID, "negative shape");
+    *bytes = make_layout(B, Tq, Tk, D, dtype, flags).total;
+    return DC_OK;
+}
+
+int dc_aft_fwd(const void *Q, const void *K, const void *V, const float *w, int ldw, void *Z,
+               int B, int Tq, int Tk, int D, int dtype, int flags, void *workspace,
+               size_t workspace_bytes, void *stream)
+{
+    clear_error();
+    DC_TRY(validate(Q, K, V, w, ldw, B, Tq, Tk, D, dtype, flags));
+    if ((long long)B * Tq * D == 0) return DC_OK;
+    if (!Z) return fail(DC_ERR_INVALID, "Z is NULL");
+    cudaStream_t st = as_stream(stream);
+    Layout L = make_layout(B, Tq, Tk, D, dtype, flags);
+    Workspace ws;
+    DC_TRY(get_workspace(ws, L, workspace, workspace_bytes, st));
+    if (dtype == DC_BF16)
+        return fwd_impl<__nv_bfloat16, __nv_bfloat16>(Q, K, V, w, ldw, Z, L, flags, ws.base, st);
+    if (L.esz == 2)
+        return fwd_impl<float, __nv_bfloat16>(Q, K, V, w, ldw, Z, L, flags, ws.base, st);
+    return fwd_impl<float, float>(Q, K, V, w, ldw, Z, L, flags, ws.base, st);
+}
+
+int dc_aft_bwd(const void *Q, const void *K, const void *V, const float *w, int ldw,
+               const void *dZ, void *dQ, void *dK, void *dV, float *dW, int B, int Tq, int Tk,
+               int D, int dtype, int flags, void *workspace, size_t workspace_bytes,
+               void *stream)
+{
+    clear_error();
+    DC_TRY(validate(Q, K, V, w, ldw, B, Tq, Tk, D, dtype, flags));
+    if ((long long)B * Tq * D == 0) return DC_OK;
+    if (!dZ || !dQ || !dK || !dV || !dW) return fail(DC_ERR_INVALID, "null gradient pointer");
+    cudaStream_t st = as_stream(stream);
+    Layout L = make_layout(B, Tq, Tk, D, dtype, flags);
+    Workspace ws;
+    DC_TRY(get_workspace(ws, L, workspace, workspace_bytes, st));
+    if (dtype == DC_BF16)
+        return bwd_impl<__nv_bfloat16, __nv_bfloat16>(Q, K, V, w, ldw, dZ, dQ, dK, dV, dW, L,
+                                                      flags, ws.base, st);
+    if (L.esz == 2)
+        return bwd_impl<float, __nv_bfloat16>(Q, K, V, w, ldw, dZ, dQ, dK, dV, dW, L, flags,
+                                              ws.base, st);
+    return bwd_impl<float, float>(Q, K, V, w, ldw, dZ, dQ, dK, dV, dW, L, flags, ws.base, st);
+}
+
+}  // extern "C"

@@ -1,0 +1,59 @@
+// Host-side helpers shared by the translation units of libmat_mul.so.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdio.h>
+
+#include <string>
+
+#include "../../include/dart_cuda_b200.h"
+
+namespace dc {
+
+// Record a message for dc_last_error() and return `code`.
+int fail(int code, const char *fmt, ...);
+void clear_error();
+
+// Convert and check a CUDA runtime result.
+#define DC_CUDA_TRY(expr)                                                             \
+    do {                                                                              \
+        cudaError_t _e = (expr);                                                      \
+        if (_e != cudaSuccess)                                                        \
+            return ::dc::fail(DC_ERR_CUDA, "%s failed: %s (%s:%d)", #expr,            \
+                              cudaGetErrorString(_e), __FILE__, __LINE__);            \
+    } while (0)
+
+#define DC_TRY(...)                  \
+    do {                             \
+        int _s = (__VA_ARGS__);      \
+        if (_s != DC_OK) return _s;  \
+    } while (0)
+
+// Per-device status word that kernels OR error bits into (bounded waits).
+int *device_status_word();
+
+// cuTensorMapEncodeTiled obtained through the runtime's driver entry point,
+// so the library does not link libcuda directly.
+int encode_tmap(CUtensorMap *map, CUtensorMapDataType dtype, int rank, const void *base,
+                const uint64_t *dims, const uint64_t *strides_bytes, const uint32_t *box);
+
+inline cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
+
+// Number of SMs of the current device (cached per device).
+int sm_count();
+
+// Kernel timing (off unless dc_profile_enable(1)): brackets a launch with
+// CUDA events on its stream and files the pair under `name`.
+struct KernelTimer {
+    const char *name;
+    cudaStream_t stream;
+    cudaEvent_t start = nullptr;
+    KernelTimer(const char *n, cudaStream_t s);
+    ~KernelTimer();
+};
+bool profiling_enabled();
+
+}  // namespace dc

@@ -1,0 +1,715 @@
+// HBM-bound row kernels of the training step: affine LayerNorm, row-broadcast
+// bias add, label-smoothed cross-entropy with fused log-softmax, AdamW.
+//
+// Each kernel touches every element once in the forward (one read, one
+// write) and reduces with warp shuffles; column reductions of the backward
+// (dgamma, dbeta, bias grad) are two-stage (per-CTA partials, then a column
+// pass) instead of the reference's per-row atomics.
+#include <math.h>
+
+#include <algorithm>
+
+#include "dc_internal.h"
+
+namespace dc {
+namespace rows {
+
+__device__ __forceinline__ float warp_sum(float v)
+{
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v)
+{
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// block-wide sum; `red` holds >= 32 floats; every thread gets the result
+__device__ __forceinline__ float block_sum(float v, float *red)
+{
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    v = warp_sum(v);
+    __syncthreads();
+    if (lane == 0) red[wid] = v;
+    __syncthreads();
+    const int nw = (blockDim.x + 31) >> 5;
+    float r = (lane < nw) ? red[lane] : 0.f;
+    return warp_sum(r);
+}
+__device__ __forceinline__ float block_max(float v, float *red)
+{
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    v = warp_max(v);
+    __syncthreads();
+    if (lane == 0) red[wid] = v;
+    __syncthreads();
+    const int nw = (blockDim.x + 31) >> 5;
+    float r = (lane < nw) ? red[lane] : -INFINITY;
+    return warp_max(r);
+}
+
+// ====================================================================== LN
+// One warp per row, the row held in registers (NV float4 per lane, C <= 128*NV).
+// Two-pass mean/variance over the registers, as the reference computes it
+// (native/src/kernels/layernorm_embed.cuh:140-176), with one global read.
+template <int NV>
+__global__ void ln_fwd_warp(const float *__restrict__ x, const float *__restrict__ gamma,
+                            const float *__restrict__ beta, float *__restrict__ y, int R, int C,
+                            float eps)
+{
+    const int lane = threadIdx.x & 31;
+    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (row >= R) return;
+    const int C4 = C >> 2;
+    const float4 *xr = reinterpret_cast<const float4 *>(x + (size_t)row * C);
+    float4 v[NV];
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+        const int j = lane + 32 * k;
+        v[k] = (j < C4) ? xr[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+        s += (v[k].x + v[k].y) + (v[k].z + v[k].w);
+    }
+    const float mean = warp_sum(s) / (float)C;
+    float q = 0.f;
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+        const int j = lane + 32 * k;
+        if (j < C4) {
+            float a = v[k].x - mean, b = v[k].y - mean, c = v[k].z - mean, d = v[k].w - mean;
+            q += (a * a + b * b) + (c * c + d * d);
+        }
+    }
+    const float inv_std = rsqrtf(warp_sum(q) / (float)C + eps);
+    const float4 *g4 = reinterpret_cast<const float4 *>(gamma);
+    const float4 *b4 = reinterpret_cast<const float4 *>(beta);
+    float4 *yr = reinterpret_cast<float4 *>(y + (size_t)row * C);
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+        const int j = lane + 32 * k;
+        if (j < C4) {
+            const float4 g = g4[j], bb = b4[j];
+            float4 o;
+            o.x = (v[k].x - mean) * inv_std * g.x + bb.x;
+            o.y = (v[k].y - mean) * inv_std * g.y + bb.y;
+            o.z = (v[k].z - mean) * inv_std * g.z + bb.z;
+            o.w = (v[k].w - mean) * inv_std * g.w + bb.w;
+            yr[j] = o;
+        }
+    }
+}
+
+// General fallback: one block per row, loops over the row (any C).
+__global__ void ln_fwd_block(const float *__restrict__ x, const float *__restrict__ gamma,
+                             const float *__restrict__ beta, float *__restrict__ y, int R, int C,
+                             float eps)
+{
+    __shared__ float red[32];
+    const int row = blockIdx.x;
+    const float *xr = x + (size_t)row * C;
+    float s = 0.f;
+    for (int j = threadIdx.x; j < C; j += blockDim.x) s += xr[j];
+    const float mean = block_sum(s, red) / (float)C;
+    float q = 0.f;
+    for (int j = threadIdx.x; j < C; j += blockDim.x) {
+        float d = xr[j] - mean;
+        q += d * d;
+    }
+    const float inv_std = rsqrtf(block_sum(q, red) / (float)C + eps);
+    float *yr = y + (size_t)row * C;
+    for (int j = threadIdx.x; j < C; j += blockDim.x)
+        yr[j] = (xr[j] - mean) * inv_std * gamma[j] + beta[j];
+}
+
+// Backward, one warp per row; each CTA also accumulates its rows'
+// contributions to dgamma/dbeta and writes them as one partial row
+// part[blockIdx.x][0:C] (dgamma) and part[blockIdx.x][C:2C] (dbeta).
+template <int NV>
+__global__ void ln_bwd_warp(const float *__restrict__ x, const float *__restrict__ gamma,
+                            const float *__restrict__ dy, float *__restrict__ dx,
+                            float *__restrict__ part, int R, int C, float eps, int accumulate,
+                            int rows_per_cta)
+{
+    extern __shared__ float sh[];  // [nwarps][2C]
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int C4 = C >> 2;
+    float4 gg[NV], gb[NV];
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+        gg[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+        gb[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    const float4 *g4 = reinterpret_cast<const float4 *>(gamma);
+    const int r0 = blockIdx.x * rows_per_cta;
+    const int r1 = min(R, r0 + rows_per_cta);
+    for (int row = r0 + wid; row < r1; row += nw) {
+        const float4 *xr = reinterpret_cast<const float4 *>(x + (size_t)row * C);
+        const float4 *gr = reinterpret_cast<const float4 *>(dy + (size_t)row * C);
+        float4 v[NV], g[NV];
+        float s = 0.f;
+#pragma unroll
+        for (int k = 0; k < NV; ++k) {
+            const int j = lane + 32 * k;
+            const bool in = j < C4;
+            v[k] = in ? xr[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+            g[k] = in ? gr[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+            s += (v[k].x + v[k].y) + (v[k].z + v[k].w);
+        }
+        const float mean = warp_sum(s) / (float)C;
+        float q = 0.f;
+#pragma unroll
+        for (int k = 0; k < NV; ++k) {
+            const int j = lane + 32 * k;
+            if (j < C4) {
+                float a = v[k].x - mean, b = v[k].y - mean, c = v[k].z - mean, d = v[k].w - mean;
+                q += (a * a + b * b) + (c * c + d * d);
+            }
+        }
+        const float inv_std = rsqrtf(warp_sum(q) / (float)C + eps);
+        float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+        for (int k = 0; k < NV; ++k) {
+            const int j = lane + 32 * k;
+            if (j < C4) {
+                const float4 ga = g4[j];
+                float4 xh;
+                xh.x = (v[k].x - mean) * inv_std;
+                xh.y = (v[k].y - mean) * inv_std;
+                xh.z = (v[k].z - mean) * inv_std;
+                xh.w = (v[k].w - mean) * inv_std;
+                s1 += (g[k].x * ga.x + g[k].y * ga.y) + (g[k].z * ga.z + g[k].w * ga.w);
+                s2 += (g[k].x * ga.x * xh.x + g[k].y * ga.y * xh.y) +
+                      (g[k].z * ga.z * xh.z + g[k].w * ga.w * xh.w);
+                gg[k].x += g[k].x * xh.x;
+                gg[k].y += g[k].y * xh.y;
+                gg[k].z += g[k].z * xh.z;
+                gg[k].w += g[k].w * xh.w;
+                gb[k].x += g[k].x;
+                gb[k].y += g[k].y;
+                gb[k].z += g[k].z;
+                gb[k].w += g[k].w;
+                v[k] = xh;
+            }
+        }
+        const float invC = 1.0f / (float)C;
+        const float m1 = warp_sum(s1) * invC, m2 = warp_sum(s2) * invC;
+        float4 *dr = reinterpret_cast<float4 *>(dx + (size_t)row * C);
+#pragma unroll
+        for (int k = 0; k < NV; ++k) {
+            const int j = lane + 32 * k;
+            if (j < C4) {
+                const float4 ga = g4[j];
+                float4 o;
+                o.x = inv_std * (g[k].x * ga.x - m1 - v[k].x * m2);
+                o.y = inv_std * (g[k].y * ga.y - m1 - v[k].y * m2);
+                o.z = inv_std * (g[k].z * ga.z - m1 - v[k].z * m2);
+                o.w = inv_std * (g[k].w * ga.w - m1 - v[k].w * m2);
+                if (accumulate) {
+                    const float4 old = dr[j];
+                    o.x += old.x;
+                    o.y += old.y;
+                    o.z += old.z;
+                    o.w += old.w;
+                }
+                dr[j] = o;
+            }
+        }
+    }
+    // CTA partials of dgamma/dbeta
+    float4 *myg = reinterpret_cast<float4 *>(sh + (size_t)wid * 2 * C);
+    float4 *myb = reinterpret_cast<float4 *>(sh + (size_t)wid * 2 * C + C);
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+        const int j = lane + 32 * k;
+        if (j < C4) {
+            myg[j] = gg[k];
+            myb[j] = gb[k];
+        }
+    }
+    __syncthreads();
+    for (int j = threadIdx.x; j < 2 * C; j += blockDim.x) {
+        float acc = 0.f;
+        for (int w = 0; w < nw; ++w) acc += sh[(size_t)w * 2 * C + j];
+        part[(size_t)blockIdx.x * 2 * C + j] = acc;
+    }
+}
+
+// Generic backward, one block per row; partials one row per CTA (= per row).
+__global__ void ln_bwd_block(const float *__restrict__ x, const float *__restrict__ gamma,
+                             const float *__restrict__ dy, float *__restrict__ dx,
+                             float *__restrict__ part, int R, int C, float eps, int accumulate)
+{
+    __shared__ float red[32];
+    const int row = blockIdx.x;
+    const float *xr = x + (size_t)row * C;
+    const float *gr = dy + (size_t)row * C;
+    float s = 0.f;
+    for (int j = threadIdx.x; j < C; j += blockDim.x) s += xr[j];
+    const float mean = block_sum(s, red) / (float)C;
+    float q = 0.f;
+    for (int j = threadIdx.x; j < C; j += blockDim.x) {
+        float d = xr[j] - mean;
+        q += d * d;
+    }
+    const float inv_std = rsqrtf(block_sum(q, red) / (float)C + eps);
+    float s1 = 0.f, s2 = 0.f;
+    for (int j = threadIdx.x; j < C; j += blockDim.x) {
+        const float xh = (xr[j] - mean) * inv_std;
+        const float dxh = gr[j] * gamma[j];
+        s1 += dxh;
+        s2 += dxh * xh;
+        part[(size_t)row * 2 * C + j] = gr[j] * xh;
+        part[(size_t)row * 2 * C + C + j] = gr[j];
+    }
+    const float invC = 1.0f / (float)C;
+    const float m1 = block_sum(s1, red) * invC;
+    const float m2 = block_sum(s2, red) * invC;
+    for (int j = threadIdx.x; j < C; j += blockDim.x) {
+        const float xh = (xr[j] - mean) * inv_std;
+        float o = inv_std * (gr[j] * gamma[j] - m1 - xh * m2);
+        if (accumulate) o += dx[(size_t)row * C + j];
+        dx[(size_t)row * C + j] = o;
+    }
+}
+
+// Sum `nparts` partial rows of width W into out (+= when accumulate).
+__global__ void colsum_parts(const float *__restrict__ part, int nparts, int W,
+                             float *out0, float *out1, int split,
+                             int accumulate)
+{
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= W) return;
+    float acc = 0.f;
+    for (int p = 0; p < nparts; ++p) acc += part[(size_t)p * W + j];
+    float *o = (j < split) ? out0 + j : out1 + (j - split);
+    *o = accumulate ? *o + acc : acc;
+}
+
+// ==================================================================== bias
+__global__ void bias_fwd_vec(const float4 *__restrict__ a, const float4 *__restrict__ b,
+                             float4 *__restrict__ out, size_t n4, int N4)
+{
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4;
+         i += (size_t)gridDim.x * blockDim.x) {
+        const float4 x = a[i], y = b[i % N4];
+        out[i] = make_float4(x.x + y.x, x.y + y.y, x.z + y.z, x.w + y.w);
+    }
+}
+__global__ void bias_fwd_scalar(const float *__restrict__ a, const float *__restrict__ b,
+                                float *__restrict__ out, size_t n, int N)
+{
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (size_t)gridDim.x * blockDim.x)
+        out[i] = a[i] + b[i % N];
+}
+
+// block (32, 8): 32 columns x row slice; da (+)= dy; column partial sums.
+__global__ void bias_bwd_kernel(const float *__restrict__ dy, float *__restrict__ da,
+                                float *__restrict__ part, int M, int N, int rows_per_cta,
+                                int accumulate)
+{
+    __shared__ float red[8][33];
+    const int col = blockIdx.x * 32 + threadIdx.x;
+    const int r0 = blockIdx.y * rows_per_cta, r1 = min(M, r0 + rows_per_cta);
+    float acc = 0.f;
+    if (col < N) {
+        for (int r = r0 + threadIdx.y; r < r1; r += 8) {
+            const size_t o = (size_t)r * N + col;
+            const float g = dy[o];
+            acc += g;
+            if (da) da[o] = accumulate ? da[o] + g : g;
+        }
+    }
+    red[threadIdx.y][threadIdx.x] = acc;
+    __syncthreads();
+    if (threadIdx.y == 0 && col < N) {
+        float s = 0.f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) s += red[k][threadIdx.x];
+        part[(size_t)blockIdx.y * N + col] = s;
+    }
+}
+
+// ===================================================================== CE
+// One warp per row (V small) or one block per row; online max/sum-exp with a
+// single read of the row.  loss_row = (1-eps)(lse - x_y) + eps(lse - mean x),
+// lse = max + log(sum exp(x - max) + 1e-12)  (loss_optim.cuh:163-205).
+__device__ __forceinline__ void online_update(float &m, float &s, float x)
+{
+    if (x > m) {
+        s = s * __expf(m - x) + 1.0f;
+        m = x;
+    } else {
+        s += __expf(x - m);
+    }
+}
+__device__ __forceinline__ void online_merge(float &m, float &s, float m2, float s2)
+{
+    const float mm = fmaxf(m, m2);
+    if (mm == -INFINITY) return;
+    s = s * __expf(m - mm) + s2 * __expf(m2 - mm);
+    m = mm;
+}
+
+__global__ void ce_fwd_warp(const float *__restrict__ logits, const int32_t *__restrict__ tgt,
+                            float *__restrict__ row_loss, int T, int V, float eps)
+{
+    const int lane = threadIdx.x & 31;
+    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (row >= T) return;
+    const float *xr = logits + (size_t)row * V;
+    float m = -INFINITY, s = 0.f, sx = 0.f;
+    for (int v = lane; v < V; v += 32) {
+        const float x = xr[v];
+        online_update(m, s, x);
+        sx += x;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+        const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+        online_merge(m, s, m2, s2);
+    }
+    sx = warp_sum(sx);
+    if (lane == 0) {
+        const float lse = m + logf(s + 1e-12f);
+        const float xt = xr[tgt[row]];
+        row_loss[row] = (1.0f - eps) * (lse - xt) + eps * (lse - sx / (float)V);
+    }
+}
+
+__global__ void ce_fwd_block(const float *__restrict__ logits, const int32_t *__restrict__ tgt,
+                             float *__restrict__ row_loss, int T, int V, float eps)
+{
+    __shared__ float rm[32], rs[32], red[32];
+    const int row = blockIdx.x;
+    const float *xr = logits + (size_t)row * V;
+    float m = -INFINITY, s = 0.f, sx = 0.f;
+    for (int v = threadIdx.x; v < V; v += blockDim.x) {
+        const float x = xr[v];
+        online_update(m, s, x);
+        sx += x;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+        const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+        online_merge(m, s, m2, s2);
+    }
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    if (lane == 0) {
+        rm[wid] = m;
+        rs[wid] = s;
+    }
+    sx = block_sum(sx, red);
+    if (wid == 0) {
+        m = lane < nw ? rm[lane] : -INFINITY;
+        s = lane < nw ? rs[lane] : 0.f;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+            const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+            online_merge(m, s, m2, s2);
+        }
+        if (lane == 0) {
+            const float lse = m + logf(s + 1e-12f);
+            const float xt = xr[tgt[row]];
+            row_loss[row] = (1.0f - eps) * (lse - xt) + eps * (lse - sx / (float)V);
+        }
+    }
+}
+
+// mean of the row losses (ce_mean_reduce, engine.cu:829-837), deterministic
+__global__ void mean_kernel(const float *__restrict__ v, int n, float *__restrict__ out)
+{
+    __shared__ float red[32];
+    float s = 0.f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) s += v[i];
+    s = block_sum(s, red);
+    if (threadIdx.x == 0) out[0] = s / (float)n;
+}
+
+// grad = (softmax - ((1-eps) 1_y + eps/V)) * g / T, written (not accumulated)
+// (loss_optim.cuh:207-244)
+__global__ void ce_bwd_warp(const float *__restrict__ logits, const int32_t *__restrict__ tgt,
+                            const float *__restrict__ gscale, float *__restrict__ grad, int T,
+                            int V, float eps)
+{
+    const int lane = threadIdx.x & 31;
+    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (row >= T) return;
+    const float *xr = logits + (size_t)row * V;
+    float m = -INFINITY, s = 0.f;
+    for (int v = lane; v < V; v += 32) online_update(m, s, xr[v]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+        const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+        online_merge(m, s, m2, s2);
+    }
+    const float inv = 1.0f / (s + 1e-12f);
+    const float scale = (gscale ? gscale[0] : 1.0f) / (float)T;
+    const int y = tgt[row];
+    const float off = eps / (float)V;
+    float *gr = grad + (size_t)row * V;
+    for (int v = lane; v < V; v += 32) {
+        const float sm = __expf(xr[v] - m) * inv;
+        const float tp = (v == y ? (1.0f - eps) : 0.f) + off;
+        gr[v] = (sm - tp) * scale;
+    }
+}
+
+__global__ void ce_bwd_block(const float *__restrict__ logits, const int32_t *__restrict__ tgt,
+                             const float *__restrict__ gscale, float *__restrict__ grad, int T,
+                             int V, float eps)
+{
+    __shared__ float rm[32], rs[32];
+    const int row = blockIdx.x;
+    const float *xr = logits + (size_t)row * V;
+    float m = -INFINITY, s = 0.f;
+    for (int v = threadIdx.x; v < V; v += blockDim.x) online_update(m, s, xr[v]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+        const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+        online_merge(m, s, m2, s2);
+    }
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    if (lane == 0) {
+        rm[wid] = m;
+        rs[wid] = s;
+    }
+    __syncthreads();
+    m = lane < nw ? rm[lane] : -INFINITY;
+    s = lane < nw ? rs[lane] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+        const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+        online_merge(m, s, m2, s2);
+    }
+    const float inv = 1.0f / (s + 1e-12f);
+    const float scale = (gscale ? gscale[0] : 1.0f) / (float)T;
+    const int y = tgt[row];
+    const float off = eps / (float)V;
+    float *gr = grad + (size_t)row * V;
+    for (int v = threadIdx.x; v < V; v += blockDim.x) {
+        const float sm = __expf(xr[v] - m) * inv;
+        const float tp = (v == y ? (1.0f - eps) : 0.f) + off;
+        gr[v] = (sm - tp) * scale;
+    }
+}
+
+// =================================================================== Adam
+// loss_optim.cuh:255-298: step = t+1, p -= lr*mhat/(sqrt(vhat)+eps) + lr*wd*p
+__global__ void adam_kernel(float *__restrict__ p, const float *__restrict__ g,
+                            float *__restrict__ m, float *__restrict__ v, int64_t n, float lr,
+                            float b1, float b2, float eps, float wd, float c1, float c2)
+{
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const float gr = g[i];
+        const float mi = b1 * m[i] + (1.0f - b1) * gr;
+        const float vi = b2 * v[i] + (1.0f - b2) * (gr * gr);
+        m[i] = mi;
+        v[i] = vi;
+        const float mh = mi / c1, vh = vi / c2;
+        const float pi = p[i];
+        p[i] = pi - lr * mh / (sqrtf(vh) + eps) - lr * wd * pi;
+    }
+}
+
+}  // namespace rows
+}  // namespace dc
+
+using namespace dc;
+using namespace dc::rows;
+
+static bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+extern "C" {
+
+int dc_layernorm_fwd(const float *x, const float *gamma, const float *beta, float *y, int R,
+                     int C, float eps, void *stream)
+{
+    clear_error();
+    if (R < 0 || C < 0) return fail(DC_ERR_INVALID, "negative shape");
+    if ((long long)R * C == 0) return DC_OK;
+    if (!x || !gamma || !beta || !y) return fail(DC_ERR_INVALID, "null pointer");
+    cudaStream_t st = as_stream(stream);
+    const bool vec = (C % 4 == 0) && aligned16(x) && aligned16(y) && aligned16(gamma) &&
+                     aligned16(beta);
+    const int wpb = 8;
+    const unsigned grid = (unsigned)((R + wpb - 1) / wpb);
+    if (vec && C <= 128)
+        ln_fwd_warp<1><<<grid, 32 * wpb, 0, st>>>(x, gamma, beta, y, R, C, eps);
+    else if (vec && C <= 256)
+        ln_fwd_warp<2><<<grid, 32 * wpb, 0, st>>>(x, gamma, beta, y, R, C, eps);
+    else if (vec && C <= 512)
+        ln_fwd_warp<4><<<grid, 32 * wpb, 0, st>>>(x, gamma, beta, y, R, C, eps);
+    else if (vec && C <= 1024)
+        ln_fwd_warp<8><<<grid, 32 * wpb, 0, st>>>(x, gamma, beta, y, R, C, eps);
+    else
+        ln_fwd_block<<<R, 256, 0, st>>>(x, gamma, beta, y, R, C, eps);
+    DC_CUDA_TRY(cudaGetLastError());
+    return DC_OK;
+}
+
+int dc_layernorm_bwd(const float *x, const float *gamma, const float *dy, float *dx,
+                     float *dgamma, float *dbeta, int R, int C, float eps, int accumulate,
+                     void *stream)
+{
+    clear_error();
+    if (R < 0 || C < 0) return fail(DC_ERR_INVALID, "negative shape");
+    if ((long long)R * C == 0) return DC_OK;
+    if (!x || !gamma || !dy || !dx || !dgamma || !dbeta)
+        return fail(DC_ERR_INVALID, "null pointer");
+    cudaStream_t st = as_stream(stream);
+    const bool vec = (C % 4 == 0) && aligned16(x) && aligned16(dy) && aligned16(dx) &&
+                     aligned16(gamma) && C <= 1024;
+    int nparts;
+    int rows_per_cta = 0;
+    const int wpb = 8;
+    if (vec) {
+        const int target = sm_count() * 4;
+        rows_per_cta = std::max(wpb, (R + target - 1) / target);
+        nparts = (R + rows_per_cta - 1) / rows_per_cta;
+    } else {
+        nparts = R;
+    }
+    float *part = nullptr;
+    DC_CUDA_TRY(cudaMallocAsync(&part, (size_t)nparts * 2 * C * sizeof(float), st));
+    const size_t shbytes = (size_t)wpb * 2 * C * sizeof(float);
+    int rc = DC_OK;
+    if (vec) {
+        if (C <= 128)
+            ln_bwd_warp<1><<<nparts, 32 * wpb, shbytes, st>>>(x, gamma, dy, dx, part, R, C, eps,
+                                                              accumulate, rows_per_cta);
+        else if (C <= 256)
+            ln_bwd_warp<2><<<nparts, 32 * wpb, shbytes, st>>>(x, gamma, dy, dx, part, R, C, eps,
+                                                              accumulate, rows_per_cta);
+        else if (C <= 512)
+            ln_bwd_warp<4><<<nparts, 32 * wpb, shbytes, st>>>(x, gamma, dy, dx, part, R, C, eps,
+                                                              accumulate, rows_per_cta);
+        else {
+            static bool attr = false;
+            if (!attr) {
+                cudaFuncSetAttribute(ln_bwd_warp<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)shbytes);
+                attr = true;
+            }
+            ln_bwd_warp<8><<<nparts, 32 * wpb, shbytes, st>>>(x, gamma, dy, dx, part, R, C, eps,
+                                                              accumulate, rows_per_cta);
+        }
+    } else {
+        ln_bwd_block<<<R, 256, 0, st>>>(x, gamma, dy, dx, part, R, C, eps, accumulate);
+    }
+    if (cudaGetLastError() != cudaSuccess) rc = fail(DC_ERR_CUDA, "layernorm bwd launch failed");
+    if (rc == DC_OK) {
+        colsum_parts<<<(2 * C + 255) / 256, 256, 0, st>>>(part, nparts, 2 * C, dgamma, dbeta, C,
+                                                          accumulate);
+        if (cudaGetLastError() != cudaSuccess)
+            rc = fail(DC_ERR_CUDA, "layernorm colsum launch failed");
+    }
+    cudaFreeAsync(part, st);
+    return rc;
+}
+
+int dc_bias_fwd(const float *a, const float *b, float *out, int M, int N, void *stream)
+{
+    clear_error();
+    if (M < 0 || N < 0) return fail(DC_ERR_INVALID, "negative shape");
+    if ((long long)M * N == 0) return DC_OK;
+    if (!a || !b || !out) return fail(DC_ERR_INVALID, "null pointer");
+    cudaStream_t st = as_stream(stream);
+    const size_t n = (size_t)M * N;
+    const int blocks = (int)std::min<size_t>((n + 1023) / 1024, (size_t)sm_count() * 8);
+    if (N % 4 == 0 && aligned16(a) && aligned16(b) && aligned16(out))
+        bias_fwd_vec<<<blocks, 256, 0, st>>>((const float4 *)a, (const float4 *)b, (float4 *)out,
+                                              n / 4, N / 4);
+    else
+        bias_fwd_scalar<<<blocks, 256, 0, st>>>(a, b, out, n, N);
+    DC_CUDA_TRY(cudaGetLastError());
+    return DC_OK;
+}
+
+int dc_bias_bwd(const float *dy, float *da, float *db, int M, int N, int accumulate,
+                void *stream)
+{
+    clear_error();
+    if (M < 0 || N < 0) return fail(DC_ERR_INVALID, "negative shape");
+    if ((long long)M * N == 0) return DC_OK;
+    if (!dy || !db) return fail(DC_ERR_INVALID, "null pointer");
+    cudaStream_t st = as_stream(stream);
+    const int cblocks = (N + 31) / 32;
+    const int target = std::max(1, sm_count() * 8 / cblocks);
+    const int rows_per_cta = std::max(8, (M + target - 1) / target);
+    const int rblocks = (M + rows_per_cta - 1) / rows_per_cta;
+    float *part = nullptr;
+    DC_CUDA_TRY(cudaMallocAsync(&part, (size_t)rblocks * N * sizeof(float), st));
+    bias_bwd_kernel<<<dim3(cblocks, rblocks), dim3(32, 8), 0, st>>>(dy, da, part, M, N,
+                                                                     rows_per_cta, accumulate);
+    colsum_parts<<<(N + 255) / 256, 256, 0, st>>>(part, rblocks, N, db, db, N, accumulate);
+    cudaError_t e = cudaGetLastError();
+    cudaFreeAsync(part, st);
+    if (e != cudaSuccess) return fail(DC_ERR_CUDA, "bias bwd: %s", cudaGetErrorString(e));
+    return DC_OK;
+}
+
+int dc_ce_fwd(const float *logits, const int32_t *targets, float *loss, float *row_loss, int T,
+              int V, float eps, void *stream)
+{
+    clear_error();
+    if (T < 0 || V <= 0) return fail(DC_ERR_INVALID, "bad shape T=%d V=%d", T, V);
+    if (T == 0) return DC_OK;
+    if (!logits || !targets || !loss) return fail(DC_ERR_INVALID, "null pointer");
+    cudaStream_t st = as_stream(stream);
+    float *rows = row_loss;
+    if (!rows) DC_CUDA_TRY(cudaMallocAsync(&rows, (size_t)T * sizeof(float), st));
+    if (V <= 1024)
+        ce_fwd_warp<<<(T + 7) / 8, 256, 0, st>>>(logits, targets, rows, T, V, eps);
+    else
+        ce_fwd_block<<<T, 256, 0, st>>>(logits, targets, rows, T, V, eps);
+    mean_kernel<<<1, 1024, 0, st>>>(rows, T, loss);
+    cudaError_t e = cudaGetLastError();
+    if (!row_loss) cudaFreeAsync(rows, st);
+    if (e != cudaSuccess) return fail(DC_ERR_CUDA, "ce fwd: %s", cudaGetErrorString(e));
+    return DC_OK;
+}
+
+int dc_ce_bwd(const float *logits, const int32_t *targets, const float *grad_scale,
+              float *dlogits, int T, int V, float eps, void *stream)
+{
+    clear_error();
+    if (T < 0 || V <= 0) return fail(DC_ERR_INVALID, "bad shape T=%d V=%d", T, V);
+    if (T == 0) return DC_OK;
+    if (!logits || !targets || !dlogits) return fail(DC_ERR_INVALID, "null pointer");
+    cudaStream_t st = as_stream(stream);
+    if (V <= 1024)
+        ce_bwd_warp<<<(T + 7) / 8, 256, 0, st>>>(logits, targets, grad_scale, dlogits, T, V, eps);
+    else
+        ce_bwd_block<<<T, 256, 0, st>>>(logits, targets, grad_scale, dlogits, T, V, eps);
+    DC_CUDA_TRY(cudaGetLastError());
+    return DC_OK;
+}
+
+int dc_adam_step(float *p, const float *g, float *m, float *v, int64_t n, int t, float lr,
+                 float b1, float b2, float eps, float weight_decay, void *stream)
+{
+    clear_error();
+    if (n < 0) return fail(DC_ERR_INVALID, "negative size");
+    if (n == 0) return DC_OK;
+    if (!p || !g || !m || !v) return fail(DC_ERR_INVALID, "null pointer");
+    const float step = (float)t + 1.0f;
+    const float c1 = 1.0f - powf(b1, step), c2 = 1.0f - powf(b2, step);
+    const int blocks = (int)std::min<int64_t>((n + 255) / 256, (int64_t)sm_count() * 8);
+    adam_kernel<<<blocks, 256, 0, as_stream(stream)>>>(p, g, m, v, n, lr, b1, b2, eps,
+                                                       weight_decay, c1, c2);
+    DC_CUDA_TRY(cudaGetLastError());
+    return DC_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,212 @@
+"""PyTorch-facing calls of the batched C ABI (``dc_*`` entry points).
+
+PyTorch supplies device memory and the current CUDA stream only; every
+computation runs in ``libmat_mul.so``.  All tensors must be CUDA tensors.
+
+AFT-full operator (reference: native/src/kernels/attention.cuh:6-40 forward,
+native/src/engine.cu:522-590 backward), batched over B sequences that share
+the pairwise bias ``w``:
+
+    Z = aft_fwd(Q, K, V, w, causal=True)
+    dQ, dK, dV, dW = aft_bwd(Q, K, V, w, dZ, causal=True)
+"""
+from __future__ import annotations
+
+from ctypes import byref, c_int, c_size_t
+
+import torch
+
+from ._lib import (DC_AFT_ACCUMULATE, DC_AFT_CAUSAL, DC_AFT_COMPUTE_BF16, DC_AFT_SIMT,
+                   DC_AFT_WS_VALID, DC_BF16, DC_F32, DcError, check, lib)
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _dtype_code(t: torch.Tensor) -> int:
+    if t.dtype == torch.float32:
+        return DC_F32
+    if t.dtype == torch.bfloat16:
+        return DC_BF16
+    raise DcError(f"unsupported dtype {t.dtype}")
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def _need(t: torch.Tensor, name: str, rows_strided=False):
+    if not t.is_cuda:
+        raise DcError(f"{name} must be a CUDA tensor")
+    if rows_strided:
+        if t.dim() != 2 or t.stride(1) != 1:
+            raise DcError(f"{name} must be 2-D with unit column stride")
+    elif not t.is_contiguous():
+        raise DcError(f"{name} must be contiguous")
+
+
+def _as3d(t: torch.Tensor) -> torch.Tensor:
+    return t.unsqueeze(0) if t.dim() == 2 else t
+
+
+class AftWorkspace:
+    """Device scratch for one AFT shape: the operand panels (A', E'V, E'),
+    the row/column maxima and the backward's g/n panels.  A workspace filled
+    by ``aft_fwd`` can be handed to ``aft_bwd`` with ``ws_valid=True`` so the
+    backward skips recomputing the panels."""
+
+    def __init__(self, B, Tq, Tk, D, dtype: torch.dtype, flags: int = 0, device=None):
+        n = c_size_t(0)
+        code = DC_F32 if dtype == torch.float32 else DC_BF16
+        check(lib().dc_aft_workspace_size(B, Tq, Tk, D, code, flags, byref(n)), "dc_aft_workspace_size")
+        self.nbytes = int(n.value)
+        self._buf = torch.empty(self.nbytes + 1024, dtype=torch.uint8, device=device or "cuda")
+        base = self._buf.data_ptr()
+        self.ptr = (base + 1023) // 1024 * 1024
+
+
+def _flags(causal, accumulate=False, ws_valid=False, simt=False, compute_bf16=False):
+    f = 0
+    if causal:
+        f |= DC_AFT_CAUSAL
+    if accumulate:
+        f |= DC_AFT_ACCUMULATE
+    if ws_valid:
+        f |= DC_AFT_WS_VALID
+    if simt:
+        f |= DC_AFT_SIMT
+    if compute_bf16:
+        f |= DC_AFT_COMPUTE_BF16
+    return f
+
+
+def aft_fwd(Q, K, V, w, causal=True, out=None, workspace: AftWorkspace | None = None,
+            ws_valid=False, simt=False, compute_bf16=False):
+    Q3, K3, V3 = _as3d(Q), _as3d(K), _as3d(V)
+    for t, n in ((Q3, "Q"), (K3, "K"), (V3, "V")):
+        _need(t, n)
+    _need(w, "w", rows_strided=True)
+    B, Tq, D = Q3.shape
+    Tk = K3.shape[1]
+    if w.dtype != torch.float32 or w.dim() != 2:
+        raise DcError("w must be a 2-D float32 tensor")
+    Z = torch.empty_like(Q) if out is None else out
+    ws = workspace.ptr if workspace is not None else None
+    nb = workspace.nbytes if workspace is not None else 0
+    flags = _flags(causal, ws_valid=ws_valid, simt=simt, compute_bf16=compute_bf16)
+    check(lib().dc_aft_fwd(Q3.data_ptr(), K3.data_ptr(), V3.data_ptr(), w.data_ptr(), w.stride(0),
+                           Z.data_ptr(), B, Tq, Tk, D, _dtype_code(Q3), flags, ws, nb, _stream()),
+          "dc_aft_fwd")
+    return Z
+
+
+def aft_bwd(Q, K, V, w, dZ, causal=True, grads=None, accumulate=False,
+            workspace: AftWorkspace | None = None, ws_valid=False, simt=False, compute_bf16=False):
+    Q3, K3, V3, G3 = _as3d(Q), _as3d(K), _as3d(V), _as3d(dZ)
+    for t, n in ((Q3, "Q"), (K3, "K"), (V3, "V"), (G3, "dZ")):
+        _need(t, n)
+    _need(w, "w", rows_strided=True)
+    B, Tq, D = Q3.shape
+    Tk = K3.shape[1]
+    if grads is None:
+        grads = (torch.empty_like(Q), torch.empty_like(K), torch.empty_like(V),
+                 torch.empty(w.shape[0], w.stride(0), device=w.device)[:, : w.shape[1]])
+    dQ, dK, dV, dW = grads
+    if dW.dtype != torch.float32 or dW.stride(0) != w.stride(0) or dW.stride(1) != 1:
+        raise DcError("dW must be float32 with the row stride of w")
+    ws = workspace.ptr if workspace is not None else None
+    nb = workspace.nbytes if workspace is not None else 0
+    flags = _flags(causal, accumulate, ws_valid, simt, compute_bf16)
+    check(lib().dc_aft_bwd(Q3.data_ptr(), K3.data_ptr(), V3.data_ptr(), w.data_ptr(), w.stride(0),
+                           G3.data_ptr(), dQ.data_ptr(), dK.data_ptr(), dV.data_ptr(), dW.data_ptr(),
+                           B, Tq, Tk, D, _dtype_code(Q3), flags, ws, nb, _stream()),
+          "dc_aft_bwd")
+    return dQ, dK, dV, dW
+
+
+def device_status(sync_stream=True) -> int:
+    """Synchronise and return the device status bits (0 = no kernel gave up a
+    bounded wait); raises DcError when bits are set."""
+    bits = c_int(0)
+    check(lib().dc_device_status(_stream(), byref(bits)), "dc_device_status")
+    return bits.value
+
+
+# ---------------------------------------------------------------- row ops
+def layernorm_fwd(x, gamma, beta, eps=1e-5, out=None):
+    R, C = x.shape
+    y = torch.empty_like(x) if out is None else out
+    check(lib().dc_layernorm_fwd(x.data_ptr(), gamma.data_ptr(), beta.data_ptr(), y.data_ptr(), R, C,
+                                 eps, _stream()), "dc_layernorm_fwd")
+    return y
+
+
+def layernorm_bwd(x, gamma, dy, eps=1e-5, grads=None, accumulate=False):
+    R, C = x.shape
+    if grads is None:
+        grads = (torch.empty_like(x), torch.empty(C, device=x.device), torch.empty(C, device=x.device))
+    dx, dg, db = grads
+    check(lib().dc_layernorm_bwd(x.data_ptr(), gamma.data_ptr(), dy.data_ptr(), dx.data_ptr(),
+                                 dg.data_ptr(), db.data_ptr(), R, C, eps, int(accumulate), _stream()),
+          "dc_layernorm_bwd")
+    return dx, dg, db
+
+
+def bias_fwd(a, b, out=None):
+    M, N = a.shape
+    y = torch.empty_like(a) if out is None else out
+    check(lib().dc_bias_fwd(a.data_ptr(), b.data_ptr(), y.data_ptr(), M, N, _stream()), "dc_bias_fwd")
+    return y
+
+
+def bias_bwd(dy, grads=None, accumulate=False):
+    M, N = dy.shape
+    if grads is None:
+        grads = (torch.empty_like(dy), torch.empty(N, device=dy.device))
+    da, db = grads
+    check(lib().dc_bias_bwd(dy.data_ptr(), _ptr(da), db.data_ptr(), M, N, int(accumulate), _stream()),
+          "dc_bias_bwd")
+    return da, db
+
+
+def ce_fwd(logits, targets, eps=0.1, row_loss=None):
+    T, V = logits.shape
+    loss = torch.empty(1, device=logits.device)
+    check(lib().dc_ce_fwd(logits.data_ptr(), targets.data_ptr(), loss.data_ptr(), _ptr(row_loss), T, V,
+                          eps, _stream()), "dc_ce_fwd")
+    return loss
+
+
+def ce_bwd(logits, targets, grad_scale=None, eps=0.1, out=None):
+    T, V = logits.shape
+    g = torch.empty_like(logits) if out is None else out
+    check(lib().dc_ce_bwd(logits.data_ptr(), targets.data_ptr(), _ptr(grad_scale), g.data_ptr(), T, V,
+                          eps, _stream()), "dc_ce_bwd")
+    return g
+
+
+def adam_step(p, g, m, v, t, lr, b1=0.9, b2=0.999, eps=1e-8, weight_decay=0.001):
+    check(lib().dc_adam_step(p.data_ptr(), g.data_ptr(), m.data_ptr(), v.data_ptr(), p.numel(), int(t),
+                             lr, b1, b2, eps, weight_decay, _stream()), "dc_adam_step")
+
+
+# ---------------------------------------------------------------- timing
+def profile_enable(on: bool = True) -> None:
+    """Bracket every library kernel launch with CUDA events (drops old records)."""
+    check(lib().dc_profile_enable(int(on)), "dc_profile_enable")
+
+
+def profile_read(max_entries: int = 64) -> dict:
+    """{kernel name: (total ms, launches)} of the launches recorded so far."""
+    import ctypes
+
+    names = ctypes.create_string_buffer(64 * max_entries)
+    ms = (ctypes.c_float * max_entries)()
+    cnt = (c_int * max_entries)()
+    n = lib().dc_profile_read(names, ms, cnt, max_entries)
+    out = {}
+    for k in range(min(n, max_entries)):
+        name = names.raw[64 * k: 64 * (k + 1)].split(b"\0", 1)[0].decode()
+        out[name] = (float(ms[k]), int(cnt[k]))
+    return out

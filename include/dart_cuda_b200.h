@@ -1,0 +1,162 @@
+/*
+ * dart_cuda_b200 — C ABI of libmat_mul.so, a B200 (sm_100a) implementation
+ * of G-Tensor's AFT-full training hot path.
+ *
+ * Two layers of entry points live in the same shared library:
+ *
+ *  1. The reference's own handle-based ABI (section "legacy"), with the same
+ *     symbol names, argument order and semantics as the reference engine
+ *     (native/src/engine.cu), so the reference's Dart FFI bridge
+ *     (lib/core/tensor/cuda_engine.dart:316-425) and Python ctypes bridge
+ *     (python/dart_cuda/core/tensor/cuda_engine.py:92-199) bind it unchanged.
+ *     Handles are opaque pointers to engine-owned fp32 tensors with a grad
+ *     buffer and an autograd closure; `backward(root)` runs the tape.
+ *
+ *  2. Batched raw-pointer entry points (prefix dc_) with explicit shapes, a
+ *     dtype, a CUDA stream and an int status (0 = DC_OK).  They take device
+ *     pointers, never allocate on the caller's behalf unless workspace is
+ *     NULL, and never synchronise the device.
+ *
+ * All pointers passed to dc_ functions are device pointers unless stated.
+ */
+#ifndef DART_CUDA_B200_H
+#define DART_CUDA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+#include <stdbool.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------ status */
+#define DC_OK 0
+#define DC_ERR_INVALID 1       /* bad argument (shape, pointer, alignment)   */
+#define DC_ERR_CUDA 2          /* a CUDA runtime/driver call failed          */
+#define DC_ERR_UNSUPPORTED 3   /* valid request this build does not handle   */
+#define DC_ERR_NOMEM 4         /* allocation failed or workspace too small   */
+#define DC_ERR_DEVICE 5        /* a kernel reported a bounded-wait timeout   */
+
+/* dtypes of the user-facing tensors */
+#define DC_F32 0
+#define DC_BF16 1
+
+/* flags of the AFT entry points */
+#define DC_AFT_CAUSAL 0x1        /* mask i > t (the reference's masked=true)   */
+#define DC_AFT_ACCUMULATE 0x2    /* dQ/dK/dV/dW += instead of =                 */
+#define DC_AFT_WS_VALID 0x4      /* workspace already holds this call's prep   */
+#define DC_AFT_SIMT 0x8          /* CUDA-core contraction (cross-check path)   */
+#define DC_AFT_COMPUTE_BF16 0x10 /* f32 tensors, bf16 tensor-core operands     */
+
+/* Message of the last failing call on this host thread ("" if none). */
+const char *dc_last_error(void);
+
+/* Synchronise `stream`, read and clear the device status word of the current
+ * device.  Returns DC_OK, DC_ERR_DEVICE (a kernel gave up a bounded wait; the
+ * bits are stored in *bits when non-NULL) or DC_ERR_CUDA. */
+int dc_device_status(void *stream, int *bits);
+
+/* Library version string. */
+const char *dc_version(void);
+
+/* Kernel timing.  dc_profile_enable(1) brackets every kernel the library
+ * launches with CUDA events on the launch stream (0 turns it off; both drop
+ * earlier records).  dc_profile_read synchronises those events and writes, per
+ * distinct kernel name, the name (64-byte slots in `names`), the summed
+ * milliseconds and the launch count; it returns the number of kernels. */
+int dc_profile_enable(int on);
+int dc_profile_read(char *names, float *total_ms, int *counts, int max_entries);
+
+/* ---------------------------------------------------------- AFT-full op
+ * Z[b,t,:] = sigmoid(Q[b,t,:]) * sum_{i in S(t)} e^{K[b,i,:]+w[t,i]} V[b,i,:]
+ *                               / sum_{i in S(t)} e^{K[b,i,:]+w[t,i]}
+ * with S(t) = {i <= t} when DC_AFT_CAUSAL (Tq == Tk required), else all i<Tk.
+ * Q, Z, dZ, dQ: [B, Tq, D]; K, V, dK, dV: [B, Tk, D]; contiguous, `dtype`.
+ * w, dW: fp32, Tq rows of row stride ldw >= Tk (w[t*ldw + i]); w is shared
+ * by the batch and dW is the sum over the batch.
+ *
+ * Replaces: aft_full_fwd (native/src/kernels/attention.cuh:6-40),
+ * aft_full_bwd (native/src/engine.cu:522-590), aft_cross_fwd/bwd
+ * (native/src/kernels/attention.cuh:41-128), batched over B sequences.
+ */
+int dc_aft_workspace_size(int B, int Tq, int Tk, int D, int dtype, int flags, size_t *bytes);
+
+int dc_aft_fwd(const void *Q, const void *K, const void *V, const float *w, int ldw, void *Z,
+               int B, int Tq, int Tk, int D, int dtype, int flags, void *workspace,
+               size_t workspace_bytes, void *stream);
+
+int dc_aft_bwd(const void *Q, const void *K, const void *V, const float *w, int ldw,
+               const void *dZ, void *dQ, void *dK, void *dV, float *dW, int B, int Tq, int Tk,
+               int D, int dtype, int flags, void *workspace, size_t workspace_bytes,
+               void *stream);
+
+/* ------------------------------------------------- row-wise training ops
+ * Affine LayerNorm over the last dim.  Replaces layernorm_fwd/bwd
+ * (native/src/kernels/layernorm_embed.cuh:140-240).  x, y, dy, dx: [R, C]
+ * fp32; gamma, beta, dgamma, dbeta: [C].  Backward accumulates into dx,
+ * dgamma, dbeta when `accumulate` != 0 (the reference always accumulates).
+ * dc_layernorm_bwd needs R*2 floats of workspace for the per-row partial
+ * parameter gradients only when workspace is non-NULL; with NULL it
+ * allocates stream-ordered scratch. */
+int dc_layernorm_fwd(const float *x, const float *gamma, const float *beta, float *y, int R,
+                     int C, float eps, void *stream);
+int dc_layernorm_bwd(const float *x, const float *gamma, const float *dy, float *dx,
+                     float *dgamma, float *dbeta, int R, int C, float eps, int accumulate,
+                     void *stream);
+
+/* Row-broadcast bias add out[i,j] = a[i,j] + b[j] and its backward
+ * (da += dy, db += column sums).  Replaces add_row_broadcast_fwd/bwd
+ * (native/src/kernels/elementwise.cuh:64-89). */
+int dc_bias_fwd(const float *a, const float *b, float *out, int M, int N, void *stream);
+int dc_bias_bwd(const float *dy, float *da, float *db, int M, int N, int accumulate,
+                void *stream);
+
+/* Label-smoothed cross-entropy with fused log-softmax.  Replaces
+ * cross_entropy_fwd_hyper/bwd_hyper + ce_mean_reduce
+ * (native/src/kernels/loss_optim.cuh:163-244, native/src/engine.cu:825-877).
+ * logits [T, V] fp32, targets [T] int32 (device).  fwd writes the mean loss
+ * to loss[0] (and the per-row losses to row_loss when non-NULL).  bwd
+ * WRITES dlogits = (softmax - ((1-eps)1_y + eps/V)) * g / T, where g is read
+ * from the device scalar grad_scale when non-NULL, else g = 1. */
+int dc_ce_fwd(const float *logits, const int32_t *targets, float *loss, float *row_loss, int T,
+              int V, float eps, void *stream);
+int dc_ce_bwd(const float *logits, const int32_t *targets, const float *grad_scale,
+              float *dlogits, int T, int V, float eps, void *stream);
+
+/* AdamW exactly as the reference applies it (step = t+1, decoupled weight
+ * decay p -= lr*wd*p with wd = 0.001 in the reference).  Replaces
+ * adam_kernel (native/src/kernels/loss_optim.cuh:255-298). */
+int dc_adam_step(float *p, const float *g, float *m, float *v, int64_t n, int t, float lr,
+                 float b1, float b2, float eps, float weight_decay, void *stream);
+
+/* ------------------------------------------------------------------ legacy
+ * The reference's handle ABI (native/src/engine.cu).  Every returned handle
+ * is owned by the caller and released with destroy_tensor; op outputs keep
+ * their inputs alive for backward.  Calls run on the library's stream and
+ * return after device work is ordered; host copies synchronise. */
+void *create_tensor(int rows, int cols, float *host_data);           /* engine.cu:93  */
+void destroy_tensor(void *h);                                          /* engine.cu:100 */
+void get_tensor_data(void *h, float *host_out);                        /* engine.cu:123 */
+void get_tensor_grad(void *h, float *host_out);                        /* engine.cu:128 */
+void tensor_to_host(void *h, float *host_out);                         /* engine.cu:879 */
+void set_tensor_data(void *h, float *host_in);                         /* engine.cu:939 */
+void zero_grad(void *h);                                               /* engine.cu:133 */
+void tensor_step(void *h, float lr);                                   /* engine.cu:138 */
+void backward(void *root);                                             /* engine.cu:145 */
+void *aft_forward(void *Q, void *K, void *V, void *WB, bool masked);   /* engine.cu:592 */
+void *aft_cross_forward(void *Q, void *K, void *V, void *WB);          /* engine.cu:616 */
+void *layernorm_forward(void *x, void *gamma, void *beta, float eps);  /* engine.cu:766 */
+void *add_tensor_row_broadcast(void *a, void *b);                      /* engine.cu:352 */
+void *cross_entropy_loss(void *logits, int32_t *host_targets, int32_t T, int32_t V); /* engine.cu:839 */
+void adam_step(void *p, void *m, void *v, int32_t t, float lr, float b1, float b2,
+               float eps);                                             /* engine.cu:887 */
+void *add_tensors(void *a, void *b);                                   /* engine.cu:318 */
+void *mul_tensors(void *a, void *b);                                   /* engine.cu:392 */
+void *sum_tensor(void *a);                                             /* engine.cu:1141 */
+void *mean_tensor(void *a);                                            /* engine.cu:1168 */
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* DART_CUDA_B200_H */

@@ -1,0 +1,194 @@
+"""AFT-full forward/backward on the GPU against the CPU oracle.
+
+Parity metric: normwise relative error max|got - ref| / max|ref|, per output.
+Tolerances (from the operator's spec): 1e-3 with fp32 tensors (TF32 tensor-core
+operands), 1e-2 with bf16 tensors.  bf16 cases compare against the oracle run
+on the bf16-rounded inputs.
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+TOL = {torch.float32: 1e-3, torch.bfloat16: 1e-2}
+
+
+@pytest.fixture(scope="module")
+def dev():
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    return torch.device("cuda:0")
+
+
+@pytest.fixture(scope="module")
+def ops():
+    from dart_cuda_b200 import ops as _ops
+
+    return _ops
+
+
+def relerr(got, ref):
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    return float(np.max(np.abs(got - ref)) / max(np.max(np.abs(ref)), 1e-30))
+
+
+def make_inputs(seed, B, Tq, Tk, D, wscale=0.02):
+    rng = np.random.default_rng(seed)
+    Q = rng.standard_normal((B, Tq, D)).astype(np.float32)
+    K = rng.standard_normal((B, Tk, D)).astype(np.float32)
+    V = rng.standard_normal((B, Tk, D)).astype(np.float32)
+    W = (wscale * rng.standard_normal((Tq, Tk))).astype(np.float32)
+    dZ = rng.standard_normal((B, Tq, D)).astype(np.float32)
+    return Q, K, V, W, dZ
+
+
+def to_dev(dev, dtype, *arrs):
+    return [torch.from_numpy(a).to(dev).to(dtype) for a in arrs]
+
+
+def rounded(dtype, *arrs):
+    """The inputs as the kernel sees them (bf16-rounded when dtype is bf16)."""
+    return [torch.from_numpy(a).to(dtype).float().numpy() for a in arrs]
+
+
+def oracle_ref(Q, K, V, W, dZ, causal):
+    B, Tq, D = Q.shape
+    Tk = K.shape[1]
+    if causal or Tq == Tk:
+        Z = oracle.aft_full_fwd(Q, K, V, W, causal)
+        g = oracle.aft_full_bwd(Q, K, V, W, dZ, causal)
+        return (Z,) + tuple(g)
+    Z = np.stack([oracle.aft_cross_fwd(Q[b], K[b], V[b], W) for b in range(B)])
+    gs = [oracle.aft_cross_bwd(Q[b], K[b], V[b], W, dZ[b]) for b in range(B)]
+    dQ = np.stack([g[0] for g in gs]); dK = np.stack([g[1] for g in gs]); dV = np.stack([g[2] for g in gs])
+    dW = sum(g[3] for g in gs)
+    return Z, dQ, dK, dV, dW
+
+
+def run_case(ops, dev, seed, B, Tq, Tk, D, causal, dtype=torch.float32, wscale=0.02, **kw):
+    Q, K, V, W, dZ = make_inputs(seed, B, Tq, Tk, D, wscale)
+    tq, tk, tv, tg = to_dev(dev, dtype, Q, K, V, dZ)
+    tw = torch.from_numpy(W).to(dev)
+    Z = ops.aft_fwd(tq, tk, tv, tw, causal=causal, **kw)
+    grads = ops.aft_bwd(tq, tk, tv, tw, tg, causal=causal, **kw)
+    assert ops.device_status() == 0
+    Qr, Kr, Vr, dZr = rounded(dtype, Q, K, V, dZ)
+    ref = oracle_ref(Qr, Kr, Vr, W, dZr, causal)
+    got = (Z,) + tuple(grads)
+    errs = {n: relerr(g.float().cpu().numpy(), r) for n, g, r in zip(("Z", "dQ", "dK", "dV", "dW"), got, ref)}
+    return errs
+
+
+def assert_errs(errs, tol):
+    bad = {k: v for k, v in errs.items() if not v < tol}
+    assert not bad, f"over tolerance {tol}: {bad} (all: {errs})"
+
+
+# ----------------------------------------------------------- fp32 (TF32 MMA)
+@pytest.mark.parametrize("simt", [False, True])
+def test_c1_fp32_causal(ops, dev, simt):
+    """B=4, T=64, d=128 fp32, w ~ N(0, 0.02): the reference's own CPU-sized case."""
+    assert_errs(run_case(ops, dev, 1, 4, 64, 64, 128, True, simt=simt), 1e-3)
+
+
+@pytest.mark.parametrize("B,T,D", [(1, 1, 1), (3, 7, 5), (2, 130, 24), (1, 300, 136), (2, 256, 256)])
+def test_ragged_fp32_causal(ops, dev, B, T, D):
+    assert_errs(run_case(ops, dev, 2, B, T, T, D, True, wscale=0.5), 1e-3)
+
+
+@pytest.mark.parametrize("B,T,D", [(1, 33, 9), (2, 200, 64)])
+def test_full_fp32_noncausal(ops, dev, B, T, D):
+    assert_errs(run_case(ops, dev, 3, B, T, T, D, False, wscale=0.5), 1e-3)
+
+
+@pytest.mark.parametrize("Tq,Tk,D", [(9, 5, 12), (16, 1, 8), (130, 70, 40)])
+def test_cross_fp32(ops, dev, Tq, Tk, D):
+    assert_errs(run_case(ops, dev, 4, 2, Tq, Tk, D, False, wscale=0.3), 1e-3)
+
+
+def test_fp32_with_bf16_operands(ops, dev):
+    assert_errs(run_case(ops, dev, 5, 2, 128, 128, 128, True, compute_bf16=True), 1e-2)
+
+
+# ----------------------------------------------------------- bf16
+@pytest.mark.parametrize("simt", [False, True])
+def test_bf16_causal(ops, dev, simt):
+    assert_errs(run_case(ops, dev, 6, 4, 256, 256, 256, True, dtype=torch.bfloat16, simt=simt), 1e-2)
+
+
+def test_c2_bf16_full_size(ops, dev):
+    """B=32, T=512, d=512 bf16 operands / fp32 accumulate, against the oracle."""
+    assert_errs(run_case(ops, dev, 7, 32, 512, 512, 512, True, dtype=torch.bfloat16), 1e-2)
+
+
+def test_bf16_ragged(ops, dev):
+    assert_errs(run_case(ops, dev, 8, 3, 100, 100, 72, True, dtype=torch.bfloat16, wscale=0.5), 1e-2)
+
+
+# ----------------------------------------------------------- semantics
+def test_accumulate_and_workspace_reuse(ops, dev):
+    B, T, D = 2, 96, 64
+    Q, K, V, W, dZ = make_inputs(9, B, T, T, D)
+    tq, tk, tv, tg = to_dev(dev, torch.float32, Q, K, V, dZ)
+    tw = torch.from_numpy(W).to(dev)
+    ws = ops.AftWorkspace(B, T, T, D, torch.float32, flags=1)
+    Z = ops.aft_fwd(tq, tk, tv, tw, causal=True, workspace=ws)
+    g1 = ops.aft_bwd(tq, tk, tv, tw, tg, causal=True, workspace=ws, ws_valid=True)
+    g1 = [x.clone() for x in g1]
+    g2 = ops.aft_bwd(tq, tk, tv, tw, tg, causal=True, grads=[x.clone() for x in g1], accumulate=True)
+    for a, b in zip(g1, g2):
+        torch.testing.assert_close(b, 2 * a, rtol=1e-5, atol=1e-6)
+    Z2 = ops.aft_fwd(tq, tk, tv, tw, causal=True)
+    torch.testing.assert_close(Z, Z2, rtol=0, atol=0)
+
+
+def test_deterministic_forward(ops, dev):
+    Q, K, V, W, _ = make_inputs(10, 2, 256, 256, 128)
+    tq, tk, tv = to_dev(dev, torch.bfloat16, Q, K, V)
+    tw = torch.from_numpy(W).to(dev)
+    a = ops.aft_fwd(tq, tk, tv, tw)
+    b = ops.aft_fwd(tq, tk, tv, tw)
+    assert torch.equal(a, b)
+
+
+def test_ldw_stride(ops, dev):
+    """w with a row stride wider than Tk (the reference's [maxSeqLen]^2 bias)."""
+    B, T, D, Tmax = 2, 40, 32, 64
+    Q, K, V, _, dZ = make_inputs(11, B, T, T, D)
+    rng = np.random.default_rng(12)
+    Wbig = (0.3 * rng.standard_normal((Tmax, Tmax))).astype(np.float32)
+    tq, tk, tv, tg = to_dev(dev, torch.float32, Q, K, V, dZ)
+    twb = torch.from_numpy(Wbig).to(dev)
+    tw = twb[:T, :T]  # row stride Tmax
+    Z = ops.aft_fwd(tq, tk, tv, tw)
+    dW = torch.zeros_like(twb)
+    grads = (torch.empty_like(tq), torch.empty_like(tk), torch.empty_like(tv), dW[:T, :T])
+    ops.aft_bwd(tq, tk, tv, tw, tg, grads=grads)
+    W = np.ascontiguousarray(Wbig[:T, :T])
+    Zr = oracle.aft_full_fwd(Q, K, V, W, True)
+    gr = oracle.aft_full_bwd(Q, K, V, W, dZ, True)
+    assert relerr(Z.cpu().numpy(), Zr) < 1e-3
+    assert relerr(dW[:T, :T].cpu().numpy(), gr[3]) < 1e-3
+    assert float(dW[T:].abs().max()) == 0.0 and float(dW[:, T:].abs().max()) == 0.0
+
+
+def test_empty_batch_is_noop(ops, dev):
+    z = torch.empty(0, 16, 8, device=dev)
+    w = torch.zeros(16, 16, device=dev)
+    out = ops.aft_fwd(z, z, z, w)
+    assert out.shape == (0, 16, 8)
+
+
+def test_rejects_bad_shapes(ops, dev):
+    from dart_cuda_b200 import DcError
+
+    q = torch.zeros(1, 8, 4, device=dev)
+    k = torch.zeros(1, 6, 4, device=dev)
+    w = torch.zeros(8, 6, device=dev)
+    with pytest.raises(DcError):
+        ops.aft_fwd(q, k, k, w, causal=True)  # causal needs Tq == Tk
+    with pytest.raises(DcError):
+        ops.aft_fwd(q, q, q, torch.zeros(8, 4, device=dev), causal=False)  # ldw < Tk
