@@ -87,7 +87,8 @@ struct Params {
     int ldw;
     const float *m;   // [Tqp]
     const float *c;   // [B][dp]
-    void *G1, *G2;    // [B][Tqp][dp] operand precision
+    void *G1, *G2;    // g and n = -g*r, [B][Tqp][dp] operand precision
+    void *G1l, *G2l;  // their rounding residuals (g - G1, n - G2), same layout
     int *status;
 };
 
@@ -121,9 +122,15 @@ __device__ __forceinline__ void epi_bwd1(const Params &p, int b, int t, int d, f
         g = dz * s / den;
         n = -g * r;
     }
+    // hi/lo split: the dW contraction sums g*E'V + n*E' over d, which cancel
+    // where V ~ r; rounding g and n alone would leave an error of the
+    // operand precision times |g E' V| there, so the residuals are kept too.
     size_t go = ((size_t)b * p.Tqp + t) * p.dp + d;
-    ((E *)p.G1)[go] = to_op<E>(g);
-    ((E *)p.G2)[go] = to_op<E>(n);
+    const E gh = to_op<E>(g), nh = to_op<E>(n);
+    ((E *)p.G1)[go] = gh;
+    ((E *)p.G2)[go] = nh;
+    ((E *)p.G1l)[go] = to_op<E>(g - from_op(gh));
+    ((E *)p.G2l)[go] = to_op<E>(n - from_op(nh));
 }
 
 template <class IO>
@@ -310,7 +317,9 @@ __global__ void aft_simt_kernel(const Params p, const E *__restrict__ Ap,
             for (int d = 0; d < p.dp; ++d) {
                 const size_t og = ((size_t)b * p.Tqp + t) * p.dp + d;
                 const size_t op = ((size_t)b * p.Tkp + i) * p.dp + d;
-                acc += from_op(G1[og]) * from_op(PV[op]) + from_op(G2[og]) * from_op(PE[op]);
+                const float gg = from_op(G1[og]) + from_op(((const E *)p.G1l)[og]);
+                const float nn = from_op(G2[og]) + from_op(((const E *)p.G2l)[og]);
+                acc += gg * from_op(PV[op]) + nn * from_op(PE[op]);
             }
         epi_wgrad(p, t, i, acc);
     }
@@ -327,13 +336,19 @@ struct TcCfg {
     static constexpr int BOX_MN = 128 / (int)sizeof(E);// elements in one 128 B MN block
     static constexpr int A_BYTES = BM * 128;
     static constexpr int B_BYTES = BN * 128;
-    static constexpr int STAGE_BYTES = 2 * A_BYTES + (W ? 2 : 1) * B_BYTES;
-    static constexpr int STAGES = W ? 3 : 4;
+    static constexpr int NA = W ? 4 : 2;               // A tiles per stage (WGRAD: g, n, g lo, n lo)
+    static constexpr int NB = W ? 2 : 1;               // B tiles per stage
+    static constexpr int STAGE_BYTES = NA * A_BYTES + NB * B_BYTES;
+    static constexpr int STAGES = W ? 2 : 4;
     static constexpr uint32_t TMEM_COLS = W ? 128 : 256;
     static constexpr uint32_t A_MN = W ? 0 : 1;
     static constexpr uint32_t B_MN = MODE == HGRAD ? 1 : 0;
     static constexpr uint32_t IDESC = umma_idesc(TF32 ? 2u : 1u, BM, BN, A_MN, B_MN);
     static constexpr uint32_t MN_LBO = BKe * 128;      // bytes between MN blocks
+    // MN-major swizzle: 16 B atoms / 8-row groups (bf16) or 32 B atoms / 4-row
+    // groups (tf32); K-major tiles always use 16 B atoms / 8-row groups.
+    static constexpr uint32_t MN_LAYOUT = TF32 ? 1u : 2u;
+    static constexpr uint32_t MN_SBO = TF32 ? 512u : 1024u;
     static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
 };
 
@@ -358,7 +373,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     aft_tc_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtensorMap mapA1,
                   const __grid_constant__ CUtensorMap mapA2,
                   const __grid_constant__ CUtensorMap mapB1,
-                  const __grid_constant__ CUtensorMap mapB2)
+                  const __grid_constant__ CUtensorMap mapB2,
+                  const __grid_constant__ CUtensorMap mapA3,
+                  const __grid_constant__ CUtensorMap mapA4)
 {
     using C = TcCfg<MODE, E>;
     extern __shared__ uint8_t smem_raw[];
@@ -408,7 +425,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_prefetch(&mapA1);
         tma_prefetch(&mapA2);
         tma_prefetch(&mapB1);
-        if (C::W) tma_prefetch(&mapB2);
+        if (C::W) {
+            tma_prefetch(&mapB2);
+            tma_prefetch(&mapA3);
+            tma_prefetch(&mapA4);
+        }
     }
     if (warp == 5) {
         tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
@@ -454,11 +475,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 } else {
                     const int bb = kk / p.kpb, kd = kk % p.kpb;
-                    tma_load_3d(st, &mapA1, fb, kd * C::BKe, mchunk * BM, bb);
-                    tma_load_3d(st + C::A_BYTES, &mapA2, fb, kd * C::BKe, mchunk * BM, bb);
-                    tma_load_3d(st + 2 * C::A_BYTES, &mapB1, fb, kd * C::BKe, nt * BN, bb);
-                    tma_load_3d(st + 2 * C::A_BYTES + C::B_BYTES, &mapB2, fb, kd * C::BKe,
-                                nt * BN, bb);
+                    const int x = kd * C::BKe;
+                    tma_load_3d(st, &mapA1, fb, x, mchunk * BM, bb);
+                    tma_load_3d(st + C::A_BYTES, &mapA2, fb, x, mchunk * BM, bb);
+                    tma_load_3d(st + 2 * C::A_BYTES, &mapA3, fb, x, mchunk * BM, bb);
+                    tma_load_3d(st + 3 * C::A_BYTES, &mapA4, fb, x, mchunk * BM, bb);
+                    tma_load_3d(st + 4 * C::A_BYTES, &mapB1, fb, x, nt * BN, bb);
+                    tma_load_3d(st + 4 * C::A_BYTES + C::B_BYTES, &mapB2, fb, x, nt * BN, bb);
                 }
                 ++issued;
             }
@@ -481,29 +504,36 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_fence_after();
                 const uint32_t a1 = smem_u32(smem + s * C::STAGE_BYTES);
                 const uint32_t a2 = a1 + C::A_BYTES;
-                const uint32_t b1 = a1 + 2 * C::A_BYTES;
+                const uint32_t b1 = a1 + C::NA * C::A_BYTES;
                 const uint32_t b2 = b1 + C::B_BYTES;
 #pragma unroll
                 for (int u = 0; u < C::NSUB; ++u) {
                     const uint32_t accum = (k > 0 || u > 0) ? 1u : 0u;
+                    // K-major: step 32 B along the swizzled row; MN-major: step UK rows
+                    const uint32_t koff = u * C::UK * (int)sizeof(E);
+                    const uint32_t moff = u * C::UK * 128;
                     uint64_t da1, da2, db1, db2;
                     if (C::A_MN) {
-                        da1 = sw128_desc(a1 + u * C::UK * 128, C::MN_LBO, 1024);
-                        da2 = sw128_desc(a2 + u * C::UK * 128, C::MN_LBO, 1024);
+                        da1 = sw128_desc(a1 + moff, C::MN_LBO, C::MN_SBO, C::MN_LAYOUT);
+                        da2 = sw128_desc(a2 + moff, C::MN_LBO, C::MN_SBO, C::MN_LAYOUT);
                     } else {
-                        da1 = sw128_desc(a1 + u * C::UK * (int)sizeof(E), 16, 1024);
-                        da2 = sw128_desc(a2 + u * C::UK * (int)sizeof(E), 16, 1024);
+                        da1 = sw128_desc(a1 + koff, 16, 1024);
+                        da2 = sw128_desc(a2 + koff, 16, 1024);
                     }
                     if (C::B_MN) {
-                        db1 = sw128_desc(b1 + u * C::UK * 128, C::MN_LBO, 1024);
+                        db1 = sw128_desc(b1 + moff, C::MN_LBO, C::MN_SBO, C::MN_LAYOUT);
                         db2 = db1;
                     } else {
-                        db1 = sw128_desc(b1 + u * C::UK * (int)sizeof(E), 16, 1024);
-                        db2 = sw128_desc(b2 + u * C::UK * (int)sizeof(E), 16, 1024);
+                        db1 = sw128_desc(b1 + koff, 16, 1024);
+                        db2 = sw128_desc(b2 + koff, 16, 1024);
                     }
                     if (C::W) {
+                        const uint64_t da3 = sw128_desc(a1 + 2 * C::A_BYTES + koff, 16, 1024);
+                        const uint64_t da4 = sw128_desc(a1 + 3 * C::A_BYTES + koff, 16, 1024);
                         umma<C::TF32>(tmem, da1, db1, C::IDESC, accum);
                         umma<C::TF32>(tmem, da2, db2, C::IDESC, 1u);
+                        umma<C::TF32>(tmem, da3, db1, C::IDESC, 1u);
+                        umma<C::TF32>(tmem, da4, db2, C::IDESC, 1u);
                     } else {
                         umma<C::TF32>(tmem, da1, db1, C::IDESC, accum);
                         umma<C::TF32>(tmem + BN, da2, db1, C::IDESC, accum);
@@ -562,7 +592,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ------------------------------------------------------------ host side
 struct Layout {
     int B, Tq, Tk, D, Tqp, Tkp, dp, esz, nsplit, rows_per_split;
-    size_t off_m, off_c, off_cpart, off_ap, off_pv, off_pe, off_g1, off_g2, total;
+    size_t off_m, off_c, off_cpart, off_ap, off_pv, off_pe, off_g1, off_g2, off_g1l, off_g2l;
+    size_t total;
 };
 
 static int operand_size(int dtype, int flags)
@@ -600,6 +631,8 @@ static Layout make_layout(int B, int Tq, int Tk, int D, int dtype, int flags)
     L.off_pe = take((size_t)B * L.Tkp * L.dp * L.esz);
     L.off_g1 = take((size_t)B * L.Tqp * L.dp * L.esz);
     L.off_g2 = take((size_t)B * L.Tqp * L.dp * L.esz);
+    L.off_g1l = take((size_t)B * L.Tqp * L.dp * L.esz);
+    L.off_g2l = take((size_t)B * L.Tqp * L.dp * L.esz);
     L.total = off;
     return L;
 }
@@ -689,23 +722,35 @@ static CUtensorMapDataType tmap_type(int esz)
     return esz == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
 }
 
+// Swizzle of a TMA box: MN-major tiles of 32-bit operands need the 32-byte
+// atom variant of the 128-byte swizzle (the smem form tcgen05 reads for
+// MN-major tf32); everything else uses the 16-byte-atom 128-byte swizzle.
+static CUtensorMapSwizzle tile_swizzle(const Layout &L, bool mn_major)
+{
+    return (mn_major && L.esz == 4) ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
+                                    : CU_TENSOR_MAP_SWIZZLE_128B;
+}
+
 // [B][rows][dp] operand buffer; box of `bx` (inner, d) x `by` rows.
 static int map_3d(CUtensorMap *m, const void *base, const Layout &L, int rows, uint32_t bx,
-                  uint32_t by)
+                  uint32_t by, bool mn_major)
 {
     uint64_t dims[3] = {(uint64_t)L.dp, (uint64_t)rows, (uint64_t)L.B};
     uint64_t strides[2] = {(uint64_t)L.dp * L.esz, (uint64_t)rows * L.dp * L.esz};
     uint32_t box[3] = {bx, by, 1};
-    return encode_tmap(m, tmap_type(L.esz), 3, base, dims, strides, box);
+    return encode_tmap(m, tmap_type(L.esz), 3, base, dims, strides, box,
+                       tile_swizzle(L, mn_major));
 }
 
 // A' [Tqp][Tkp]; box of `bx` (inner, i) x `by` rows (t).
-static int map_ap(CUtensorMap *m, const void *base, const Layout &L, uint32_t bx, uint32_t by)
+static int map_ap(CUtensorMap *m, const void *base, const Layout &L, uint32_t bx, uint32_t by,
+                  bool mn_major)
 {
     uint64_t dims[2] = {(uint64_t)L.Tkp, (uint64_t)L.Tqp};
     uint64_t strides[1] = {(uint64_t)L.Tkp * L.esz};
     uint32_t box[2] = {bx, by};
-    return encode_tmap(m, tmap_type(L.esz), 2, base, dims, strides, box);
+    return encode_tmap(m, tmap_type(L.esz), 2, base, dims, strides, box,
+                       tile_swizzle(L, mn_major));
 }
 
 template <int MODE, class E, class IO>
@@ -722,23 +767,25 @@ static int launch_tc(const Params &p, const Layout &L, char *ws, cudaStream_t st
                                          C::SMEM_BYTES));
         attr_set[dev] = true;
     }
-    CUtensorMap mA1, mA2, mB1, mB2;
+    CUtensorMap mA1, mA2, mB1, mB2, mA3, mA4;
     const uint32_t BK = C::BKe, BOX = C::BOX_MN;
     if (MODE == FWD || MODE == BWD1) {
-        DC_TRY(map_3d(&mA1, ws + L.off_pv, L, L.Tkp, BOX, BK));
-        DC_TRY(map_3d(&mA2, ws + L.off_pe, L, L.Tkp, BOX, BK));
-        DC_TRY(map_ap(&mB1, ws + L.off_ap, L, BK, BN));
-        mB2 = mB1;
+        DC_TRY(map_3d(&mA1, ws + L.off_pv, L, L.Tkp, BOX, BK, true));
+        DC_TRY(map_3d(&mA2, ws + L.off_pe, L, L.Tkp, BOX, BK, true));
+        DC_TRY(map_ap(&mB1, ws + L.off_ap, L, BK, BN, false));
+        mB2 = mA3 = mA4 = mB1;
     } else if (MODE == HGRAD) {
-        DC_TRY(map_3d(&mA1, ws + L.off_g1, L, L.Tqp, BOX, BK));
-        DC_TRY(map_3d(&mA2, ws + L.off_g2, L, L.Tqp, BOX, BK));
-        DC_TRY(map_ap(&mB1, ws + L.off_ap, L, BOX, BK));
-        mB2 = mB1;
+        DC_TRY(map_3d(&mA1, ws + L.off_g1, L, L.Tqp, BOX, BK, true));
+        DC_TRY(map_3d(&mA2, ws + L.off_g2, L, L.Tqp, BOX, BK, true));
+        DC_TRY(map_ap(&mB1, ws + L.off_ap, L, BOX, BK, true));
+        mB2 = mA3 = mA4 = mB1;
     } else {
-        DC_TRY(map_3d(&mA1, ws + L.off_g1, L, L.Tqp, BK, BM));
-        DC_TRY(map_3d(&mA2, ws + L.off_g2, L, L.Tqp, BK, BM));
-        DC_TRY(map_3d(&mB1, ws + L.off_pv, L, L.Tkp, BK, BN));
-        DC_TRY(map_3d(&mB2, ws + L.off_pe, L, L.Tkp, BK, BN));
+        DC_TRY(map_3d(&mA1, ws + L.off_g1, L, L.Tqp, BK, BM, false));
+        DC_TRY(map_3d(&mA2, ws + L.off_g2, L, L.Tqp, BK, BM, false));
+        DC_TRY(map_3d(&mA3, ws + L.off_g1l, L, L.Tqp, BK, BM, false));
+        DC_TRY(map_3d(&mA4, ws + L.off_g2l, L, L.Tqp, BK, BM, false));
+        DC_TRY(map_3d(&mB1, ws + L.off_pv, L, L.Tkp, BK, BN, false));
+        DC_TRY(map_3d(&mB2, ws + L.off_pe, L, L.Tkp, BK, BN, false));
     }
     dim3 grid;
     if (MODE == FWD || MODE == BWD1)
@@ -754,7 +801,8 @@ static int launch_tc(const Params &p, const Layout &L, char *ws, cudaStream_t st
                                    "aft_tc_dw"};
     {
         KernelTimer kt(names[MODE], st);
-        aft_tc_kernel<MODE, E, IO><<<grid, kThreads, C::SMEM_BYTES, st>>>(p, mA1, mA2, mB1, mB2);
+        aft_tc_kernel<MODE, E, IO><<<grid, kThreads, C::SMEM_BYTES, st>>>(p, mA1, mA2, mB1, mB2, mA3,
+                                                                          mA4);
     }
     DC_CUDA_TRY(cudaGetLastError());
     return DC_OK;
@@ -801,6 +849,8 @@ static Params make_params(const Layout &L, char *ws, int flags)
     p.c = reinterpret_cast<const float *>(ws + L.off_c);
     p.G1 = ws + L.off_g1;
     p.G2 = ws + L.off_g2;
+    p.G1l = ws + L.off_g1l;
+    p.G2l = ws + L.off_g2l;
     p.status = device_status_word();
     return p;
 }

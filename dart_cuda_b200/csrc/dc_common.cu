@@ -76,7 +76,8 @@ static EncodeTiledFn get_encode()
 }
 
 int encode_tmap(CUtensorMap *map, CUtensorMapDataType dtype, int rank, const void *base,
-                const uint64_t *dims, const uint64_t *strides_bytes, const uint32_t *box)
+                const uint64_t *dims, const uint64_t *strides_bytes, const uint32_t *box,
+                CUtensorMapSwizzle swizzle)
 {
     EncodeTiledFn fn = get_encode();
     if (!fn) return fail(DC_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
@@ -85,7 +86,7 @@ int encode_tmap(CUtensorMap *map, CUtensorMapDataType dtype, int rank, const voi
                     reinterpret_cast<const cuuint64_t *>(dims),
                     reinterpret_cast<const cuuint64_t *>(strides_bytes),
                     reinterpret_cast<const cuuint32_t *>(box), estr,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS)
         return fail(DC_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) rank=%d dims=%llu,%llu box=%u,%u",

@@ -36,7 +36,8 @@ int *device_status_word();
 // cuTensorMapEncodeTiled obtained through the runtime's driver entry point,
 // so the library does not link libcuda directly.
 int encode_tmap(CUtensorMap *map, CUtensorMapDataType dtype, int rank, const void *base,
-                const uint64_t *dims, const uint64_t *strides_bytes, const uint32_t *box);
+                const uint64_t *dims, const uint64_t *strides_bytes, const uint32_t *box,
+                CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B);
 
 inline cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s); }
 

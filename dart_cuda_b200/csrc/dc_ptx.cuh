@@ -198,14 +198,18 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32])
 //   K-major : rows of 128 B, 8-row swizzle atoms 1024 B apart -> sbo = 1024
 //   MN-major: 128 B of MN per K-row; 8 K-rows per 1024 B atom -> sbo = 1024,
 //             lbo = byte distance between consecutive 128 B-wide MN blocks.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo)
+// layout: 2 = 128-byte swizzle with 16-byte atoms (SW128); 1 = 128-byte
+// swizzle with 32-byte atoms, the only MN-major form tcgen05 accepts for
+// 32-bit (tf32) operands, whose 4-row swizzle atoms are 512 B apart.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo,
+                                               uint32_t layout = 2)
 {
     uint64_t d = 0;
     d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
     d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
     d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
     d |= static_cast<uint64_t>(1) << 46;  // descriptor version for tcgen05
-    d |= static_cast<uint64_t>(2) << 61;  // 128-byte swizzle
+    d |= static_cast<uint64_t>(layout & 7u) << 61;
     return d;
 }
 

@@ -140,7 +140,7 @@ void destroy_tensor(void *h);                                          /* engine
 void get_tensor_data(void *h, float *host_out);                        /* engine.cu:123 */
 void get_tensor_grad(void *h, float *host_out);                        /* engine.cu:128 */
 void tensor_to_host(void *h, float *host_out);                         /* engine.cu:879 */
-void set_tensor_data(void *h, float *host_in);                         /* engine.cu:939 */
+void set_tensor_data(void *h, float *host_in);                         /* engine.cu:936 */
 void zero_grad(void *h);                                               /* engine.cu:133 */
 void tensor_step(void *h, float lr);                                   /* engine.cu:138 */
 void backward(void *root);                                             /* engine.cu:145 */
@@ -151,10 +151,10 @@ void *add_tensor_row_broadcast(void *a, void *b);                      /* engine
 void *cross_entropy_loss(void *logits, int32_t *host_targets, int32_t T, int32_t V); /* engine.cu:839 */
 void adam_step(void *p, void *m, void *v, int32_t t, float lr, float b1, float b2,
                float eps);                                             /* engine.cu:887 */
-void *add_tensors(void *a, void *b);                                   /* engine.cu:318 */
+void *add_tensors(void *a, void *b);                                   /* engine.cu:327 */
 void *mul_tensors(void *a, void *b);                                   /* engine.cu:392 */
 void *sum_tensor(void *a);                                             /* engine.cu:1141 */
-void *mean_tensor(void *a);                                            /* engine.cu:1168 */
+void *mean_tensor(void *a);                                            /* engine.cu:1164 */
 
 #ifdef __cplusplus
 }
