@@ -161,6 +161,134 @@ __device__ __forceinline__ void epi_wgrad(const Params &p, int t, int i, float a
     }
 }
 
+// ------------------------------------------------------------ tile epilogues
+// The tensor-core epilogue handles 32 accumulator columns per thread at a
+// time.  All global loads of the block are issued first (read-only path)
+// and only then are results stored, so the 32 loads overlap instead of each
+// waiting behind the previous store.
+__device__ __forceinline__ float ldg_io(const float *p) { return __ldg(p); }
+__device__ __forceinline__ float ldg_io(const __nv_bfloat16 *p)
+{
+    return __bfloat162float(__ldg(p));
+}
+
+// acc rows = d, columns = t0..t0+31
+template <class IO>
+__device__ __forceinline__ void epi32_fwd(const Params &p, int b, int t0, int d,
+                                          const float (&num)[32], const float (&den)[32])
+{
+    const bool dok = d < p.D;
+    const size_t base = (size_t)b * p.Tq * p.D + d;
+    const IO *__restrict__ Q = (const IO *)p.Q + base;
+    float q[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+        q[j] = (dok && t0 + j < p.Tq) ? ldg_io(Q + (size_t)(t0 + j) * p.D) : 0.f;
+    IO *__restrict__ Z = (IO *)p.Z + base;
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+        if (dok && t0 + j < p.Tq) st_io(Z, (size_t)(t0 + j) * p.D, sigmoidf_(q[j]) * (num[j] / den[j]));
+}
+
+// acc rows = d, columns = t0..t0+31; writes dQ and the g/n panels
+template <class IO, class E>
+__device__ __forceinline__ void epi32_bwd1(const Params &p, int b, int t0, int d,
+                                           const float (&num)[32], const float (&den)[32])
+{
+    const bool dok = d < p.D;
+    const size_t base = (size_t)b * p.Tq * p.D + d;
+    const IO *__restrict__ Q = (const IO *)p.Q + base;
+    const IO *__restrict__ dZ = (const IO *)p.dZ + base;
+    float q[32], dz[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        const bool in = dok && t0 + j < p.Tq;
+        q[j] = in ? ldg_io(Q + (size_t)(t0 + j) * p.D) : 0.f;
+        dz[j] = in ? ldg_io(dZ + (size_t)(t0 + j) * p.D) : 0.f;
+    }
+    IO *__restrict__ dQ = (IO *)p.dQ + base;
+    float dqo[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+        dqo[j] = (p.accumulate && dok && t0 + j < p.Tq) ? ld_io(dQ, (size_t)(t0 + j) * p.D) : 0.f;
+    const size_t gbase = ((size_t)b * p.Tqp + t0) * p.dp + d;
+    E *__restrict__ G1 = (E *)p.G1 + gbase;
+    E *__restrict__ G2 = (E *)p.G2 + gbase;
+    E *__restrict__ G1l = (E *)p.G1l + gbase;
+    E *__restrict__ G2l = (E *)p.G2l + gbase;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        const bool in = dok && t0 + j < p.Tq;
+        const float s = sigmoidf_(q[j]);
+        const float r = num[j] / den[j];
+        const float g = in ? dz[j] * s / den[j] : 0.f;
+        const float n = in ? -g * r : 0.f;
+        if (in) st_io(dQ, (size_t)(t0 + j) * p.D, dz[j] * r * s * (1.0f - s) + dqo[j]);
+        const E gh = to_op<E>(g), nh = to_op<E>(n);
+        const size_t o = (size_t)j * p.dp;
+        G1[o] = gh;
+        G2[o] = nh;
+        G1l[o] = to_op<E>(g - from_op(gh));
+        G2l[o] = to_op<E>(n - from_op(nh));
+    }
+}
+
+// acc rows = d, columns = i0..i0+31
+template <class IO>
+__device__ __forceinline__ void epi32_hgrad(const Params &p, int b, int i0, int d,
+                                            const float (&h1)[32], const float (&h2)[32])
+{
+    const bool dok = d < p.D;
+    const size_t base = (size_t)b * p.Tk * p.D + d;
+    const IO *__restrict__ K = (const IO *)p.K + base;
+    const IO *__restrict__ V = (const IO *)p.V + base;
+    const float c = dok ? __ldg(p.c + (size_t)b * p.dp + d) : 0.f;
+    float k[32], v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        const bool in = dok && i0 + j < p.Tk;
+        k[j] = in ? ldg_io(K + (size_t)(i0 + j) * p.D) : 0.f;
+        v[j] = in ? ldg_io(V + (size_t)(i0 + j) * p.D) : 0.f;
+    }
+    IO *__restrict__ dK = (IO *)p.dK + base;
+    IO *__restrict__ dV = (IO *)p.dV + base;
+    float dko[32], dvo[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        const bool in = p.accumulate && dok && i0 + j < p.Tk;
+        dko[j] = in ? ld_io(dK, (size_t)(i0 + j) * p.D) : 0.f;
+        dvo[j] = in ? ld_io(dV, (size_t)(i0 + j) * p.D) : 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        if (dok && i0 + j < p.Tk) {
+            const float e = __expf(k[j] - c);
+            st_io(dV, (size_t)(i0 + j) * p.D, e * h1[j] + dvo[j]);
+            st_io(dK, (size_t)(i0 + j) * p.D, e * (v[j] * h1[j] + h2[j]) + dko[j]);
+        }
+    }
+}
+
+// acc rows = t, columns = i0..i0+31; dW += A' * acc (one atomic per element)
+__device__ __forceinline__ void epi32_wgrad(const Params &p, int t, int i0, const float (&acc)[32])
+{
+    if (t >= p.Tq) return;
+    const float *__restrict__ w = p.w + (size_t)t * p.ldw;
+    const float m = __ldg(p.m + t);
+    float a[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        const int i = i0 + j;
+        a[j] = (i < p.Tk && (!p.causal || i <= t)) ? __expf(__ldg(w + i) - m) : 0.f;
+    }
+    float *dW = p.dW + (size_t)t * p.ldw;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        const int i = i0 + j;
+        if (i < p.Tk && (!p.causal || i <= t)) atomicAdd(dW + i, a[j] * acc[j]);
+    }
+}
+
 // ------------------------------------------------------------ reductions
 __device__ __forceinline__ float warp_max(float v)
 {
@@ -305,6 +433,10 @@ __global__ void aft_simt_kernel(const Params p, const E *__restrict__ Ap,
             const size_t o = ((size_t)b * p.Tqp + t) * p.dp + d;
             h1 += a * from_op(G1[o]);
             h2 += a * from_op(G2[o]);
+            if (sizeof(E) == 4) {  // tf32 operands: add the low parts, as the tensor-core path does
+                h1 += a * from_op(((const E *)p.G1l)[o]);
+                h2 += a * from_op(((const E *)p.G2l)[o]);
+            }
         }
         epi_hgrad<IO>(p, b, i, d, h1, h2);
     } else {
@@ -336,10 +468,13 @@ struct TcCfg {
     static constexpr int BOX_MN = 128 / (int)sizeof(E);// elements in one 128 B MN block
     static constexpr int A_BYTES = BM * 128;
     static constexpr int B_BYTES = BN * 128;
-    static constexpr int NA = W ? 4 : 2;               // A tiles per stage (WGRAD: g, n, g lo, n lo)
+    // A tiles per stage: g and n (+ their low parts for dW, and for dK/dV at
+    // tf32, where the 1e-3 bar leaves no room for rounding g and n once).
+    static constexpr bool LO = W || (MODE == HGRAD && TF32);
+    static constexpr int NA = LO ? 4 : 2;
     static constexpr int NB = W ? 2 : 1;               // B tiles per stage
     static constexpr int STAGE_BYTES = NA * A_BYTES + NB * B_BYTES;
-    static constexpr int STAGES = W ? 2 : 4;
+    static constexpr int STAGES = LO ? 2 : 4;
     static constexpr uint32_t TMEM_COLS = W ? 128 : 256;
     static constexpr uint32_t A_MN = W ? 0 : 1;
     static constexpr uint32_t B_MN = MODE == HGRAD ? 1 : 0;
@@ -462,16 +597,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                         tma_load_3d(st + j * C::MN_LBO, &mapA1, fb, x, kk * C::BKe, b);
                         tma_load_3d(st + C::A_BYTES + j * C::MN_LBO, &mapA2, fb, x,
                                     kk * C::BKe, b);
+                        if (C::NA == 4) {
+                            tma_load_3d(st + 2 * C::A_BYTES + j * C::MN_LBO, &mapA3, fb, x,
+                                        kk * C::BKe, b);
+                            tma_load_3d(st + 3 * C::A_BYTES + j * C::MN_LBO, &mapA4, fb, x,
+                                        kk * C::BKe, b);
+                        }
                     }
+                    const uint32_t sb = st + C::NA * C::A_BYTES;
                     if (MODE == HGRAD) {
                         // B: A'[t rows (K), i cols (N)], MN-major boxes
 #pragma unroll
                         for (int j = 0; j < BN / C::BOX_MN; ++j)
-                            tma_load_2d(st + 2 * C::A_BYTES + j * C::MN_LBO, &mapB1, fb,
-                                        nt * BN + j * C::BOX_MN, kk * C::BKe);
+                            tma_load_2d(sb + j * C::MN_LBO, &mapB1, fb, nt * BN + j * C::BOX_MN,
+                                        kk * C::BKe);
                     } else {
                         // B: A'[t rows (N), i cols (K)], K-major box
-                        tma_load_2d(st + 2 * C::A_BYTES, &mapB1, fb, kk * C::BKe, nt * BN);
+                        tma_load_2d(sb, &mapB1, fb, kk * C::BKe, nt * BN);
                     }
                 } else {
                     const int bb = kk / p.kpb, kd = kk % p.kpb;
@@ -537,6 +679,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                     } else {
                         umma<C::TF32>(tmem, da1, db1, C::IDESC, accum);
                         umma<C::TF32>(tmem + BN, da2, db1, C::IDESC, accum);
+                        if (C::NA == 4) {
+                            const uint64_t da3 = sw128_desc(a1 + 2 * C::A_BYTES + moff, C::MN_LBO,
+                                                            C::MN_SBO, C::MN_LAYOUT);
+                            const uint64_t da4 = sw128_desc(a1 + 3 * C::A_BYTES + moff, C::MN_LBO,
+                                                            C::MN_SBO, C::MN_LAYOUT);
+                            umma<C::TF32>(tmem, da3, db1, C::IDESC, 1u);
+                            umma<C::TF32>(tmem + BN, da4, db1, C::IDESC, 1u);
+                        }
                     }
                 }
                 umma_commit(smem_u32(&empty[s]));
@@ -560,24 +710,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tmem_ld32(lane_addr + cb * 32, v1);
                 if (!C::W) tmem_ld32(lane_addr + BN + cb * 32, v2);
                 const int col0 = nt * BN + cb * 32;
-                if (MODE == FWD) {
-                    const int d = mchunk * BM + row;
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) epi_fwd<IO>(p, b, col0 + j, d, v1[j], v2[j]);
-                } else if (MODE == BWD1) {
-                    const int d = mchunk * BM + row;
-#pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        epi_bwd1<IO, E>(p, b, col0 + j, d, v1[j], v2[j]);
-                } else if (MODE == HGRAD) {
-                    const int d = mchunk * BM + row;
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) epi_hgrad<IO>(p, b, col0 + j, d, v1[j], v2[j]);
-                } else {
-                    const int t = mchunk * BM + row;
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) epi_wgrad(p, t, col0 + j, v1[j]);
-                }
+                const int r = mchunk * BM + row;  // d (FWD/BWD1/HGRAD) or t (WGRAD)
+                if (MODE == FWD)
+                    epi32_fwd<IO>(p, b, col0, r, v1, v2);
+                else if (MODE == BWD1)
+                    epi32_bwd1<IO, E>(p, b, col0, r, v1, v2);
+                else if (MODE == HGRAD)
+                    epi32_hgrad<IO>(p, b, col0, r, v1, v2);
+                else
+                    epi32_wgrad(p, r, col0, v1);
             }
         }
         tc_fence_before();
@@ -777,8 +918,10 @@ static int launch_tc(const Params &p, const Layout &L, char *ws, cudaStream_t st
     } else if (MODE == HGRAD) {
         DC_TRY(map_3d(&mA1, ws + L.off_g1, L, L.Tqp, BOX, BK, true));
         DC_TRY(map_3d(&mA2, ws + L.off_g2, L, L.Tqp, BOX, BK, true));
+        DC_TRY(map_3d(&mA3, ws + L.off_g1l, L, L.Tqp, BOX, BK, true));
+        DC_TRY(map_3d(&mA4, ws + L.off_g2l, L, L.Tqp, BOX, BK, true));
         DC_TRY(map_ap(&mB1, ws + L.off_ap, L, BOX, BK, true));
-        mB2 = mA3 = mA4 = mB1;
+        mB2 = mB1;
     } else {
         DC_TRY(map_3d(&mA1, ws + L.off_g1, L, L.Tqp, BK, BM, false));
         DC_TRY(map_3d(&mA2, ws + L.off_g2, L, L.Tqp, BK, BM, false));

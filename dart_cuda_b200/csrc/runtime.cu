@@ -10,62 +10,34 @@
 // buffers come from the stream-ordered pool; all work is issued on the legacy
 // default stream, so host copies (which synchronise) observe every prior op.
 #include <algorithm>
-#include <functional>
-#include <memory>
 #include <mutex>
 #include <unordered_map>
 #include <unordered_set>
-#include <vector>
 
-#include "dc_internal.h"
+#include "runtime.h"
 
 namespace dc {
 namespace rt {
 
-static cudaStream_t kStream = 0;  // legacy default stream
+Node::Node(int r, int c) : rows(r), cols(c), size((size_t)std::max(r, 0) * std::max(c, 0))
+{
+    if (size) {
+        if (cudaMallocAsync(&data, size * 4, kStream) != cudaSuccess) data = nullptr;
+        if (cudaMallocAsync(&grad, size * 4, kStream) != cudaSuccess) grad = nullptr;
+        if (grad) cudaMemsetAsync(grad, 0, size * 4, kStream);
+    }
+}
 
-struct DevBuf {
-    void *p = nullptr;
-    explicit DevBuf(size_t bytes)
-    {
-        if (bytes && cudaMallocAsync(&p, bytes, kStream) != cudaSuccess) p = nullptr;
-    }
-    ~DevBuf()
-    {
-        if (p) cudaFreeAsync(p, kStream);
-    }
-    DevBuf(const DevBuf &) = delete;
-    DevBuf &operator=(const DevBuf &) = delete;
-};
-
-struct Node {
-    float *data = nullptr;
-    float *grad = nullptr;
-    int rows = 0, cols = 0;
-    size_t size = 0;
-    std::vector<std::shared_ptr<Node>> inputs;
-    std::function<void()> backward_fn;
-    std::vector<std::shared_ptr<DevBuf>> saved;  // op state kept for backward
-
-    Node(int r, int c) : rows(r), cols(c), size((size_t)std::max(r, 0) * std::max(c, 0))
-    {
-        if (size) {
-            if (cudaMallocAsync(&data, size * 4, kStream) != cudaSuccess) data = nullptr;
-            if (cudaMallocAsync(&grad, size * 4, kStream) != cudaSuccess) grad = nullptr;
-            if (grad) cudaMemsetAsync(grad, 0, size * 4, kStream);
-        }
-    }
-    ~Node()
-    {
-        if (data) cudaFreeAsync(data, kStream);
-        if (grad) cudaFreeAsync(grad, kStream);
-    }
-};
+Node::~Node()
+{
+    if (data) cudaFreeAsync(data, kStream);
+    if (grad) cudaFreeAsync(grad, kStream);
+}
 
 static std::unordered_map<Node *, std::shared_ptr<Node>> g_registry;
 static std::mutex g_mutex;
 
-static std::shared_ptr<Node> ref(void *h)
+std::shared_ptr<Node> ref(void *h)
 {
     if (!h) return nullptr;
     std::lock_guard<std::mutex> lock(g_mutex);
@@ -76,7 +48,7 @@ static std::shared_ptr<Node> ref(void *h)
     return std::shared_ptr<Node>(std::shared_ptr<Node>{}, static_cast<Node *>(h));
 }
 
-static Node *make(int r, int c)
+Node *make(int r, int c)
 {
     auto n = std::make_shared<Node>(r, c);
     Node *raw = n.get();
@@ -85,7 +57,7 @@ static Node *make(int r, int c)
     return raw;
 }
 
-static void report(int status, const char *what)
+void report(int status, const char *what)
 {
     if (status != DC_OK) fprintf(stderr, "[libmat_mul] %s: %s\n", what, dc_last_error());
 }
@@ -156,11 +128,6 @@ __global__ void k_step(float *d, float *g, float lr, size_t n)
         d[i] -= lr * g[i];
         g[i] = 0.f;
     }
-}
-
-static unsigned blocks_for(size_t n)
-{
-    return (unsigned)std::max<size_t>(1, std::min<size_t>((n + 255) / 256, 148 * 16));
 }
 
 }  // namespace rt

@@ -156,6 +156,38 @@ void *mul_tensors(void *a, void *b);                                   /* engine
 void *sum_tensor(void *a);                                             /* engine.cu:1141 */
 void *mean_tensor(void *a);                                            /* engine.cu:1164 */
 
+/* The rest of the reference ABI: present so the reference's loaders, which
+ * bind every symbol eagerly, open this library; not on the AFT hot path. */
+void *sub_tensors(void *a, void *b);                                   /* engine.cu:373  */
+void *div_tensors(void *a, void *b);                                   /* engine.cu:414  */
+void *add_tensor_scalar(void *a, void *scalar);                        /* engine.cu:268  */
+void *sub_tensor_scalar(void *a, void *scalar);                        /* engine.cu:282  */
+void *mul_tensor_scalar(void *a, void *scalar);                        /* engine.cu:296  */
+void *div_tensor_scalar(void *a, void *scalar);                        /* engine.cu:311  */
+void *pow_tensor(void *a, float exponent);                             /* engine.cu:424  */
+void *relu_tensor(void *a);                                            /* engine.cu:434  */
+void *gelu_tensor(void *a);                                            /* engine.cu:445  */
+void *sigmoid_tensor(void *a);                                         /* engine.cu:460  */
+void *tanh_tensor(void *a);                                            /* engine.cu:470  */
+void *matmul_tensors(void *a, void *b);                                /* engine.cu:480  */
+void *log_tensor(void *a);                                             /* engine.cu:510  */
+void *concat_tensors_gpu(void **handles, int num_tensors);             /* engine.cu:637  */
+void *concat_tensors_axis0_gpu(void **handles, int num_tensors);       /* engine.cu:686  */
+void *embedding_forward(int *host_indices, void *wte, void *wpe, int T, int D); /* engine.cu:794 */
+void sdg_step(void *p, void *m, void *v, int t, float lr);             /* engine.cu:907  */
+void clip_gradients(void *h, float limit);                             /* engine.cu:925  */
+void *slice_tensor(void *h, int start_row, int num_rows);              /* engine.cu:986  */
+void *abs_tensor(void *a);                                             /* engine.cu:1023 */
+void *softmax_forward(void *a);                                        /* engine.cu:1086 */
+void *transpose_tensor(void *a);                                       /* engine.cu:1106 */
+void compute_cost_matrix(void *pred_boxes, void *gt_boxes, void *cost); /* engine.cu:1127 */
+void tensor_xavier_init(void *p, int n_in, int n_out, int seed);       /* engine.cu:1185 */
+void tensor_zero_init(void *p);                                        /* engine.cu:1197 */
+void *layer_norm_tensor(void *a, float eps);                           /* engine.cu:1228 */
+void im2col_cuda(void *input, int channels, int height, int width, int kernel_h, int kernel_w,
+                 int pad_h, int pad_w, int stride_h, int stride_w, void *output); /* engine.cu:1251 */
+void col2im_cuda(float *d_col, int c, int h, int w, int k, int p, int s, float *d_im); /* engine.cu:1282 */
+
 #ifdef __cplusplus
 }
 #endif

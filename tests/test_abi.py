@@ -47,3 +47,28 @@ def test_library_is_sm100a_only():
     from dart_cuda_b200 import build
 
     assert build.ARCH == ["-gencode", "arch=compute_100a,code=sm_100a"]
+
+
+# Every symbol the reference's loaders bind eagerly
+# (python/dart_cuda/core/tensor/cuda_engine.py:99-199,
+#  lib/core/tensor/cuda_engine.dart:320-420): a missing one fails their import.
+REFERENCE_UNION = """
+create_tensor destroy_tensor get_tensor_data get_tensor_grad tensor_to_host set_tensor_data
+backward zero_grad tensor_step clip_gradients add_tensors sub_tensors mul_tensors div_tensors
+add_tensor_scalar sub_tensor_scalar mul_tensor_scalar div_tensor_scalar add_tensor_row_broadcast
+matmul_tensors pow_tensor relu_tensor gelu_tensor tanh_tensor sigmoid_tensor log_tensor abs_tensor
+softmax_forward transpose_tensor sum_tensor mean_tensor aft_forward aft_cross_forward
+concat_tensors_gpu concat_tensors_axis0_gpu layernorm_forward embedding_forward cross_entropy_loss
+adam_step sdg_step slice_tensor tensor_xavier_init tensor_zero_init layer_norm_tensor
+compute_cost_matrix im2col_cuda col2im_cuda
+""".split()
+
+
+def test_exports_reference_symbol_union():
+    from dart_cuda_b200 import _lib
+
+    lib = ctypes.CDLL(str(_lib.LIB_PATH))
+    assert len(REFERENCE_UNION) == 47
+    missing = [n for n in REFERENCE_UNION if not hasattr(lib, n)]
+    assert not missing, missing
+    assert set(REFERENCE_UNION) <= set(declared_functions())

@@ -77,8 +77,15 @@ def run_case(ops, dev, seed, B, Tq, Tk, D, causal, dtype=torch.float32, wscale=0
     assert ops.device_status() == 0
     Qr, Kr, Vr, dZr = rounded(dtype, Q, K, V, dZ)
     ref = oracle_ref(Qr, Kr, Vr, W, dZr, causal)
-    got = (Z,) + tuple(grads)
-    errs = {n: relerr(g.float().cpu().numpy(), r) for n, g, r in zip(("Z", "dQ", "dK", "dV", "dW"), got, ref)}
+    got = [g.float().cpu().numpy() for g in (Z,) + tuple(grads)]
+    errs = {n: relerr(g, r) for n, g, r in zip(("Z", "dQ", "dK", "dV", "dW"), got, ref)}
+    if Tk == 1:
+        # With one key row, r_t = V_0 exactly, so dK = E'(V H1 + H2) and dW are
+        # identically zero and both sides hold rounding noise only: measure
+        # them against the scale of the terms that cancel (|V| * |dV|).
+        scale = float(np.abs(ref[3]).max() * np.abs(Vr).max())
+        errs["dK"] = float(np.abs(got[2] - ref[2]).max()) / scale
+        errs["dW"] = float(np.abs(got[4] - ref[4]).max()) / (scale * D)
     return errs
 
 
