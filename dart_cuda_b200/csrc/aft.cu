@@ -18,17 +18,20 @@
 //   H1 = A'^T g, H2 = A'^T n          ->  dV = E'*H1,  dK = E'*(V*H1 + H2)
 //   dW = A' (.) sum_b (g_b PV_b^T + n_b PE_b^T)
 //
-// Four tcgen05 contraction modes share one warp-specialised kernel:
-//   FWD   : acc[d, t] = sum_i PV[i,d] A'[t,i]  (+ PE)   -> Z
-//   BWD1  : same contraction                            -> dQ, g, n
-//   HGRAD : acc[d, i] = sum_t G[t,d] A'[t,i]            -> dK, dV
-//   WGRAD : acc[t, i] = sum_{b,d} G[b,t,d] P[b,i,d]     -> dW (split-K, atomics)
+// Four tcgen05 contraction modes share one persistent, warp-specialised
+// kernel (aft_tc.cuh):
+//   FWD   : acc[t, d] = sum_i A'[t,i] PV[i,d]  (and PE)  -> Z
+//   BWD1  : same contraction                             -> dQ, g, n
+//   HGRAD : acc[i, d] = sum_t A'[t,i] G[t,d]   (and N)   -> dK, dV
+//   WGRAD : acc[t, i] = sum_{b,d} G[b,t,d] P[b,i,d]      -> dW (split-K, atomics)
 // Operands are staged by TMA into 128-byte-swizzled shared memory; one thread
-// issues the MMAs into TMEM; four warps read TMEM back in the epilogue.
+// issues the MMAs into double-buffered TMEM accumulators; eight warps read
+// TMEM back and apply the element-wise epilogue with 16-byte accesses.
 #include <cuda_bf16.h>
 #include <math.h>
 
 #include <algorithm>
+#include <initializer_list>
 
 #include "dc_internal.h"
 #include "dc_ptx.cuh"
@@ -40,7 +43,6 @@ constexpr int BM = 128;        // accumulator rows = TMEM lanes
 constexpr int BN = 128;        // accumulator columns (one accumulator)
 constexpr int T_ALIGN = 128;   // workspace padding of Tq and Tk
 constexpr int D_ALIGN = 128;   // workspace padding of D
-constexpr int kThreads = 192;  // warps 0-3 epilogue, warp 4 TMA, warp 5 MMA
 
 enum Mode { FWD = 0, BWD1 = 1, HGRAD = 2, WGRAD = 3 };
 
@@ -77,9 +79,11 @@ __device__ __forceinline__ float sigmoidf_(float q) { return 1.0f / (1.0f + __ex
 struct Params {
     int B, Tq, Tk, D, Tqp, Tkp, dp;
     int causal, accumulate;
-    int n_tiles;      // tiles along t (FWD/BWD1) or i (HGRAD, WGRAD)
+    int n_tiles;      // tensor-core path: number of output tiles of the launch
     int kpb;          // WGRAD: K steps per batch element (dp / BKe)
     int splits;       // WGRAD: split-K factor
+    int vec_io;       // user tensors allow 16-byte vector access along D
+    int vec_w;        // w / dW allow 16-byte vector access along a row
     const void *Q, *K, *V, *dZ;
     void *Z, *dQ, *dK, *dV;
     float *dW;
@@ -158,134 +162,6 @@ __device__ __forceinline__ void epi_wgrad(const Params &p, int t, int i, float a
         size_t o = (size_t)t * p.ldw + i;
         float a = __expf(p.w[o] - p.m[t]);
         atomicAdd(p.dW + o, a * acc);
-    }
-}
-
-// ------------------------------------------------------------ tile epilogues
-// The tensor-core epilogue handles 32 accumulator columns per thread at a
-// time.  All global loads of the block are issued first (read-only path)
-// and only then are results stored, so the 32 loads overlap instead of each
-// waiting behind the previous store.
-__device__ __forceinline__ float ldg_io(const float *p) { return __ldg(p); }
-__device__ __forceinline__ float ldg_io(const __nv_bfloat16 *p)
-{
-    return __bfloat162float(__ldg(p));
-}
-
-// acc rows = d, columns = t0..t0+31
-template <class IO>
-__device__ __forceinline__ void epi32_fwd(const Params &p, int b, int t0, int d,
-                                          const float (&num)[32], const float (&den)[32])
-{
-    const bool dok = d < p.D;
-    const size_t base = (size_t)b * p.Tq * p.D + d;
-    const IO *__restrict__ Q = (const IO *)p.Q + base;
-    float q[32];
-#pragma unroll
-    for (int j = 0; j < 32; ++j)
-        q[j] = (dok && t0 + j < p.Tq) ? ldg_io(Q + (size_t)(t0 + j) * p.D) : 0.f;
-    IO *__restrict__ Z = (IO *)p.Z + base;
-#pragma unroll
-    for (int j = 0; j < 32; ++j)
-        if (dok && t0 + j < p.Tq) st_io(Z, (size_t)(t0 + j) * p.D, sigmoidf_(q[j]) * (num[j] / den[j]));
-}
-
-// acc rows = d, columns = t0..t0+31; writes dQ and the g/n panels
-template <class IO, class E>
-__device__ __forceinline__ void epi32_bwd1(const Params &p, int b, int t0, int d,
-                                           const float (&num)[32], const float (&den)[32])
-{
-    const bool dok = d < p.D;
-    const size_t base = (size_t)b * p.Tq * p.D + d;
-    const IO *__restrict__ Q = (const IO *)p.Q + base;
-    const IO *__restrict__ dZ = (const IO *)p.dZ + base;
-    float q[32], dz[32];
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-        const bool in = dok && t0 + j < p.Tq;
-        q[j] = in ? ldg_io(Q + (size_t)(t0 + j) * p.D) : 0.f;
-        dz[j] = in ? ldg_io(dZ + (size_t)(t0 + j) * p.D) : 0.f;
-    }
-    IO *__restrict__ dQ = (IO *)p.dQ + base;
-    float dqo[32];
-#pragma unroll
-    for (int j = 0; j < 32; ++j)
-        dqo[j] = (p.accumulate && dok && t0 + j < p.Tq) ? ld_io(dQ, (size_t)(t0 + j) * p.D) : 0.f;
-    const size_t gbase = ((size_t)b * p.Tqp + t0) * p.dp + d;
-    E *__restrict__ G1 = (E *)p.G1 + gbase;
-    E *__restrict__ G2 = (E *)p.G2 + gbase;
-    E *__restrict__ G1l = (E *)p.G1l + gbase;
-    E *__restrict__ G2l = (E *)p.G2l + gbase;
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-        const bool in = dok && t0 + j < p.Tq;
-        const float s = sigmoidf_(q[j]);
-        const float r = num[j] / den[j];
-        const float g = in ? dz[j] * s / den[j] : 0.f;
-        const float n = in ? -g * r : 0.f;
-        if (in) st_io(dQ, (size_t)(t0 + j) * p.D, dz[j] * r * s * (1.0f - s) + dqo[j]);
-        const E gh = to_op<E>(g), nh = to_op<E>(n);
-        const size_t o = (size_t)j * p.dp;
-        G1[o] = gh;
-        G2[o] = nh;
-        G1l[o] = to_op<E>(g - from_op(gh));
-        G2l[o] = to_op<E>(n - from_op(nh));
-    }
-}
-
-// acc rows = d, columns = i0..i0+31
-template <class IO>
-__device__ __forceinline__ void epi32_hgrad(const Params &p, int b, int i0, int d,
-                                            const float (&h1)[32], const float (&h2)[32])
-{
-    const bool dok = d < p.D;
-    const size_t base = (size_t)b * p.Tk * p.D + d;
-    const IO *__restrict__ K = (const IO *)p.K + base;
-    const IO *__restrict__ V = (const IO *)p.V + base;
-    const float c = dok ? __ldg(p.c + (size_t)b * p.dp + d) : 0.f;
-    float k[32], v[32];
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-        const bool in = dok && i0 + j < p.Tk;
-        k[j] = in ? ldg_io(K + (size_t)(i0 + j) * p.D) : 0.f;
-        v[j] = in ? ldg_io(V + (size_t)(i0 + j) * p.D) : 0.f;
-    }
-    IO *__restrict__ dK = (IO *)p.dK + base;
-    IO *__restrict__ dV = (IO *)p.dV + base;
-    float dko[32], dvo[32];
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-        const bool in = p.accumulate && dok && i0 + j < p.Tk;
-        dko[j] = in ? ld_io(dK, (size_t)(i0 + j) * p.D) : 0.f;
-        dvo[j] = in ? ld_io(dV, (size_t)(i0 + j) * p.D) : 0.f;
-    }
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-        if (dok && i0 + j < p.Tk) {
-            const float e = __expf(k[j] - c);
-            st_io(dV, (size_t)(i0 + j) * p.D, e * h1[j] + dvo[j]);
-            st_io(dK, (size_t)(i0 + j) * p.D, e * (v[j] * h1[j] + h2[j]) + dko[j]);
-        }
-    }
-}
-
-// acc rows = t, columns = i0..i0+31; dW += A' * acc (one atomic per element)
-__device__ __forceinline__ void epi32_wgrad(const Params &p, int t, int i0, const float (&acc)[32])
-{
-    if (t >= p.Tq) return;
-    const float *__restrict__ w = p.w + (size_t)t * p.ldw;
-    const float m = __ldg(p.m + t);
-    float a[32];
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-        const int i = i0 + j;
-        a[j] = (i < p.Tk && (!p.causal || i <= t)) ? __expf(__ldg(w + i) - m) : 0.f;
-    }
-    float *dW = p.dW + (size_t)t * p.ldw;
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-        const int i = i0 + j;
-        if (i < p.Tk && (!p.causal || i <= t)) atomicAdd(dW + i, a[j] * acc[j]);
     }
 }
 
@@ -458,277 +334,13 @@ __global__ void aft_simt_kernel(const Params p, const E *__restrict__ Ap,
 }
 
 // ------------------------------------------------------------ tensor-core path
-template <int MODE, class E>
-struct TcCfg {
-    static constexpr bool TF32 = sizeof(E) == 4;
-    static constexpr bool W = MODE == WGRAD;
-    static constexpr int BKe = 128 / (int)sizeof(E);   // K elements per stage
-    static constexpr int UK = TF32 ? 8 : 16;           // K per MMA instruction
-    static constexpr int NSUB = BKe / UK;              // MMAs per stage and accumulator
-    static constexpr int BOX_MN = 128 / (int)sizeof(E);// elements in one 128 B MN block
-    static constexpr int A_BYTES = BM * 128;
-    static constexpr int B_BYTES = BN * 128;
-    // A tiles per stage: g and n (+ their low parts for dW, and for dK/dV at
-    // tf32, where the 1e-3 bar leaves no room for rounding g and n once).
-    static constexpr bool LO = W || (MODE == HGRAD && TF32);
-    static constexpr int NA = LO ? 4 : 2;
-    static constexpr int NB = W ? 2 : 1;               // B tiles per stage
-    static constexpr int STAGE_BYTES = NA * A_BYTES + NB * B_BYTES;
-    static constexpr int STAGES = LO ? 2 : 4;
-    static constexpr uint32_t TMEM_COLS = W ? 128 : 256;
-    static constexpr uint32_t A_MN = W ? 0 : 1;
-    static constexpr uint32_t B_MN = MODE == HGRAD ? 1 : 0;
-    static constexpr uint32_t IDESC = umma_idesc(TF32 ? 2u : 1u, BM, BN, A_MN, B_MN);
-    static constexpr uint32_t MN_LBO = BKe * 128;      // bytes between MN blocks
-    // MN-major swizzle: 16 B atoms / 8-row groups (bf16) or 32 B atoms / 4-row
-    // groups (tf32); K-major tiles always use 16 B atoms / 8-row groups.
-    static constexpr uint32_t MN_LAYOUT = TF32 ? 1u : 2u;
-    static constexpr uint32_t MN_SBO = TF32 ? 512u : 1024u;
-    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
-};
+}  // namespace aft
+}  // namespace dc
 
-// Decode the WGRAD tile index into (mt, nt): causal tiles are the lower
-// triangle nt <= mt listed row by row.
-__device__ __forceinline__ void wgrad_tile(int L, int causal, int n_tiles, int &mt, int &nt)
-{
-    if (!causal) {
-        mt = L / n_tiles;
-        nt = L % n_tiles;
-        return;
-    }
-    int r = (int)((sqrtf(8.0f * (float)L + 1.0f) - 1.0f) * 0.5f);
-    while ((r + 1) * (r + 2) / 2 <= L) ++r;
-    while (r * (r + 1) / 2 > L) --r;
-    mt = r;
-    nt = L - r * (r + 1) / 2;
-}
+#include "aft_tc.cuh"
 
-template <int MODE, class E, class IO>
-__global__ void __launch_bounds__(kThreads, 1)
-    aft_tc_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtensorMap mapA1,
-                  const __grid_constant__ CUtensorMap mapA2,
-                  const __grid_constant__ CUtensorMap mapB1,
-                  const __grid_constant__ CUtensorMap mapB2,
-                  const __grid_constant__ CUtensorMap mapA3,
-                  const __grid_constant__ CUtensorMap mapA4)
-{
-    using C = TcCfg<MODE, E>;
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t *smem = reinterpret_cast<uint8_t *>(
-        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::STAGES * C::STAGE_BYTES);
-    uint64_t *full = bars;                  // [STAGES]
-    uint64_t *empty = bars + C::STAGES;     // [STAGES]
-    uint64_t *accf = bars + 2 * C::STAGES;  // [1]
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * C::STAGES + 1);
-    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
-
-    const int warp = threadIdx.x >> 5;
-    const int lane = threadIdx.x & 31;
-
-    // ---- tile coordinates and K range
-    int b = 0, mchunk = 0, nt = 0, k0 = 0, k1 = 0;
-    if (MODE == FWD || MODE == BWD1) {
-        nt = p.n_tiles - 1 - (int)blockIdx.x;  // long (late-t) tiles first
-        mchunk = blockIdx.y;
-        b = blockIdx.z;
-        k1 = (p.causal ? min(p.Tkp, (nt + 1) * BN) : p.Tkp) / C::BKe;
-    } else if (MODE == HGRAD) {
-        nt = blockIdx.x;
-        mchunk = blockIdx.y;
-        b = blockIdx.z;
-        k0 = p.causal ? (nt * BN) / C::BKe : 0;
-        k1 = p.Tqp / C::BKe;
-    } else {
-        wgrad_tile(blockIdx.x, p.causal, p.n_tiles, mchunk, nt);
-        const int total = p.B * p.kpb;
-        k0 = (int)(((long long)blockIdx.y * total) / p.splits);
-        k1 = (int)(((long long)(blockIdx.y + 1) * total) / p.splits);
-    }
-    const int nk = k1 - k0;
-
-    if (threadIdx.x == 0) {
-        *abort_flag = 0;
-        for (int s = 0; s < C::STAGES; ++s) {
-            mbar_init(smem_u32(&full[s]), 1);
-            mbar_init(smem_u32(&empty[s]), 1);
-        }
-        mbar_init(smem_u32(accf), 1);
-        fence_mbar_init();
-    }
-    if (warp == 4 && lane == 0) {
-        tma_prefetch(&mapA1);
-        tma_prefetch(&mapA2);
-        tma_prefetch(&mapB1);
-        if (C::W) {
-            tma_prefetch(&mapB2);
-            tma_prefetch(&mapA3);
-            tma_prefetch(&mapA4);
-        }
-    }
-    if (warp == 5) {
-        tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
-        tmem_relinquish();
-    }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem = *tmem_slot;
-
-    if (warp == 4) {
-        // ------------------------------------------------ TMA producer
-        if (lane == 0) {
-            int issued = 0;
-            for (int k = 0; k < nk; ++k) {
-                const int s = k % C::STAGES;
-                const uint32_t ph = (k / C::STAGES) & 1;
-                if (!mbar_wait(smem_u32(&empty[s]), ph ^ 1, abort_flag, p.status,
-                               DC_DEVERR_TIMEOUT_EMPTY))
-                    break;
-                const uint32_t fb = smem_u32(&full[s]);
-                mbar_arrive_expect_tx(fb, C::STAGE_BYTES);
-                const uint32_t st = smem_u32(smem + s * C::STAGE_BYTES);
-                const int kk = k0 + k;
-                if (MODE == FWD || MODE == BWD1 || MODE == HGRAD) {
-                    // A1/A2: [BKe rows of K] x [128 of d], MN-major boxes
-#pragma unroll
-                    for (int j = 0; j < BM / C::BOX_MN; ++j) {
-                        const int x = mchunk * BM + j * C::BOX_MN;
-                        tma_load_3d(st + j * C::MN_LBO, &mapA1, fb, x, kk * C::BKe, b);
-                        tma_load_3d(st + C::A_BYTES + j * C::MN_LBO, &mapA2, fb, x,
-                                    kk * C::BKe, b);
-                        if (C::NA == 4) {
-                            tma_load_3d(st + 2 * C::A_BYTES + j * C::MN_LBO, &mapA3, fb, x,
-                                        kk * C::BKe, b);
-                            tma_load_3d(st + 3 * C::A_BYTES + j * C::MN_LBO, &mapA4, fb, x,
-                                        kk * C::BKe, b);
-                        }
-                    }
-                    const uint32_t sb = st + C::NA * C::A_BYTES;
-                    if (MODE == HGRAD) {
-                        // B: A'[t rows (K), i cols (N)], MN-major boxes
-#pragma unroll
-                        for (int j = 0; j < BN / C::BOX_MN; ++j)
-                            tma_load_2d(sb + j * C::MN_LBO, &mapB1, fb, nt * BN + j * C::BOX_MN,
-                                        kk * C::BKe);
-                    } else {
-                        // B: A'[t rows (N), i cols (K)], K-major box
-                        tma_load_2d(sb, &mapB1, fb, kk * C::BKe, nt * BN);
-                    }
-                } else {
-                    const int bb = kk / p.kpb, kd = kk % p.kpb;
-                    const int x = kd * C::BKe;
-                    tma_load_3d(st, &mapA1, fb, x, mchunk * BM, bb);
-                    tma_load_3d(st + C::A_BYTES, &mapA2, fb, x, mchunk * BM, bb);
-                    tma_load_3d(st + 2 * C::A_BYTES, &mapA3, fb, x, mchunk * BM, bb);
-                    tma_load_3d(st + 3 * C::A_BYTES, &mapA4, fb, x, mchunk * BM, bb);
-                    tma_load_3d(st + 4 * C::A_BYTES, &mapB1, fb, x, nt * BN, bb);
-                    tma_load_3d(st + 4 * C::A_BYTES + C::B_BYTES, &mapB2, fb, x, nt * BN, bb);
-                }
-                ++issued;
-            }
-            if (*abort_flag) {
-                // let the copies already in flight land before the CTA exits
-                for (int k = max(0, issued - C::STAGES); k < issued; ++k)
-                    mbar_wait(smem_u32(&full[k % C::STAGES]), (k / C::STAGES) & 1, nullptr,
-                              p.status, DC_DEVERR_TIMEOUT_DRAIN);
-            }
-        }
-    } else if (warp == 5) {
-        // ------------------------------------------------ MMA issuer
-        if (lane == 0) {
-            for (int k = 0; k < nk; ++k) {
-                const int s = k % C::STAGES;
-                const uint32_t ph = (k / C::STAGES) & 1;
-                if (!mbar_wait(smem_u32(&full[s]), ph, abort_flag, p.status,
-                               DC_DEVERR_TIMEOUT_FULL))
-                    break;
-                tc_fence_after();
-                const uint32_t a1 = smem_u32(smem + s * C::STAGE_BYTES);
-                const uint32_t a2 = a1 + C::A_BYTES;
-                const uint32_t b1 = a1 + C::NA * C::A_BYTES;
-                const uint32_t b2 = b1 + C::B_BYTES;
-#pragma unroll
-                for (int u = 0; u < C::NSUB; ++u) {
-                    const uint32_t accum = (k > 0 || u > 0) ? 1u : 0u;
-                    // K-major: step 32 B along the swizzled row; MN-major: step UK rows
-                    const uint32_t koff = u * C::UK * (int)sizeof(E);
-                    const uint32_t moff = u * C::UK * 128;
-                    uint64_t da1, da2, db1, db2;
-                    if (C::A_MN) {
-                        da1 = sw128_desc(a1 + moff, C::MN_LBO, C::MN_SBO, C::MN_LAYOUT);
-                        da2 = sw128_desc(a2 + moff, C::MN_LBO, C::MN_SBO, C::MN_LAYOUT);
-                    } else {
-                        da1 = sw128_desc(a1 + koff, 16, 1024);
-                        da2 = sw128_desc(a2 + koff, 16, 1024);
-                    }
-                    if (C::B_MN) {
-                        db1 = sw128_desc(b1 + moff, C::MN_LBO, C::MN_SBO, C::MN_LAYOUT);
-                        db2 = db1;
-                    } else {
-                        db1 = sw128_desc(b1 + koff, 16, 1024);
-                        db2 = sw128_desc(b2 + koff, 16, 1024);
-                    }
-                    if (C::W) {
-                        const uint64_t da3 = sw128_desc(a1 + 2 * C::A_BYTES + koff, 16, 1024);
-                        const uint64_t da4 = sw128_desc(a1 + 3 * C::A_BYTES + koff, 16, 1024);
-                        umma<C::TF32>(tmem, da1, db1, C::IDESC, accum);
-                        umma<C::TF32>(tmem, da2, db2, C::IDESC, 1u);
-                        umma<C::TF32>(tmem, da3, db1, C::IDESC, 1u);
-                        umma<C::TF32>(tmem, da4, db2, C::IDESC, 1u);
-                    } else {
-                        umma<C::TF32>(tmem, da1, db1, C::IDESC, accum);
-                        umma<C::TF32>(tmem + BN, da2, db1, C::IDESC, accum);
-                        if (C::NA == 4) {
-                            const uint64_t da3 = sw128_desc(a1 + 2 * C::A_BYTES + moff, C::MN_LBO,
-                                                            C::MN_SBO, C::MN_LAYOUT);
-                            const uint64_t da4 = sw128_desc(a1 + 3 * C::A_BYTES + moff, C::MN_LBO,
-                                                            C::MN_SBO, C::MN_LAYOUT);
-                            umma<C::TF32>(tmem, da3, db1, C::IDESC, 1u);
-                            umma<C::TF32>(tmem + BN, da4, db1, C::IDESC, 1u);
-                        }
-                    }
-                }
-                umma_commit(smem_u32(&empty[s]));
-            }
-            umma_commit(smem_u32(accf));
-            if (*abort_flag)  // MMAs must finish before TMEM is released
-                mbar_wait(smem_u32(accf), 0, nullptr, p.status, DC_DEVERR_TIMEOUT_DRAIN);
-        }
-    } else {
-        // ------------------------------------------------ epilogue (warps 0-3)
-        // warp-uniform, because the TMEM loads below are warp-collective
-        const bool ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(accf), 0, abort_flag, p.status,
-                                                          DC_DEVERR_TIMEOUT_ACC));
-        tc_fence_after();
-        if (ok && nk > 0) {
-            const int row = warp * 32 + lane;
-            const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
-#pragma unroll 1
-            for (int cb = 0; cb < BN / 32; ++cb) {
-                float v1[32], v2[32];
-                tmem_ld32(lane_addr + cb * 32, v1);
-                if (!C::W) tmem_ld32(lane_addr + BN + cb * 32, v2);
-                const int col0 = nt * BN + cb * 32;
-                const int r = mchunk * BM + row;  // d (FWD/BWD1/HGRAD) or t (WGRAD)
-                if (MODE == FWD)
-                    epi32_fwd<IO>(p, b, col0, r, v1, v2);
-                else if (MODE == BWD1)
-                    epi32_bwd1<IO, E>(p, b, col0, r, v1, v2);
-                else if (MODE == HGRAD)
-                    epi32_hgrad<IO>(p, b, col0, r, v1, v2);
-                else
-                    epi32_wgrad(p, r, col0, v1);
-            }
-        }
-        tc_fence_before();
-    }
-    __syncthreads();
-    if (warp == 5) {
-        tc_fence_after();
-        tmem_dealloc(tmem, C::TMEM_COLS);
-    }
-}
+namespace dc {
+namespace aft {
 
 // ------------------------------------------------------------ host side
 struct Layout {
@@ -895,7 +507,7 @@ static int map_ap(CUtensorMap *m, const void *base, const Layout &L, uint32_t bx
 }
 
 template <int MODE, class E, class IO>
-static int launch_tc(const Params &p, const Layout &L, char *ws, cudaStream_t st)
+static int launch_tc(Params p, const Layout &L, char *ws, cudaStream_t st)
 {
     using C = TcCfg<MODE, E>;
     static bool attr_set[64] = {false};  // per instantiation and device
@@ -908,44 +520,43 @@ static int launch_tc(const Params &p, const Layout &L, char *ws, cudaStream_t st
                                          C::SMEM_BYTES));
         attr_set[dev] = true;
     }
-    CUtensorMap mA1, mA2, mB1, mB2, mA3, mA4;
+    // tensor maps: A, B1..B4 (B3/B4 only for the tf32 dK/dV low parts), A2..A4 (dW)
+    CUtensorMap mA, mB1, mB2, mB3, mB4, mA2, mA3, mA4;
     const uint32_t BK = C::BKe, BOX = C::BOX_MN;
+    const int nd = L.dp / BN;
     if (MODE == FWD || MODE == BWD1) {
-        DC_TRY(map_3d(&mA1, ws + L.off_pv, L, L.Tkp, BOX, BK, true));
-        DC_TRY(map_3d(&mA2, ws + L.off_pe, L, L.Tkp, BOX, BK, true));
-        DC_TRY(map_ap(&mB1, ws + L.off_ap, L, BK, BN, false));
-        mB2 = mA3 = mA4 = mB1;
+        DC_TRY(map_ap(&mA, ws + L.off_ap, L, BK, BM, false));
+        DC_TRY(map_3d(&mB1, ws + L.off_pv, L, L.Tkp, BOX, BK, true));
+        DC_TRY(map_3d(&mB2, ws + L.off_pe, L, L.Tkp, BOX, BK, true));
+        mB3 = mB4 = mA2 = mA3 = mA4 = mA;
+        p.n_tiles = (L.Tqp / BM) * nd * L.B;
     } else if (MODE == HGRAD) {
-        DC_TRY(map_3d(&mA1, ws + L.off_g1, L, L.Tqp, BOX, BK, true));
-        DC_TRY(map_3d(&mA2, ws + L.off_g2, L, L.Tqp, BOX, BK, true));
-        DC_TRY(map_3d(&mA3, ws + L.off_g1l, L, L.Tqp, BOX, BK, true));
-        DC_TRY(map_3d(&mA4, ws + L.off_g2l, L, L.Tqp, BOX, BK, true));
-        DC_TRY(map_ap(&mB1, ws + L.off_ap, L, BOX, BK, true));
-        mB2 = mB1;
+        DC_TRY(map_ap(&mA, ws + L.off_ap, L, BOX, BK, true));
+        DC_TRY(map_3d(&mB1, ws + L.off_g1, L, L.Tqp, BOX, BK, true));
+        DC_TRY(map_3d(&mB2, ws + L.off_g2, L, L.Tqp, BOX, BK, true));
+        DC_TRY(map_3d(&mB3, ws + L.off_g1l, L, L.Tqp, BOX, BK, true));
+        DC_TRY(map_3d(&mB4, ws + L.off_g2l, L, L.Tqp, BOX, BK, true));
+        mA2 = mA3 = mA4 = mA;
+        p.n_tiles = (L.Tkp / BM) * nd * L.B;
     } else {
-        DC_TRY(map_3d(&mA1, ws + L.off_g1, L, L.Tqp, BK, BM, false));
+        DC_TRY(map_3d(&mA, ws + L.off_g1, L, L.Tqp, BK, BM, false));
         DC_TRY(map_3d(&mA2, ws + L.off_g2, L, L.Tqp, BK, BM, false));
         DC_TRY(map_3d(&mA3, ws + L.off_g1l, L, L.Tqp, BK, BM, false));
         DC_TRY(map_3d(&mA4, ws + L.off_g2l, L, L.Tqp, BK, BM, false));
         DC_TRY(map_3d(&mB1, ws + L.off_pv, L, L.Tkp, BK, BN, false));
         DC_TRY(map_3d(&mB2, ws + L.off_pe, L, L.Tkp, BK, BN, false));
-    }
-    dim3 grid;
-    if (MODE == FWD || MODE == BWD1)
-        grid = dim3(L.Tqp / BN, L.dp / BM, L.B);
-    else if (MODE == HGRAD)
-        grid = dim3(L.Tkp / BN, L.dp / BM, L.B);
-    else {
+        mB3 = mB4 = mB1;
         const int mt = L.Tqp / BM, nt = L.Tkp / BN;
-        const int tiles = p.causal ? mt * (mt + 1) / 2 : mt * nt;
-        grid = dim3(tiles, p.splits, 1);
+        p.n_tiles = (p.causal ? mt * (mt + 1) / 2 : mt * nt) * p.splits;
     }
+    // persistent: one CTA per SM (shared memory admits one), tiles round-robin
+    const int grid = std::max(1, std::min(p.n_tiles, sm_count()));
     static const char *names[4] = {"aft_tc_fwd", "aft_tc_bwd_recompute", "aft_tc_dkdv",
                                    "aft_tc_dw"};
     {
         KernelTimer kt(names[MODE], st);
-        aft_tc_kernel<MODE, E, IO><<<grid, kThreads, C::SMEM_BYTES, st>>>(p, mA1, mA2, mB1, mB2, mA3,
-                                                                          mA4);
+        aft_tc_kernel<MODE, E, IO><<<grid, kTcThreads, C::SMEM_BYTES, st>>>(
+            p, mA, mB1, mB2, mB3, mB4, mA2, mA3, mA4);
     }
     DC_CUDA_TRY(cudaGetLastError());
     return DC_OK;
@@ -998,6 +609,17 @@ static Params make_params(const Layout &L, char *ws, int flags)
     return p;
 }
 
+// 16-byte vector access along D: rows start on 16-byte boundaries when D is a
+// multiple of 16 bytes' worth of elements and every base pointer is aligned.
+template <class IO>
+static int vec_ok(int D, std::initializer_list<const void *> ptrs)
+{
+    if ((D * (int)sizeof(IO)) % 16 != 0) return 0;
+    for (const void *q : ptrs)
+        if (reinterpret_cast<uintptr_t>(q) & 15) return 0;
+    return 1;
+}
+
 template <class IO, class E>
 static int fwd_impl(const void *Q, const void *K, const void *V, const float *w, int ldw,
                     void *Z, const Layout &L, int flags, char *ws, cudaStream_t st)
@@ -1012,7 +634,7 @@ static int fwd_impl(const void *Q, const void *K, const void *V, const float *w,
     p.Z = Z;
     p.w = w;
     p.ldw = ldw;
-    p.n_tiles = L.Tqp / BN;
+    p.vec_io = vec_ok<IO>(L.D, {Q, Z});
     return launch<FWD, E, IO>(p, L, ws, st, flags);
 }
 
@@ -1037,9 +659,9 @@ static int bwd_impl(const void *Q, const void *K, const void *V, const float *w,
     p.dW = dW;
     p.w = w;
     p.ldw = ldw;
-    p.n_tiles = L.Tqp / BN;
+    p.vec_io = vec_ok<IO>(L.D, {Q, K, V, dZ, dQ, dK, dV});
+    p.vec_w = (ldw % 4 == 0) && ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(dW)) & 15) == 0;
     DC_TRY((launch<BWD1, E, IO>(p, L, ws, st, flags)));
-    p.n_tiles = L.Tkp / BN;
     DC_TRY((launch<HGRAD, E, IO>(p, L, ws, st, flags)));
     // split-K factor for dW: enough CTAs to cover the SMs, >= 4 K steps each
     p.kpb = L.dp / TcCfg<WGRAD, E>::BKe;
@@ -1049,7 +671,6 @@ static int bwd_impl(const void *Q, const void *K, const void *V, const float *w,
     int splits = (sm_count() + tiles - 1) / tiles;
     splits = std::max(1, std::min(splits, ktot / 4));
     p.splits = std::max(1, std::min(splits, ktot));
-    p.n_tiles = L.Tkp / BN;
     return launch<WGRAD, E, IO>(p, L, ws, st, flags);
 }
 

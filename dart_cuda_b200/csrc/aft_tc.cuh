@@ -1,0 +1,606 @@
+// Persistent, warp-specialised tcgen05 contraction kernel of the AFT-full
+// operator (included by aft.cu; uses its Params, element helpers and modes).
+//
+// Accumulator rows (TMEM lanes) are the query / key positions and columns are
+// channels d, so every epilogue thread owns contiguous runs of d and moves
+// them with 16-byte vector loads and stores:
+//
+//   FWD, BWD1 : acc[t, d]  = sum_i A'[t,i] PV[i,d]   and   sum_i A'[t,i] PE[i,d]
+//   HGRAD     : acc[i, d]  = sum_t A'[t,i] G[t,d]    and   sum_t A'[t,i] N[t,d]
+//   WGRAD     : acc[t, i]  = sum_{b,d} (G PV^T + N PE^T + G_lo PV^T + N_lo PE^T)
+//
+// Warp roles (320 threads): warps 0-7 epilogue (warp w reads TMEM lanes
+// 32*(w%4).. and half w/4 of the columns), warp 8 TMA producer, warp 9 TMEM
+// allocator + MMA issuer.  Each CTA loops over tiles tile = blockIdx.x +
+// k*gridDim.x; the accumulator is double-buffered in TMEM so the epilogue of
+// one tile overlaps the main loop of the next.
+#pragma once
+
+namespace dc {
+namespace aft {
+
+constexpr int kEpiWarps = 8;
+constexpr int kTcThreads = (kEpiWarps + 2) * 32;
+constexpr int kSmemBudget = 227 * 1024;
+
+template <int MODE, class E>
+struct TcCfg {
+    static constexpr bool TF32 = sizeof(E) == 4;
+    static constexpr bool W = MODE == WGRAD;
+    static constexpr bool H = MODE == HGRAD;
+    static constexpr int BKe = 128 / (int)sizeof(E);   // K elements per stage (one 128 B row)
+    static constexpr int UK = TF32 ? 8 : 16;           // K per MMA instruction
+    static constexpr int NSUB = BKe / UK;              // MMAs per stage and operand pair
+    static constexpr int BOX_MN = 128 / (int)sizeof(E);// elements in one 128 B MN block
+    static constexpr int TILE_BYTES = 128 * 128;       // one 128 x (128 B) operand tile
+    // dK/dV at tf32 also adds the low parts of g and n (1e-3 bar)
+    static constexpr bool LO = W || (H && TF32);
+    static constexpr int NA = W ? 4 : 1;               // A tiles per stage
+    static constexpr int NB = W ? 2 : (LO ? 4 : 2);    // B tiles per stage
+    static constexpr int STAGE_BYTES = (NA + NB) * TILE_BYTES;
+    static constexpr int STAGES_FIT = (kSmemBudget - 2048) / STAGE_BYTES;
+    static constexpr int STAGES = STAGES_FIT < 4 ? STAGES_FIT : 4;
+    static constexpr int NACC = W ? 1 : 2;             // accumulators per tile
+    static constexpr uint32_t ACC_COLS = NACC * BN;
+    static constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;  // double buffered
+    static constexpr uint32_t A_MN = H ? 1 : 0;
+    static constexpr uint32_t B_MN = W ? 0 : 1;
+    static constexpr uint32_t IDESC = umma_idesc(TF32 ? 2u : 1u, BM, BN, A_MN, B_MN);
+    static constexpr uint32_t MN_LBO = BKe * 128;      // bytes between 128 B MN blocks
+    static constexpr uint32_t MN_LAYOUT = TF32 ? 1u : 2u;
+    static constexpr uint32_t MN_SBO = TF32 ? 512u : 1024u;
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 512;
+    static_assert(STAGES >= 2, "pipeline needs two stages");
+    static_assert(SMEM_BYTES <= kSmemBudget, "shared memory budget");
+};
+
+// ----------------------------------------------------------- vector I/O
+// bf16 <-> fp32 by bit placement: a bf16 is the high half of an fp32.
+__device__ __forceinline__ void unpack8(const uint4 x, float (&v)[16], int o)
+{
+    v[o + 0] = __uint_as_float(x.x << 16);
+    v[o + 1] = __uint_as_float(x.x & 0xFFFF0000u);
+    v[o + 2] = __uint_as_float(x.y << 16);
+    v[o + 3] = __uint_as_float(x.y & 0xFFFF0000u);
+    v[o + 4] = __uint_as_float(x.z << 16);
+    v[o + 5] = __uint_as_float(x.z & 0xFFFF0000u);
+    v[o + 6] = __uint_as_float(x.w << 16);
+    v[o + 7] = __uint_as_float(x.w & 0xFFFF0000u);
+}
+__device__ __forceinline__ uint32_t pack2(float a, float b)
+{
+    return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(a)) |
+           ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(b)) << 16);
+}
+__device__ __forceinline__ void ld16g(const float *p, float (&v)[16])
+{
+    const float4 *q = reinterpret_cast<const float4 *>(p);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const float4 x = __ldg(q + k);
+        v[4 * k] = x.x;
+        v[4 * k + 1] = x.y;
+        v[4 * k + 2] = x.z;
+        v[4 * k + 3] = x.w;
+    }
+}
+__device__ __forceinline__ void ld16g(const __nv_bfloat16 *p, float (&v)[16])
+{
+    const uint4 *q = reinterpret_cast<const uint4 *>(p);
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        const uint4 x = __ldg(q + k);
+        unpack8(x, v, 8 * k);
+    }
+}
+// plain (coherent) loads for outputs read back when accumulating
+__device__ __forceinline__ void ld16(const float *p, float (&v)[16])
+{
+    const float4 *q = reinterpret_cast<const float4 *>(p);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const float4 x = q[k];
+        v[4 * k] = x.x;
+        v[4 * k + 1] = x.y;
+        v[4 * k + 2] = x.z;
+        v[4 * k + 3] = x.w;
+    }
+}
+__device__ __forceinline__ void ld16(const __nv_bfloat16 *p, float (&v)[16])
+{
+    const uint4 *q = reinterpret_cast<const uint4 *>(p);
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        const uint4 x = q[k];
+        unpack8(x, v, 8 * k);
+    }
+}
+__device__ __forceinline__ void st16(float *p, const float (&v)[16])
+{
+    float4 *q = reinterpret_cast<float4 *>(p);
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+        q[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+}
+__device__ __forceinline__ void st16(__nv_bfloat16 *p, const float (&v)[16])
+{
+    uint4 *q = reinterpret_cast<uint4 *>(p);
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        const int o = 8 * k;
+        q[k] = make_uint4(pack2(v[o], v[o + 1]), pack2(v[o + 2], v[o + 3]), pack2(v[o + 4], v[o + 5]),
+                          pack2(v[o + 6], v[o + 7]));
+    }
+}
+// operand-precision store: bf16, or tf32-rounded fp32
+__device__ __forceinline__ void st16op(__nv_bfloat16 *p, const float (&v)[16]) { st16(p, v); }
+__device__ __forceinline__ void st16op(float *p, const float (&v)[16])
+{
+    float r[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) r[k] = to_op<float>(v[k]);
+    st16(p, r);
+}
+__device__ __forceinline__ void round16(const float (&v)[16], float (&hi)[16], float (&lo)[16],
+                                        bool bf16)
+{
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+        hi[k] = bf16 ? __bfloat162float(__float2bfloat16_rn(v[k])) : to_op<float>(v[k]);
+        lo[k] = v[k] - hi[k];
+    }
+}
+
+__device__ __forceinline__ float fast_sigmoid(float q) { return __fdividef(1.0f, 1.0f + __expf(-q)); }
+
+// ----------------------------------------------------------- epilogues
+// One thread, one accumulator row, 16 consecutive columns starting at c0.
+// `full` = the row and all 16 columns are inside the logical tensor and the
+// tensors allow 16-byte vector access; otherwise an element-wise path runs.
+
+template <class IO>
+__device__ __forceinline__ void epi16_fwd(const Params &p, int b, int t, int d0,
+                                          const float (&num)[16], const float (&den)[16])
+{
+    if (t >= p.Tq) return;
+    const size_t o = ((size_t)b * p.Tq + t) * p.D + d0;
+    if (p.vec_io && d0 + 16 <= p.D) {
+        float q[16], z[16];
+        ld16g((const IO *)p.Q + o, q);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) z[j] = __fdividef(num[j], den[j] * (1.0f + __expf(-q[j])));
+        st16((IO *)p.Z + o, z);
+    } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            if (d0 + j >= p.D) break;
+            const float q = ld_io((const IO *)p.Q, o + j);
+            st_io((IO *)p.Z, o + j, __fdividef(num[j], den[j] * (1.0f + __expf(-q))));
+        }
+    }
+}
+
+template <class IO, class E>
+__device__ __forceinline__ void epi16_bwd1(const Params &p, int b, int t, int d0,
+                                           const float (&num)[16], const float (&den)[16])
+{
+    float g[16], n[16];
+    const bool trow = t < p.Tq;
+    const size_t o = ((size_t)b * p.Tq + t) * p.D + d0;
+    if (trow && p.vec_io && d0 + 16 <= p.D) {
+        float q[16], dz[16], dq[16];
+        ld16g((const IO *)p.Q + o, q);
+        ld16g((const IO *)p.dZ + o, dz);
+        if (p.accumulate) ld16((const IO *)p.dQ + o, dq);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const float s = fast_sigmoid(q[j]);
+            const float inv = __fdividef(1.0f, den[j]);
+            const float r = num[j] * inv;
+            const float add = dz[j] * r * s * (1.0f - s);
+            dq[j] = p.accumulate ? dq[j] + add : add;
+            g[j] = dz[j] * s * inv;
+            n[j] = -g[j] * r;
+        }
+        st16((IO *)p.dQ + o, dq);
+    } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            g[j] = 0.f;
+            n[j] = 0.f;
+        }
+        if (trow) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                if (d0 + j >= p.D) break;
+                const float q = ld_io((const IO *)p.Q, o + j);
+                const float dz = ld_io((const IO *)p.dZ, o + j);
+                const float s = fast_sigmoid(q);
+                const float inv = __fdividef(1.0f, den[j]);
+                const float r = num[j] * inv;
+                float dq = dz * r * s * (1.0f - s);
+                if (p.accumulate) dq += ld_io((const IO *)p.dQ, o + j);
+                st_io((IO *)p.dQ, o + j, dq);
+                g[j] = dz * s * inv;
+                n[j] = -g[j] * r;
+            }
+        }
+    }
+    // g, n and their rounding residuals, over the whole padded tile
+    const size_t go = ((size_t)b * p.Tqp + t) * p.dp + d0;
+    float hi[16], lo[16];
+    constexpr bool BF = sizeof(E) == 2;
+    round16(g, hi, lo, BF);
+    st16op((E *)p.G1 + go, hi);
+    st16op((E *)p.G1l + go, lo);
+    round16(n, hi, lo, BF);
+    st16op((E *)p.G2 + go, hi);
+    st16op((E *)p.G2l + go, lo);
+}
+
+template <class IO>
+__device__ __forceinline__ void epi16_hgrad(const Params &p, int b, int i, int d0,
+                                            const float (&h1)[16], const float (&h2)[16])
+{
+    if (i >= p.Tk) return;
+    const size_t o = ((size_t)b * p.Tk + i) * p.D + d0;
+    const float *cb = p.c + (size_t)b * p.dp + d0;
+    if (p.vec_io && d0 + 16 <= p.D) {
+        float k[16], v[16], c[16], dk[16], dv[16];
+        ld16g((const IO *)p.K + o, k);
+        ld16g((const IO *)p.V + o, v);
+        ld16g(cb, c);
+        if (p.accumulate) {
+            ld16((const IO *)p.dK + o, dk);
+            ld16((const IO *)p.dV + o, dv);
+        }
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const float e = __expf(k[j] - c[j]);
+            const float a = e * h1[j], bk = e * (v[j] * h1[j] + h2[j]);
+            dv[j] = p.accumulate ? dv[j] + a : a;
+            dk[j] = p.accumulate ? dk[j] + bk : bk;
+        }
+        st16((IO *)p.dV + o, dv);
+        st16((IO *)p.dK + o, dk);
+    } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            if (d0 + j >= p.D) break;
+            const float e = __expf(ld_io((const IO *)p.K, o + j) - cb[j]);
+            const float v = ld_io((const IO *)p.V, o + j);
+            float dv = e * h1[j], dk = e * (v * h1[j] + h2[j]);
+            if (p.accumulate) {
+                dv += ld_io((const IO *)p.dV, o + j);
+                dk += ld_io((const IO *)p.dK, o + j);
+            }
+            st_io((IO *)p.dV, o + j, dv);
+            st_io((IO *)p.dK, o + j, dk);
+        }
+    }
+}
+
+__device__ __forceinline__ void epi16_wgrad(const Params &p, int t, int i0, const float (&acc)[16])
+{
+    if (t >= p.Tq || i0 >= p.Tk || (p.causal && i0 > t)) return;
+    const float m = __ldg(p.m + t);
+    const float *w = p.w + (size_t)t * p.ldw;
+    float *dW = p.dW + (size_t)t * p.ldw;
+    if (p.vec_w && i0 + 16 <= p.Tk && (!p.causal || i0 + 15 <= t)) {
+        float wv[16];
+        ld16g(w + i0, wv);
+        float4 *d4 = reinterpret_cast<float4 *>(dW + i0);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            float4 v;
+            v.x = __expf(wv[4 * k] - m) * acc[4 * k];
+            v.y = __expf(wv[4 * k + 1] - m) * acc[4 * k + 1];
+            v.z = __expf(wv[4 * k + 2] - m) * acc[4 * k + 2];
+            v.w = __expf(wv[4 * k + 3] - m) * acc[4 * k + 3];
+            atomicAdd(d4 + k, v);
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const int i = i0 + j;
+            if (i < p.Tk && (!p.causal || i <= t)) atomicAdd(dW + i, __expf(__ldg(w + i) - m) * acc[j]);
+        }
+    }
+}
+
+// ----------------------------------------------------------- tile schedule
+struct Tile {
+    int b, mrow, ncol, k0, k1;  // mrow/ncol: 128-row block of the accumulator / 128-col block
+};
+
+template <int MODE, int BKe>
+__device__ __forceinline__ Tile decode_tile(const Params &p, int idx)
+{
+    Tile t{};
+    if (MODE == FWD || MODE == BWD1) {
+        // rows t (heavy, late-t tiles first), columns d
+        const int nd = p.dp / BN;
+        const int per = nd * p.B;
+        t.mrow = p.Tqp / BM - 1 - idx / per;
+        const int rem = idx % per;
+        t.ncol = rem % nd;
+        t.b = rem / nd;
+        t.k0 = 0;
+        t.k1 = (p.causal ? min(p.Tkp, (t.mrow + 1) * BM) : p.Tkp) / BKe;
+    } else if (MODE == HGRAD) {
+        // rows i (heavy, early-i tiles first), columns d
+        const int nd = p.dp / BN;
+        const int per = nd * p.B;
+        t.mrow = idx / per;
+        const int rem = idx % per;
+        t.ncol = rem % nd;
+        t.b = rem / nd;
+        t.k0 = p.causal ? (t.mrow * BM) / BKe : 0;
+        t.k1 = p.Tqp / BKe;
+    } else {
+        const int pair = idx / p.splits, s = idx % p.splits;
+        if (!p.causal) {
+            t.mrow = pair / (p.Tkp / BN);
+            t.ncol = pair % (p.Tkp / BN);
+        } else {
+            int r = (int)((sqrtf(8.0f * (float)pair + 1.0f) - 1.0f) * 0.5f);
+            while ((r + 1) * (r + 2) / 2 <= pair) ++r;
+            while (r * (r + 1) / 2 > pair) --r;
+            t.mrow = r;
+            t.ncol = pair - r * (r + 1) / 2;
+        }
+        const int total = p.B * p.kpb;
+        t.k0 = (int)(((long long)s * total) / p.splits);
+        t.k1 = (int)(((long long)(s + 1) * total) / p.splits);
+    }
+    return t;
+}
+
+// ----------------------------------------------------------- the kernel
+template <int MODE, class E, class IO>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    aft_tc_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtensorMap mapA,
+                  const __grid_constant__ CUtensorMap mapB1,
+                  const __grid_constant__ CUtensorMap mapB2,
+                  const __grid_constant__ CUtensorMap mapB3,
+                  const __grid_constant__ CUtensorMap mapB4,
+                  const __grid_constant__ CUtensorMap mapA2,
+                  const __grid_constant__ CUtensorMap mapA3,
+                  const __grid_constant__ CUtensorMap mapA4)
+{
+    using C = TcCfg<MODE, E>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::STAGES * C::STAGE_BYTES);
+    uint64_t *full = bars;                   // [STAGES]  TMA -> MMA
+    uint64_t *empty = bars + C::STAGES;      // [STAGES]  MMA -> TMA
+    uint64_t *accf = bars + 2 * C::STAGES;   // [2]       MMA -> epilogue
+    uint64_t *acce = accf + 2;               // [2]       epilogue -> MMA
+    uint64_t *drainb = acce + 2;             // [1]       MMA drain after an abort
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drainb + 1);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        *abort_flag = 0;
+        for (int s = 0; s < C::STAGES; ++s) {
+            mbar_init(smem_u32(&full[s]), 1);
+            mbar_init(smem_u32(&empty[s]), 1);
+        }
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(smem_u32(&accf[s]), 1);
+            mbar_init(smem_u32(&acce[s]), kEpiWarps);
+        }
+        mbar_init(smem_u32(drainb), 1);
+        fence_mbar_init();
+    }
+    if (warp == kEpiWarps && lane == 0) {
+        tma_prefetch(&mapA);
+        tma_prefetch(&mapB1);
+        tma_prefetch(&mapB2);
+        if (C::NB == 4) {
+            tma_prefetch(&mapB3);
+            tma_prefetch(&mapB4);
+        }
+        if (C::NA == 4) {
+            tma_prefetch(&mapA2);
+            tma_prefetch(&mapA3);
+            tma_prefetch(&mapA4);
+        }
+    }
+    if (warp == kEpiWarps + 1) {
+        tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const int ntiles = p.n_tiles;
+
+    if (warp == kEpiWarps) {
+        // ------------------------------------------------ TMA producer
+        if (lane == 0) {
+            uint32_t g = 0;
+            bool stop = false;
+            for (int tile = blockIdx.x; tile < ntiles && !stop; tile += gridDim.x) {
+                const Tile tl = decode_tile<MODE, C::BKe>(p, tile);
+                for (int k = tl.k0; k < tl.k1; ++k, ++g) {
+                    const int s = g % C::STAGES;
+                    const uint32_t ph = (g / C::STAGES) & 1;
+                    if (!mbar_wait(smem_u32(&empty[s]), ph ^ 1, abort_flag, p.status,
+                                   DC_DEVERR_TIMEOUT_EMPTY)) {
+                        stop = true;
+                        break;
+                    }
+                    const uint32_t fb = smem_u32(&full[s]);
+                    mbar_arrive_expect_tx(fb, C::STAGE_BYTES);
+                    const uint32_t sa = smem_u32(smem + s * C::STAGE_BYTES);
+                    const uint32_t sb = sa + C::NA * C::TILE_BYTES;
+                    if (MODE == FWD || MODE == BWD1) {
+                        // A: A'[t rows, i cols] K-major; B: PV/PE [i rows, d cols] MN-major
+                        tma_load_2d(sa, &mapA, fb, k * C::BKe, tl.mrow * BM);
+#pragma unroll
+                        for (int j = 0; j < BN / C::BOX_MN; ++j) {
+                            const int x = tl.ncol * BN + j * C::BOX_MN;
+                            tma_load_3d(sb + j * C::MN_LBO, &mapB1, fb, x, k * C::BKe, tl.b);
+                            tma_load_3d(sb + C::TILE_BYTES + j * C::MN_LBO, &mapB2, fb, x,
+                                        k * C::BKe, tl.b);
+                        }
+                    } else if (MODE == HGRAD) {
+                        // A: A'[t rows (K), i cols (M)] MN-major; B: G/N [t rows, d cols] MN-major
+#pragma unroll
+                        for (int j = 0; j < BM / C::BOX_MN; ++j)
+                            tma_load_2d(sa + j * C::MN_LBO, &mapA, fb, tl.mrow * BM + j * C::BOX_MN,
+                                        k * C::BKe);
+#pragma unroll
+                        for (int j = 0; j < BN / C::BOX_MN; ++j) {
+                            const int x = tl.ncol * BN + j * C::BOX_MN;
+                            tma_load_3d(sb + j * C::MN_LBO, &mapB1, fb, x, k * C::BKe, tl.b);
+                            tma_load_3d(sb + C::TILE_BYTES + j * C::MN_LBO, &mapB2, fb, x,
+                                        k * C::BKe, tl.b);
+                            if (C::NB == 4) {
+                                tma_load_3d(sb + 2 * C::TILE_BYTES + j * C::MN_LBO, &mapB3, fb, x,
+                                            k * C::BKe, tl.b);
+                                tma_load_3d(sb + 3 * C::TILE_BYTES + j * C::MN_LBO, &mapB4, fb, x,
+                                            k * C::BKe, tl.b);
+                            }
+                        }
+                    } else {
+                        // A: G, N, G lo, N lo [t rows, d cols] K-major; B: PV, PE [i rows, d] K-major
+                        const int bb = k / p.kpb, x = (k % p.kpb) * C::BKe;
+                        tma_load_3d(sa, &mapA, fb, x, tl.mrow * BM, bb);
+                        tma_load_3d(sa + C::TILE_BYTES, &mapA2, fb, x, tl.mrow * BM, bb);
+                        tma_load_3d(sa + 2 * C::TILE_BYTES, &mapA3, fb, x, tl.mrow * BM, bb);
+                        tma_load_3d(sa + 3 * C::TILE_BYTES, &mapA4, fb, x, tl.mrow * BM, bb);
+                        tma_load_3d(sb, &mapB1, fb, x, tl.ncol * BN, bb);
+                        tma_load_3d(sb + C::TILE_BYTES, &mapB2, fb, x, tl.ncol * BN, bb);
+                    }
+                }
+            }
+            if (*abort_flag) {
+                // let the copies already in flight land before the CTA exits
+                const uint32_t first = g > (uint32_t)C::STAGES ? g - C::STAGES : 0;
+                for (uint32_t q = first; q < g; ++q)
+                    mbar_wait(smem_u32(&full[q % C::STAGES]), (q / C::STAGES) & 1, nullptr,
+                              p.status, DC_DEVERR_TIMEOUT_DRAIN);
+            }
+        }
+    } else if (warp == kEpiWarps + 1) {
+        // ------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            uint32_t g = 0, j = 0;
+            bool stop = false;
+            for (int tile = blockIdx.x; tile < ntiles && !stop; tile += gridDim.x, ++j) {
+                const Tile tl = decode_tile<MODE, C::BKe>(p, tile);
+                const uint32_t buf = j & 1, use = j >> 1;
+                if (!mbar_wait(smem_u32(&acce[buf]), (use & 1) ^ 1, abort_flag, p.status,
+                               DC_DEVERR_TIMEOUT_ACC))
+                    break;
+                tc_fence_after();
+                const uint32_t acc = tmem + buf * C::ACC_COLS;
+                for (int k = tl.k0; k < tl.k1; ++k, ++g) {
+                    const int s = g % C::STAGES;
+                    if (!mbar_wait(smem_u32(&full[s]), (g / C::STAGES) & 1, abort_flag, p.status,
+                                   DC_DEVERR_TIMEOUT_FULL)) {
+                        stop = true;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = smem_u32(smem + s * C::STAGE_BYTES);
+                    const uint32_t sb = sa + C::NA * C::TILE_BYTES;
+#pragma unroll
+                    for (int u = 0; u < C::NSUB; ++u) {
+                        const uint32_t first = (k == tl.k0 && u == 0) ? 0u : 1u;
+                        const uint32_t koff = u * C::UK * (int)sizeof(E);  // K-major step
+                        const uint32_t moff = u * C::UK * 128;             // MN-major step
+                        if (C::W) {
+                            const uint64_t b1 = sw128_desc(sb + koff, 16, 1024);
+                            const uint64_t b2 = sw128_desc(sb + C::TILE_BYTES + koff, 16, 1024);
+                            umma<C::TF32>(acc, sw128_desc(sa + koff, 16, 1024), b1, C::IDESC, first);
+                            umma<C::TF32>(acc, sw128_desc(sa + C::TILE_BYTES + koff, 16, 1024), b2,
+                                          C::IDESC, 1u);
+                            umma<C::TF32>(acc, sw128_desc(sa + 2 * C::TILE_BYTES + koff, 16, 1024),
+                                          b1, C::IDESC, 1u);
+                            umma<C::TF32>(acc, sw128_desc(sa + 3 * C::TILE_BYTES + koff, 16, 1024),
+                                          b2, C::IDESC, 1u);
+                        } else {
+                            const uint64_t a = C::H ? sw128_desc(sa + moff, C::MN_LBO, C::MN_SBO,
+                                                                 C::MN_LAYOUT)
+                                                    : sw128_desc(sa + koff, 16, 1024);
+                            const uint64_t b1 =
+                                sw128_desc(sb + moff, C::MN_LBO, C::MN_SBO, C::MN_LAYOUT);
+                            const uint64_t b2 = sw128_desc(sb + C::TILE_BYTES + moff, C::MN_LBO,
+                                                           C::MN_SBO, C::MN_LAYOUT);
+                            umma<C::TF32>(acc, a, b1, C::IDESC, first);
+                            umma<C::TF32>(acc + BN, a, b2, C::IDESC, first);
+                            if (C::NB == 4) {
+                                const uint64_t b3 = sw128_desc(sb + 2 * C::TILE_BYTES + moff,
+                                                               C::MN_LBO, C::MN_SBO, C::MN_LAYOUT);
+                                const uint64_t b4 = sw128_desc(sb + 3 * C::TILE_BYTES + moff,
+                                                               C::MN_LBO, C::MN_SBO, C::MN_LAYOUT);
+                                umma<C::TF32>(acc, a, b3, C::IDESC, 1u);
+                                umma<C::TF32>(acc + BN, a, b4, C::IDESC, 1u);
+                            }
+                        }
+                    }
+                    umma_commit(smem_u32(&empty[s]));
+                }
+                if (stop) break;
+                umma_commit(smem_u32(&accf[buf]));
+            }
+            if (*abort_flag) {  // MMAs must finish before TMEM is released
+                umma_commit(smem_u32(drainb));
+                mbar_wait(smem_u32(drainb), 0, nullptr, p.status, DC_DEVERR_TIMEOUT_DRAIN);
+            }
+        }
+    } else {
+        // ------------------------------------------------ epilogue (warps 0-7)
+        const int quad = warp & 3;           // TMEM lanes 32*quad .. 32*quad+31
+        const int half = warp >> 2;          // columns half*64 .. half*64+63
+        const int row = quad * 32 + lane;
+        uint32_t j = 0;
+        for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++j) {
+            const Tile tl = decode_tile<MODE, C::BKe>(p, tile);
+            const uint32_t buf = j & 1, use = j >> 1;
+            // warp-uniform, because the TMEM loads below are warp-collective
+            const bool ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&accf[buf]), use & 1,
+                                                              abort_flag, p.status,
+                                                              DC_DEVERR_TIMEOUT_ACC));
+            if (!ok) break;
+            tc_fence_after();
+            const uint32_t lane_addr =
+                tmem + buf * C::ACC_COLS + ((uint32_t)(quad * 32) << 16) + half * 64;
+            const int r = tl.mrow * BM + row;  // t (FWD, BWD1, WGRAD) or i (HGRAD)
+#pragma unroll 1
+            for (int sb = 0; sb < 4; ++sb) {
+                float v1[16], v2[16];
+                tmem_ld16(lane_addr + sb * 16, v1);
+                if (!C::W) tmem_ld16(lane_addr + BN + sb * 16, v2);
+                const int c0 = tl.ncol * BN + half * 64 + sb * 16;  // d, or i for WGRAD
+                if (MODE == FWD)
+                    epi16_fwd<IO>(p, tl.b, r, c0, v1, v2);
+                else if (MODE == BWD1)
+                    epi16_bwd1<IO, E>(p, tl.b, r, c0, v1, v2);
+                else if (MODE == HGRAD)
+                    epi16_hgrad<IO>(p, tl.b, r, c0, v1, v2);
+                else
+                    epi16_wgrad(p, r, c0, v1);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&acce[buf]));
+        }
+    }
+    __syncthreads();
+    if (warp == kEpiWarps + 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, C::TMEM_COLS);
+    }
+}
+
+}  // namespace aft
+}  // namespace dc
