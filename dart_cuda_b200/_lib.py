@@ -38,6 +38,7 @@ SIGNATURES = {
     "dc_device_status": (c_int, [_VP, POINTER(c_int)]),
     "dc_profile_enable": (c_int, [c_int]),
     "dc_profile_read": (c_int, [ctypes.c_char_p, _FP, POINTER(c_int), c_int]),
+    "dc_aft_trace": (c_int, [_VP, c_size_t, c_int]),
     "dc_aft_workspace_size": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, POINTER(c_size_t)]),
     "dc_aft_fwd": (c_int, [_VP, _VP, _VP, _VP, c_int, _VP, c_int, c_int, c_int, c_int, c_int, c_int,
                            _VP, c_size_t, _VP]),

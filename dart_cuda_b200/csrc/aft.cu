@@ -94,7 +94,13 @@ struct Params {
     void *G1, *G2;    // g and n = -g*r, [B][Tqp][dp] operand precision
     void *G1l, *G2l;  // their rounding residuals (g - G1, n - G2), same layout
     int *status;
+    unsigned long long *trace;  // optional per-tile timeline (nullptr: off)
 };
+
+// Per-tile timeline of the tensor-core launches whose mode bit is set in
+// g_trace_modes (bit MODE); see trace_at() in aft_tc.cuh.
+static unsigned long long *g_trace_buf = nullptr;
+static int g_trace_modes = 0;
 
 // ------------------------------------------------------------ epilogues
 // Shared by the tensor-core and CUDA-core paths so both apply identical
@@ -214,19 +220,61 @@ __global__ void prep_w_kernel(const float *__restrict__ w, int ldw, int Tq, int 
         row[i] = to_op<E>(i < lim ? __expf(wr[i] - mx) : 0.f);
 }
 
-// Partial column maxima of K over row slices: cpart[s][b][d].
+// Partial column maxima of K over row slices: cpart[s][b][d].  Block of
+// 32 x 8 threads: each thread owns 8 consecutive columns (one 16-byte load
+// for bf16) and every 8th row of the slice; the 8 row lanes then combine.
+__device__ __forceinline__ void ld8(const float *p, float (&v)[8])
+{
+    const float4 a = __ldg(reinterpret_cast<const float4 *>(p));
+    const float4 b = __ldg(reinterpret_cast<const float4 *>(p) + 1);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+__device__ __forceinline__ void ld8(const __nv_bfloat16 *p, float (&v)[8])
+{
+    const uint4 x = __ldg(reinterpret_cast<const uint4 *>(p));
+    v[0] = __uint_as_float(x.x << 16); v[1] = __uint_as_float(x.x & 0xFFFF0000u);
+    v[2] = __uint_as_float(x.y << 16); v[3] = __uint_as_float(x.y & 0xFFFF0000u);
+    v[4] = __uint_as_float(x.z << 16); v[5] = __uint_as_float(x.z & 0xFFFF0000u);
+    v[6] = __uint_as_float(x.w << 16); v[7] = __uint_as_float(x.w & 0xFFFF0000u);
+}
+
 template <class IO>
 __global__ void prep_colmax_kernel(const IO *__restrict__ K, int B, int Tk, int D, int dp,
-                                   int rows_per_split, float *__restrict__ cpart)
+                                   int rows_per_split, int vec, float *__restrict__ cpart)
 {
-    const int d = blockIdx.x * blockDim.x + threadIdx.x;
+    __shared__ float red[8][32 * 8 + 1];
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+    const int d0 = (blockIdx.x * 32 + tx) * 8;
     const int s = blockIdx.y, b = blockIdx.z;
-    if (d >= D) return;
     const int i0 = s * rows_per_split, i1 = min(Tk, i0 + rows_per_split);
     const IO *Kb = K + (size_t)b * Tk * D;
-    float mx = -INFINITY;
-    for (int i = i0; i < i1; ++i) mx = fmaxf(mx, ld_io(Kb, (size_t)i * D + d));
-    cpart[((size_t)s * B + b) * dp + d] = mx;
+    float mx[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) mx[k] = -INFINITY;
+    if (vec && d0 + 8 <= D) {
+        for (int i = i0 + ty; i < i1; i += 8) {
+            float v[8];
+            ld8(Kb + (size_t)i * D + d0, v);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) mx[k] = fmaxf(mx[k], v[k]);
+        }
+    } else if (d0 < D) {
+        for (int i = i0 + ty; i < i1; i += 8)
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+                if (d0 + k < D) mx[k] = fmaxf(mx[k], ld_io(Kb, (size_t)i * D + d0 + k));
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) red[ty][tx * 8 + k] = mx[k];
+    __syncthreads();
+    // 256 threads finish 256 columns: column j = threadIdx.x of this block
+    const int j = threadIdx.x;
+    float m = red[0][j];
+#pragma unroll
+    for (int r = 1; r < 8; ++r) m = fmaxf(m, red[r][j]);
+    const int d = blockIdx.x * 256 + j;
+    if (d < D) cpart[((size_t)s * B + b) * dp + d] = m;
 }
 
 __global__ void prep_colmax_final_kernel(const float *__restrict__ cpart, int nsplit, int B,
@@ -243,28 +291,72 @@ __global__ void prep_colmax_final_kernel(const float *__restrict__ cpart, int ns
     c[idx] = mx;
 }
 
-// PV = exp(K - c) * V and PE = exp(K - c) over the padded [B, Tkp, dp] space.
+// PV = exp(K - c) * V and PE = exp(K - c) over the padded [B, Tkp, dp] space,
+// eight consecutive d per thread (16-byte loads and stores when `vec`).
+__device__ __forceinline__ void st8op(__nv_bfloat16 *p, const float (&v)[8])
+{
+    uint4 x;
+    x.x = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v[0])) |
+          ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v[1])) << 16);
+    x.y = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v[2])) |
+          ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v[3])) << 16);
+    x.z = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v[4])) |
+          ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v[5])) << 16);
+    x.w = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v[6])) |
+          ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v[7])) << 16);
+    *reinterpret_cast<uint4 *>(p) = x;
+}
+__device__ __forceinline__ void st8op(float *p, const float (&v)[8])
+{
+    float4 a, b;
+    a.x = to_op<float>(v[0]); a.y = to_op<float>(v[1]); a.z = to_op<float>(v[2]); a.w = to_op<float>(v[3]);
+    b.x = to_op<float>(v[4]); b.y = to_op<float>(v[5]); b.z = to_op<float>(v[6]); b.w = to_op<float>(v[7]);
+    reinterpret_cast<float4 *>(p)[0] = a;
+    reinterpret_cast<float4 *>(p)[1] = b;
+}
+
 template <class IO, class E>
 __global__ void prep_p_kernel(const IO *__restrict__ K, const IO *__restrict__ V,
                               const float *__restrict__ c, int B, int Tk, int D, int Tkp,
-                              int dp, E *__restrict__ PV, E *__restrict__ PE)
+                              int dp, int vec, E *__restrict__ PV, E *__restrict__ PE)
 {
-    const size_t total = (size_t)B * Tkp * dp;
+    const int nch = dp / 8;
+    const size_t total = (size_t)B * Tkp * nch;
     for (size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
          idx += (size_t)gridDim.x * blockDim.x) {
-        const int d = (int)(idx % dp);
-        const size_t r = idx / dp;
+        const int d0 = (int)(idx % nch) * 8;
+        const size_t r = idx / nch;
         const int i = (int)(r % Tkp);
         const int b = (int)(r / Tkp);
-        float pv = 0.f, pe = 0.f;
-        if (i < Tk && d < D) {
-            const size_t src = ((size_t)b * Tk + i) * D + d;
-            const float e = __expf(ld_io(K, src) - c[(size_t)b * dp + d]);
-            pe = e;
-            pv = e * ld_io(V, src);
+        float pv[8], pe[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) pv[k] = pe[k] = 0.f;
+        if (i < Tk) {
+            const size_t src = ((size_t)b * Tk + i) * D + d0;
+            const float *cb = c + (size_t)b * dp + d0;
+            float cc[8];
+            ld8(cb, cc);
+            if (vec && d0 + 8 <= D) {
+                float k8[8], v8[8];
+                ld8(K + src, k8);
+                ld8(V + src, v8);
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    pe[k] = __expf(k8[k] - cc[k]);
+                    pv[k] = pe[k] * v8[k];
+                }
+            } else {
+#pragma unroll
+                for (int k = 0; k < 8; ++k)
+                    if (d0 + k < D) {
+                        pe[k] = __expf(ld_io(K, src + k) - cc[k]);
+                        pv[k] = pe[k] * ld_io(V, src + k);
+                    }
+            }
         }
-        PV[idx] = to_op<E>(pv);
-        PE[idx] = to_op<E>(pe);
+        const size_t dst = ((size_t)b * Tkp + i) * dp + d0;
+        st8op(PV + dst, pv);
+        st8op(PE + dst, pe);
     }
 }
 
@@ -451,20 +543,24 @@ static int run_prep(const Layout &L, const IO *K, const IO *V, const float *w, i
         KernelTimer kt("aft_prep_w", st);
         prep_w_kernel<E><<<L.Tqp, 256, 0, st>>>(w, ldw, L.Tq, L.Tk, L.Tkp, causal, m, Ap);
     }
+    // 16-byte access to K and V rows: D a multiple of 8 and aligned bases
+    const int vec = (L.D % 8 == 0) &&
+                    ((reinterpret_cast<uintptr_t>(K) | reinterpret_cast<uintptr_t>(V)) & 15) == 0;
     {
         KernelTimer kt("aft_prep_colmax", st);
         dim3 g1((L.D + 255) / 256, L.nsplit, L.B);
         prep_colmax_kernel<IO><<<g1, 256, 0, st>>>(K, L.B, L.Tk, L.D, L.dp, L.rows_per_split,
-                                                   cpart);
+                                                   vec, cpart);
         const int nbd = L.B * L.dp;
         prep_colmax_final_kernel<<<(nbd + 255) / 256, 256, 0, st>>>(cpart, L.nsplit, L.B, L.D,
                                                                       L.dp, c);
     }
     {
         KernelTimer kt("aft_prep_p", st);
-        const size_t total = (size_t)L.B * L.Tkp * L.dp;
+        const size_t total = (size_t)L.B * L.Tkp * (L.dp / 8);
         const int blocks = (int)std::min<size_t>((total + 255) / 256, (size_t)sm_count() * 16);
-        prep_p_kernel<IO, E><<<blocks, 256, 0, st>>>(K, V, c, L.B, L.Tk, L.D, L.Tkp, L.dp, PV, PE);
+        prep_p_kernel<IO, E><<<blocks, 256, 0, st>>>(K, V, c, L.B, L.Tk, L.D, L.Tkp, L.dp, vec, PV,
+                                                     PE);
     }
     DC_CUDA_TRY(cudaGetLastError());
     return DC_OK;
@@ -549,8 +645,9 @@ static int launch_tc(Params p, const Layout &L, char *ws, cudaStream_t st)
         const int mt = L.Tqp / BM, nt = L.Tkp / BN;
         p.n_tiles = (p.causal ? mt * (mt + 1) / 2 : mt * nt) * p.splits;
     }
-    // persistent: one CTA per SM (shared memory admits one), tiles round-robin
+    // persistent: one CTA per SM (shared memory admits one)
     const int grid = std::max(1, std::min(p.n_tiles, sm_count()));
+    p.trace = (g_trace_modes >> MODE) & 1 ? g_trace_buf : nullptr;
     static const char *names[4] = {"aft_tc_fwd", "aft_tc_bwd_recompute", "aft_tc_dkdv",
                                    "aft_tc_dw"};
     {
@@ -668,9 +765,20 @@ static int bwd_impl(const void *Q, const void *K, const void *V, const float *w,
     const int mt = L.Tqp / BM;
     const int tiles = causal ? mt * (mt + 1) / 2 : mt * (L.Tkp / BN);
     const int ktot = L.B * p.kpb;
-    int splits = (sm_count() + tiles - 1) / tiles;
-    splits = std::max(1, std::min(splits, ktot / 4));
-    p.splits = std::max(1, std::min(splits, ktot));
+    // split-K: pick the split count whose tiles fill the persistent CTAs with
+    // the least time (waves x work per tile), each split >= 8 K steps
+    const int sms = sm_count();
+    int best = 1;
+    double best_cost = 1e30;
+    for (int sp = 1; sp <= std::max(1, ktot / 8); ++sp) {
+        const int waves = (tiles * sp + sms - 1) / sms;
+        const double cost = (double)waves / sp * (1.0 + 0.002 * sp);  // atomics grow with sp
+        if (cost < best_cost) {
+            best_cost = cost;
+            best = sp;
+        }
+    }
+    p.splits = best;
     return launch<WGRAD, E, IO>(p, L, ws, st, flags);
 }
 
@@ -681,6 +789,16 @@ using namespace dc;
 using namespace dc::aft;
 
 extern "C" {
+
+int dc_aft_trace(void *device_buffer, size_t bytes, int mode_mask)
+{
+    const size_t need = (size_t)sm_count() * 64 * 8 * sizeof(unsigned long long);
+    if (device_buffer && bytes < need)
+        return fail(DC_ERR_NOMEM, "trace buffer needs %zu bytes", need);
+    g_trace_buf = static_cast<unsigned long long *>(device_buffer);
+    g_trace_modes = device_buffer ? mode_mask : 0;
+    return DC_OK;
+}
 
 int dc_aft_workspace_size(int B, int Tq, int Tk, int D, int dtype, int flags, size_t *bytes)
 {

@@ -356,6 +356,24 @@ __device__ __forceinline__ Tile decode_tile(const Params &p, int idx)
     return t;
 }
 
+// Tile of this CTA's j-th iteration: tiles are listed heavy-first and dealt
+// boustrophedon (round j even: c, odd: G-1-c) so each CTA pairs heavy and
+// light tiles.  -1 once the CTA has no more tiles.
+__device__ __forceinline__ int sched_tile(int j, int ntiles)
+{
+    const int G = gridDim.x, c = blockIdx.x;
+    const int t = j * G + ((j & 1) ? (G - 1 - c) : c);
+    return t < ntiles ? t : -1;
+}
+
+// Optional per-tile timeline (Params::trace): 8 words per (CTA, local tile):
+// 0 producer start, 1 MMA start, 2 MMA done, 3 epilogue start, 4 epilogue
+// done (global-timer ns), 5 tile index, 6 K steps.  Up to 64 tiles per CTA.
+__device__ __forceinline__ void trace_at(const Params &p, int j, int field, unsigned long long v)
+{
+    if (p.trace && j < 64) p.trace[((size_t)blockIdx.x * 64 + j) * 8 + field] = v;
+}
+
 // ----------------------------------------------------------- the kernel
 template <int MODE, class E, class IO>
 __global__ void __launch_bounds__(kTcThreads, 1)
@@ -426,8 +444,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (lane == 0) {
             uint32_t g = 0;
             bool stop = false;
-            for (int tile = blockIdx.x; tile < ntiles && !stop; tile += gridDim.x) {
+            for (int jt = 0; !stop; ++jt) {
+                const int tile = sched_tile(jt, ntiles);
+                if (tile < 0) break;
                 const Tile tl = decode_tile<MODE, C::BKe>(p, tile);
+                trace_at(p, jt, 0, global_timer());
                 for (int k = tl.k0; k < tl.k1; ++k, ++g) {
                     const int s = g % C::STAGES;
                     const uint32_t ph = (g / C::STAGES) & 1;
@@ -494,13 +515,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (lane == 0) {
             uint32_t g = 0, j = 0;
             bool stop = false;
-            for (int tile = blockIdx.x; tile < ntiles && !stop; tile += gridDim.x, ++j) {
+            for (; !stop; ++j) {
+                const int tile = sched_tile(j, ntiles);
+                if (tile < 0) break;
                 const Tile tl = decode_tile<MODE, C::BKe>(p, tile);
                 const uint32_t buf = j & 1, use = j >> 1;
                 if (!mbar_wait(smem_u32(&acce[buf]), (use & 1) ^ 1, abort_flag, p.status,
                                DC_DEVERR_TIMEOUT_ACC))
                     break;
                 tc_fence_after();
+                trace_at(p, j, 1, global_timer());
+                trace_at(p, j, 5, tile);
+                trace_at(p, j, 6, tl.k1 - tl.k0);
                 const uint32_t acc = tmem + buf * C::ACC_COLS;
                 for (int k = tl.k0; k < tl.k1; ++k, ++g) {
                     const int s = g % C::STAGES;
@@ -551,6 +577,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 }
                 if (stop) break;
                 umma_commit(smem_u32(&accf[buf]));
+                trace_at(p, j, 2, global_timer());
             }
             if (*abort_flag) {  // MMAs must finish before TMEM is released
                 umma_commit(smem_u32(drainb));
@@ -562,8 +589,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int quad = warp & 3;           // TMEM lanes 32*quad .. 32*quad+31
         const int half = warp >> 2;          // columns half*64 .. half*64+63
         const int row = quad * 32 + lane;
-        uint32_t j = 0;
-        for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++j) {
+        for (uint32_t j = 0;; ++j) {
+            const int tile = sched_tile(j, ntiles);
+            if (tile < 0) break;
             const Tile tl = decode_tile<MODE, C::BKe>(p, tile);
             const uint32_t buf = j & 1, use = j >> 1;
             // warp-uniform, because the TMEM loads below are warp-collective
@@ -572,6 +600,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                                                               DC_DEVERR_TIMEOUT_ACC));
             if (!ok) break;
             tc_fence_after();
+            if (threadIdx.x == 0) trace_at(p, j, 3, global_timer());
             const uint32_t lane_addr =
                 tmem + buf * C::ACC_COLS + ((uint32_t)(quad * 32) << 16) + half * 64;
             const int r = tl.mrow * BM + row;  // t (FWD, BWD1, WGRAD) or i (HGRAD)
@@ -593,6 +622,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(&acce[buf]));
+            if (threadIdx.x == 0) trace_at(p, j, 4, global_timer());
         }
     }
     __syncthreads();

@@ -210,3 +210,16 @@ def profile_read(max_entries: int = 64) -> dict:
         name = names.raw[64 * k: 64 * (k + 1)].split(b"\0", 1)[0].decode()
         out[name] = (float(ms[k]), int(cnt[k]))
     return out
+
+
+def aft_trace(enable: bool = True, modes: int = 0xF, device=None):
+    """Turn on the per-tile timeline of the AFT tensor-core kernels (mode bits:
+    1 forward, 2 backward recompute, 4 dK/dV, 8 dW).  Returns the trace tensor
+    [SMs, 64, 8] (uint64 stored as int64) that later launches fill, or None."""
+    if not enable:
+        check(lib().dc_aft_trace(None, 0, 0), "dc_aft_trace")
+        return None
+    props = torch.cuda.get_device_properties(device or torch.cuda.current_device())
+    buf = torch.zeros(props.multi_processor_count, 64, 8, dtype=torch.int64, device=device or "cuda")
+    check(lib().dc_aft_trace(buf.data_ptr(), buf.numel() * 8, int(modes)), "dc_aft_trace")
+    return buf

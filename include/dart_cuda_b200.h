@@ -68,6 +68,14 @@ const char *dc_version(void);
 int dc_profile_enable(int on);
 int dc_profile_read(char *names, float *total_ms, int *counts, int max_entries);
 
+/* Per-tile timeline of the AFT tensor-core kernels (development aid).  With
+ * a device buffer of at least SMs*64*8*8 bytes, every later launch of a mode
+ * whose bit is set in mode_mask (bit 0 forward, 1 backward recompute, 2 dK/dV,
+ * 3 dW) writes, per CTA and local tile, 8 uint64 words: producer start, MMA
+ * start, MMA done, epilogue start, epilogue done (global timer, ns), tile
+ * index, K steps.  NULL turns it off. */
+int dc_aft_trace(void *device_buffer, size_t bytes, int mode_mask);
+
 /* ---------------------------------------------------------- AFT-full op
  * Z[b,t,:] = sigmoid(Q[b,t,:]) * sum_{i in S(t)} e^{K[b,i,:]+w[t,i]} V[b,i,:]
  *                               / sum_{i in S(t)} e^{K[b,i,:]+w[t,i]}
