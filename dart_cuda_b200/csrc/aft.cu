@@ -26,7 +26,7 @@
 //   WGRAD : acc[t, i] = sum_{b,d} G[b,t,d] P[b,i,d]      -> dW (split-K, atomics)
 // Operands are staged by TMA into 128-byte-swizzled shared memory; one thread
 // issues the MMAs into double-buffered TMEM accumulators; eight warps read
-// TMEM back and apply the element-wise epilogue with 16-byte accesses.
+// TMEM back and apply the element-wise epilogue with 32-byte accesses.
 #include <cuda_bf16.h>
 #include <math.h>
 
@@ -82,8 +82,8 @@ struct Params {
     int n_tiles;      // tensor-core path: number of output tiles of the launch
     int kpb;          // WGRAD: K steps per batch element (dp / BKe)
     int splits;       // WGRAD: split-K factor
-    int vec_io;       // user tensors allow 16-byte vector access along D
-    int vec_w;        // w / dW allow 16-byte vector access along a row
+    int vec_io;       // user tensors allow 32-byte vector access along D
+    int vec_w;        // w / dW allow 32-byte vector access along a row
     const void *Q, *K, *V, *dZ;
     void *Z, *dQ, *dK, *dV;
     float *dW;
@@ -706,14 +706,15 @@ static Params make_params(const Layout &L, char *ws, int flags)
     return p;
 }
 
-// 16-byte vector access along D: rows start on 16-byte boundaries when D is a
-// multiple of 16 bytes' worth of elements and every base pointer is aligned.
+// 32-byte vector access along D: every 16-element run of a row starts on a
+// 32-byte boundary when a row holds a multiple of 32 bytes and every base
+// pointer is 32-byte aligned.
 template <class IO>
 static int vec_ok(int D, std::initializer_list<const void *> ptrs)
 {
-    if ((D * (int)sizeof(IO)) % 16 != 0) return 0;
+    if ((D * (int)sizeof(IO)) % 32 != 0) return 0;
     for (const void *q : ptrs)
-        if (reinterpret_cast<uintptr_t>(q) & 15) return 0;
+        if (reinterpret_cast<uintptr_t>(q) & 31) return 0;
     return 1;
 }
 
@@ -757,7 +758,7 @@ static int bwd_impl(const void *Q, const void *K, const void *V, const float *w,
     p.w = w;
     p.ldw = ldw;
     p.vec_io = vec_ok<IO>(L.D, {Q, K, V, dZ, dQ, dK, dV});
-    p.vec_w = (ldw % 4 == 0) && ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(dW)) & 15) == 0;
+    p.vec_w = (ldw % 8 == 0) && ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(dW)) & 31) == 0;
     DC_TRY((launch<BWD1, E, IO>(p, L, ws, st, flags)));
     DC_TRY((launch<HGRAD, E, IO>(p, L, ws, st, flags)));
     // split-K factor for dW: enough CTAs to cover the SMs, >= 4 K steps each

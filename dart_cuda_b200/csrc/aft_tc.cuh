@@ -3,7 +3,7 @@
 //
 // Accumulator rows (TMEM lanes) are the query / key positions and columns are
 // channels d, so every epilogue thread owns contiguous runs of d and moves
-// them with 16-byte vector loads and stores:
+// them with 32-byte vector loads and stores:
 //
 //   FWD, BWD1 : acc[t, d]  = sum_i A'[t,i] PV[i,d]   and   sum_i A'[t,i] PE[i,d]
 //   HGRAD     : acc[i, d]  = sum_t A'[t,i] G[t,d]    and   sum_t A'[t,i] N[t,d]
@@ -56,81 +56,93 @@ struct TcCfg {
 
 // ----------------------------------------------------------- vector I/O
 // bf16 <-> fp32 by bit placement: a bf16 is the high half of an fp32.
-__device__ __forceinline__ void unpack8(const uint4 x, float (&v)[16], int o)
-{
-    v[o + 0] = __uint_as_float(x.x << 16);
-    v[o + 1] = __uint_as_float(x.x & 0xFFFF0000u);
-    v[o + 2] = __uint_as_float(x.y << 16);
-    v[o + 3] = __uint_as_float(x.y & 0xFFFF0000u);
-    v[o + 4] = __uint_as_float(x.z << 16);
-    v[o + 5] = __uint_as_float(x.z & 0xFFFF0000u);
-    v[o + 6] = __uint_as_float(x.w << 16);
-    v[o + 7] = __uint_as_float(x.w & 0xFFFF0000u);
-}
 __device__ __forceinline__ uint32_t pack2(float a, float b)
 {
     return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(a)) |
            ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(b)) << 16);
 }
+// 256-bit accesses: one full 32-byte sector per thread per instruction
+// (sm_100 global v8 loads/stores); callers guarantee 32-byte alignment.
+__device__ __forceinline__ void ld32B_nc(const void *p, uint32_t (&r)[8])
+{
+    asm volatile("ld.global.nc.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                   "=r"(r[6]), "=r"(r[7])
+                 : "l"(p));
+}
+__device__ __forceinline__ void ld32B(const void *p, uint32_t (&r)[8])
+{
+    asm volatile("ld.global.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                   "=r"(r[6]), "=r"(r[7])
+                 : "l"(p)
+                 : "memory");
+}
+__device__ __forceinline__ void st32B(void *p, const uint32_t (&r)[8])
+{
+    asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(r[0]),
+                 "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+                 : "memory");
+}
+__device__ __forceinline__ void words_to_f32(const uint32_t (&r)[8], float (&v)[16], int o)
+{
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[o + k] = __uint_as_float(r[k]);
+}
+__device__ __forceinline__ void words_to_bf16(const uint32_t (&r)[8], float (&v)[16])
+{
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        v[2 * k] = __uint_as_float(r[k] << 16);
+        v[2 * k + 1] = __uint_as_float(r[k] & 0xFFFF0000u);
+    }
+}
+
 __device__ __forceinline__ void ld16g(const float *p, float (&v)[16])
 {
-    const float4 *q = reinterpret_cast<const float4 *>(p);
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        const float4 x = __ldg(q + k);
-        v[4 * k] = x.x;
-        v[4 * k + 1] = x.y;
-        v[4 * k + 2] = x.z;
-        v[4 * k + 3] = x.w;
-    }
+    uint32_t r[8];
+    ld32B_nc(p, r);
+    words_to_f32(r, v, 0);
+    ld32B_nc(p + 8, r);
+    words_to_f32(r, v, 8);
 }
 __device__ __forceinline__ void ld16g(const __nv_bfloat16 *p, float (&v)[16])
 {
-    const uint4 *q = reinterpret_cast<const uint4 *>(p);
-#pragma unroll
-    for (int k = 0; k < 2; ++k) {
-        const uint4 x = __ldg(q + k);
-        unpack8(x, v, 8 * k);
-    }
+    uint32_t r[8];
+    ld32B_nc(p, r);
+    words_to_bf16(r, v);
 }
 // plain (coherent) loads for outputs read back when accumulating
 __device__ __forceinline__ void ld16(const float *p, float (&v)[16])
 {
-    const float4 *q = reinterpret_cast<const float4 *>(p);
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        const float4 x = q[k];
-        v[4 * k] = x.x;
-        v[4 * k + 1] = x.y;
-        v[4 * k + 2] = x.z;
-        v[4 * k + 3] = x.w;
-    }
+    uint32_t r[8];
+    ld32B(p, r);
+    words_to_f32(r, v, 0);
+    ld32B(p + 8, r);
+    words_to_f32(r, v, 8);
 }
 __device__ __forceinline__ void ld16(const __nv_bfloat16 *p, float (&v)[16])
 {
-    const uint4 *q = reinterpret_cast<const uint4 *>(p);
-#pragma unroll
-    for (int k = 0; k < 2; ++k) {
-        const uint4 x = q[k];
-        unpack8(x, v, 8 * k);
-    }
+    uint32_t r[8];
+    ld32B(p, r);
+    words_to_bf16(r, v);
 }
 __device__ __forceinline__ void st16(float *p, const float (&v)[16])
 {
-    float4 *q = reinterpret_cast<float4 *>(p);
+    uint32_t r[8];
 #pragma unroll
-    for (int k = 0; k < 4; ++k)
-        q[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+    for (int k = 0; k < 8; ++k) r[k] = __float_as_uint(v[k]);
+    st32B(p, r);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) r[k] = __float_as_uint(v[8 + k]);
+    st32B(p + 8, r);
 }
 __device__ __forceinline__ void st16(__nv_bfloat16 *p, const float (&v)[16])
 {
-    uint4 *q = reinterpret_cast<uint4 *>(p);
+    uint32_t r[8];
 #pragma unroll
-    for (int k = 0; k < 2; ++k) {
-        const int o = 8 * k;
-        q[k] = make_uint4(pack2(v[o], v[o + 1]), pack2(v[o + 2], v[o + 3]), pack2(v[o + 4], v[o + 5]),
-                          pack2(v[o + 6], v[o + 7]));
-    }
+    for (int k = 0; k < 8; ++k) r[k] = pack2(v[2 * k], v[2 * k + 1]);
+    st32B(p, r);
 }
 // operand-precision store: bf16, or tf32-rounded fp32
 __device__ __forceinline__ void st16op(__nv_bfloat16 *p, const float (&v)[16]) { st16(p, v); }
@@ -156,7 +168,7 @@ __device__ __forceinline__ float fast_sigmoid(float q) { return __fdividef(1.0f,
 // ----------------------------------------------------------- epilogues
 // One thread, one accumulator row, 16 consecutive columns starting at c0.
 // `full` = the row and all 16 columns are inside the logical tensor and the
-// tensors allow 16-byte vector access; otherwise an element-wise path runs.
+// tensors allow 32-byte vector access; otherwise an element-wise path runs.
 
 template <class IO>
 __device__ __forceinline__ void epi16_fwd(const Params &p, int b, int t, int d0,
