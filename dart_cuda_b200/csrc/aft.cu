@@ -574,21 +574,23 @@ static CUtensorMapDataType tmap_type(int esz)
 // Swizzle of a TMA box: MN-major tiles of 32-bit operands need the 32-byte
 // atom variant of the 128-byte swizzle (the smem form tcgen05 reads for
 // MN-major tf32); everything else uses the 16-byte-atom 128-byte swizzle.
-static CUtensorMapSwizzle tile_swizzle(const Layout &L, bool mn_major)
+static CUtensorMapSwizzle tile_swizzle(const Layout &L, bool mn_major, int krow = 128)
 {
-    return (mn_major && L.esz == 4) ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
-                                    : CU_TENSOR_MAP_SWIZZLE_128B;
+    if (mn_major)
+        return L.esz == 4 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B;
+    return krow == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
 }
 
-// [B][rows][dp] operand buffer; box of `bx` (inner, d) x `by` rows.
+// [B][rows][dp] operand buffer; box of `bx` (inner, d) x `by` rows.  K-major
+// boxes of `krow` bytes per row use the matching 128- or 64-byte swizzle.
 static int map_3d(CUtensorMap *m, const void *base, const Layout &L, int rows, uint32_t bx,
-                  uint32_t by, bool mn_major)
+                  uint32_t by, bool mn_major, int krow = 128)
 {
     uint64_t dims[3] = {(uint64_t)L.dp, (uint64_t)rows, (uint64_t)L.B};
     uint64_t strides[2] = {(uint64_t)L.dp * L.esz, (uint64_t)rows * L.dp * L.esz};
     uint32_t box[3] = {bx, by, 1};
     return encode_tmap(m, tmap_type(L.esz), 3, base, dims, strides, box,
-                       tile_swizzle(L, mn_major));
+                       tile_swizzle(L, mn_major, krow));
 }
 
 // A' [Tqp][Tkp]; box of `bx` (inner, i) x `by` rows (t).
@@ -635,12 +637,13 @@ static int launch_tc(Params p, const Layout &L, char *ws, cudaStream_t st)
         mA2 = mA3 = mA4 = mA;
         p.n_tiles = (L.Tkp / BM) * nd * L.B;
     } else {
-        DC_TRY(map_3d(&mA, ws + L.off_g1, L, L.Tqp, BK, BM, false));
-        DC_TRY(map_3d(&mA2, ws + L.off_g2, L, L.Tqp, BK, BM, false));
-        DC_TRY(map_3d(&mA3, ws + L.off_g1l, L, L.Tqp, BK, BM, false));
-        DC_TRY(map_3d(&mA4, ws + L.off_g2l, L, L.Tqp, BK, BM, false));
-        DC_TRY(map_3d(&mB1, ws + L.off_pv, L, L.Tkp, BK, BN, false));
-        DC_TRY(map_3d(&mB2, ws + L.off_pe, L, L.Tkp, BK, BN, false));
+        const int kr = C::KROW;
+        DC_TRY(map_3d(&mA, ws + L.off_g1, L, L.Tqp, BK, BM, false, kr));
+        DC_TRY(map_3d(&mA2, ws + L.off_g2, L, L.Tqp, BK, BM, false, kr));
+        DC_TRY(map_3d(&mA3, ws + L.off_g1l, L, L.Tqp, BK, BM, false, kr));
+        DC_TRY(map_3d(&mA4, ws + L.off_g2l, L, L.Tqp, BK, BM, false, kr));
+        DC_TRY(map_3d(&mB1, ws + L.off_pv, L, L.Tkp, BK, BN, false, kr));
+        DC_TRY(map_3d(&mB2, ws + L.off_pe, L, L.Tkp, BK, BN, false, kr));
         mB3 = mB4 = mB1;
         const int mt = L.Tqp / BM, nt = L.Tkp / BN;
         p.n_tiles = (p.causal ? mt * (mt + 1) / 2 : mt * nt) * p.splits;

@@ -9,17 +9,18 @@
 //   HGRAD     : acc[i, d]  = sum_t A'[t,i] G[t,d]    and   sum_t A'[t,i] N[t,d]
 //   WGRAD     : acc[t, i]  = sum_{b,d} (G PV^T + N PE^T + G_lo PV^T + N_lo PE^T)
 //
-// Warp roles (320 threads): warps 0-7 epilogue (warp w reads TMEM lanes
-// 32*(w%4).. and half w/4 of the columns), warp 8 TMA producer, warp 9 TMEM
-// allocator + MMA issuer.  Each CTA loops over tiles tile = blockIdx.x +
-// k*gridDim.x; the accumulator is double-buffered in TMEM so the epilogue of
-// one tile overlaps the main loop of the next.
+// Warp roles (576 threads): warps 0-15 epilogue (warp w reads TMEM lanes
+// 32*(w%4).. and the 32-column slice w/4), warp 16 TMA producer, warp 17
+// TMEM allocator + MMA issuer.  Sixteen epilogue warps (four per SM
+// sub-partition) hide the latency of the element-wise epilogue.  Each CTA
+// walks its tiles (sched_tile); the accumulator is double-buffered in TMEM
+// so the epilogue of one tile overlaps the main loop of the next.
 #pragma once
 
 namespace dc {
 namespace aft {
 
-constexpr int kEpiWarps = 8;
+constexpr int kEpiWarps = 16;
 constexpr int kTcThreads = (kEpiWarps + 2) * 32;
 constexpr int kSmemBudget = 227 * 1024;
 
@@ -28,11 +29,17 @@ struct TcCfg {
     static constexpr bool TF32 = sizeof(E) == 4;
     static constexpr bool W = MODE == WGRAD;
     static constexpr bool H = MODE == HGRAD;
-    static constexpr int BKe = 128 / (int)sizeof(E);   // K elements per stage (one 128 B row)
+    // bytes of K per operand row and stage: dW streams six K-major tiles per
+    // stage, so it uses 64 B rows (64-byte swizzle) to keep four stages.
+    static constexpr int KROW = W ? 64 : 128;
+    static constexpr int BKe = KROW / (int)sizeof(E);  // K elements per stage
     static constexpr int UK = TF32 ? 8 : 16;           // K per MMA instruction
     static constexpr int NSUB = BKe / UK;              // MMAs per stage and operand pair
     static constexpr int BOX_MN = 128 / (int)sizeof(E);// elements in one 128 B MN block
-    static constexpr int TILE_BYTES = 128 * 128;       // one 128 x (128 B) operand tile
+    static constexpr int TILE_BYTES = 128 * KROW;      // one operand tile of 128 rows
+    // K-major descriptor: swizzle mode (2 = 128 B, 4 = 64 B), 8-row atom stride
+    static constexpr uint32_t K_LAYOUT = KROW == 64 ? 4u : 2u;
+    static constexpr uint32_t K_SBO = 8 * KROW;
     // dK/dV at tf32 also adds the low parts of g and n (1e-3 bar)
     static constexpr bool LO = W || (H && TF32);
     static constexpr int NA = W ? 4 : 1;               // A tiles per stage
@@ -556,19 +563,23 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         const uint32_t koff = u * C::UK * (int)sizeof(E);  // K-major step
                         const uint32_t moff = u * C::UK * 128;             // MN-major step
                         if (C::W) {
-                            const uint64_t b1 = sw128_desc(sb + koff, 16, 1024);
-                            const uint64_t b2 = sw128_desc(sb + C::TILE_BYTES + koff, 16, 1024);
-                            umma<C::TF32>(acc, sw128_desc(sa + koff, 16, 1024), b1, C::IDESC, first);
-                            umma<C::TF32>(acc, sw128_desc(sa + C::TILE_BYTES + koff, 16, 1024), b2,
-                                          C::IDESC, 1u);
-                            umma<C::TF32>(acc, sw128_desc(sa + 2 * C::TILE_BYTES + koff, 16, 1024),
+                            const uint32_t T = C::TILE_BYTES;
+                            const uint64_t b1 = sw128_desc(sb + koff, 16, C::K_SBO, C::K_LAYOUT);
+                            const uint64_t b2 = sw128_desc(sb + T + koff, 16, C::K_SBO, C::K_LAYOUT);
+                            umma<C::TF32>(acc, sw128_desc(sa + koff, 16, C::K_SBO, C::K_LAYOUT), b1,
+                                          C::IDESC, first);
+                            umma<C::TF32>(acc, sw128_desc(sa + T + koff, 16, C::K_SBO, C::K_LAYOUT),
+                                          b2, C::IDESC, 1u);
+                            umma<C::TF32>(acc,
+                                          sw128_desc(sa + 2 * T + koff, 16, C::K_SBO, C::K_LAYOUT),
                                           b1, C::IDESC, 1u);
-                            umma<C::TF32>(acc, sw128_desc(sa + 3 * C::TILE_BYTES + koff, 16, 1024),
+                            umma<C::TF32>(acc,
+                                          sw128_desc(sa + 3 * T + koff, 16, C::K_SBO, C::K_LAYOUT),
                                           b2, C::IDESC, 1u);
                         } else {
                             const uint64_t a = C::H ? sw128_desc(sa + moff, C::MN_LBO, C::MN_SBO,
                                                                  C::MN_LAYOUT)
-                                                    : sw128_desc(sa + koff, 16, 1024);
+                                                    : sw128_desc(sa + koff, 16, C::K_SBO, C::K_LAYOUT);
                             const uint64_t b1 =
                                 sw128_desc(sb + moff, C::MN_LBO, C::MN_SBO, C::MN_LAYOUT);
                             const uint64_t b2 = sw128_desc(sb + C::TILE_BYTES + moff, C::MN_LBO,
@@ -597,9 +608,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
         }
     } else {
-        // ------------------------------------------------ epilogue (warps 0-7)
+        // ------------------------------------------------ epilogue (warps 0-15)
         const int quad = warp & 3;           // TMEM lanes 32*quad .. 32*quad+31
-        const int half = warp >> 2;          // columns half*64 .. half*64+63
+        const int slice = warp >> 2;         // columns slice*32 .. slice*32+31
         const int row = quad * 32 + lane;
         for (uint32_t j = 0;; ++j) {
             const int tile = sched_tile(j, ntiles);
@@ -614,14 +625,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             tc_fence_after();
             if (threadIdx.x == 0) trace_at(p, j, 3, global_timer());
             const uint32_t lane_addr =
-                tmem + buf * C::ACC_COLS + ((uint32_t)(quad * 32) << 16) + half * 64;
+                tmem + buf * C::ACC_COLS + ((uint32_t)(quad * 32) << 16) + slice * 32;
             const int r = tl.mrow * BM + row;  // t (FWD, BWD1, WGRAD) or i (HGRAD)
 #pragma unroll 1
-            for (int sb = 0; sb < 4; ++sb) {
+            for (int sb = 0; sb < 2; ++sb) {
                 float v1[16], v2[16];
                 tmem_ld16(lane_addr + sb * 16, v1);
                 if (!C::W) tmem_ld16(lane_addr + BN + sb * 16, v2);
-                const int c0 = tl.ncol * BN + half * 64 + sb * 16;  // d, or i for WGRAD
+                const int c0 = tl.ncol * BN + slice * 32 + sb * 16;  // d, or i for WGRAD
                 if (MODE == FWD)
                     epi16_fwd<IO>(p, tl.b, r, c0, v1, v2);
                 else if (MODE == BWD1)
