@@ -8,6 +8,7 @@
 #include <math.h>
 
 #include <algorithm>
+#include <mutex>
 
 #include "dc_internal.h"
 
@@ -677,6 +678,69 @@ int dc_ce_fwd(const float *logits, const int32_t *targets, float *loss, float *r
     cudaError_t e = cudaGetLastError();
     if (!row_loss) cudaFreeAsync(rows, st);
     if (e != cudaSuccess) return fail(DC_ERR_CUDA, "ce fwd: %s", cudaGetErrorString(e));
+    return DC_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Cross-entropy forward for callers that must not allocate device memory.
+//
+// dc_ce_fwd needs T floats of scratch for the per-row losses before it
+// reduces them to the mean; without a caller buffer it takes them from the
+// stream-ordered allocator.  Some callers cannot allow any allocation inside
+// the loss call: a host runtime that owns all device memory up front and
+// forbids the library from allocating, or a step that must never wait on or
+// grow the allocator pool.  This entry point keeps the per-row losses in a
+// fixed array compiled into the library instead.
+//
+// Limit: T <= DC_CE_NOALLOC_MAX_ROWS (65536 rows, 256 KiB per GPU).  The array
+// exists on every GPU that loads the library and stays resident until the
+// process exits.  It is shared by every call on a device and holds the last
+// call's row losses; each call overwrites all T entries it reads, so nothing
+// needs clearing, but calls that overlap on the GPU (other streams, other
+// host threads) race on it and must be serialised by the caller.
+// The first call on each device looks the array's device address up (the
+// host-side symbol is only a stand-in for it); make that first call before
+// any stream capture.
+// ---------------------------------------------------------------------------
+#define DC_CE_NOALLOC_MAX_ROWS 65536
+
+static __device__ __align__(256) float g_ce_noalloc_rows[DC_CE_NOALLOC_MAX_ROWS];
+
+static float *ce_noalloc_rows_ptr()
+{
+    static float *ptrs[64] = {nullptr};
+    static std::mutex mu;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!ptrs[dev]) {
+        void *p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_ce_noalloc_rows) != cudaSuccess) return nullptr;
+        ptrs[dev] = static_cast<float *>(p);
+    }
+    return ptrs[dev];
+}
+
+int dc_ce_fwd_noalloc(const float *logits, const int32_t *targets, float *loss, int T, int V,
+                      float eps, void *stream)
+{
+    clear_error();
+    if (T < 0 || V <= 0) return fail(DC_ERR_INVALID, "bad shape T=%d V=%d", T, V);
+    if (T > DC_CE_NOALLOC_MAX_ROWS)
+        return fail(DC_ERR_INVALID, "dc_ce_fwd_noalloc: T=%d rows exceeds the fixed scratch of %d rows",
+                    T, DC_CE_NOALLOC_MAX_ROWS);
+    if (T == 0) return DC_OK;
+    if (!logits || !targets || !loss) return fail(DC_ERR_INVALID, "null pointer");
+    float *rows = ce_noalloc_rows_ptr();
+    if (!rows) return fail(DC_ERR_CUDA, "dc_ce_fwd_noalloc: cannot resolve the scratch array address");
+    cudaStream_t st = as_stream(stream);
+    if (V <= 1024)
+        ce_fwd_warp<<<(T + 7) / 8, 256, 0, st>>>(logits, targets, rows, T, V, eps);
+    else
+        ce_fwd_block<<<T, 256, 0, st>>>(logits, targets, rows, T, V, eps);
+    mean_kernel<<<1, 1024, 0, st>>>(rows, T, loss);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(DC_ERR_CUDA, "ce fwd noalloc: %s", cudaGetErrorString(e));
     return DC_OK;
 }
 

@@ -132,6 +132,17 @@ int dc_ce_fwd(const float *logits, const int32_t *targets, float *loss, float *r
 int dc_ce_bwd(const float *logits, const int32_t *targets, const float *grad_scale,
               float *dlogits, int T, int V, float eps, void *stream);
 
+/* Cross-entropy forward that allocates nothing (no counterpart in the
+ * reference).  Same result as dc_ce_fwd(..., row_loss = NULL, ...), for
+ * callers that cannot let the library allocate device memory during the
+ * call.  The per-row losses live in a fixed array inside the library, so
+ * T <= 65536; larger T returns DC_ERR_INVALID.  The array is shared by all
+ * calls on a device: calls that overlap on the GPU race and must be
+ * serialised by the caller.  The first call on each device resolves the
+ * array's device address; make it before any stream capture. */
+int dc_ce_fwd_noalloc(const float *logits, const int32_t *targets, float *loss, int T, int V,
+                      float eps, void *stream);
+
 /* AdamW exactly as the reference applies it (step = t+1, decoupled weight
  * decay p -= lr*wd*p with wd = 0.001 in the reference).  Replaces
  * adam_kernel (native/src/kernels/loss_optim.cuh:255-298). */
