@@ -197,13 +197,13 @@ __device__ __forceinline__ float block_max(float v, float *red)
 
 // ------------------------------------------------------------ prep kernels
 // Row maxima m_t over the visible set and A' = exp(w - m) (0 outside the
-// set and in the padding), one block per padded row.
+// set and in the padding), one block per padded row t.
 template <class E>
-__global__ void prep_w_kernel(const float *__restrict__ w, int ldw, int Tq, int Tk, int Tkp,
-                              int causal, float *__restrict__ m, E *__restrict__ Ap)
+__device__ __forceinline__ void prep_w_row(int t, const float *__restrict__ w, int ldw, int Tq,
+                                           int Tk, int Tkp, int causal, float *__restrict__ m,
+                                           E *__restrict__ Ap)
 {
     __shared__ float red[32];
-    const int t = blockIdx.x;
     E *row = Ap + (size_t)t * Tkp;
     if (t >= Tq) {
         for (int i = threadIdx.x; i < Tkp; i += blockDim.x) row[i] = to_op<E>(0.f);
@@ -240,13 +240,14 @@ __device__ __forceinline__ void ld8(const __nv_bfloat16 *p, float (&v)[8])
 }
 
 template <class IO>
-__global__ void prep_colmax_kernel(const IO *__restrict__ K, int B, int Tk, int D, int dp,
-                                   int rows_per_split, int vec, float *__restrict__ cpart)
+__device__ __forceinline__ void prep_colmax_block(int bx, int s, int b, const IO *__restrict__ K,
+                                                  int B, int Tk, int D, int dp,
+                                                  int rows_per_split, int vec,
+                                                  float *__restrict__ cpart)
 {
     __shared__ float red[8][32 * 8 + 1];
     const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
-    const int d0 = (blockIdx.x * 32 + tx) * 8;
-    const int s = blockIdx.y, b = blockIdx.z;
+    const int d0 = (bx * 32 + tx) * 8;
     const int i0 = s * rows_per_split, i1 = min(Tk, i0 + rows_per_split);
     const IO *Kb = K + (size_t)b * Tk * D;
     float mx[8];
@@ -273,22 +274,29 @@ __global__ void prep_colmax_kernel(const IO *__restrict__ K, int B, int Tk, int 
     float m = red[0][j];
 #pragma unroll
     for (int r = 1; r < 8; ++r) m = fmaxf(m, red[r][j]);
-    const int d = blockIdx.x * 256 + j;
+    const int d = bx * 256 + j;
     if (d < D) cpart[((size_t)s * B + b) * dp + d] = m;
 }
 
-__global__ void prep_colmax_final_kernel(const float *__restrict__ cpart, int nsplit, int B,
-                                         int D, int dp, float *__restrict__ c)
+// First prep launch: blocks [0, Tqp) build the rows of A' and m; the
+// remaining blocks compute the partial column maxima of K (ncb column blocks
+// of 256 x nsplit row slices x B).
+template <class IO, class E>
+__global__ void __launch_bounds__(256)
+    prep_wc_kernel(const float *__restrict__ w, int ldw, int Tq, int Tk, int Tkp, int causal,
+                   float *__restrict__ m, E *__restrict__ Ap, const IO *__restrict__ K, int B,
+                   int D, int dp, int ncb, int nsplit, int rows_per_split, int vec,
+                   float *__restrict__ cpart)
 {
-    const int idx = blockIdx.x * blockDim.x + threadIdx.x;
-    if (idx >= B * dp) return;
-    const int d = idx % dp;
-    float mx = 0.f;
-    if (d < D) {
-        mx = -INFINITY;
-        for (int s = 0; s < nsplit; ++s) mx = fmaxf(mx, cpart[(size_t)s * B * dp + idx]);
+    const int bid = blockIdx.x;
+    const int Tqp = gridDim.x - ncb * nsplit * B;
+    if (bid < Tqp) {
+        prep_w_row<E>(bid, w, ldw, Tq, Tk, Tkp, causal, m, Ap);
+        return;
     }
-    c[idx] = mx;
+    const int q = bid - Tqp;
+    prep_colmax_block<IO>(q % ncb, (q / ncb) % nsplit, q / (ncb * nsplit), K, B, Tk, D, dp,
+                          rows_per_split, vec, cpart);
 }
 
 // PV = exp(K - c) * V and PE = exp(K - c) over the padded [B, Tkp, dp] space,
@@ -315,27 +323,42 @@ __device__ __forceinline__ void st8op(float *p, const float (&v)[8])
     reinterpret_cast<float4 *>(p)[1] = b;
 }
 
+// Block (128 columns x 16 row lanes) of batch b = blockIdx.z: the block first
+// finishes the column maxima of its 128 columns from the nsplit partials (and
+// stores them to c for the backward's epilogue), then walks its row range.
 template <class IO, class E>
-__global__ void prep_p_kernel(const IO *__restrict__ K, const IO *__restrict__ V,
-                              const float *__restrict__ c, int B, int Tk, int D, int Tkp,
-                              int dp, int vec, E *__restrict__ PV, E *__restrict__ PE)
+__global__ void __launch_bounds__(256)
+    prep_p_kernel(const IO *__restrict__ K, const IO *__restrict__ V,
+                  const float *__restrict__ cpart, int nsplit, float *__restrict__ c, int B,
+                  int Tk, int D, int Tkp, int dp, int rows_per_block, int vec,
+                  E *__restrict__ PV, E *__restrict__ PE)
 {
-    const int nch = dp / 8;
-    const size_t total = (size_t)B * Tkp * nch;
-    for (size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
-         idx += (size_t)gridDim.x * blockDim.x) {
-        const int d0 = (int)(idx % nch) * 8;
-        const size_t r = idx / nch;
-        const int i = (int)(r % Tkp);
-        const int b = (int)(r / Tkp);
+    __shared__ __align__(16) float cs[128];
+    const int b = blockIdx.z;
+    const int dblk = blockIdx.x * 128;
+    if (threadIdx.x < 128) {
+        const int d = dblk + threadIdx.x;
+        float mx = 0.f;
+        if (d < D) {
+            mx = -INFINITY;
+            for (int s = 0; s < nsplit; ++s) mx = fmaxf(mx, cpart[((size_t)s * B + b) * dp + d]);
+        }
+        cs[threadIdx.x] = mx;
+        if (blockIdx.y == 0) c[(size_t)b * dp + d] = mx;
+    }
+    __syncthreads();
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    const int d0 = dblk + tx * 8;
+    float cc[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) cc[k] = cs[tx * 8 + k];
+    const int r0 = blockIdx.y * rows_per_block, r1 = min(Tkp, r0 + rows_per_block);
+    for (int i = r0 + ty; i < r1; i += 16) {
         float pv[8], pe[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k) pv[k] = pe[k] = 0.f;
         if (i < Tk) {
             const size_t src = ((size_t)b * Tk + i) * D + d0;
-            const float *cb = c + (size_t)b * dp + d0;
-            float cc[8];
-            ld8(cb, cc);
             if (vec && d0 + 8 <= D) {
                 float k8[8], v8[8];
                 ld8(K + src, k8);
@@ -539,28 +562,28 @@ static int run_prep(const Layout &L, const IO *K, const IO *V, const float *w, i
     E *Ap = reinterpret_cast<E *>(ws + L.off_ap);
     E *PV = reinterpret_cast<E *>(ws + L.off_pv);
     E *PE = reinterpret_cast<E *>(ws + L.off_pe);
-    {
-        KernelTimer kt("aft_prep_w", st);
-        prep_w_kernel<E><<<L.Tqp, 256, 0, st>>>(w, ldw, L.Tq, L.Tk, L.Tkp, causal, m, Ap);
-    }
     // 16-byte access to K and V rows: D a multiple of 8 and aligned bases
     const int vec = (L.D % 8 == 0) &&
                     ((reinterpret_cast<uintptr_t>(K) | reinterpret_cast<uintptr_t>(V)) & 15) == 0;
     {
-        KernelTimer kt("aft_prep_colmax", st);
-        dim3 g1((L.D + 255) / 256, L.nsplit, L.B);
-        prep_colmax_kernel<IO><<<g1, 256, 0, st>>>(K, L.B, L.Tk, L.D, L.dp, L.rows_per_split,
-                                                   vec, cpart);
-        const int nbd = L.B * L.dp;
-        prep_colmax_final_kernel<<<(nbd + 255) / 256, 256, 0, st>>>(cpart, L.nsplit, L.B, L.D,
-                                                                      L.dp, c);
+        // A' rows and the partial column maxima of K in one launch
+        KernelTimer kt("aft_prep_w_colmax", st);
+        const int ncb = (L.D + 255) / 256;
+        const int grid = L.Tqp + ncb * L.nsplit * L.B;
+        prep_wc_kernel<IO, E><<<grid, 256, 0, st>>>(w, ldw, L.Tq, L.Tk, L.Tkp, causal, m, Ap, K,
+                                                    L.B, L.D, L.dp, ncb, L.nsplit,
+                                                    L.rows_per_split, vec, cpart);
     }
     {
         KernelTimer kt("aft_prep_p", st);
-        const size_t total = (size_t)L.B * L.Tkp * (L.dp / 8);
-        const int blocks = (int)std::min<size_t>((total + 255) / 256, (size_t)sm_count() * 16);
-        prep_p_kernel<IO, E><<<blocks, 256, 0, st>>>(K, V, c, L.B, L.Tk, L.D, L.Tkp, L.dp, vec, PV,
-                                                     PE);
+        const int ndb = L.dp / 128;
+        const int target = sm_count() * 4;
+        int rsplit = std::max(1, (target + ndb * L.B - 1) / (ndb * L.B));
+        rsplit = std::min(rsplit, std::max(1, L.Tkp / 16));
+        const int rows_per_block = (L.Tkp + rsplit - 1) / rsplit;
+        rsplit = (L.Tkp + rows_per_block - 1) / rows_per_block;
+        prep_p_kernel<IO, E><<<dim3(ndb, rsplit, L.B), 256, 0, st>>>(
+            K, V, cpart, L.nsplit, c, L.B, L.Tk, L.D, L.Tkp, L.dp, rows_per_block, vec, PV, PE);
     }
     DC_CUDA_TRY(cudaGetLastError());
     return DC_OK;
