@@ -326,17 +326,23 @@ def main():
                       "GB/s": gbs, "TFLOP/s": tfs,
                       "hbm_frac": gbs / P["hbm_gbs"], "tensor_frac": tfs / P["bf16_tflops"]}
     dom = max(prof, key=lambda k: prof[k][0]) if prof else None
+    # measured DRAM traffic per launch (ncu capture summarised under profiles/)
+    traffic = None
+    tf = ROOT / "profiles" / f"aft_{args.config}_traffic.json"
+    if dom and tf.exists():
+        traffic = json.loads(tf.read_text())["dram_bytes_per_launch"].get(dom)
     roof = None
     if dom:
         k = kern[dom]
         bound = "tensor" if k["tensor_frac"] > k["hbm_frac"] else "hbm"
         if bound == "tensor":
             roof = {"bound": "tensor", "achieved": k["TFLOP/s"], "peak": P["bf16_tflops"], "unit": "TFLOP/s",
-                    "frac": k["tensor_frac"], "traffic": None, "kernel": dom,
+                    "frac": k["tensor_frac"], "traffic": traffic, "kernel": dom,
                     "peak_source": P["source"] + " bf16 burst"}
         else:
             roof = {"bound": "hbm", "achieved": k["GB/s"], "peak": P["hbm_gbs"], "unit": "GB/s",
-                    "frac": k["hbm_frac"], "traffic": None, "kernel": dom, "peak_source": P["source"]}
+                    "frac": k["hbm_frac"], "traffic": traffic, "kernel": dom, "peak_source": P["source"],
+                    "algorithmic_bytes": bytes_per.get(dom)}
 
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
