@@ -93,6 +93,7 @@ struct Params {
     const float *c;   // [B][dp]
     void *G1, *G2;    // g and n = -g*r, [B][Tqp][dp] operand precision
     void *G1l, *G2l;  // their rounding residuals (g - G1, n - G2), same layout
+    int lo_rows;      // the residuals exist for query rows t < lo_rows (multiple of 128)
     int *status;
     unsigned long long *trace;  // optional per-tile timeline (nullptr: off)
 };
@@ -728,6 +729,12 @@ static Params make_params(const Layout &L, char *ws, int flags)
     p.G2 = ws + L.off_g2;
     p.G1l = ws + L.off_g1l;
     p.G2l = ws + L.off_g2l;
+    // Where the rounding residuals of g and n are kept.  dW's terms
+    // g*E'V + n*E' cancel most (and g = dZ*sigmoid(Q)/den' is largest) in the
+    // first query rows, where den' sums few terms; with bf16 operands the
+    // residuals of rows t < 128 bring dW to the accuracy of keeping them all.
+    // tf32 keeps them everywhere (they also enter dK/dV there).
+    p.lo_rows = L.esz == 4 ? L.Tqp : std::min(L.Tqp, BM);
     p.status = device_status_word();
     return p;
 }

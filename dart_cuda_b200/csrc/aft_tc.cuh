@@ -249,12 +249,13 @@ __device__ __forceinline__ void epi16_bwd1(const Params &p, int b, int t, int d0
     const size_t go = ((size_t)b * p.Tqp + t) * p.dp + d0;
     float hi[16], lo[16];
     constexpr bool BF = sizeof(E) == 2;
+    const bool keep_lo = t < p.lo_rows;
     round16(g, hi, lo, BF);
     st16op((E *)p.G1 + go, hi);
-    st16op((E *)p.G1l + go, lo);
+    if (keep_lo) st16op((E *)p.G1l + go, lo);
     round16(n, hi, lo, BF);
     st16op((E *)p.G2 + go, hi);
-    st16op((E *)p.G2l + go, lo);
+    if (keep_lo) st16op((E *)p.G2l + go, lo);
 }
 
 template <class IO>
@@ -477,7 +478,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         break;
                     }
                     const uint32_t fb = smem_u32(&full[s]);
-                    mbar_arrive_expect_tx(fb, C::STAGE_BYTES);
+                    // dW tiles past the first row block carry no low parts
+                    const bool w_lo = !C::W || tl.mrow * BM < p.lo_rows;
+                    mbar_arrive_expect_tx(fb, w_lo ? C::STAGE_BYTES
+                                                   : C::STAGE_BYTES - 2 * C::TILE_BYTES);
                     const uint32_t sa = smem_u32(smem + s * C::STAGE_BYTES);
                     const uint32_t sb = sa + C::NA * C::TILE_BYTES;
                     if (MODE == FWD || MODE == BWD1) {
@@ -514,8 +518,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         const int bb = k / p.kpb, x = (k % p.kpb) * C::BKe;
                         tma_load_3d(sa, &mapA, fb, x, tl.mrow * BM, bb);
                         tma_load_3d(sa + C::TILE_BYTES, &mapA2, fb, x, tl.mrow * BM, bb);
-                        tma_load_3d(sa + 2 * C::TILE_BYTES, &mapA3, fb, x, tl.mrow * BM, bb);
-                        tma_load_3d(sa + 3 * C::TILE_BYTES, &mapA4, fb, x, tl.mrow * BM, bb);
+                        if (w_lo) {
+                            tma_load_3d(sa + 2 * C::TILE_BYTES, &mapA3, fb, x, tl.mrow * BM, bb);
+                            tma_load_3d(sa + 3 * C::TILE_BYTES, &mapA4, fb, x, tl.mrow * BM, bb);
+                        }
                         tma_load_3d(sb, &mapB1, fb, x, tl.ncol * BN, bb);
                         tma_load_3d(sb + C::TILE_BYTES, &mapB2, fb, x, tl.ncol * BN, bb);
                     }
@@ -547,6 +553,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 trace_at(p, j, 5, tile);
                 trace_at(p, j, 6, tl.k1 - tl.k0);
                 const uint32_t acc = tmem + buf * C::ACC_COLS;
+                const bool w_lo = tl.mrow * BM < p.lo_rows;
                 for (int k = tl.k0; k < tl.k1; ++k, ++g) {
                     const int s = g % C::STAGES;
                     if (!mbar_wait(smem_u32(&full[s]), (g / C::STAGES) & 1, abort_flag, p.status,
@@ -570,6 +577,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                                           C::IDESC, first);
                             umma<C::TF32>(acc, sw128_desc(sa + T + koff, 16, C::K_SBO, C::K_LAYOUT),
                                           b2, C::IDESC, 1u);
+                            if (!w_lo) continue;
                             umma<C::TF32>(acc,
                                           sw128_desc(sa + 2 * T + koff, 16, C::K_SBO, C::K_LAYOUT),
                                           b1, C::IDESC, 1u);
