@@ -141,17 +141,23 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of a CUDA graph")
+    ap.add_argument("--backward", default="auto", choices=["auto", "stats", "recompute"],
+                    help="stats: the forward keeps r, 1/den for the backward; recompute: the backward "
+                         "repeats the forward contraction; auto: stats from T >= 1024, where the "
+                         "contraction costs more than the 16 bytes per element of saved statistics")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     args = ap.parse_args()
 
     B, T, d, dt, desc = CONFIGS[args.config]
+    stats = args.backward == "stats" or (args.backward == "auto" and T >= 1024)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     config = {"workload": desc, "B_per_gpu": B, "T": T, "d": d, "causal": True,
               "global_batch": B * world, "seq_len": T, "parallelism": f"batch-shard x{world}",
               "l2": "flushed between steps (256 MiB write)",
-              "cuda_graph": not args.no_graph}
+              "cuda_graph": not args.no_graph,
+              "backward": "reads the forward's r, 1/den" if stats else "recomputes num/den"}
 
     if args.impl == "reference":
         if rank != 0:
@@ -198,7 +204,7 @@ def main():
     Z = torch.empty_like(Q)
     dQ, dK, dV = torch.empty_like(Q), torch.empty_like(K_), torch.empty_like(V)
     dW = torch.empty(T, T, device=dev)
-    ws = ops.AftWorkspace(B, T, T, d, tdt, flags=1, device=dev)
+    ws = ops.AftWorkspace(B, T, T, d, tdt, flags=1, device=dev, save_stats=stats)
     flush = torch.empty(256 * 1024 * 1024 // 4, device=dev)
 
     def compute():
@@ -307,11 +313,13 @@ def main():
     io = B * T * d * esz           # one user tensor
     pan = B * Tp * dp_ * esz        # one operand panel (E'V, E', g or n)
     ap_ = Tp * Tp * esz
+    stat = B * Tp * dp_ * 4 if stats else 0  # one saved statistic (r or 1/den)
     bytes_per = {
         "aft_prep_w_colmax": T * T * 4 + ap_ + io,
         "aft_prep_p": 2 * io + 2 * pan,
-        "aft_tc_fwd": 2 * pan + ap_ + 2 * io,
+        "aft_tc_fwd": 2 * pan + ap_ + 2 * io + 2 * stat,
         "aft_tc_bwd_recompute": 2 * pan + ap_ + 3 * io + 2 * pan,
+        "aft_bwd_from_stats": 3 * io + 2 * stat + 2 * pan,
         "aft_tc_dkdv": 2 * pan + ap_ + 4 * io,
         "aft_tc_dw": 4 * pan + 2 * T * T * 4,
     }

@@ -21,6 +21,7 @@ DC_AFT_ACCUMULATE = 0x2
 DC_AFT_WS_VALID = 0x4
 DC_AFT_SIMT = 0x8
 DC_AFT_COMPUTE_BF16 = 0x10
+DC_AFT_SAVE_STATS = 0x20
 
 _lib = None
 

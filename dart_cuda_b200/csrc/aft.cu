@@ -94,6 +94,7 @@ struct Params {
     void *G1, *G2;    // g and n = -g*r, [B][Tqp][dp] operand precision
     void *G1l, *G2l;  // their rounding residuals (g - G1, n - G2), same layout
     int lo_rows;      // the residuals exist for query rows t < lo_rows (multiple of 128)
+    float *Rs, *Is;   // forward statistics r = num/den and 1/den, [B][Tqp][dp] (nullptr: not kept)
     int *status;
     unsigned long long *trace;  // optional per-tile timeline (nullptr: off)
 };
@@ -458,10 +459,37 @@ __global__ void aft_simt_kernel(const Params p, const E *__restrict__ Ap,
 namespace dc {
 namespace aft {
 
+// Backward from the forward's saved statistics: the element-wise maths of the
+// recompute epilogue (epi16_bwd1) with r and 1/den read back, so the backward
+// needs no second pass of the forward contraction.  One thread per 16
+// columns of one padded row; consecutive threads walk a row.
+template <class IO, class E>
+__global__ void __launch_bounds__(256) bwd_stats_kernel(const Params p)
+{
+    const int groups = p.dp / 16;
+    const size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= (size_t)p.B * p.Tqp * groups) return;
+    const int d0 = (int)(idx % groups) * 16;
+    const size_t bt = idx / groups;
+    const int t = (int)(bt % p.Tqp);
+    const int b = (int)(bt / p.Tqp);
+    float r[16], inv[16];
+    if (t < p.Tq) {
+        const size_t so = ((size_t)b * p.Tqp + t) * p.dp + d0;
+        ld16g(p.Rs + so, r);
+        ld16g(p.Is + so, inv);
+    } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) r[j] = inv[j] = 0.f;
+    }
+    epi16_grads<IO, E>(p, b, t, d0, r, inv);
+}
+
 // ------------------------------------------------------------ host side
 struct Layout {
     int B, Tq, Tk, D, Tqp, Tkp, dp, esz, nsplit, rows_per_split;
     size_t off_m, off_c, off_cpart, off_ap, off_pv, off_pe, off_g1, off_g2, off_g1l, off_g2l;
+    size_t off_rs, off_is;  // saved forward statistics (DC_AFT_SAVE_STATS only)
     size_t total;
 };
 
@@ -502,6 +530,9 @@ static Layout make_layout(int B, int Tq, int Tk, int D, int dtype, int flags)
     L.off_g2 = take((size_t)B * L.Tqp * L.dp * L.esz);
     L.off_g1l = take((size_t)B * L.Tqp * L.dp * L.esz);
     L.off_g2l = take((size_t)B * L.Tqp * L.dp * L.esz);
+    const size_t nstat = (flags & DC_AFT_SAVE_STATS) ? (size_t)B * L.Tqp * L.dp * 4 : 0;
+    L.off_rs = take(nstat);
+    L.off_is = take(nstat);
     L.total = off;
     return L;
 }
@@ -711,6 +742,12 @@ static int launch(const Params &p, const Layout &L, char *ws, cudaStream_t st, i
     return launch_tc<MODE, E, IO>(p, L, ws, st);
 }
 
+// The tensor-core forward keeps r and 1/den for the backward.
+static bool saves_stats(int flags)
+{
+    return (flags & DC_AFT_SAVE_STATS) && !(flags & DC_AFT_SIMT);
+}
+
 static Params make_params(const Layout &L, char *ws, int flags)
 {
     Params p{};
@@ -735,6 +772,10 @@ static Params make_params(const Layout &L, char *ws, int flags)
     // residuals of rows t < 128 bring dW to the accuracy of keeping them all.
     // tf32 keeps them everywhere (they also enter dK/dV there).
     p.lo_rows = L.esz == 4 ? L.Tqp : std::min(L.Tqp, BM);
+    if (saves_stats(flags)) {
+        p.Rs = reinterpret_cast<float *>(ws + L.off_rs);
+        p.Is = reinterpret_cast<float *>(ws + L.off_is);
+    }
     p.status = device_status_word();
     return p;
 }
@@ -792,7 +833,14 @@ static int bwd_impl(const void *Q, const void *K, const void *V, const float *w,
     p.ldw = ldw;
     p.vec_io = vec_ok<IO>(L.D, {Q, K, V, dZ, dQ, dK, dV});
     p.vec_w = (ldw % 8 == 0) && ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(dW)) & 31) == 0;
-    DC_TRY((launch<BWD1, E, IO>(p, L, ws, st, flags)));
+    if ((flags & DC_AFT_WS_VALID) && saves_stats(flags)) {
+        KernelTimer kt("aft_bwd_from_stats", st);
+        const size_t n = (size_t)L.B * L.Tqp * (L.dp / 16);
+        bwd_stats_kernel<IO, E><<<(unsigned)((n + 255) / 256), 256, 0, st>>>(p);
+        DC_CUDA_TRY(cudaGetLastError());
+    } else {
+        DC_TRY((launch<BWD1, E, IO>(p, L, ws, st, flags)));
+    }
     DC_TRY((launch<HGRAD, E, IO>(p, L, ws, st, flags)));
     // split-K factor for dW: enough CTAs to cover the SMs, >= 4 K steps each
     p.kpb = L.dp / TcCfg<WGRAD, E>::BKe;

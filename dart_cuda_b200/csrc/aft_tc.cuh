@@ -182,6 +182,17 @@ __device__ __forceinline__ void epi16_fwd(const Params &p, int b, int t, int d0,
                                           const float (&num)[16], const float (&den)[16])
 {
     if (t >= p.Tq) return;
+    if (p.Rs) {  // r and 1/den for the backward, exactly as epi16_bwd1 forms them
+        const size_t so = ((size_t)b * p.Tqp + t) * p.dp + d0;
+        float r[16], inv[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            inv[j] = __fdividef(1.0f, den[j]);
+            r[j] = num[j] * inv[j];
+        }
+        st16(p.Rs + so, r);
+        st16(p.Is + so, inv);
+    }
     const size_t o = ((size_t)b * p.Tq + t) * p.D + d0;
     if (p.vec_io && d0 + 16 <= p.D) {
         float q[16], z[16];
@@ -199,9 +210,11 @@ __device__ __forceinline__ void epi16_fwd(const Params &p, int b, int t, int d0,
     }
 }
 
+// dQ, and g = dZ*sigmoid(Q)/den and n = -g*r as operand panels, from the
+// forward's r = num/den and inv = 1/den of 16 columns of row t.
 template <class IO, class E>
-__device__ __forceinline__ void epi16_bwd1(const Params &p, int b, int t, int d0,
-                                           const float (&num)[16], const float (&den)[16])
+__device__ __forceinline__ void epi16_grads(const Params &p, int b, int t, int d0,
+                                            const float (&rr)[16], const float (&iv)[16])
 {
     float g[16], n[16];
     const bool trow = t < p.Tq;
@@ -214,8 +227,8 @@ __device__ __forceinline__ void epi16_bwd1(const Params &p, int b, int t, int d0
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
             const float s = fast_sigmoid(q[j]);
-            const float inv = __fdividef(1.0f, den[j]);
-            const float r = num[j] * inv;
+            const float inv = iv[j];
+            const float r = rr[j];
             const float add = dz[j] * r * s * (1.0f - s);
             dq[j] = p.accumulate ? dq[j] + add : add;
             g[j] = dz[j] * s * inv;
@@ -235,8 +248,8 @@ __device__ __forceinline__ void epi16_bwd1(const Params &p, int b, int t, int d0
                 const float q = ld_io((const IO *)p.Q, o + j);
                 const float dz = ld_io((const IO *)p.dZ, o + j);
                 const float s = fast_sigmoid(q);
-                const float inv = __fdividef(1.0f, den[j]);
-                const float r = num[j] * inv;
+                const float inv = iv[j];
+                const float r = rr[j];
                 float dq = dz * r * s * (1.0f - s);
                 if (p.accumulate) dq += ld_io((const IO *)p.dQ, o + j);
                 st_io((IO *)p.dQ, o + j, dq);
@@ -256,6 +269,19 @@ __device__ __forceinline__ void epi16_bwd1(const Params &p, int b, int t, int d0
     round16(n, hi, lo, BF);
     st16op((E *)p.G2 + go, hi);
     if (keep_lo) st16op((E *)p.G2l + go, lo);
+}
+
+template <class IO, class E>
+__device__ __forceinline__ void epi16_bwd1(const Params &p, int b, int t, int d0,
+                                           const float (&num)[16], const float (&den)[16])
+{
+    float r[16], inv[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+        inv[j] = __fdividef(1.0f, den[j]);
+        r[j] = num[j] * inv[j];
+    }
+    epi16_grads<IO, E>(p, b, t, d0, r, inv);
 }
 
 template <class IO>

@@ -226,7 +226,8 @@ void *aft_forward(void *qh, void *kh, void *vh, void *wh, bool masked)
     const int T = Q->rows, D = Q->cols;
     Node *out = make(T, D);
     out->inputs = {Q, K, V, W};
-    const int flags = masked ? DC_AFT_CAUSAL : 0;
+    // the forward keeps r and 1/den so the backward skips its second contraction
+    const int flags = (masked ? DC_AFT_CAUSAL : 0) | DC_AFT_SAVE_STATS;
     size_t bytes = 0;
     dc_aft_workspace_size(1, T, T, D, DC_F32, flags, &bytes);
     auto ws = std::make_shared<DevBuf>(bytes);
@@ -253,18 +254,19 @@ void *aft_cross_forward(void *qh, void *kh, void *vh, void *wh)
     Node *out = make(TDec, D);
     out->inputs = {Q, K, V, W};
     size_t bytes = 0;
-    dc_aft_workspace_size(1, TDec, TEnc, D, DC_F32, 0, &bytes);
+    dc_aft_workspace_size(1, TDec, TEnc, D, DC_F32, DC_AFT_SAVE_STATS, &bytes);
     auto ws = std::make_shared<DevBuf>(bytes);
     out->saved.push_back(ws);
     report(dc_aft_fwd(Q->data, K->data, V->data, W->data, TEnc, out->data, 1, TDec, TEnc, D,
-                      DC_F32, 0, ws->p, bytes, kStream),
+                      DC_F32, DC_AFT_SAVE_STATS, ws->p, bytes, kStream),
            "aft_cross_forward");
     Node *o = out;
     Node *q = Q.get(), *k = K.get(), *v = V.get(), *w = W.get();
     out->backward_fn = [o, q, k, v, w, TDec, TEnc, D, ws, bytes]() {
         report(dc_aft_bwd(q->data, k->data, v->data, w->data, TEnc, o->grad, q->grad, k->grad,
                           v->grad, w->grad, 1, TDec, TEnc, D, DC_F32,
-                          DC_AFT_ACCUMULATE | DC_AFT_WS_VALID, ws->p, bytes, kStream),
+                          DC_AFT_SAVE_STATS | DC_AFT_ACCUMULATE | DC_AFT_WS_VALID, ws->p, bytes,
+                          kStream),
                "aft_cross_forward backward");
     };
     return out;

@@ -16,8 +16,8 @@ from ctypes import byref, c_int, c_size_t
 
 import torch
 
-from ._lib import (DC_AFT_ACCUMULATE, DC_AFT_CAUSAL, DC_AFT_COMPUTE_BF16, DC_AFT_SIMT,
-                   DC_AFT_WS_VALID, DC_BF16, DC_F32, DcError, check, lib)
+from ._lib import (DC_AFT_ACCUMULATE, DC_AFT_CAUSAL, DC_AFT_COMPUTE_BF16, DC_AFT_SAVE_STATS,
+                   DC_AFT_SIMT, DC_AFT_WS_VALID, DC_BF16, DC_F32, DcError, check, lib)
 
 
 def _stream() -> int:
@@ -54,10 +54,16 @@ class AftWorkspace:
     """Device scratch for one AFT shape: the operand panels (A', E'V, E'),
     the row/column maxima and the backward's g/n panels.  A workspace filled
     by ``aft_fwd`` can be handed to ``aft_bwd`` with ``ws_valid=True`` so the
-    backward skips recomputing the panels."""
+    backward skips recomputing the panels.  With ``save_stats=True`` the
+    forward also keeps r and 1/den there and such a backward skips the second
+    pass of the forward contraction as well."""
 
-    def __init__(self, B, Tq, Tk, D, dtype: torch.dtype, flags: int = 0, device=None):
+    def __init__(self, B, Tq, Tk, D, dtype: torch.dtype, flags: int = 0, device=None,
+                 save_stats=False):
         n = c_size_t(0)
+        self.save_stats = bool(save_stats or flags & DC_AFT_SAVE_STATS)
+        if self.save_stats:
+            flags |= DC_AFT_SAVE_STATS
         code = DC_F32 if dtype == torch.float32 else DC_BF16
         check(lib().dc_aft_workspace_size(B, Tq, Tk, D, code, flags, byref(n)), "dc_aft_workspace_size")
         self.nbytes = int(n.value)
@@ -95,6 +101,8 @@ def aft_fwd(Q, K, V, w, causal=True, out=None, workspace: AftWorkspace | None = 
     ws = workspace.ptr if workspace is not None else None
     nb = workspace.nbytes if workspace is not None else 0
     flags = _flags(causal, ws_valid=ws_valid, simt=simt, compute_bf16=compute_bf16)
+    if workspace is not None and workspace.save_stats:
+        flags |= DC_AFT_SAVE_STATS
     check(lib().dc_aft_fwd(Q3.data_ptr(), K3.data_ptr(), V3.data_ptr(), w.data_ptr(), w.stride(0),
                            Z.data_ptr(), B, Tq, Tk, D, _dtype_code(Q3), flags, ws, nb, _stream()),
           "dc_aft_fwd")
@@ -118,6 +126,8 @@ def aft_bwd(Q, K, V, w, dZ, causal=True, grads=None, accumulate=False,
     ws = workspace.ptr if workspace is not None else None
     nb = workspace.nbytes if workspace is not None else 0
     flags = _flags(causal, accumulate, ws_valid, simt, compute_bf16)
+    if workspace is not None and workspace.save_stats:
+        flags |= DC_AFT_SAVE_STATS
     check(lib().dc_aft_bwd(Q3.data_ptr(), K3.data_ptr(), V3.data_ptr(), w.data_ptr(), w.stride(0),
                            G3.data_ptr(), dQ.data_ptr(), dK.data_ptr(), dV.data_ptr(), dW.data_ptr(),
                            B, Tq, Tk, D, _dtype_code(Q3), flags, ws, nb, _stream()),

@@ -48,6 +48,13 @@ extern "C" {
 #define DC_AFT_WS_VALID 0x4      /* workspace already holds this call's prep   */
 #define DC_AFT_SIMT 0x8          /* CUDA-core contraction (cross-check path)   */
 #define DC_AFT_COMPUTE_BF16 0x10 /* f32 tensors, bf16 tensor-core operands     */
+#define DC_AFT_SAVE_STATS 0x20   /* forward keeps r and 1/den in the workspace;
+                                    a WS_VALID backward reads them back instead
+                                    of recomputing the forward contraction
+                                    (ignored with DC_AFT_SIMT).  Costs 16 bytes
+                                    of HBM traffic per element of Z; pays off
+                                    from Tk of about 1024 on.  Forward and
+                                    backward must pass the same flags.        */
 
 /* Message of the last failing call on this host thread ("" if none). */
 const char *dc_last_error(void);

@@ -152,6 +152,35 @@ def test_accumulate_and_workspace_reuse(ops, dev):
     torch.testing.assert_close(Z, Z2, rtol=0, atol=0)
 
 
+@pytest.mark.parametrize("dtype,B,T,D", [(torch.bfloat16, 4, 512, 256), (torch.bfloat16, 2, 200, 72),
+                                         (torch.float32, 2, 130, 40), (torch.float32, 3, 256, 128)])
+@pytest.mark.parametrize("accumulate", [False, True])
+def test_saved_stats_match_recompute(ops, dev, dtype, B, T, D, accumulate):
+    """A backward that reads the forward's r and 1/den back gives the same
+    gradients as one that recomputes the forward contraction: dQ, dK and dV
+    bit for bit, dW up to the order of its split-K additions."""
+    Q, K, V, W, dZ = make_inputs(21, B, T, T, D)
+    tq, tk, tv, tg = to_dev(dev, dtype, Q, K, V, dZ)
+    tw = torch.from_numpy(W).to(dev)
+    base = [torch.from_numpy(x).to(dev, dtype) for x in make_inputs(22, B, T, T, D)[:3]]
+    base.append(0.1 * torch.from_numpy(W).to(dev))
+
+    def grads(save):
+        ws = ops.AftWorkspace(B, T, T, D, dtype, flags=1, save_stats=save)
+        Z = ops.aft_fwd(tq, tk, tv, tw, causal=True, workspace=ws)
+        g = ops.aft_bwd(tq, tk, tv, tw, tg, causal=True, grads=[x.clone() for x in base],
+                        accumulate=accumulate, workspace=ws, ws_valid=True)
+        return Z, g
+
+    Z0, g0 = grads(False)
+    Z1, g1 = grads(True)
+    assert torch.equal(Z0, Z1)
+    for a, b in zip(g0[:3], g1[:3]):
+        assert torch.equal(a, b)
+    torch.testing.assert_close(g1[3], g0[3], rtol=1e-5, atol=1e-6)
+    assert ops.device_status() == 0
+
+
 def test_deterministic_forward(ops, dev):
     Q, K, V, W, _ = make_inputs(10, 2, 256, 256, 128)
     tq, tk, tv = to_dev(dev, torch.bfloat16, Q, K, V)
