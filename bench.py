@@ -131,6 +131,55 @@ def cpu_baseline(B, T, d, dtype_name, budget_s=10.0):
     return n * T / tn, cores, f"{n} of {B} sequences (T={T}, d={d}) fwd+bwd, fp32, {cores} threads, {tn:.2f} s"
 
 
+# ------------------------------------------------------------------ row ops
+def row_kernels(dev, P, reps=10):
+    """HBM bandwidth of the training step's row kernels on tensors larger than
+    L2 (no flush needed): LayerNorm and bias over [262144, 256] fp32 (the C3
+    activation width), cross-entropy over [65536, 8192] fp32 logits (the C5
+    vocabulary).  Bytes = one read of every input row and one write of every
+    output row (parameter vectors are negligible)."""
+    import torch
+    from dart_cuda_b200 import ops
+
+    torch.manual_seed(0)
+    R, C = 262144, 256
+    x = torch.randn(R, C, device=dev)
+    dy = torch.randn(R, C, device=dev)
+    gam, bet = torch.randn(C, device=dev), torch.randn(C, device=dev)
+    y, dx = torch.empty_like(x), torch.empty_like(x)
+    dg, db = torch.empty(C, device=dev), torch.empty(C, device=dev)
+    T, V = 65536, 8192
+    logits = torch.randn(T, V, device=dev)
+    tgt = torch.randint(0, V, (T,), device=dev, dtype=torch.int32)
+    g = torch.empty_like(logits)
+    scale = torch.ones(1, device=dev)
+    act = R * C * 4
+    cases = {
+        "layernorm_fwd": (lambda: ops.layernorm_fwd(x, gam, bet, out=y), 2 * act),
+        "layernorm_bwd": (lambda: ops.layernorm_bwd(x, gam, dy, grads=(dx, dg, db)), 3 * act),
+        "bias_fwd": (lambda: ops.bias_fwd(x, bet, out=y), 2 * act),
+        "bias_bwd": (lambda: ops.bias_bwd(dy, grads=(dx, db)), 2 * act),
+        "ce_fwd": (lambda: ops.ce_fwd(logits, tgt), T * V * 4),
+        "ce_bwd": (lambda: ops.ce_bwd(logits, tgt, grad_scale=scale, out=g), 2 * T * V * 4),
+    }
+    out = {}
+    stream = torch.cuda.current_stream()
+    for name, (fn, nbytes) in cases.items():
+        for _ in range(3):
+            fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        gbs = nbytes / (ms / 1e3) / 1e9
+        out[name] = {"us": ms * 1e3, "GB/s": gbs, "hbm_frac": gbs / P["hbm_gbs"], "bytes": nbytes}
+    out["shapes"] = f"LN/bias [{R},{C}] fp32, CE [{T},{V}] fp32"
+    return out
+
+
 # ------------------------------------------------------------------ main
 def main():
     ap = argparse.ArgumentParser()
@@ -146,6 +195,7 @@ def main():
                          "repeats the forward contraction; auto: stats from T >= 1024, where the "
                          "contraction costs more than the 16 bytes per element of saved statistics")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
+    ap.add_argument("--no-rows", action="store_true", help="skip the LayerNorm/bias/CE bandwidth pass")
     args = ap.parse_args()
 
     B, T, d, dt, desc = CONFIGS[args.config]
@@ -361,6 +411,8 @@ def main():
         "roofline": roof, "kernels": kern, "gpu_launches": launches * args.steps,
         "clocks": sampler.summary(),
     }
+    if rank == 0 and world == 1 and not args.no_rows:
+        line["row_kernels"] = row_kernels(dev, P)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         tok_s, cores, sample = cpu_baseline(B, T, d, dt, budget_s=args.cpu_budget)
         line["cpu_baseline"] = {"value": tok_s, "unit": "tokens/s", "cores": cores, "kind": "port",

@@ -22,6 +22,12 @@ DC_AFT_WS_VALID = 0x4
 DC_AFT_SIMT = 0x8
 DC_AFT_COMPUTE_BF16 = 0x10
 DC_AFT_SAVE_STATS = 0x20
+DC_GEMM_TRANS_A = 0x1
+DC_GEMM_TRANS_B = 0x2
+DC_GEMM_BIAS = 0x4
+DC_GEMM_GELU = 0x8
+DC_GEMM_GELU_BWD = 0x10
+DC_GEMM_ACCUMULATE = 0x20
 
 _lib = None
 
@@ -53,6 +59,8 @@ SIGNATURES = {
     "dc_ce_bwd": (c_int, [_VP, _VP, _VP, _VP, c_int, c_int, c_float, _VP]),
     "dc_adam_step": (c_int, [_VP, _VP, _VP, _VP, c_int64, c_int, c_float, c_float, c_float, c_float,
                              c_float, _VP]),
+    "dc_gemm": (c_int, [_VP, c_int, _VP, c_int, _VP, c_int, c_int, c_int, c_int, c_int, c_int, c_float,
+                        _VP, _VP, c_int, _VP, c_int, _VP]),
     # the reference's handle ABI
     "create_tensor": (_VP, [c_int32, c_int32, _FP]),
     "destroy_tensor": (None, [_VP]),

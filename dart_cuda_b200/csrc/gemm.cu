@@ -1,0 +1,520 @@
+// General tcgen05 GEMM of the decoder's dense layers (Q/K/V, projections,
+// FFN, LM head) and of their backward:
+//
+//   C[M,N] = epilogue( alpha * op(A)[M,K] . op(B)[K,N] )
+//
+// op(A) = A ([M,K] row-major, K-major for the tensor core) or A^T (A stored
+// [K,M], MN-major); op(B) = B ([K,N] row-major, MN-major) or B^T (B stored
+// [N,K], K-major).  Forward layers are NN (X . W), the input gradient is NT
+// (dY . W^T) and the weight gradient TN (X^T . dY).  fp32 tensors run with
+// tf32 operands, bf16 tensors with bf16 operands; accumulation and C are
+// fp32.  The epilogue fuses what follows a layer's product in the reference
+// (native/src/engine.cu:480-507 matmul, :352-372 row-broadcast bias,
+// native/src/kernels/elementwise.cuh:328-351 tanh GELU and its derivative,
+// residual adds): bias, GELU (keeping the pre-activation for the backward),
+// the GELU derivative, and a residual / accumulate input.
+//
+// One persistent CTA per SM walks 128x128 output tiles (split along K when
+// the tiles alone cannot fill the SMs and the epilogue is linear): warp 16
+// issues TMA loads into a 6-deep ring of 32 KB stages, warp 17 owns TMEM and
+// issues the MMAs into a double-buffered accumulator, warps 0-15 drain it.
+#include <cuda_bf16.h>
+
+#include "dc_internal.h"
+#include "dc_ptx.cuh"
+
+namespace dc {
+namespace gemm {
+
+constexpr int BM = 128, BN = 128;
+constexpr int kEpiWarps = 16;
+constexpr int kThreads = (kEpiWarps + 2) * 32;
+
+enum : int {
+    EPI_BIAS = 1,      // + bias[n] (split 0 only under split-K)
+    EPI_GELU = 2,      // aux = pre-activation (if aux), C = gelu(pre)
+    EPI_GELU_BWD = 4,  // C = value * gelu'(aux)
+    EPI_RESID = 8,     // + R[m, n] before the activation (R may alias C)
+    EPI_ATOMIC = 16,   // split-K: C += value with atomics (C pre-initialised)
+};
+
+template <class E, bool A_MN, bool B_MN>
+struct Cfg {
+    static constexpr bool TF32 = sizeof(E) == 4;
+    static constexpr int BKe = 128 / (int)sizeof(E);     // K elements per stage (128 B rows)
+    static constexpr int UK = TF32 ? 8 : 16;             // K per MMA instruction
+    static constexpr int NSUB = BKe / UK;
+    static constexpr int BOX_MN = 128 / (int)sizeof(E);  // MN elements in one 128 B block
+    static constexpr int TILE_BYTES = 128 * 128;
+    static constexpr int STAGE_BYTES = 2 * TILE_BYTES;
+    static constexpr int STAGES = 6;
+    static constexpr uint32_t IDESC = umma_idesc(TF32 ? 2u : 1u, BM, BN, A_MN, B_MN);
+    static constexpr uint32_t MN_LBO = BKe * 128;
+    static constexpr uint32_t MN_LAYOUT = TF32 ? 1u : 2u;
+    static constexpr uint32_t MN_SBO = TF32 ? 512u : 1024u;
+    static constexpr uint32_t TMEM_COLS = 2 * BN;
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 512;
+    static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+};
+
+struct Params {
+    int M, N, K;
+    int ldc, ldr, ldx;
+    float alpha;
+    float *C;
+    const float *R;
+    const float *bias;
+    float *aux;
+    int epi;
+    int tiles_m, tiles_n, splits, ksteps, n_tiles;
+    int vec;
+    int *status;
+};
+
+// tanh-approximated GELU and its derivative, the forms of the reference's
+// gelu_fwd / gelu_bwd (native/src/kernels/elementwise.cuh:328-351).
+__device__ __forceinline__ float gelu_f(float x)
+{
+    return 0.5f * x * (1.0f + tanhf(0.7978845608f * (x + 0.044715f * x * x * x)));
+}
+__device__ __forceinline__ float gelu_d(float x)
+{
+    const float x2 = x * x;
+    const float t = tanhf(0.7978845608f * (x + 0.044715f * x2 * x));
+    return 0.5f * (1.0f + t) + 0.5f * x * (1.0f - t * t) * 0.7978845608f * (1.0f + 3.0f * 0.044715f * x2);
+}
+
+__device__ __forceinline__ void ld16f(const float *p, float (&v)[16])
+{
+    const float4 *q = reinterpret_cast<const float4 *>(p);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const float4 f = q[k];
+        v[4 * k] = f.x;
+        v[4 * k + 1] = f.y;
+        v[4 * k + 2] = f.z;
+        v[4 * k + 3] = f.w;
+    }
+}
+__device__ __forceinline__ void st16f(float *p, const float (&v)[16])
+{
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+        asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p + 8 * h),
+                     "r"(__float_as_uint(v[8 * h])), "r"(__float_as_uint(v[8 * h + 1])),
+                     "r"(__float_as_uint(v[8 * h + 2])), "r"(__float_as_uint(v[8 * h + 3])),
+                     "r"(__float_as_uint(v[8 * h + 4])), "r"(__float_as_uint(v[8 * h + 5])),
+                     "r"(__float_as_uint(v[8 * h + 6])), "r"(__float_as_uint(v[8 * h + 7]))
+                     : "memory");
+}
+
+// 16 consecutive accumulator columns of one row.
+__device__ __forceinline__ void epilogue16(const Params &p, int r, int c0, int split,
+                                           float (&v)[16])
+{
+    if (r >= p.M || c0 >= p.N) return;
+    const bool first = split == 0;
+    const int epi = p.epi;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] *= p.alpha;
+    if (p.vec && c0 + 16 <= p.N) {
+        float t[16];
+        if ((epi & EPI_BIAS) && first) {
+            ld16f(p.bias + c0, t);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] += t[j];
+        }
+        float *c = p.C + (size_t)r * p.ldc + c0;
+        if (epi & EPI_ATOMIC) {
+            float4 *c4 = reinterpret_cast<float4 *>(c);
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                atomicAdd(c4 + k, make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]));
+            return;
+        }
+        if (epi & EPI_RESID) {
+            ld16f(p.R + (size_t)r * p.ldr + c0, t);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] += t[j];
+        }
+        if (epi & EPI_GELU) {
+            if (p.aux) st16f(p.aux + (size_t)r * p.ldx + c0, v);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = gelu_f(v[j]);
+        } else if (epi & EPI_GELU_BWD) {
+            ld16f(p.aux + (size_t)r * p.ldx + c0, t);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] *= gelu_d(t[j]);
+        }
+        st16f(c, v);
+        return;
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+        const int c = c0 + j;
+        if (c >= p.N) break;
+        float x = v[j];
+        if ((epi & EPI_BIAS) && first) x += p.bias[c];
+        float *dst = p.C + (size_t)r * p.ldc + c;
+        if (epi & EPI_ATOMIC) {
+            atomicAdd(dst, x);
+            continue;
+        }
+        if (epi & EPI_RESID) x += p.R[(size_t)r * p.ldr + c];
+        if (epi & EPI_GELU) {
+            if (p.aux) p.aux[(size_t)r * p.ldx + c] = x;
+            x = gelu_f(x);
+        } else if (epi & EPI_GELU_BWD) {
+            x *= gelu_d(p.aux[(size_t)r * p.ldx + c]);
+        }
+        *dst = x;
+    }
+}
+
+struct Tile {
+    int m0, n0, k0, k1, split;
+};
+
+__device__ __forceinline__ Tile decode_tile(const Params &p, int idx)
+{
+    Tile t;
+    const int per = p.tiles_m * p.tiles_n;
+    t.split = idx / per;
+    const int rem = idx % per;
+    t.m0 = (rem / p.tiles_n) * BM;
+    t.n0 = (rem % p.tiles_n) * BN;
+    t.k0 = (int)(((long long)t.split * p.ksteps) / p.splits);
+    t.k1 = (int)(((long long)(t.split + 1) * p.ksteps) / p.splits);
+    return t;
+}
+
+__device__ __forceinline__ int sched_tile(int j, int ntiles)
+{
+    const int t = j * (int)gridDim.x + (int)blockIdx.x;
+    return t < ntiles ? t : -1;
+}
+
+template <class E, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtensorMap mapA,
+                   const __grid_constant__ CUtensorMap mapB)
+{
+    using C = Cfg<E, A_MN, B_MN>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::STAGES * C::STAGE_BYTES);
+    uint64_t *full = bars;
+    uint64_t *empty = bars + C::STAGES;
+    uint64_t *accf = bars + 2 * C::STAGES;
+    uint64_t *acce = accf + 2;
+    uint64_t *drainb = acce + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drainb + 1);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        *abort_flag = 0;
+        for (int s = 0; s < C::STAGES; ++s) {
+            mbar_init(smem_u32(&full[s]), 1);
+            mbar_init(smem_u32(&empty[s]), 1);
+        }
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(smem_u32(&accf[s]), 1);
+            mbar_init(smem_u32(&acce[s]), kEpiWarps);
+        }
+        mbar_init(smem_u32(drainb), 1);
+        fence_mbar_init();
+    }
+    if (warp == kEpiWarps && lane == 0) {
+        tma_prefetch(&mapA);
+        tma_prefetch(&mapB);
+    }
+    if (warp == kEpiWarps + 1) {
+        tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const int ntiles = p.n_tiles;
+
+    if (warp == kEpiWarps) {
+        // ------------------------------------------------ TMA producer
+        if (lane == 0) {
+            uint32_t g = 0;
+            bool stop = false;
+            for (int jt = 0; !stop; ++jt) {
+                const int tile = sched_tile(jt, ntiles);
+                if (tile < 0) break;
+                const Tile tl = decode_tile(p, tile);
+                for (int k = tl.k0; k < tl.k1; ++k, ++g) {
+                    const int s = g % C::STAGES;
+                    if (!mbar_wait(smem_u32(&empty[s]), ((g / C::STAGES) & 1) ^ 1, abort_flag,
+                                   p.status, DC_DEVERR_TIMEOUT_EMPTY)) {
+                        stop = true;
+                        break;
+                    }
+                    const uint32_t fb = smem_u32(&full[s]);
+                    mbar_arrive_expect_tx(fb, C::STAGE_BYTES);
+                    const uint32_t sa = smem_u32(smem + s * C::STAGE_BYTES);
+                    const uint32_t sb = sa + C::TILE_BYTES;
+                    const int kx = k * C::BKe;
+                    if (A_MN) {
+#pragma unroll
+                        for (int j = 0; j < BM / C::BOX_MN; ++j)
+                            tma_load_2d(sa + j * C::MN_LBO, &mapA, fb, tl.m0 + j * C::BOX_MN, kx);
+                    } else {
+                        tma_load_2d(sa, &mapA, fb, kx, tl.m0);
+                    }
+                    if (B_MN) {
+#pragma unroll
+                        for (int j = 0; j < BN / C::BOX_MN; ++j)
+                            tma_load_2d(sb + j * C::MN_LBO, &mapB, fb, tl.n0 + j * C::BOX_MN, kx);
+                    } else {
+                        tma_load_2d(sb, &mapB, fb, kx, tl.n0);
+                    }
+                }
+            }
+            if (*abort_flag) {
+                const uint32_t first = g > (uint32_t)C::STAGES ? g - C::STAGES : 0;
+                for (uint32_t q = first; q < g; ++q)
+                    mbar_wait(smem_u32(&full[q % C::STAGES]), (q / C::STAGES) & 1, nullptr,
+                              p.status, DC_DEVERR_TIMEOUT_DRAIN);
+            }
+        }
+    } else if (warp == kEpiWarps + 1) {
+        // ------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            uint32_t g = 0;
+            bool stop = false;
+            for (uint32_t j = 0; !stop; ++j) {
+                const int tile = sched_tile(j, ntiles);
+                if (tile < 0) break;
+                const Tile tl = decode_tile(p, tile);
+                const uint32_t buf = j & 1, use = j >> 1;
+                if (!mbar_wait(smem_u32(&acce[buf]), (use & 1) ^ 1, abort_flag, p.status,
+                               DC_DEVERR_TIMEOUT_ACC))
+                    break;
+                tc_fence_after();
+                const uint32_t acc = tmem + buf * BN;
+                for (int k = tl.k0; k < tl.k1; ++k, ++g) {
+                    const int s = g % C::STAGES;
+                    if (!mbar_wait(smem_u32(&full[s]), (g / C::STAGES) & 1, abort_flag, p.status,
+                                   DC_DEVERR_TIMEOUT_FULL)) {
+                        stop = true;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = smem_u32(smem + s * C::STAGE_BYTES);
+                    const uint32_t sb = sa + C::TILE_BYTES;
+#pragma unroll
+                    for (int u = 0; u < C::NSUB; ++u) {
+                        const uint32_t koff = u * C::UK * (int)sizeof(E);
+                        const uint32_t moff = u * C::UK * 128;
+                        const uint64_t a = A_MN ? sw128_desc(sa + moff, C::MN_LBO, C::MN_SBO,
+                                                             C::MN_LAYOUT)
+                                                : sw128_desc(sa + koff, 16, 1024, 2);
+                        const uint64_t b = B_MN ? sw128_desc(sb + moff, C::MN_LBO, C::MN_SBO,
+                                                             C::MN_LAYOUT)
+                                                : sw128_desc(sb + koff, 16, 1024, 2);
+                        umma<C::TF32>(acc, a, b, C::IDESC, (k == tl.k0 && u == 0) ? 0u : 1u);
+                    }
+                    umma_commit(smem_u32(&empty[s]));
+                }
+                if (stop) break;
+                umma_commit(smem_u32(&accf[buf]));
+            }
+            if (*abort_flag) {
+                umma_commit(smem_u32(drainb));
+                mbar_wait(smem_u32(drainb), 0, nullptr, p.status, DC_DEVERR_TIMEOUT_DRAIN);
+            }
+        }
+    } else {
+        // ------------------------------------------------ epilogue (warps 0-15)
+        const int quad = warp & 3;
+        const int slice = warp >> 2;
+        const int row = quad * 32 + lane;
+        for (uint32_t j = 0;; ++j) {
+            const int tile = sched_tile(j, ntiles);
+            if (tile < 0) break;
+            const Tile tl = decode_tile(p, tile);
+            const uint32_t buf = j & 1, use = j >> 1;
+            const bool ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&accf[buf]), use & 1,
+                                                              abort_flag, p.status,
+                                                              DC_DEVERR_TIMEOUT_ACC));
+            if (!ok) break;
+            tc_fence_after();
+            const uint32_t lane_addr = tmem + buf * BN + ((uint32_t)(quad * 32) << 16) + slice * 32;
+#pragma unroll 1
+            for (int sb = 0; sb < 2; ++sb) {
+                float v[16];
+                tmem_ld16(lane_addr + sb * 16, v);
+                epilogue16(p, tl.m0 + row, tl.n0 + slice * 32 + sb * 16, tl.split, v);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&acce[buf]));
+        }
+    }
+    __syncthreads();
+    if (warp == kEpiWarps + 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, C::TMEM_COLS);
+    }
+}
+
+// ------------------------------------------------------------ host side
+static CUtensorMapDataType tmap_type(int esz)
+{
+    return esz == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+}
+
+// Row-major [rows, cols] operand with leading dimension ld (elements).
+// K-major: box of BKe (K) x 128 rows, 128-byte swizzle.  MN-major: box of
+// one 128-byte MN block x BKe K-rows, in the swizzle tcgen05 reads for that
+// majorness (32-byte atoms for 32-bit operands).
+static int map_operand(CUtensorMap *m, const void *base, int esz, int rows, int cols, int ld,
+                       bool mn_major)
+{
+    const uint32_t bke = 128 / esz;
+    uint64_t dims[2] = {(uint64_t)cols, (uint64_t)rows};
+    uint64_t strides[1] = {(uint64_t)ld * esz};
+    uint32_t box[2];
+    CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_128B;
+    if (mn_major) {
+        box[0] = 128 / esz;
+        box[1] = bke;
+        if (esz == 4) sw = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
+    } else {
+        box[0] = bke;
+        box[1] = 128;
+    }
+    return encode_tmap(m, tmap_type(esz), 2, base, dims, strides, box, sw);
+}
+
+template <class E, bool A_MN, bool B_MN>
+static int launch(Params p, const void *A, int lda, const void *B, int ldb, cudaStream_t st)
+{
+    using C = Cfg<E, A_MN, B_MN>;
+    static bool attr_set[64] = {false};
+    int dev = 0;
+    DC_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return fail(DC_ERR_UNSUPPORTED, "device ordinal %d", dev);
+    if (!attr_set[dev]) {
+        DC_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel<E, A_MN, B_MN>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         C::SMEM_BYTES));
+        attr_set[dev] = true;
+    }
+    const int esz = (int)sizeof(E);
+    CUtensorMap mA, mB;
+    // A: op(A) is [M,K]; stored [M,K] (K-major) or [K,M] (MN-major)
+    DC_TRY(A_MN ? map_operand(&mA, A, esz, p.K, p.M, lda, true)
+                : map_operand(&mA, A, esz, p.M, p.K, lda, false));
+    // B: op(B) is [K,N]; stored [K,N] (MN-major) or [N,K] (K-major)
+    DC_TRY(B_MN ? map_operand(&mB, B, esz, p.K, p.N, ldb, true)
+                : map_operand(&mB, B, esz, p.N, p.K, ldb, false));
+    const int grid = std::max(1, std::min(p.n_tiles, sm_count()));
+    {
+        KernelTimer kt("gemm_tc", st);
+        gemm_tc_kernel<E, A_MN, B_MN><<<grid, kThreads, C::SMEM_BYTES, st>>>(p, mA, mB);
+    }
+    DC_CUDA_TRY(cudaGetLastError());
+    return DC_OK;
+}
+
+template <class E>
+static int dispatch(const Params &p, bool ta, bool tb, const void *A, int lda, const void *B,
+                    int ldb, cudaStream_t st)
+{
+    // op(B) = B   -> B stored [K,N] -> MN-major;  op(B) = B^T -> K-major
+    if (!ta && !tb) return launch<E, false, true>(p, A, lda, B, ldb, st);
+    if (!ta && tb) return launch<E, false, false>(p, A, lda, B, ldb, st);
+    if (ta && !tb) return launch<E, true, true>(p, A, lda, B, ldb, st);
+    return launch<E, true, false>(p, A, lda, B, ldb, st);
+}
+
+static bool aligned(const void *q, int bytes)
+{
+    return (reinterpret_cast<uintptr_t>(q) & (uintptr_t)(bytes - 1)) == 0;
+}
+
+}  // namespace gemm
+}  // namespace dc
+
+using namespace dc;
+
+extern "C" int dc_gemm(const void *A, int lda, const void *B, int ldb, float *C, int ldc, int M,
+                       int N, int K, int dtype, int flags, float alpha, const float *bias,
+                       const float *R, int ldr, float *aux, int ldaux, void *stream)
+{
+    using namespace dc::gemm;
+    clear_error();
+    if (M < 0 || N < 0 || K < 0) return fail(DC_ERR_INVALID, "negative shape M=%d N=%d K=%d", M, N, K);
+    if ((long long)M * N == 0) return DC_OK;
+    if (K == 0) return fail(DC_ERR_INVALID, "K == 0");
+    if (dtype != DC_F32 && dtype != DC_BF16) return fail(DC_ERR_INVALID, "dtype %d", dtype);
+    if (!A || !B || !C) return fail(DC_ERR_INVALID, "null operand");
+    const bool ta = flags & DC_GEMM_TRANS_A, tb = flags & DC_GEMM_TRANS_B;
+    const int esz = dtype == DC_F32 ? 4 : 2;
+    if (lda < (ta ? M : K) || ldb < (tb ? K : N) || ldc < N)
+        return fail(DC_ERR_INVALID, "leading dimension too small (lda=%d ldb=%d ldc=%d)", lda, ldb, ldc);
+    if ((lda * esz) % 16 || (ldb * esz) % 16 || !aligned(A, 16) || !aligned(B, 16))
+        return fail(DC_ERR_INVALID, "A and B need 16-byte aligned bases and row strides");
+    const bool gelu = flags & DC_GEMM_GELU, gelu_bwd = flags & DC_GEMM_GELU_BWD;
+    if (gelu && gelu_bwd) return fail(DC_ERR_INVALID, "GELU and GELU_BWD are exclusive");
+    if (gelu_bwd && !aux) return fail(DC_ERR_INVALID, "GELU_BWD needs the pre-activation in aux");
+    if ((flags & DC_GEMM_BIAS) && !bias) return fail(DC_ERR_INVALID, "BIAS without a bias vector");
+    if (flags & DC_GEMM_ACCUMULATE) {
+        if (R && R != C) return fail(DC_ERR_INVALID, "ACCUMULATE with a separate residual");
+        R = C;
+        ldr = ldc;
+    }
+    if (R && ldr < N) return fail(DC_ERR_INVALID, "ldr < N");
+    if (aux && ldaux < N) return fail(DC_ERR_INVALID, "ldaux < N");
+
+    Params p{};
+    p.M = M;
+    p.N = N;
+    p.K = K;
+    p.ldc = ldc;
+    p.ldr = ldr;
+    p.ldx = ldaux;
+    p.alpha = alpha;
+    p.C = C;
+    p.R = R;
+    p.bias = bias;
+    p.aux = aux;
+    p.epi = ((flags & DC_GEMM_BIAS) ? EPI_BIAS : 0) | (gelu ? EPI_GELU : 0) |
+            (gelu_bwd ? EPI_GELU_BWD : 0) | (R ? EPI_RESID : 0);
+    p.tiles_m = (M + BM - 1) / BM;
+    p.tiles_n = (N + BN - 1) / BN;
+    const int bke = 128 / esz;
+    p.ksteps = (K + bke - 1) / bke;
+    // split K when the tiles leave SMs idle and the epilogue is linear
+    const int tiles = p.tiles_m * p.tiles_n, sms = sm_count();
+    int splits = 1;
+    if (!gelu && !gelu_bwd && tiles * 2 <= sms)
+        splits = std::max(1, std::min(sms / tiles, p.ksteps / 4));
+    p.splits = splits;
+    p.n_tiles = tiles * splits;
+    p.vec = (ldc % 8 == 0) && gemm::aligned(C, 32) && (!R || (ldr % 8 == 0 && gemm::aligned(R, 32))) &&
+            (!aux || (ldaux % 8 == 0 && gemm::aligned(aux, 32))) && (!bias || gemm::aligned(bias, 32));
+    p.status = device_status_word();
+    cudaStream_t st = as_stream(stream);
+    if (splits > 1) {
+        // C starts as the residual (or zero) and every split adds its part
+        if (!R)
+            DC_CUDA_TRY(cudaMemset2DAsync(C, (size_t)ldc * 4, 0, (size_t)N * 4, M, st));
+        else if (R != C)
+            DC_CUDA_TRY(cudaMemcpy2DAsync(C, (size_t)ldc * 4, R, (size_t)ldr * 4, (size_t)N * 4, M,
+                                          cudaMemcpyDeviceToDevice, st));
+        p.epi = (p.epi & EPI_BIAS) | EPI_ATOMIC;
+    }
+    if (dtype == DC_F32) return dispatch<float>(p, ta, tb, A, lda, B, ldb, st);
+    return dispatch<__nv_bfloat16>(p, ta, tb, A, lda, B, ldb, st);
+}

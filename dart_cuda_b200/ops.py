@@ -17,7 +17,9 @@ from ctypes import byref, c_int, c_size_t
 import torch
 
 from ._lib import (DC_AFT_ACCUMULATE, DC_AFT_CAUSAL, DC_AFT_COMPUTE_BF16, DC_AFT_SAVE_STATS,
-                   DC_AFT_SIMT, DC_AFT_WS_VALID, DC_BF16, DC_F32, DcError, check, lib)
+                   DC_AFT_SIMT, DC_AFT_WS_VALID, DC_BF16, DC_F32, DC_GEMM_ACCUMULATE, DC_GEMM_BIAS,
+                   DC_GEMM_GELU, DC_GEMM_GELU_BWD, DC_GEMM_TRANS_A, DC_GEMM_TRANS_B, DcError, check,
+                   lib)
 
 
 def _stream() -> int:
@@ -199,6 +201,46 @@ def ce_bwd(logits, targets, grad_scale=None, eps=0.1, out=None):
 def adam_step(p, g, m, v, t, lr, b1=0.9, b2=0.999, eps=1e-8, weight_decay=0.001):
     check(lib().dc_adam_step(p.data_ptr(), g.data_ptr(), m.data_ptr(), v.data_ptr(), p.numel(), int(t),
                              lr, b1, b2, eps, weight_decay, _stream()), "dc_adam_step")
+
+
+# ---------------------------------------------------------------- dense layers
+def _ld(t: torch.Tensor, name: str) -> int:
+    if t.dim() != 2 or t.stride(1) != 1:
+        raise DcError(f"{name} must be 2-D with unit column stride")
+    return t.stride(0)
+
+
+def gemm(A, B, out=None, trans_a=False, trans_b=False, bias=None, residual=None, accumulate=False,
+         gelu=False, gelu_aux=None, gelu_bwd_aux=None, alpha=1.0):
+    """C = epilogue(alpha * op(A) @ op(B)) through ``dc_gemm``: A and B fp32
+    (tf32 tensor-core operands) or bf16, C fp32.  ``residual`` (or C itself
+    with ``accumulate``) is added after the bias; ``gelu`` applies the tanh
+    GELU and stores the pre-activation in ``gelu_aux`` when given;
+    ``gelu_bwd_aux`` multiplies by the GELU derivative at that
+    pre-activation."""
+    if A.dtype != B.dtype:
+        raise DcError("A and B must share a dtype")
+    M = A.shape[1] if trans_a else A.shape[0]
+    K = A.shape[0] if trans_a else A.shape[1]
+    N = B.shape[0] if trans_b else B.shape[1]
+    if (B.shape[1] if trans_b else B.shape[0]) != K:
+        raise DcError(f"inner dimensions differ: op(A) [{M},{K}], B {tuple(B.shape)}")
+    C = torch.empty(M, N, device=A.device) if out is None else out
+    flags = ((DC_GEMM_TRANS_A if trans_a else 0) | (DC_GEMM_TRANS_B if trans_b else 0) |
+             (DC_GEMM_BIAS if bias is not None else 0) | (DC_GEMM_ACCUMULATE if accumulate else 0))
+    aux, ldx = None, 0
+    if gelu:
+        flags |= DC_GEMM_GELU
+        if gelu_aux is not None:
+            aux, ldx = gelu_aux.data_ptr(), _ld(gelu_aux, "gelu_aux")
+    if gelu_bwd_aux is not None:
+        flags |= DC_GEMM_GELU_BWD
+        aux, ldx = gelu_bwd_aux.data_ptr(), _ld(gelu_bwd_aux, "gelu_bwd_aux")
+    R, ldr = (None, 0) if residual is None else (residual.data_ptr(), _ld(residual, "residual"))
+    check(lib().dc_gemm(A.data_ptr(), _ld(A, "A"), B.data_ptr(), _ld(B, "B"), C.data_ptr(), _ld(C, "C"),
+                        M, N, K, _dtype_code(A), flags, float(alpha), _ptr(bias), R, ldr, aux, ldx,
+                        _stream()), "dc_gemm")
+    return C
 
 
 # ---------------------------------------------------------------- timing

@@ -156,6 +156,31 @@ int dc_ce_fwd_noalloc(const float *logits, const int32_t *targets, float *loss, 
 int dc_adam_step(float *p, const float *g, float *m, float *v, int64_t n, int t, float lr,
                  float b1, float b2, float eps, float weight_decay, void *stream);
 
+/* ------------------------------------------------------- dense layers
+ * C[M,N] = epilogue(alpha * op(A) . op(B)) on the tensor cores (tf32
+ * operands for DC_F32, bf16 for DC_BF16; fp32 accumulate, fp32 C).
+ * op(A) = A stored [M,K] (lda >= K), or A^T with A stored [K,M] under
+ * DC_GEMM_TRANS_A; op(B) = B stored [K,N] (ldb >= N), or B^T with B stored
+ * [N,K] under DC_GEMM_TRANS_B.  A and B need 16-byte aligned bases and row
+ * strides.  Epilogue, in this order: + bias[N] (DC_GEMM_BIAS); + R[M,N]
+ * (ldr; or C itself under DC_GEMM_ACCUMULATE); then DC_GEMM_GELU (aux, when
+ * non-NULL, receives the pre-activation; C = gelu(pre)) or DC_GEMM_GELU_BWD
+ * (C = value * gelu'(aux)).  GELU is the reference's tanh form.  Linear
+ * epilogues may split K across CTAs and add with atomics (the summation
+ * order then varies between runs).  Replaces matmul_fwd / the matmul closure
+ * (native/src/engine.cu:480-507, native/src/kernels/matmul.cuh:27-131) plus
+ * the bias add, GELU and residual adds of a Layer / FeedForward forward and
+ * backward. */
+#define DC_GEMM_TRANS_A 0x1
+#define DC_GEMM_TRANS_B 0x2
+#define DC_GEMM_BIAS 0x4
+#define DC_GEMM_GELU 0x8
+#define DC_GEMM_GELU_BWD 0x10
+#define DC_GEMM_ACCUMULATE 0x20
+int dc_gemm(const void *A, int lda, const void *B, int ldb, float *C, int ldc, int M, int N,
+            int K, int dtype, int flags, float alpha, const float *bias, const float *R, int ldr,
+            float *aux, int ldaux, void *stream);
+
 /* ------------------------------------------------------------------ legacy
  * The reference's handle ABI (native/src/engine.cu).  Every returned handle
  * is owned by the caller and released with destroy_tensor; op outputs keep

@@ -1,0 +1,118 @@
+"""dc_gemm (tcgen05 dense layers) against float64 products on the host.
+
+tf32 operands keep 10 mantissa bits, so fp32 inputs are checked normwise to
+2e-3; bf16 inputs are exact in the MMA and only the fp32 accumulation order
+differs (1e-5)."""
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ops():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a GPU")
+    from dart_cuda_b200 import ops as _ops
+    return _ops
+
+
+def rel(got, ref):
+    got = got.double().cpu()
+    return float((got - ref).norm() / max(ref.norm(), 1e-30))
+
+
+def gelu64(x):
+    return 0.5 * x * (1.0 + torch.tanh(0.7978845608 * (x + 0.044715 * x ** 3)))
+
+
+def gelu_d64(x):
+    t = torch.tanh(0.7978845608 * (x + 0.044715 * x ** 3))
+    return 0.5 * (1 + t) + 0.5 * x * (1 - t * t) * 0.7978845608 * (1 + 3 * 0.044715 * x * x)
+
+
+def operands(M, N, K, ta, tb, dtype, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    A = torch.randn((K, M) if ta else (M, K), generator=g)
+    B = torch.randn((N, K) if tb else (K, N), generator=g)
+    A64, B64 = A.to(dtype).double(), B.to(dtype).double()
+    ref = (A64.T if ta else A64) @ (B64.T if tb else B64)
+    return A.to(dtype).cuda(), B.to(dtype).cuda(), ref
+
+
+TOL = {torch.float32: 2e-3, torch.bfloat16: 1e-5}
+
+
+@pytest.mark.parametrize("ta,tb", [(False, False), (False, True), (True, False), (True, True)])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("M,N,K", [(128, 128, 128), (300, 200, 72), (1000, 384, 256)])
+def test_layouts(ops, ta, tb, dtype, M, N, K):
+    if dtype == torch.bfloat16 and (M % 8 or N % 8 or K % 8):
+        pytest.skip("bf16 rows must be 16-byte multiples")
+    A, B, ref = operands(M, N, K, ta, tb, dtype)
+    C = ops.gemm(A, B, trans_a=ta, trans_b=tb)
+    torch.cuda.synchronize()
+    assert rel(C, ref) < TOL[dtype]
+
+
+@pytest.mark.parametrize("M,N,K", [(64, 512, 512), (64, 2048, 512), (64, 512, 2048), (7, 65, 256)])
+def test_skinny_split_k(ops, M, N, K):
+    """Few output tiles: K is split across CTAs (bias once, residual kept)."""
+    if N % 4:  # row stride padded to 16 bytes, as the LM head of a 65-token vocabulary
+        Bfull = torch.randn(K, N + (4 - N % 4)).cuda()
+        B = Bfull[:, :N]
+        ref_B = B.double().cpu()
+    else:
+        B = torch.randn(K, N).cuda()
+        ref_B = B.double().cpu()
+    A = torch.randn(M, K).cuda()
+    bias = torch.randn(N).cuda()
+    R = torch.randn(M, N).cuda()
+    C = ops.gemm(A, B, bias=bias, residual=R)
+    ref = A.double().cpu() @ ref_B + bias.double().cpu() + R.double().cpu()
+    assert rel(C, ref) < TOL[torch.float32]
+    acc = R.clone()
+    ops.gemm(A, B, out=acc, accumulate=True)
+    assert rel(acc, A.double().cpu() @ ref_B + R.double().cpu()) < TOL[torch.float32]
+
+
+def test_gelu_and_its_backward(ops):
+    M, N, K = 512, 1024, 256
+    A, B, ref = operands(M, N, K, False, False, torch.float32, seed=3)
+    A = A * 0.2
+    ref = ref * 0.2
+    bias = torch.randn(N).cuda()
+    pre = torch.empty(M, N, device="cuda")
+    H = ops.gemm(A, B, bias=bias, gelu=True, gelu_aux=pre)
+    pre_ref = ref + bias.double().cpu()
+    assert rel(pre, pre_ref) < TOL[torch.float32]
+    assert rel(H, gelu64(pre_ref)) < TOL[torch.float32]
+    # backward of the following layer: dPre = (dY @ W^T) * gelu'(pre)
+    dY = torch.randn(M, 384).cuda()
+    W = torch.randn(N, 384).cuda()
+    dP = ops.gemm(dY, W, trans_b=True, gelu_bwd_aux=pre)
+    dref = (dY.double().cpu() @ W.double().cpu().T) * gelu_d64(pre.double().cpu())
+    assert rel(dP, dref) < TOL[torch.float32]
+
+
+def test_alpha_and_strided_views(ops):
+    """Leading dimensions wider than the logical shape (column views)."""
+    M, N, K = 200, 96, 128
+    Abig = torch.randn(M, K + 32).cuda()
+    Bbig = torch.randn(K, N + 64).cuda()
+    Cbig = torch.zeros(M, N + 16, device="cuda")
+    A, B, C = Abig[:, 8:8 + K], Bbig[:, 16:16 + N], Cbig[:, :N]
+    ops.gemm(A, B, out=C, alpha=0.5)
+    ref = 0.5 * (A.double().cpu() @ B.double().cpu())
+    assert rel(C, ref) < TOL[torch.float32]
+    assert torch.count_nonzero(Cbig[:, N:]) == 0
+
+
+def test_rejects_unaligned(ops):
+    A = torch.randn(64, 66).cuda()  # 264-byte rows: not a multiple of 16
+    B = torch.randn(66, 64).cuda()
+    with pytest.raises(ops.DcError):
+        ops.gemm(A, B)
+    assert ops.device_status() == 0
