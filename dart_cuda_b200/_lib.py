@@ -61,6 +61,20 @@ SIGNATURES = {
                              c_float, _VP]),
     "dc_gemm": (c_int, [_VP, c_int, _VP, c_int, _VP, c_int, c_int, c_int, c_int, c_int, c_int, c_float,
                         _VP, _VP, c_int, _VP, c_int, _VP]),
+    "dc_aft_fwd_strided": (c_int, [_VP, _VP, _VP, _VP, c_int, _VP, c_int, c_int, c_int, c_int, c_int,
+                                   c_int, c_int, c_int, _VP, c_size_t, _VP]),
+    "dc_aft_bwd_strided": (c_int, [_VP, _VP, _VP, _VP, c_int, _VP, _VP, _VP, _VP, _VP, c_int, c_int,
+                                   c_int, c_int, c_int, c_int, c_int, c_int, _VP, c_size_t, _VP]),
+    "dc_embedding_fwd": (c_int, [_VP, _VP, _VP, _VP, c_int, c_int, c_int, c_int, _VP]),
+    "dc_embedding_bwd": (c_int, [_VP, _VP, _VP, _VP, c_int, c_int, c_int, c_int, _VP]),
+    "dc_gate_fwd": (c_int, [_VP, c_int, _VP, _VP, c_int, c_int, c_int, _VP]),
+    "dc_gate_bwd": (c_int, [_VP, c_int, _VP, _VP, c_int, _VP, c_int, _VP, c_int, c_int, _VP]),
+    "dc_greedy_embed": (c_int, [_VP, c_int, c_int, c_int, _VP, _VP, _VP, c_int, _VP, c_int, _VP, _VP]),
+    "dc_aft_decode_workspace_size": (c_size_t, [c_int, c_int, c_int]),
+    "dc_aft_decode": (c_int, [_VP, c_int, _VP, c_int, ctypes.c_longlong, _VP, c_int, c_int, c_int, _VP,
+                              c_int, _VP, c_int, _VP, c_size_t, _VP]),
+    "dc_kv_cache_fill": (c_int, [_VP, c_int, c_int, c_int, c_int, _VP, _VP]),
+    "dc_copy2d": (c_int, [_VP, c_size_t, _VP, c_size_t, c_size_t, c_size_t, _VP]),
     # the reference's handle ABI
     "create_tensor": (_VP, [c_int32, c_int32, _FP]),
     "destroy_tensor": (None, [_VP]),

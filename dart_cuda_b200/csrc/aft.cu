@@ -79,6 +79,8 @@ __device__ __forceinline__ float sigmoidf_(float q) { return 1.0f / (1.0f + __ex
 struct Params {
     int B, Tq, Tk, D, Tqp, Tkp, dp;
     int causal, accumulate;
+    int ldi;          // row stride of Q, K, V, dQ, dK, dV (elements, >= D)
+    int ldo;          // row stride of Z and dZ (elements, >= D)
     int n_tiles;      // tensor-core path: number of output tiles of the launch
     int kpb;          // WGRAD: K steps per batch element (dp / BKe)
     int splits;       // WGRAD: split-K factor
@@ -112,9 +114,9 @@ __device__ __forceinline__ void epi_fwd(const Params &p, int b, int t, int d, fl
                                         float den)
 {
     if (t < p.Tq && d < p.D) {
-        size_t o = ((size_t)b * p.Tq + t) * p.D + d;
-        float s = sigmoidf_(ld_io((const IO *)p.Q, o));
-        st_io((IO *)p.Z, o, s * (num / den));
+        const size_t row = (size_t)b * p.Tq + t;
+        float s = sigmoidf_(ld_io((const IO *)p.Q, row * p.ldi + d));
+        st_io((IO *)p.Z, row * p.ldo + d, s * (num / den));
     }
 }
 
@@ -124,9 +126,10 @@ __device__ __forceinline__ void epi_bwd1(const Params &p, int b, int t, int d, f
 {
     float g = 0.f, n = 0.f;
     if (t < p.Tq && d < p.D) {
-        size_t o = ((size_t)b * p.Tq + t) * p.D + d;
+        const size_t row = (size_t)b * p.Tq + t;
+        const size_t o = row * p.ldi + d;
         float s = sigmoidf_(ld_io((const IO *)p.Q, o));
-        float dz = ld_io((const IO *)p.dZ, o);
+        float dz = ld_io((const IO *)p.dZ, row * p.ldo + d);
         float r = num / den;
         float dq = dz * r * s * (1.0f - s);
         if (p.accumulate) dq += ld_io((const IO *)p.dQ, o);
@@ -150,7 +153,7 @@ __device__ __forceinline__ void epi_hgrad(const Params &p, int b, int i, int d, 
                                           float h2)
 {
     if (i < p.Tk && d < p.D) {
-        size_t o = ((size_t)b * p.Tk + i) * p.D + d;
+        const size_t o = ((size_t)b * p.Tk + i) * p.ldi + d;
         float e = __expf(ld_io((const IO *)p.K, o) - p.c[(size_t)b * p.dp + d]);
         float v = ld_io((const IO *)p.V, o);
         float dv = e * h1;
@@ -243,7 +246,7 @@ __device__ __forceinline__ void ld8(const __nv_bfloat16 *p, float (&v)[8])
 
 template <class IO>
 __device__ __forceinline__ void prep_colmax_block(int bx, int s, int b, const IO *__restrict__ K,
-                                                  int B, int Tk, int D, int dp,
+                                                  int B, int Tk, int D, int ldk, int dp,
                                                   int rows_per_split, int vec,
                                                   float *__restrict__ cpart)
 {
@@ -251,14 +254,14 @@ __device__ __forceinline__ void prep_colmax_block(int bx, int s, int b, const IO
     const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
     const int d0 = (bx * 32 + tx) * 8;
     const int i0 = s * rows_per_split, i1 = min(Tk, i0 + rows_per_split);
-    const IO *Kb = K + (size_t)b * Tk * D;
+    const IO *Kb = K + (size_t)b * Tk * ldk;
     float mx[8];
 #pragma unroll
     for (int k = 0; k < 8; ++k) mx[k] = -INFINITY;
     if (vec && d0 + 8 <= D) {
         for (int i = i0 + ty; i < i1; i += 8) {
             float v[8];
-            ld8(Kb + (size_t)i * D + d0, v);
+            ld8(Kb + (size_t)i * ldk + d0, v);
 #pragma unroll
             for (int k = 0; k < 8; ++k) mx[k] = fmaxf(mx[k], v[k]);
         }
@@ -266,7 +269,7 @@ __device__ __forceinline__ void prep_colmax_block(int bx, int s, int b, const IO
         for (int i = i0 + ty; i < i1; i += 8)
 #pragma unroll
             for (int k = 0; k < 8; ++k)
-                if (d0 + k < D) mx[k] = fmaxf(mx[k], ld_io(Kb, (size_t)i * D + d0 + k));
+                if (d0 + k < D) mx[k] = fmaxf(mx[k], ld_io(Kb, (size_t)i * ldk + d0 + k));
     }
 #pragma unroll
     for (int k = 0; k < 8; ++k) red[ty][tx * 8 + k] = mx[k];
@@ -287,7 +290,7 @@ template <class IO, class E>
 __global__ void __launch_bounds__(256)
     prep_wc_kernel(const float *__restrict__ w, int ldw, int Tq, int Tk, int Tkp, int causal,
                    float *__restrict__ m, E *__restrict__ Ap, const IO *__restrict__ K, int B,
-                   int D, int dp, int ncb, int nsplit, int rows_per_split, int vec,
+                   int D, int ldk, int dp, int ncb, int nsplit, int rows_per_split, int vec,
                    float *__restrict__ cpart)
 {
     const int bid = blockIdx.x;
@@ -297,7 +300,7 @@ __global__ void __launch_bounds__(256)
         return;
     }
     const int q = bid - Tqp;
-    prep_colmax_block<IO>(q % ncb, (q / ncb) % nsplit, q / (ncb * nsplit), K, B, Tk, D, dp,
+    prep_colmax_block<IO>(q % ncb, (q / ncb) % nsplit, q / (ncb * nsplit), K, B, Tk, D, ldk, dp,
                           rows_per_split, vec, cpart);
 }
 
@@ -332,7 +335,7 @@ template <class IO, class E>
 __global__ void __launch_bounds__(256)
     prep_p_kernel(const IO *__restrict__ K, const IO *__restrict__ V,
                   const float *__restrict__ cpart, int nsplit, float *__restrict__ c, int B,
-                  int Tk, int D, int Tkp, int dp, int rows_per_block, int vec,
+                  int Tk, int D, int ldk, int Tkp, int dp, int rows_per_block, int vec,
                   E *__restrict__ PV, E *__restrict__ PE)
 {
     __shared__ __align__(16) float cs[128];
@@ -360,7 +363,7 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
         for (int k = 0; k < 8; ++k) pv[k] = pe[k] = 0.f;
         if (i < Tk) {
-            const size_t src = ((size_t)b * Tk + i) * D + d0;
+            const size_t src = ((size_t)b * Tk + i) * ldk + d0;
             if (vec && d0 + 8 <= D) {
                 float k8[8], v8[8];
                 ld8(K + src, k8);
@@ -488,6 +491,7 @@ __global__ void __launch_bounds__(256) bwd_stats_kernel(const Params p)
 // ------------------------------------------------------------ host side
 struct Layout {
     int B, Tq, Tk, D, Tqp, Tkp, dp, esz, nsplit, rows_per_split;
+    int ldi, ldo;  // row strides of the user tensors (Q, K, V and grads; Z and dZ)
     size_t off_m, off_c, off_cpart, off_ap, off_pv, off_pe, off_g1, off_g2, off_g1l, off_g2l;
     size_t off_rs, off_is;  // saved forward statistics (DC_AFT_SAVE_STATS only)
     size_t total;
@@ -505,6 +509,7 @@ static Layout make_layout(int B, int Tq, int Tk, int D, int dtype, int flags)
     L.Tq = Tq;
     L.Tk = Tk;
     L.D = D;
+    L.ldi = L.ldo = D;
     L.Tqp = (int)round_up(std::max(Tq, 1), T_ALIGN);
     L.Tkp = (int)round_up(std::max(Tk, 1), T_ALIGN);
     L.dp = (int)round_up(std::max(D, 1), D_ALIGN);
@@ -595,7 +600,7 @@ static int run_prep(const Layout &L, const IO *K, const IO *V, const float *w, i
     E *PV = reinterpret_cast<E *>(ws + L.off_pv);
     E *PE = reinterpret_cast<E *>(ws + L.off_pe);
     // 16-byte access to K and V rows: D a multiple of 8 and aligned bases
-    const int vec = (L.D % 8 == 0) &&
+    const int vec = (L.D % 8 == 0) && (L.ldi % 8 == 0) &&
                     ((reinterpret_cast<uintptr_t>(K) | reinterpret_cast<uintptr_t>(V)) & 15) == 0;
     {
         // A' rows and the partial column maxima of K in one launch
@@ -603,7 +608,7 @@ static int run_prep(const Layout &L, const IO *K, const IO *V, const float *w, i
         const int ncb = (L.D + 255) / 256;
         const int grid = L.Tqp + ncb * L.nsplit * L.B;
         prep_wc_kernel<IO, E><<<grid, 256, 0, st>>>(w, ldw, L.Tq, L.Tk, L.Tkp, causal, m, Ap, K,
-                                                    L.B, L.D, L.dp, ncb, L.nsplit,
+                                                    L.B, L.D, L.ldi, L.dp, ncb, L.nsplit,
                                                     L.rows_per_split, vec, cpart);
     }
     {
@@ -615,7 +620,8 @@ static int run_prep(const Layout &L, const IO *K, const IO *V, const float *w, i
         const int rows_per_block = (L.Tkp + rsplit - 1) / rsplit;
         rsplit = (L.Tkp + rows_per_block - 1) / rows_per_block;
         prep_p_kernel<IO, E><<<dim3(ndb, rsplit, L.B), 256, 0, st>>>(
-            K, V, cpart, L.nsplit, c, L.B, L.Tk, L.D, L.Tkp, L.dp, rows_per_block, vec, PV, PE);
+            K, V, cpart, L.nsplit, c, L.B, L.Tk, L.D, L.ldi, L.Tkp, L.dp, rows_per_block, vec, PV,
+            PE);
     }
     DC_CUDA_TRY(cudaGetLastError());
     return DC_OK;
@@ -755,6 +761,8 @@ static Params make_params(const Layout &L, char *ws, int flags)
     p.Tq = L.Tq;
     p.Tk = L.Tk;
     p.D = L.D;
+    p.ldi = L.ldi;
+    p.ldo = L.ldo;
     p.Tqp = L.Tqp;
     p.Tkp = L.Tkp;
     p.dp = L.dp;
@@ -781,12 +789,12 @@ static Params make_params(const Layout &L, char *ws, int flags)
 }
 
 // 32-byte vector access along D: every 16-element run of a row starts on a
-// 32-byte boundary when a row holds a multiple of 32 bytes and every base
-// pointer is 32-byte aligned.
+// 32-byte boundary when both row strides are multiples of 32 bytes and every
+// base pointer is 32-byte aligned.
 template <class IO>
-static int vec_ok(int D, std::initializer_list<const void *> ptrs)
+static int vec_ok(const Layout &L, std::initializer_list<const void *> ptrs)
 {
-    if ((D * (int)sizeof(IO)) % 32 != 0) return 0;
+    if ((L.ldi * (int)sizeof(IO)) % 32 != 0 || (L.ldo * (int)sizeof(IO)) % 32 != 0) return 0;
     for (const void *q : ptrs)
         if (reinterpret_cast<uintptr_t>(q) & 31) return 0;
     return 1;
@@ -806,7 +814,7 @@ static int fwd_impl(const void *Q, const void *K, const void *V, const float *w,
     p.Z = Z;
     p.w = w;
     p.ldw = ldw;
-    p.vec_io = vec_ok<IO>(L.D, {Q, Z});
+    p.vec_io = vec_ok<IO>(L, {Q, Z});
     return launch<FWD, E, IO>(p, L, ws, st, flags);
 }
 
@@ -831,7 +839,7 @@ static int bwd_impl(const void *Q, const void *K, const void *V, const float *w,
     p.dW = dW;
     p.w = w;
     p.ldw = ldw;
-    p.vec_io = vec_ok<IO>(L.D, {Q, K, V, dZ, dQ, dK, dV});
+    p.vec_io = vec_ok<IO>(L, {Q, K, V, dZ, dQ, dK, dV});
     p.vec_w = (ldw % 8 == 0) && ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(dW)) & 31) == 0;
     if ((flags & DC_AFT_WS_VALID) && saves_stats(flags)) {
         KernelTimer kt("aft_bwd_from_stats", st);
@@ -895,12 +903,32 @@ int dc_aft_fwd(const void *Q, const void *K, const void *V, const float *w, int 
                int B, int Tq, int Tk, int D, int dtype, int flags, void *workspace,
                size_t workspace_bytes, void *stream)
 {
+    return dc_aft_fwd_strided(Q, K, V, w, ldw, Z, B, Tq, Tk, D, D, D, dtype, flags, workspace,
+                              workspace_bytes, stream);
+}
+
+int dc_aft_bwd(const void *Q, const void *K, const void *V, const float *w, int ldw,
+               const void *dZ, void *dQ, void *dK, void *dV, float *dW, int B, int Tq, int Tk,
+               int D, int dtype, int flags, void *workspace, size_t workspace_bytes,
+               void *stream)
+{
+    return dc_aft_bwd_strided(Q, K, V, w, ldw, dZ, dQ, dK, dV, dW, B, Tq, Tk, D, D, D, dtype,
+                              flags, workspace, workspace_bytes, stream);
+}
+
+int dc_aft_fwd_strided(const void *Q, const void *K, const void *V, const float *w, int ldw,
+                       void *Z, int B, int Tq, int Tk, int D, int ldi, int ldo, int dtype,
+                       int flags, void *workspace, size_t workspace_bytes, void *stream)
+{
     clear_error();
     DC_TRY(validate(Q, K, V, w, ldw, B, Tq, Tk, D, dtype, flags));
     if ((long long)B * Tq * D == 0) return DC_OK;
     if (!Z) return fail(DC_ERR_INVALID, "Z is NULL");
+    if (ldi < D || ldo < D) return fail(DC_ERR_INVALID, "row strides (%d, %d) < D (%d)", ldi, ldo, D);
     cudaStream_t st = as_stream(stream);
     Layout L = make_layout(B, Tq, Tk, D, dtype, flags);
+    L.ldi = ldi;
+    L.ldo = ldo;
     Workspace ws;
     DC_TRY(get_workspace(ws, L, workspace, workspace_bytes, st));
     if (dtype == DC_BF16)
@@ -910,17 +938,20 @@ int dc_aft_fwd(const void *Q, const void *K, const void *V, const float *w, int 
     return fwd_impl<float, float>(Q, K, V, w, ldw, Z, L, flags, ws.base, st);
 }
 
-int dc_aft_bwd(const void *Q, const void *K, const void *V, const float *w, int ldw,
-               const void *dZ, void *dQ, void *dK, void *dV, float *dW, int B, int Tq, int Tk,
-               int D, int dtype, int flags, void *workspace, size_t workspace_bytes,
-               void *stream)
+int dc_aft_bwd_strided(const void *Q, const void *K, const void *V, const float *w, int ldw,
+                       const void *dZ, void *dQ, void *dK, void *dV, float *dW, int B, int Tq,
+                       int Tk, int D, int ldi, int ldo, int dtype, int flags, void *workspace,
+                       size_t workspace_bytes, void *stream)
 {
     clear_error();
     DC_TRY(validate(Q, K, V, w, ldw, B, Tq, Tk, D, dtype, flags));
     if ((long long)B * Tq * D == 0) return DC_OK;
     if (!dZ || !dQ || !dK || !dV || !dW) return fail(DC_ERR_INVALID, "null gradient pointer");
+    if (ldi < D || ldo < D) return fail(DC_ERR_INVALID, "row strides (%d, %d) < D (%d)", ldi, ldo, D);
     cudaStream_t st = as_stream(stream);
     Layout L = make_layout(B, Tq, Tk, D, dtype, flags);
+    L.ldi = ldi;
+    L.ldo = ldo;
     Workspace ws;
     DC_TRY(get_workspace(ws, L, workspace, workspace_bytes, st));
     if (dtype == DC_BF16)

@@ -193,19 +193,20 @@ __device__ __forceinline__ void epi16_fwd(const Params &p, int b, int t, int d0,
         st16(p.Rs + so, r);
         st16(p.Is + so, inv);
     }
-    const size_t o = ((size_t)b * p.Tq + t) * p.D + d0;
+    const size_t row = (size_t)b * p.Tq + t;
+    const size_t o = row * p.ldi + d0, oz = row * p.ldo + d0;
     if (p.vec_io && d0 + 16 <= p.D) {
         float q[16], z[16];
         ld16g((const IO *)p.Q + o, q);
 #pragma unroll
         for (int j = 0; j < 16; ++j) z[j] = __fdividef(num[j], den[j] * (1.0f + __expf(-q[j])));
-        st16((IO *)p.Z + o, z);
+        st16((IO *)p.Z + oz, z);
     } else {
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
             if (d0 + j >= p.D) break;
             const float q = ld_io((const IO *)p.Q, o + j);
-            st_io((IO *)p.Z, o + j, __fdividef(num[j], den[j] * (1.0f + __expf(-q))));
+            st_io((IO *)p.Z, oz + j, __fdividef(num[j], den[j] * (1.0f + __expf(-q))));
         }
     }
 }
@@ -218,11 +219,12 @@ __device__ __forceinline__ void epi16_grads(const Params &p, int b, int t, int d
 {
     float g[16], n[16];
     const bool trow = t < p.Tq;
-    const size_t o = ((size_t)b * p.Tq + t) * p.D + d0;
+    const size_t row = (size_t)b * p.Tq + t;
+    const size_t o = row * p.ldi + d0, oz = row * p.ldo + d0;
     if (trow && p.vec_io && d0 + 16 <= p.D) {
         float q[16], dz[16], dq[16];
         ld16g((const IO *)p.Q + o, q);
-        ld16g((const IO *)p.dZ + o, dz);
+        ld16g((const IO *)p.dZ + oz, dz);
         if (p.accumulate) ld16((const IO *)p.dQ + o, dq);
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
@@ -246,7 +248,7 @@ __device__ __forceinline__ void epi16_grads(const Params &p, int b, int t, int d
             for (int j = 0; j < 16; ++j) {
                 if (d0 + j >= p.D) break;
                 const float q = ld_io((const IO *)p.Q, o + j);
-                const float dz = ld_io((const IO *)p.dZ, o + j);
+                const float dz = ld_io((const IO *)p.dZ, oz + j);
                 const float s = fast_sigmoid(q);
                 const float inv = iv[j];
                 const float r = rr[j];
@@ -289,7 +291,7 @@ __device__ __forceinline__ void epi16_hgrad(const Params &p, int b, int i, int d
                                             const float (&h1)[16], const float (&h2)[16])
 {
     if (i >= p.Tk) return;
-    const size_t o = ((size_t)b * p.Tk + i) * p.D + d0;
+    const size_t o = ((size_t)b * p.Tk + i) * p.ldi + d0;
     const float *cb = p.c + (size_t)b * p.dp + d0;
     if (p.vec_io && d0 + 16 <= p.D) {
         float k[16], v[16], c[16], dk[16], dv[16];

@@ -106,6 +106,18 @@ int dc_aft_bwd(const void *Q, const void *K, const void *V, const float *w, int 
                int D, int dtype, int flags, void *workspace, size_t workspace_bytes,
                void *stream);
 
+/* The same with row strides (elements): ldi for Q, K, V, dQ, dK, dV and ldo
+ * for Z, dZ, so one head's columns can be read from a fused [B*T, 3*H*D]
+ * projection and written into a [B*T, H*D] head concatenation in place
+ * (MultiHeadAFT, lib/core/attention/aft_multi_head_attention.dart:32-44). */
+int dc_aft_fwd_strided(const void *Q, const void *K, const void *V, const float *w, int ldw,
+                       void *Z, int B, int Tq, int Tk, int D, int ldi, int ldo, int dtype,
+                       int flags, void *workspace, size_t workspace_bytes, void *stream);
+int dc_aft_bwd_strided(const void *Q, const void *K, const void *V, const float *w, int ldw,
+                       const void *dZ, void *dQ, void *dK, void *dV, float *dW, int B, int Tq,
+                       int Tk, int D, int ldi, int ldo, int dtype, int flags, void *workspace,
+                       size_t workspace_bytes, void *stream);
+
 /* ------------------------------------------------- row-wise training ops
  * Affine LayerNorm over the last dim.  Replaces layernorm_fwd/bwd
  * (native/src/kernels/layernorm_embed.cuh:140-240).  x, y, dy, dx: [R, C]
@@ -180,6 +192,64 @@ int dc_adam_step(float *p, const float *g, float *m, float *v, int64_t n, int t,
 int dc_gemm(const void *A, int lda, const void *B, int ldb, float *C, int ldc, int M, int N,
             int K, int dtype, int flags, float alpha, const float *bias, const float *R, int ldr,
             float *aux, int ldaux, void *stream);
+
+/* -------------------------------------------------- decoder step kernels
+ * Token + position embedding of B sequences of T ids (int32, [B*T]):
+ * out[b*T+t,:] = wte[idx,:] + wpe[t,:]; an id outside [0, V) gives a zero row
+ * and sets bit 0x20 of the device status word.  The backward adds dx rows
+ * into dwte (atomics) and the batch sums into dwpe (either may be NULL).
+ * Replaces embedding_fwd/bwd (native/src/kernels/layernorm_embed.cuh:242-269)
+ * and embedding_forward (native/src/engine.cu:794-822). */
+int dc_embedding_fwd(const int32_t *idx, const float *wte, const float *wpe, float *out, int B,
+                     int T, int D, int V, void *stream);
+int dc_embedding_bwd(const int32_t *idx, const float *dx, float *dwte, float *dwpe, int B, int T,
+                     int D, int V, void *stream);
+
+/* AFT cross-attention against a single encoder row (TEnc = 1, the decoder's
+ * dummy encoder, lib/core/transformers/aft/transformer_decoder_block.dart:63-67):
+ * the one weight cancels, so out[m,n] = sigmoid(q[m,n]) * v0[n] exactly
+ * (native/src/kernels/attention.cuh:41-128 at TEnc = 1).  The backward
+ * writes dq and adds sum_m dout*sigmoid(q) into dv0; the key and the bias
+ * entry get zero gradient. */
+int dc_gate_fwd(const float *q, int ldq, const float *v0, float *out, int ldo, int M, int N,
+                void *stream);
+int dc_gate_bwd(const float *q, int ldq, const float *v0, const float *dz, int ldz, float *dq,
+                int lddq, float *dv0, int M, int N, void *stream);
+
+/* Greedy decoding of the logits at position p = *pos (a device int):
+ * tokens[b*ldt + p+1] = argmax_v logits[b*ldl + v] (lowest index on ties),
+ * x[b,:] = wte[token,:] + wpe[p+1,:] when x is non-NULL (the next step's
+ * input), then *pos = p+1.  Past the capacity (p+1 >= ldt) nothing is
+ * written and bit 0x40 of the device status word is set.  No counterpart in
+ * the reference, which samples on the host after copying the logits back
+ * (example/bin/shakespear4.dart:216). */
+int dc_greedy_embed(const float *logits, int ldl, int B, int V, const float *wte,
+                    const float *wpe, int *pos, int D, int32_t *tokens, int ldt, float *x,
+                    void *stream);
+
+/* Device-to-device copy of `rows` rows of width_bytes between pitched
+ * buffers (stream-ordered). */
+int dc_copy2d(void *dst, size_t dst_pitch, const void *src, size_t src_pitch, size_t width_bytes,
+              size_t rows, void *stream);
+
+/* Incremental causal AFT for one new position t = *pos (a device int, so a
+ * captured step replays as the position advances) of B sequences (one layer,
+ * H heads of hs channels, D = H*hs): qkv holds the position's fused
+ * projection [B, 3D] (q | k | v, row stride ldq); w is head h's bias at
+ * w + h*head_stride_w with row stride ldw >= Tmax; cache is the layer's k/v history
+ * [Tmax][B*D/4][8] fp32 (rows < t filled, by earlier calls or
+ * dc_kv_cache_fill); row t is appended by this call.  Z[b,:] (row stride ldz)
+ * receives sigmoid(q) * sum_{i<=t} e^{k_i+w[t,i]} v_i / sum e^{k_i+w[t,i]}.
+ * workspace: dc_aft_decode_workspace_size bytes, zero-filled once before its
+ * first use (the kernel leaves it zeroed).  No counterpart in the reference,
+ * which recomputes the whole context per token
+ * (example/bin/shakespear4.dart:176-214). */
+size_t dc_aft_decode_workspace_size(int B, int D, int Tmax);
+int dc_aft_decode(const float *qkv, int ldq, const float *w, int ldw, long long head_stride_w,
+                  float *cache, int B, int H, int hs, const int *pos, int Tmax, float *Z, int ldz,
+                  void *workspace, size_t workspace_bytes, void *stream);
+/* Fill cache rows [0, T) from a prefill's fused projection [B*T, 3D]. */
+int dc_kv_cache_fill(const float *qkv, int ldq, int B, int T, int D, float *cache, void *stream);
 
 /* ------------------------------------------------------------------ legacy
  * The reference's handle ABI (native/src/engine.cu).  Every returned handle

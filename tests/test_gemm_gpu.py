@@ -13,8 +13,7 @@ pytestmark = pytest.mark.gpu
 
 @pytest.fixture(scope="module")
 def ops():
-    if not torch.cuda.is_available():
-        pytest.skip("needs a GPU")
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
     from dart_cuda_b200 import ops as _ops
     return _ops
 
