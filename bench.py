@@ -180,13 +180,312 @@ def row_kernels(dev, P, reps=10):
     return out
 
 
+# ------------------------------------------------------------------ decoder
+DECODER_CONFIGS = {
+    # char-level decoder training step: vocab 65, 4 blocks, d_model 256, 4 heads, FFN 4x, T 256, B 64
+    "c3": dict(vocab=65, d_model=256, n_layers=4, n_heads=4, block_size=256, B=64, T=256,
+               desc="AFT decoder training step fp32 (tf32 tensor cores) vocab 65, 4 blocks, d_model 256, "
+                    "4 heads, FFN 1024, T 256, B 64, CE eps 0.1, AdamW lr 3e-4",
+               metric="decoder training step tokens/s"),
+    # cached greedy decode: 6 blocks, d_model 512, vocab 8192, B 64, prompt 256, 256 new tokens
+    "c5": dict(vocab=8192, d_model=512, n_layers=6, n_heads=4, block_size=512, B=64, T=256, new=256,
+               desc="AFT decoder greedy decode fp32: 6 blocks, d_model 512, 4 heads, vocab 8192, B 64, "
+                    "prompt 256 + 256 new tokens, k/v history cached",
+               metric="decoder greedy decode tokens/s"),
+}
+
+
+def _timed(torch, fn, steps, flush, stream):
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    for i in range(steps):
+        flush.zero_()
+        starts[i].record(stream)
+        fn()
+        ends[i].record(stream)
+    torch.cuda.synchronize()
+    return sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+
+
+def _max_over_ranks(torch, dist, dev, v):
+    if dist is None:
+        return v
+    t = torch.tensor([v], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t)
+
+
+def _kernel_table(prof, steps, bytes_per=None, flops_per=None, P=None):
+    out = {}
+    total = max(sum(m for m, _ in prof.values()), 1e-9)
+    for name, (ms, cnt) in prof.items():
+        e = {"ms_per_step": ms / steps, "launches_per_step": cnt / steps, "share": ms / total}
+        if bytes_per and name in bytes_per:
+            e["GB/s"] = bytes_per[name] * steps / (ms / 1e3) / 1e9
+            e["hbm_frac"] = e["GB/s"] / P["hbm_gbs"]
+        if flops_per and name in flops_per:
+            e["TFLOP/s"] = flops_per[name] * steps / (ms / 1e3) / 1e12
+            e["tensor_frac"] = e["TFLOP/s"] / P["bf16_tflops"]
+        out[name] = e
+    return out
+
+
+def bench_train(args, dev, rank, world, dist):
+    """C3: one data-parallel training step of the AFT decoder per bench step
+    (forward, backward, gradient all-reduce for N > 1, AdamW)."""
+    import torch
+    from dart_cuda_b200 import decoder, ops
+
+    c = DECODER_CONFIGS["c3"]
+    cfg = decoder.DecoderConfig(vocab=c["vocab"], d_model=c["d_model"], n_layers=c["n_layers"],
+                                n_heads=c["n_heads"], block_size=c["block_size"])
+    B, T = c["B"], c["T"]
+    m = decoder.AftDecoder(cfg, device=dev, seed=0)  # the same initial weights on every rank
+    g = torch.Generator(device=dev)
+    g.manual_seed(2000 + rank)
+    idx = torch.randint(0, cfg.vocab, (B, T), device=dev, generator=g, dtype=torch.int32)
+    tgt = torch.randint(0, cfg.vocab, (B, T), device=dev, generator=g, dtype=torch.int32)
+    flush = torch.empty(256 * 1024 * 1024 // 4, device=dev)
+    stream = torch.cuda.current_stream()
+    graph = None
+
+    def fwd_bwd():
+        m.forward(idx, tgt)
+        m.backward(grad_scale=1.0 / world)
+
+    def step():
+        if graph is not None:
+            graph.replay()
+        else:
+            fwd_bwd()
+        if dist is not None:
+            dist.all_reduce(m.grad)
+        m.optimizer_step(lr=3e-4)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    barrier()
+    if not args.no_graph:
+        graph = torch.cuda.CUDAGraph()  # forward + backward; AdamW stays eager (its step count moves)
+        with torch.cuda.graph(graph):
+            fwd_bwd()
+        step()
+        barrier()
+    sampler = ClockSampler(int(os.environ.get("LOCAL_RANK", "0")))
+    with sampler:
+        barrier()
+        total_ms = _timed(torch, step, args.steps, flush, stream)
+        barrier()
+    total_ms = _max_over_ranks(torch, dist, dev, total_ms)
+    ms = total_ms / args.steps
+    value = B * T * world / (ms / 1e3)
+
+    # per-kernel pass (eager, events around every library launch)
+    ops.profile_enable(True)
+    for _ in range(args.steps):
+        flush.zero_()
+        fwd_bwd()
+        if dist is not None:
+            dist.all_reduce(m.grad)
+        m.optimizer_step(lr=3e-4)
+    torch.cuda.synchronize()
+    prof = ops.profile_read()
+    ops.profile_enable(False)
+    d, F, V, M, L = cfg.d_model, 4 * cfg.d_model, cfg.vocab, B * T, cfg.n_layers
+    fwd_gemm = L * 2 * M * d * (3 * d + d + d + d + 2 * F) + 2 * M * d * V
+    gemm_flops = 3 * fwd_gemm  # forward, input gradients, weight gradients
+    aft_flops = L * cfg.n_heads * 3 * 2 * B * cfg.head * T * (T + 1)
+    P = peaks()
+    kern = _kernel_table(prof, args.steps, flops_per={"gemm_tc": gemm_flops}, P=P)
+    dom = max(prof, key=lambda k: prof[k][0]) if prof else None
+    roof = None
+    if dom == "gemm_tc":
+        k = kern[dom]
+        roof = {"bound": "tensor", "achieved": k["TFLOP/s"], "peak": P["bf16_tflops"], "unit": "TFLOP/s",
+                "frac": k["tensor_frac"], "traffic": None, "kernel": dom,
+                "peak_source": P["source"] + " bf16 burst (the GEMMs run tf32: half that rate is their ceiling)"}
+
+    # end to end: token ids and targets from pinned host memory, the loss back
+    h_idx, h_tgt = idx.cpu().pin_memory(), tgt.cpu().pin_memory()
+    h_loss = torch.empty(1).pin_memory()
+
+    def e2e_step():
+        idx.copy_(h_idx, non_blocking=True)
+        tgt.copy_(h_tgt, non_blocking=True)
+        step()
+        h_loss.copy_(m._bufs["loss"], non_blocking=True)
+
+    e2e_ms = _max_over_ranks(torch, dist, dev, _timed(torch, e2e_step, args.steps, flush, stream))
+    line = {
+        "metric": c["metric"], "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": max(3, args.warmup), "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": c["desc"], "B_per_gpu": B, "seq_len": T, "global_batch": B * world,
+                   "parallelism": f"dp{world}", "l2": "flushed between steps (256 MiB write)",
+                   "cuda_graph": not args.no_graph},
+        "tflops": (gemm_flops + aft_flops) * world / (ms / 1e3) / 1e12,
+        "e2e": {"value": B * T * world / (e2e_ms / args.steps / 1e3), "unit": "tokens/s",
+                "h2d_bytes_per_step": 2 * B * T * 4, "d2h_bytes_per_step": 4},
+        "roofline": roof, "kernels": kern,
+        "gpu_launches": sum(cnt for _, cnt in prof.values()),
+        "clocks": sampler.summary(),
+        "cpu_baseline": None,
+    }
+    return line
+
+
+def bench_decode(args, dev, rank, world, dist):
+    """C5: one bench step = prefill of the prompt plus new-1 cached decode
+    steps (each a CUDA-graph replay) for B sequences per GPU; N GPUs run
+    independent replicas."""
+    import torch
+    from dart_cuda_b200 import decoder, ops
+
+    c = DECODER_CONFIGS["c5"]
+    cfg = decoder.DecoderConfig(vocab=c["vocab"], d_model=c["d_model"], n_layers=c["n_layers"],
+                                n_heads=c["n_heads"], block_size=c["block_size"])
+    B, T0, new = c["B"], c["T"], c["new"]
+    m = decoder.AftDecoder(cfg, device=dev, seed=0)
+    g = torch.Generator(device=dev)
+    g.manual_seed(3000 + rank)
+    prompt = torch.randint(0, cfg.vocab, (B, T0), device=dev, generator=g, dtype=torch.int32)
+    flush = torch.empty(256 * 1024 * 1024 // 4, device=dev)
+    stream = torch.cuda.current_stream()
+    m.prefill(prompt)
+    m.decode_step()
+    torch.cuda.synchronize()
+    pre_g, dec_g = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    with torch.cuda.graph(pre_g):
+        m.prefill(prompt)
+    dec_g = m.capture_decode_step()
+
+    def generation():
+        pre_g.replay()
+        for _ in range(new - 1):
+            dec_g.replay()
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(max(3, args.warmup)):
+        generation()
+    barrier()
+    steps = max(1, args.steps)
+    sampler = ClockSampler(int(os.environ.get("LOCAL_RANK", "0")))
+    with sampler:
+        barrier()
+        total_ms = _timed(torch, generation, steps, flush, stream)
+        barrier()
+    total_ms = _max_over_ranks(torch, dist, dev, total_ms)
+    ms = total_ms / steps
+    value = B * new * world / (ms / 1e3)
+    # decode-only rate: time the replays without the prefill
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    pre_g.replay()
+    e0.record(stream)
+    for _ in range(new - 1):
+        dec_g.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    dec_ms = e0.elapsed_time(e1)
+
+    # per-kernel pass: one eager generation
+    ops.profile_enable(True)
+    m.prefill(prompt)
+    for _ in range(new - 1):
+        m.decode_step()
+    torch.cuda.synchronize()
+    prof = ops.profile_read()
+    ops.profile_enable(False)
+    d, L, H = cfg.d_model, cfg.n_layers, cfg.n_heads
+    # algorithmic bytes of the decode kernel over one generation: the k/v
+    # history of positions <= t, the bias row, q|k|v in, Z out, per layer
+    dec_bytes = sum(L * ((t + 1) * B * d * 8 + H * (t + 1) * 4 + B * 3 * d * 4 + B * d * 4)
+                    for t in range(T0, T0 + new - 1))
+    P = peaks()
+    kern = _kernel_table(prof, 1, bytes_per={"aft_decode": dec_bytes}, P=P)
+    roof = None
+    if "aft_decode" in kern:
+        k = kern["aft_decode"]
+        roof = {"bound": "hbm", "achieved": k["GB/s"], "peak": P["hbm_gbs"], "unit": "GB/s",
+                "frac": k["hbm_frac"], "traffic": None, "kernel": "aft_decode", "peak_source": P["source"],
+                "algorithmic_bytes": dec_bytes / max(prof["aft_decode"][1], 1)}
+    toks = m._dec["tokens"]
+    h_prompt = prompt.cpu().pin_memory()
+    h_toks = torch.empty(B, T0 + new, dtype=torch.int32).pin_memory()
+
+    def e2e_gen():
+        prompt.copy_(h_prompt, non_blocking=True)
+        generation()
+        h_toks.copy_(toks[:, : T0 + new], non_blocking=True)
+
+    e2e_ms = _max_over_ranks(torch, dist, dev, _timed(torch, e2e_gen, steps, flush, stream))
+    line = {
+        "metric": c["metric"], "value": value, "unit": "tokens/s", "n_gpus": world, "steps": steps,
+        "warmup": max(3, args.warmup), "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": c["desc"], "B_per_gpu": B, "prompt": T0, "new_tokens": new,
+                   "global_batch": B * world, "parallelism": f"replicas x{world}",
+                   "l2": "flushed between generations (256 MiB write); the k/v history exceeds L2",
+                   "cuda_graph": True},
+        "decode_only_tokens_per_s": B * (new - 1) * world / (dec_ms / 1e3),
+        "e2e": {"value": B * new * world / (e2e_ms / steps / 1e3), "unit": "tokens/s",
+                "h2d_bytes_per_step": B * T0 * 4, "d2h_bytes_per_step": B * (T0 + new) * 4},
+        "roofline": roof, "kernels": kern,
+        "gpu_launches": sum(cnt for _, cnt in prof.values()),
+        "clocks": sampler.summary(),
+        "cpu_baseline": None,
+    }
+    return line
+
+
+def main_decoder(args):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    c = DECODER_CONFIGS[args.config]
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "metric": c["metric"],
+                              "unavailable": "the reference has no host-side decoder path to time; its "
+                                             "CPU restatement here covers the AFT operator and row ops only"}),
+                  flush=True)
+        return
+    import torch
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    try:
+        line = (bench_train if args.config == "c3" else bench_decode)(args, dev, rank, world, dist)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+    finally:
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+
+
 # ------------------------------------------------------------------ main
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
+    ap.add_argument("--config", default="c2", choices=sorted(CONFIGS) + sorted(DECODER_CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of a CUDA graph")
@@ -198,6 +497,8 @@ def main():
     ap.add_argument("--no-rows", action="store_true", help="skip the LayerNorm/bias/CE bandwidth pass")
     args = ap.parse_args()
 
+    if args.config in DECODER_CONFIGS:
+        return main_decoder(args)
     B, T, d, dt, desc = CONFIGS[args.config]
     stats = args.backward == "stats" or (args.backward == "auto" and T >= 1024)
     rank = int(os.environ.get("RANK", "0"))

@@ -37,7 +37,8 @@ namespace dec {
 constexpr int kThreads = 256;
 constexpr int kSlab = kThreads * 4;  // columns per block
 constexpr int kGroup = 8;            // history rows per online-softmax update
-constexpr int kMaxRows = 64;         // history rows per block at most
+constexpr int kMaxRows = 256;        // history rows per block at most
+constexpr int kMaxChunks = 16;       // blocks per slab at most (merged in registers)
 constexpr int kMaxHeads = 8;         // heads one slab may touch
 
 struct Params {
@@ -177,22 +178,46 @@ __global__ void __launch_bounds__(kThreads) aft_decode_kernel(Params p)
     __syncthreads();
     if (!last || !active) return;
     __threadfence();
+    // every chunk's 12 partials of this thread's 4 columns are contiguous:
+    // loads of four chunks are issued together, then combined
+    float M[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY}, n[4] = {0.f, 0.f, 0.f, 0.f},
+          d[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int q0 = 0; q0 < p.chunks; q0 += 4) {
+        float4 pr[4][3];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        float M = -INFINITY;
-        for (int q = 0; q < p.chunks; ++q) M = fmaxf(M, __ldcg(p.part + ((size_t)q * cols + c0 + j) * 3));
-        float n = 0.f, d = 0.f;
-        for (int q = 0; q < p.chunks; ++q) {
-            const float *pq = p.part + ((size_t)q * cols + c0 + j) * 3;
-            const float mq = __ldcg(pq);
-            if (mq == -INFINITY) continue;
-            const float sc = __expf(mq - M);
-            n += sc * __ldcg(pq + 1);
-            d += sc * __ldcg(pq + 2);
-        }
-        const float qv = qrow[ch + j];
-        p.Z[(size_t)b * p.ldz + ch + j] = sigm(qv) * (n / d);
+        for (int u = 0; u < 4; ++u)
+            if (q0 + u < p.chunks) {
+                const float4 *src =
+                    reinterpret_cast<const float4 *>(p.part + ((size_t)(q0 + u) * cols + c0) * 3);
+                pr[u][0] = __ldcg(src);
+                pr[u][1] = __ldcg(src + 1);
+                pr[u][2] = __ldcg(src + 2);
+            }
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+            if (q0 + u < p.chunks) {
+                const float v[12] = {pr[u][0].x, pr[u][0].y, pr[u][0].z, pr[u][0].w,
+                                     pr[u][1].x, pr[u][1].y, pr[u][1].z, pr[u][1].w,
+                                     pr[u][2].x, pr[u][2].y, pr[u][2].z, pr[u][2].w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float mq = v[3 * j];
+                    if (mq == -INFINITY) continue;
+                    const float nm = fmaxf(M[j], mq);
+                    const float a = __expf(M[j] - nm), b_ = __expf(mq - nm);
+                    n[j] = n[j] * a + v[3 * j + 1] * b_;
+                    d[j] = d[j] * a + v[3 * j + 2] * b_;
+                    M[j] = nm;
+                }
+            }
     }
+    const float4 qv = *reinterpret_cast<const float4 *>(qrow + ch);
+    float4 z;
+    z.x = sigm(qv.x) * (n[0] / d[0]);
+    z.y = sigm(qv.y) * (n[1] / d[1]);
+    z.z = sigm(qv.z) * (n[2] / d[2]);
+    z.w = sigm(qv.w) * (n[3] / d[3]);
+    *reinterpret_cast<float4 *>(p.Z + (size_t)b * p.ldz + ch) = z;
 }
 
 // Copy k and v of positions [0, T) of a prefill's fused projection
@@ -236,11 +261,13 @@ int dc_aft_decode(const float *qkv, int ldq, const float *w, int ldw, long long 
     const int D = H * hs;
     if (B <= 0 || H <= 0 || hs <= 0 || Tmax <= 0)
         return fail(DC_ERR_INVALID, "bad decode shape B=%d H=%d hs=%d Tmax=%d", B, H, hs, Tmax);
-    if (hs % 4 || ldq % 4 || ldq < 3 * D || ldz < D || ldw < Tmax)
-        return fail(DC_ERR_INVALID, "hs and ldq must be multiples of 4, ldq >= 3D, ldz >= D, ldw >= Tmax");
+    if (hs % 4 || ldq % 4 || ldz % 4 || ldq < 3 * D || ldz < D || ldw < Tmax)
+        return fail(DC_ERR_INVALID,
+                    "hs, ldq and ldz must be multiples of 4, ldq >= 3D, ldz >= D, ldw >= Tmax");
     if (!pos || !qkv || !w || !cache || !Z || !workspace) return fail(DC_ERR_INVALID, "null pointer");
-    if (((reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(cache)) & 15) != 0)
-        return fail(DC_ERR_INVALID, "qkv and cache need 16-byte alignment");
+    if (((reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(cache) |
+          reinterpret_cast<uintptr_t>(Z)) & 15) != 0)
+        return fail(DC_ERR_INVALID, "qkv, cache and Z need 16-byte alignment");
     if (workspace_bytes < dc_aft_decode_workspace_size(B, D, Tmax))
         return fail(DC_ERR_NOMEM, "decode workspace too small");
     // the heads one slab touches must fit the block's bias rows
@@ -248,10 +275,12 @@ int dc_aft_decode(const float *qkv, int ldq, const float *w, int ldw, long long 
         return fail(DC_ERR_UNSUPPORTED, "more than %d heads per %d-column slab", kMaxHeads, kSlab);
     const int cols = B * D;
     const int slabs = (cols + kSlab - 1) / kSlab;
-    // history chunks: about two blocks per SM at full length, 8..64 rows each
-    const int want = std::max(1, (2 * sm_count() + slabs - 1) / slabs);
-    int rows = std::max(kGroup, std::min(kMaxRows, (Tmax + want - 1) / want));
+    // history chunks: about two blocks per SM at full length, at most
+    // kMaxChunks per slab, a multiple of kGroup rows each
+    const int want = std::min(kMaxChunks, std::max(1, (2 * sm_count() + slabs - 1) / slabs));
+    int rows = std::max(kGroup, (Tmax + want - 1) / want);
     rows = (rows + kGroup - 1) / kGroup * kGroup;
+    if (rows > kMaxRows) return fail(DC_ERR_UNSUPPORTED, "Tmax %d above %d", Tmax, kMaxRows * kMaxChunks);
     const int max_chunks = (Tmax + rows - 1) / rows;
     Params p{};
     p.qkv = qkv;

@@ -123,12 +123,25 @@ __global__ void greedy_embed_kernel(const float *__restrict__ logits, int ldl, i
     const float *l = logits + (size_t)b * ldl;
     float best = -INFINITY;
     int bi = 0x7fffffff;
-    for (int v = threadIdx.x; v < V; v += blockDim.x) {
-        const float x_ = l[v];
+    auto take = [&](float x_, int v) {
         if (x_ > best || (x_ == best && v < bi)) {
             best = x_;
             bi = v;
         }
+    };
+    if (((ldl | V) & 3) == 0 && (reinterpret_cast<uintptr_t>(logits) & 15) == 0) {
+        // 16-byte loads, several in flight per thread
+        const float4 *l4 = reinterpret_cast<const float4 *>(l);
+#pragma unroll 4
+        for (int v = threadIdx.x; v < V / 4; v += blockDim.x) {
+            const float4 x4 = l4[v];
+            take(x4.x, 4 * v);
+            take(x4.y, 4 * v + 1);
+            take(x4.z, 4 * v + 2);
+            take(x4.w, 4 * v + 3);
+        }
+    } else {
+        for (int v = threadIdx.x; v < V; v += blockDim.x) take(l[v], v);
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {

@@ -545,6 +545,7 @@ int dc_layernorm_fwd(const float *x, const float *gamma, const float *beta, floa
                      aligned16(beta);
     const int wpb = 8;
     const unsigned grid = (unsigned)((R + wpb - 1) / wpb);
+    KernelTimer kt("layernorm_fwd", st);
     if (vec && C <= 128)
         ln_fwd_warp<1><<<grid, 32 * wpb, 0, st>>>(x, gamma, beta, y, R, C, eps);
     else if (vec && C <= 256)
@@ -585,6 +586,7 @@ int dc_layernorm_bwd(const float *x, const float *gamma, const float *dy, float 
     DC_CUDA_TRY(cudaMallocAsync(&part, (size_t)nparts * 2 * C * sizeof(float), st));
     const size_t shbytes = (size_t)wpb * 2 * C * sizeof(float);
     int rc = DC_OK;
+    KernelTimer kt("layernorm_bwd", st);
     if (vec) {
         if (C <= 128)
             ln_bwd_warp<1><<<nparts, 32 * wpb, shbytes, st>>>(x, gamma, dy, dx, part, R, C, eps,
@@ -628,6 +630,7 @@ int dc_bias_fwd(const float *a, const float *b, float *out, int M, int N, void *
     cudaStream_t st = as_stream(stream);
     const size_t n = (size_t)M * N;
     const int blocks = (int)std::min<size_t>((n + 1023) / 1024, (size_t)sm_count() * 8);
+    KernelTimer kt("bias_fwd", st);
     if (N % 4 == 0 && aligned16(a) && aligned16(b) && aligned16(out))
         bias_fwd_vec<<<blocks, 256, 0, st>>>((const float4 *)a, (const float4 *)b, (float4 *)out,
                                               n / 4, N / 4);
@@ -651,6 +654,7 @@ int dc_bias_bwd(const float *dy, float *da, float *db, int M, int N, int accumul
     const int rblocks = (M + rows_per_cta - 1) / rows_per_cta;
     float *part = nullptr;
     DC_CUDA_TRY(cudaMallocAsync(&part, (size_t)rblocks * N * sizeof(float), st));
+    KernelTimer kt("bias_bwd", st);
     bias_bwd_kernel<<<dim3(cblocks, rblocks), dim3(32, 8), 0, st>>>(dy, da, part, M, N,
                                                                      rows_per_cta, accumulate);
     colsum_parts<<<(N + 255) / 256, 256, 0, st>>>(part, rblocks, N, db, db, N, accumulate);
@@ -670,6 +674,7 @@ int dc_ce_fwd(const float *logits, const int32_t *targets, float *loss, float *r
     cudaStream_t st = as_stream(stream);
     float *rows = row_loss;
     if (!rows) DC_CUDA_TRY(cudaMallocAsync(&rows, (size_t)T * sizeof(float), st));
+    KernelTimer kt("ce_fwd", st);
     if (V <= 1024)
         ce_fwd_warp<<<(T + 7) / 8, 256, 0, st>>>(logits, targets, rows, T, V, eps);
     else
@@ -752,6 +757,7 @@ int dc_ce_bwd(const float *logits, const int32_t *targets, const float *grad_sca
     if (T == 0) return DC_OK;
     if (!logits || !targets || !dlogits) return fail(DC_ERR_INVALID, "null pointer");
     cudaStream_t st = as_stream(stream);
+    KernelTimer kt("ce_bwd", st);
     if (V <= 1024)
         ce_bwd_warp<<<(T + 7) / 8, 256, 0, st>>>(logits, targets, grad_scale, dlogits, T, V, eps);
     else
@@ -770,6 +776,7 @@ int dc_adam_step(float *p, const float *g, float *m, float *v, int64_t n, int t,
     const float step = (float)t + 1.0f;
     const float c1 = 1.0f - powf(b1, step), c2 = 1.0f - powf(b2, step);
     const int blocks = (int)std::min<int64_t>((n + 255) / 256, (int64_t)sm_count() * 8);
+    KernelTimer kt("adam", as_stream(stream));
     adam_kernel<<<blocks, 256, 0, as_stream(stream)>>>(p, g, m, v, n, lr, b1, b2, eps,
                                                        weight_decay, c1, c2);
     DC_CUDA_TRY(cudaGetLastError());

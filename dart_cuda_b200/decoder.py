@@ -213,6 +213,7 @@ class AftDecoder:
         b["dqkv"], b["dh"] = z(M, 3 * d), z(M, F)
         b["dlog"], b["dlog_pad"] = z(M, V), z(M, self.Vp)
         b["scale"] = torch.ones(1, device=dev)
+        b["loss"] = torch.zeros(1, device=dev)
         # one AFT workspace per (layer, head): the forward's panels are reused
         # by the backward; r and 1/den are kept from T >= 1024 on
         self._aft_flags = DC_AFT_CAUSAL | (DC_AFT_SAVE_STATS if T >= 1024 else 0)
@@ -291,7 +292,7 @@ class AftDecoder:
         if targets is None:
             return b["logits"], None
         b["idx"], b["targets"] = idx, targets.view(-1)
-        return b["logits"], ops.ce_fwd(b["logits"], b["targets"])
+        return b["logits"], ops.ce_fwd(b["logits"], b["targets"], out=b["loss"])
 
     def backward(self, grad_scale: float = 1.0):
         """Gradients of the last forward's loss (times grad_scale) into

@@ -182,9 +182,9 @@ def bias_bwd(dy, grads=None, accumulate=False):
     return da, db
 
 
-def ce_fwd(logits, targets, eps=0.1, row_loss=None):
+def ce_fwd(logits, targets, eps=0.1, row_loss=None, out=None):
     T, V = logits.shape
-    loss = torch.empty(1, device=logits.device)
+    loss = torch.empty(1, device=logits.device) if out is None else out
     check(lib().dc_ce_fwd(logits.data_ptr(), targets.data_ptr(), loss.data_ptr(), _ptr(row_loss), T, V,
                           eps, _stream()), "dc_ce_fwd")
     return loss
