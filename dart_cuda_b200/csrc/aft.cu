@@ -41,7 +41,8 @@ namespace aft {
 
 constexpr int BM = 128;        // accumulator rows = TMEM lanes
 constexpr int BN = 128;        // accumulator columns (one accumulator)
-constexpr int T_ALIGN = 128;   // workspace padding of Tq and Tk
+constexpr int T_ALIGN = 128;   // workspace padding of Tq and Tk (tf32 operands)
+constexpr int T_ALIGN2 = 256;  // ... with bf16 operands: CTA pairs cover 256 rows
 constexpr int D_ALIGN = 128;   // workspace padding of D
 
 enum Mode { FWD = 0, BWD1 = 1, HGRAD = 2, WGRAD = 3 };
@@ -201,6 +202,29 @@ __device__ __forceinline__ float block_max(float v, float *red)
 }
 
 // ------------------------------------------------------------ prep kernels
+// Eight operand-precision values, one 16-byte (bf16) or two (tf32) stores.
+__device__ __forceinline__ void st8op(__nv_bfloat16 *p, const float (&v)[8])
+{
+    uint4 x;
+    x.x = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v[0])) |
+          ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v[1])) << 16);
+    x.y = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v[2])) |
+          ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v[3])) << 16);
+    x.z = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v[4])) |
+          ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v[5])) << 16);
+    x.w = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v[6])) |
+          ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v[7])) << 16);
+    *reinterpret_cast<uint4 *>(p) = x;
+}
+__device__ __forceinline__ void st8op(float *p, const float (&v)[8])
+{
+    float4 a, b;
+    a.x = to_op<float>(v[0]); a.y = to_op<float>(v[1]); a.z = to_op<float>(v[2]); a.w = to_op<float>(v[3]);
+    b.x = to_op<float>(v[4]); b.y = to_op<float>(v[5]); b.z = to_op<float>(v[6]); b.w = to_op<float>(v[7]);
+    reinterpret_cast<float4 *>(p)[0] = a;
+    reinterpret_cast<float4 *>(p)[1] = b;
+}
+
 // Row maxima m_t over the visible set and A' = exp(w - m) (0 outside the
 // set and in the padding), one block per padded row t.
 template <class E>
@@ -217,12 +241,45 @@ __device__ __forceinline__ void prep_w_row(int t, const float *__restrict__ w, i
     }
     const int lim = causal ? min(t + 1, Tk) : Tk;
     const float *wr = w + (size_t)t * ldw;
+    // 16-byte loads when a row starts on a 16-byte boundary (ldw % 4 == 0):
+    // a float4 at a multiple of 4 below lim then stays inside the row
+    const bool vec = (ldw % 4 == 0) && ((reinterpret_cast<uintptr_t>(w) & 15) == 0);
     float mx = -INFINITY;
-    for (int i = threadIdx.x; i < lim; i += blockDim.x) mx = fmaxf(mx, wr[i]);
+    if (vec) {
+        for (int i = threadIdx.x * 4; i < lim; i += blockDim.x * 4) {
+            const float4 v = __ldg(reinterpret_cast<const float4 *>(wr + i));
+            mx = fmaxf(mx, v.x);
+            if (i + 1 < lim) mx = fmaxf(mx, v.y);
+            if (i + 2 < lim) mx = fmaxf(mx, v.z);
+            if (i + 3 < lim) mx = fmaxf(mx, v.w);
+        }
+    } else {
+        for (int i = threadIdx.x; i < lim; i += blockDim.x) mx = fmaxf(mx, wr[i]);
+    }
     mx = block_max(mx, red);
     if (threadIdx.x == 0) m[t] = mx;
-    for (int i = threadIdx.x; i < Tkp; i += blockDim.x)
-        row[i] = to_op<E>(i < lim ? __expf(wr[i] - mx) : 0.f);
+    if (vec) {
+        // eight A' entries per thread, one vector store (Tkp is a multiple of 8)
+        for (int i = threadIdx.x * 8; i < Tkp; i += blockDim.x * 8) {
+            float v[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) v[k] = 0.f;
+            if (i < lim) {
+                const float4 a = __ldg(reinterpret_cast<const float4 *>(wr + i));
+                v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+                if (i + 4 < lim) {
+                    const float4 b = __ldg(reinterpret_cast<const float4 *>(wr + i + 4));
+                    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+                }
+#pragma unroll
+                for (int k = 0; k < 8; ++k) v[k] = i + k < lim ? __expf(v[k] - mx) : 0.f;
+            }
+            st8op(row + i, v);
+        }
+    } else {
+        for (int i = threadIdx.x; i < Tkp; i += blockDim.x)
+            row[i] = to_op<E>(i < lim ? __expf(wr[i] - mx) : 0.f);
+    }
 }
 
 // Partial column maxima of K over row slices: cpart[s][b][d].  Block of
@@ -306,27 +363,6 @@ __global__ void __launch_bounds__(256)
 
 // PV = exp(K - c) * V and PE = exp(K - c) over the padded [B, Tkp, dp] space,
 // eight consecutive d per thread (16-byte loads and stores when `vec`).
-__device__ __forceinline__ void st8op(__nv_bfloat16 *p, const float (&v)[8])
-{
-    uint4 x;
-    x.x = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v[0])) |
-          ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v[1])) << 16);
-    x.y = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v[2])) |
-          ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v[3])) << 16);
-    x.z = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v[4])) |
-          ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v[5])) << 16);
-    x.w = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v[6])) |
-          ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v[7])) << 16);
-    *reinterpret_cast<uint4 *>(p) = x;
-}
-__device__ __forceinline__ void st8op(float *p, const float (&v)[8])
-{
-    float4 a, b;
-    a.x = to_op<float>(v[0]); a.y = to_op<float>(v[1]); a.z = to_op<float>(v[2]); a.w = to_op<float>(v[3]);
-    b.x = to_op<float>(v[4]); b.y = to_op<float>(v[5]); b.z = to_op<float>(v[6]); b.w = to_op<float>(v[7]);
-    reinterpret_cast<float4 *>(p)[0] = a;
-    reinterpret_cast<float4 *>(p)[1] = b;
-}
 
 // Block (128 columns x 16 row lanes) of batch b = blockIdx.z: the block first
 // finishes the column maxima of its 128 columns from the nsplit partials (and
@@ -510,8 +546,9 @@ static Layout make_layout(int B, int Tq, int Tk, int D, int dtype, int flags)
     L.Tk = Tk;
     L.D = D;
     L.ldi = L.ldo = D;
-    L.Tqp = (int)round_up(std::max(Tq, 1), T_ALIGN);
-    L.Tkp = (int)round_up(std::max(Tk, 1), T_ALIGN);
+    const int talign = operand_size(dtype, flags) == 2 ? T_ALIGN2 : T_ALIGN;
+    L.Tqp = (int)round_up(std::max(Tq, 1), talign);
+    L.Tkp = (int)round_up(std::max(Tk, 1), talign);
     L.dp = (int)round_up(std::max(D, 1), D_ALIGN);
     L.esz = operand_size(dtype, flags);
     const int dblocks = (D + 255) / 256;
@@ -627,6 +664,24 @@ static int run_prep(const Layout &L, const IO *K, const IO *V, const float *w, i
     return DC_OK;
 }
 
+// dW output tiles (128 query rows x 256 keys) before split-K; causal
+// launches skip the pairs above the diagonal.
+// Long sequences with bf16 operands run as CTA pairs (M = 256 per MMA, each
+// CTA loading half of B): the main loops dominate there.  Short ones keep one
+// CTA per tile: their element-wise epilogues dominate, and twice as many
+// independent workers drain them faster.
+static bool use_pairs(const Layout &L) { return L.esz == 2 && std::max(L.Tqp, L.Tkp) >= 1024; }
+
+static int wgrad_tiles(const Layout &L, int causal)
+{
+    if (use_pairs(L)) {  // CTA pairs: 256 query rows x 256 keys
+        const int mt = L.Tqp / T_ALIGN2, nt = L.Tkp / T_ALIGN2;
+        return causal ? mt * (mt + 1) / 2 : mt * nt;
+    }
+    const int mt = L.Tqp / BM, nt = L.Tkp / BN;
+    return causal ? wgrad_pairs_before(mt) : mt * ((nt + 1) / 2);
+}
+
 static CUtensorMapDataType tmap_type(int esz)
 {
     return esz == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
@@ -665,16 +720,18 @@ static int map_ap(CUtensorMap *m, const void *base, const Layout &L, uint32_t bx
                        tile_swizzle(L, mn_major));
 }
 
-template <int MODE, class E, class IO>
+template <int MODE, class E, class IO, bool P>
 static int launch_tc(Params p, const Layout &L, char *ws, cudaStream_t st)
 {
-    using C = TcCfg<MODE, E>;
+    static_assert(!P || sizeof(E) == 2, "CTA pairs run bf16 operands");
+    using C = TcCfg<MODE, E, P>;
+    constexpr int RB = P ? 2 * BM : BM;
     static bool attr_set[64] = {false};  // per instantiation and device
     int dev = 0;
     DC_CUDA_TRY(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64) return fail(DC_ERR_UNSUPPORTED, "device ordinal %d", dev);
     if (!attr_set[dev]) {
-        DC_CUDA_TRY(cudaFuncSetAttribute(aft_tc_kernel<MODE, E, IO>,
+        DC_CUDA_TRY(cudaFuncSetAttribute(aft_tc_kernel<MODE, E, IO, P>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          C::SMEM_BYTES));
         attr_set[dev] = true;
@@ -688,7 +745,7 @@ static int launch_tc(Params p, const Layout &L, char *ws, cudaStream_t st)
         DC_TRY(map_3d(&mB1, ws + L.off_pv, L, L.Tkp, BOX, BK, true));
         DC_TRY(map_3d(&mB2, ws + L.off_pe, L, L.Tkp, BOX, BK, true));
         mB3 = mB4 = mA2 = mA3 = mA4 = mA;
-        p.n_tiles = (L.Tqp / BM) * nd * L.B;
+        p.n_tiles = (L.Tqp / RB) * nd * L.B;
     } else if (MODE == HGRAD) {
         DC_TRY(map_ap(&mA, ws + L.off_ap, L, BOX, BK, true));
         DC_TRY(map_3d(&mB1, ws + L.off_g1, L, L.Tqp, BOX, BK, true));
@@ -696,28 +753,47 @@ static int launch_tc(Params p, const Layout &L, char *ws, cudaStream_t st)
         DC_TRY(map_3d(&mB3, ws + L.off_g1l, L, L.Tqp, BOX, BK, true));
         DC_TRY(map_3d(&mB4, ws + L.off_g2l, L, L.Tqp, BOX, BK, true));
         mA2 = mA3 = mA4 = mA;
-        p.n_tiles = (L.Tkp / BM) * nd * L.B;
+        p.n_tiles = (L.Tkp / RB) * nd * L.B;
     } else {
         const int kr = C::KROW;
         DC_TRY(map_3d(&mA, ws + L.off_g1, L, L.Tqp, BK, BM, false, kr));
         DC_TRY(map_3d(&mA2, ws + L.off_g2, L, L.Tqp, BK, BM, false, kr));
         DC_TRY(map_3d(&mA3, ws + L.off_g1l, L, L.Tqp, BK, BM, false, kr));
         DC_TRY(map_3d(&mA4, ws + L.off_g2l, L, L.Tqp, BK, BM, false, kr));
-        DC_TRY(map_3d(&mB1, ws + L.off_pv, L, L.Tkp, BK, BN, false, kr));
-        DC_TRY(map_3d(&mB2, ws + L.off_pe, L, L.Tkp, BK, BN, false, kr));
+        DC_TRY(map_3d(&mB1, ws + L.off_pv, L, L.Tkp, BK, C::BROWS, false, kr));
+        DC_TRY(map_3d(&mB2, ws + L.off_pe, L, L.Tkp, BK, C::BROWS, false, kr));
         mB3 = mB4 = mB1;
-        const int mt = L.Tqp / BM, nt = L.Tkp / BN;
-        p.n_tiles = (p.causal ? mt * (mt + 1) / 2 : mt * nt) * p.splits;
+        p.n_tiles = wgrad_tiles(L, p.causal) * p.splits;
     }
-    // persistent: one CTA per SM (shared memory admits one)
-    const int grid = std::max(1, std::min(p.n_tiles, sm_count()));
     p.trace = (g_trace_modes >> MODE) & 1 ? g_trace_buf : nullptr;
     static const char *names[4] = {"aft_tc_fwd", "aft_tc_bwd_recompute", "aft_tc_dkdv",
                                    "aft_tc_dw"};
+    cudaLaunchConfig_t cfg = {};
+    cfg.blockDim = dim3(kTcThreads);
+    cfg.dynamicSmemBytes = C::SMEM_BYTES;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = P ? 2 : 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    // persistent: one CTA (or CTA pair) per SM (pair); shared memory admits one.
+    // Pairs need two SMs of one GPC: ask how many clusters fit at once.
+    static int max_clusters[64] = {0};
+    if (P && max_clusters[dev] == 0) {
+        cfg.gridDim = dim3(2 * (sm_count() / 2));
+        int n = 0;
+        DC_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, aft_tc_kernel<MODE, E, IO, P>, &cfg));
+        max_clusters[dev] = std::max(1, n);
+    }
+    const int workers = P ? max_clusters[dev] : sm_count();
+    cfg.gridDim = dim3((P ? 2 : 1) * std::max(1, std::min(p.n_tiles, workers)));
     {
         KernelTimer kt(names[MODE], st);
-        aft_tc_kernel<MODE, E, IO><<<grid, kTcThreads, C::SMEM_BYTES, st>>>(
-            p, mA, mB1, mB2, mB3, mB4, mA2, mA3, mA4);
+        DC_CUDA_TRY(cudaLaunchKernelEx(&cfg, aft_tc_kernel<MODE, E, IO, P>, p, mA, mB1, mB2, mB3,
+                                       mB4, mA2, mA3, mA4));
     }
     DC_CUDA_TRY(cudaGetLastError());
     return DC_OK;
@@ -745,7 +821,9 @@ template <int MODE, class E, class IO>
 static int launch(const Params &p, const Layout &L, char *ws, cudaStream_t st, int flags)
 {
     if (flags & DC_AFT_SIMT) return launch_simt<MODE, E, IO>(p, L, ws, st);
-    return launch_tc<MODE, E, IO>(p, L, ws, st);
+    if constexpr (sizeof(E) == 2)
+        if (use_pairs(L)) return launch_tc<MODE, E, IO, true>(p, L, ws, st);
+    return launch_tc<MODE, E, IO, false>(p, L, ws, st);
 }
 
 // The tensor-core forward keeps r and 1/den for the backward.
@@ -779,7 +857,9 @@ static Params make_params(const Layout &L, char *ws, int flags)
     // first query rows, where den' sums few terms; with bf16 operands the
     // residuals of rows t < 128 bring dW to the accuracy of keeping them all.
     // tf32 keeps them everywhere (they also enter dK/dV there).
-    p.lo_rows = L.esz == 4 ? L.Tqp : std::min(L.Tqp, BM);
+    // (CTA-pair tiles span two 128-row blocks, so there the first 256 rows
+    // carry them)
+    p.lo_rows = L.esz == 4 ? L.Tqp : std::min(L.Tqp, use_pairs(L) ? 2 * BM : BM);
     if (saves_stats(flags)) {
         p.Rs = reinterpret_cast<float *>(ws + L.off_rs);
         p.Is = reinterpret_cast<float *>(ws + L.off_is);
@@ -850,20 +930,24 @@ static int bwd_impl(const void *Q, const void *K, const void *V, const float *w,
         DC_TRY((launch<BWD1, E, IO>(p, L, ws, st, flags)));
     }
     DC_TRY((launch<HGRAD, E, IO>(p, L, ws, st, flags)));
-    // split-K factor for dW: enough CTAs to cover the SMs, >= 4 K steps each
+    // split-K factor for dW: pick the split count whose tiles fill the
+    // persistent workers (CTAs, or CTA pairs) in the least time, waves x time
+    // per tile, where a tile costs at least its epilogue (the scaled atomic
+    // adds of a 128 x 256 block per CTA: measured at about 8 K steps of a
+    // single CTA's main loop, about 28 of a pair's), so splitting finer than
+    // that only adds atomics
     p.kpb = L.dp / TcCfg<WGRAD, E>::BKe;
-    const int mt = L.Tqp / BM;
-    const int tiles = causal ? mt * (mt + 1) / 2 : mt * (L.Tkp / BN);
+    const int tiles = wgrad_tiles(L, causal);
     const int ktot = L.B * p.kpb;
-    // split-K: pick the split count whose tiles fill the persistent CTAs with
-    // the least time (waves x work per tile), each split >= 8 K steps
-    const int sms = sm_count();
+    const bool pairs = use_pairs(L);
+    const int workers = pairs ? sm_count() / 2 : sm_count();
+    const double kEpiSteps = pairs ? 28.0 : 8.0;
     int best = 1;
     double best_cost = 1e30;
     for (int sp = 1; sp <= std::max(1, ktot / 8); ++sp) {
-        const int waves = (tiles * sp + sms - 1) / sms;
-        const double cost = (double)waves / sp * (1.0 + 0.002 * sp);  // atomics grow with sp
-        if (cost < best_cost) {
+        const int waves = (tiles * sp + workers - 1) / workers;
+        const double cost = waves * std::max((double)ktot / sp, kEpiSteps);
+        if (cost < 0.97 * best_cost) {  // more splits only for a clear gain (atomics)
             best_cost = cost;
             best = sp;
         }

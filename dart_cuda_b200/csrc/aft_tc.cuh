@@ -23,41 +23,63 @@ namespace aft {
 constexpr int kEpiWarps = 16;
 constexpr int kTcThreads = (kEpiWarps + 2) * 32;
 constexpr int kSmemBudget = 227 * 1024;
+#ifndef DC_WGRAD_KROW
+#define DC_WGRAD_KROW 64
+#endif
 
-template <int MODE, class E>
+// P: the launch runs CTA pairs (cta_group::2): every MMA is M = 256 over the
+// pair, each CTA loading its 128 rows of A and half of B.  bf16 operands.
+template <int MODE, class E, bool P = false>
 struct TcCfg {
+    static constexpr bool PAIR = P;
     static constexpr bool TF32 = sizeof(E) == 4;
     static constexpr bool W = MODE == WGRAD;
     static constexpr bool H = MODE == HGRAD;
-    // bytes of K per operand row and stage: dW streams six K-major tiles per
-    // stage, so it uses 64 B rows (64-byte swizzle) to keep four stages.
-    static constexpr int KROW = W ? 64 : 128;
+    // bytes of K per operand row and stage: dW streams four K-major tiles per
+    // stage (two of them 256 rows), so it uses 64 B rows (64-byte swizzle) to
+    // keep four stages.
+    static constexpr int KROW = W ? DC_WGRAD_KROW : 128;
     static constexpr int BKe = KROW / (int)sizeof(E);  // K elements per stage
     static constexpr int UK = TF32 ? 8 : 16;           // K per MMA instruction
     static constexpr int NSUB = BKe / UK;              // MMAs per stage and operand pair
     static constexpr int BOX_MN = 128 / (int)sizeof(E);// elements in one 128 B MN block
     static constexpr int TILE_BYTES = 128 * KROW;      // one operand tile of 128 rows
+    // dW accumulates a 128 x 256 tile (two i blocks): its B tiles have 256 rows
+    static constexpr int WN = W ? 2 * BN : BN;         // accumulator columns of one product
+    // dW: B rows of one product held by one CTA (K-major)
+    static constexpr int BROWS = P ? WN / 2 : WN;
+    // One B tile: dW a K-major [BROWS rows] tile; otherwise one MN-major
+    // [BN columns] tile of one product (E'V or E'; g or n).  The other modes
+    // issue one N = 256 MMA over two adjacent tiles (num | den), so a CTA
+    // holds both (or, in a pair, the even CTA the first and the odd the second).
+    static constexpr int TILE_B = W ? BROWS * KROW : BN * BKe * (int)sizeof(E);
+    static constexpr int MMA_N = W ? WN : 2 * BN;
     // K-major descriptor: swizzle mode (2 = 128 B, 4 = 64 B), 8-row atom stride
     static constexpr uint32_t K_LAYOUT = KROW == 64 ? 4u : 2u;
     static constexpr uint32_t K_SBO = 8 * KROW;
-    // dK/dV at tf32 also adds the low parts of g and n (1e-3 bar)
-    static constexpr bool LO = W || (H && TF32);
-    static constexpr int NA = W ? 4 : 1;               // A tiles per stage
-    static constexpr int NB = W ? 2 : (LO ? 4 : 2);    // B tiles per stage
-    static constexpr int STAGE_BYTES = (NA + NB) * TILE_BYTES;
+    // dK/dV at tf32 also adds the low parts of g and n (1e-3 bar); dW adds
+    // them as a second pass over K with the low-part panels as A
+    static constexpr bool LO = H && TF32;
+    static constexpr int NA = W ? 2 : 1;               // A tiles per stage
+    static constexpr int NB = W ? 2 : (P ? 1 : (LO ? 4 : 2));  // B tiles per stage and CTA
+    static constexpr int STAGE_BYTES = NA * TILE_BYTES + NB * TILE_B;
     static constexpr int STAGES_FIT = (kSmemBudget - 2048) / STAGE_BYTES;
-    static constexpr int STAGES = STAGES_FIT < 4 ? STAGES_FIT : 4;
+    static constexpr int STAGES_MAX = P ? 6 : 4;
+    static constexpr int STAGES = STAGES_FIT < STAGES_MAX ? STAGES_FIT : STAGES_MAX;
     static constexpr int NACC = W ? 1 : 2;             // accumulators per tile
-    static constexpr uint32_t ACC_COLS = NACC * BN;
+    static constexpr uint32_t ACC_COLS = W ? WN : NACC * BN;
     static constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;  // double buffered
     static constexpr uint32_t A_MN = H ? 1 : 0;
     static constexpr uint32_t B_MN = W ? 0 : 1;
-    static constexpr uint32_t IDESC = umma_idesc(TF32 ? 2u : 1u, BM, BN, A_MN, B_MN);
+    static constexpr uint32_t IDESC = umma_idesc(TF32 ? 2u : 1u, P ? 2 * BM : BM, MMA_N, A_MN, B_MN);
+    static_assert(!P || !TF32, "CTA pairs run bf16 operands");
     static constexpr uint32_t MN_LBO = BKe * 128;      // bytes between 128 B MN blocks
     static constexpr uint32_t MN_LAYOUT = TF32 ? 1u : 2u;
     static constexpr uint32_t MN_SBO = TF32 ? 512u : 1024u;
     static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 512;
     static_assert(STAGES >= 2, "pipeline needs two stages");
+    static_assert(W || TILE_B == (BN / BOX_MN) * (int)MN_LBO,
+                  "adjacent B tiles must continue the MN-block stride (one N = 256 operand)");
     static_assert(SMEM_BYTES <= kSmemBudget, "shared memory budget");
 };
 
@@ -358,23 +380,36 @@ __device__ __forceinline__ void epi16_wgrad(const Params &p, int t, int i0, cons
 
 // ----------------------------------------------------------- tile schedule
 struct Tile {
-    int b, mrow, ncol, k0, k1;  // mrow/ncol: 128-row block of the accumulator / 128-col block
+    int b, mrow, ncol, k0, k1;  // mrow/ncol: 128-row block of the accumulator / column block
+    int passes;                 // WGRAD: 2 when the low parts of g, n add a second pass over K
 };
 
-template <int MODE, int BKe>
+// dW tiles of a causal launch: row block r holds r/2 + 1 column pairs, so
+// the rows before r hold S(r) pairs: S(2m) = m(m+1), S(2m+1) = (m+1)^2.
+__host__ __device__ __forceinline__ int wgrad_pairs_before(int r)
+{
+    const int m = r >> 1;
+    return (r & 1) ? (m + 1) * (m + 1) : m * (m + 1);
+}
+
+// A tile's rows are 128-blocks (one CTA) or pairs of 128-blocks (P: the two
+// CTAs of a pair, block 2*mrow + rank each); RB is the rows it spans.
+template <int MODE, int BKe, bool P = false>
 __device__ __forceinline__ Tile decode_tile(const Params &p, int idx)
 {
+    constexpr int RB = P ? 2 * BM : BM;
     Tile t{};
+    t.passes = 1;
     if (MODE == FWD || MODE == BWD1) {
         // rows t (heavy, late-t tiles first), columns d
         const int nd = p.dp / BN;
         const int per = nd * p.B;
-        t.mrow = p.Tqp / BM - 1 - idx / per;
+        t.mrow = p.Tqp / RB - 1 - idx / per;
         const int rem = idx % per;
         t.ncol = rem % nd;
         t.b = rem / nd;
         t.k0 = 0;
-        t.k1 = (p.causal ? min(p.Tkp, (t.mrow + 1) * BM) : p.Tkp) / BKe;
+        t.k1 = (p.causal ? min(p.Tkp, (t.mrow + 1) * RB) : p.Tkp) / BKe;
     } else if (MODE == HGRAD) {
         // rows i (heavy, early-i tiles first), columns d
         const int nd = p.dp / BN;
@@ -383,33 +418,45 @@ __device__ __forceinline__ Tile decode_tile(const Params &p, int idx)
         const int rem = idx % per;
         t.ncol = rem % nd;
         t.b = rem / nd;
-        t.k0 = p.causal ? (t.mrow * BM) / BKe : 0;
+        t.k0 = p.causal ? (t.mrow * RB) / BKe : 0;
         t.k1 = p.Tqp / BKe;
     } else {
+        // RB query rows x 256 keys (two 128-blocks); ncol counts the key pairs
         const int pair = idx / p.splits, s = idx % p.splits;
         if (!p.causal) {
-            t.mrow = pair / (p.Tkp / BN);
-            t.ncol = pair % (p.Tkp / BN);
-        } else {
+            const int np = (p.Tkp / BN + 1) / 2;
+            t.mrow = pair / np;
+            t.ncol = pair % np;
+        } else if (P) {
+            // row pair m holds key pairs 0..m: triangular
             int r = (int)((sqrtf(8.0f * (float)pair + 1.0f) - 1.0f) * 0.5f);
             while ((r + 1) * (r + 2) / 2 <= pair) ++r;
             while (r * (r + 1) / 2 > pair) --r;
             t.mrow = r;
             t.ncol = pair - r * (r + 1) / 2;
+        } else {
+            int r = (int)(2.0f * sqrtf((float)pair)) - 1;  // S(r) ~ r^2/4: start just below
+            if (r < 0) r = 0;
+            while (r > 0 && wgrad_pairs_before(r) > pair) --r;
+            while (wgrad_pairs_before(r + 1) <= pair) ++r;
+            t.mrow = r;
+            t.ncol = pair - wgrad_pairs_before(r);
         }
         const int total = p.B * p.kpb;
         t.k0 = (int)(((long long)s * total) / p.splits);
         t.k1 = (int)(((long long)(s + 1) * total) / p.splits);
+        t.passes = t.mrow * RB < p.lo_rows ? 2 : 1;
     }
     return t;
 }
 
-// Tile of this CTA's j-th iteration: tiles are listed heavy-first and dealt
-// boustrophedon (round j even: c, odd: G-1-c) so each CTA pairs heavy and
-// light tiles.  -1 once the CTA has no more tiles.
+// Tile of this CTA's (or CTA pair's) j-th iteration: tiles are listed
+// heavy-first and dealt boustrophedon (round j even: c, odd: G-1-c) so each
+// worker pairs heavy and light tiles.  -1 once it has no more tiles.
+template <bool P = false>
 __device__ __forceinline__ int sched_tile(int j, int ntiles)
 {
-    const int G = gridDim.x, c = blockIdx.x;
+    const int G = P ? gridDim.x >> 1 : gridDim.x, c = P ? blockIdx.x >> 1 : blockIdx.x;
     const int t = j * G + ((j & 1) ? (G - 1 - c) : c);
     return t < ntiles ? t : -1;
 }
@@ -423,7 +470,11 @@ __device__ __forceinline__ void trace_at(const Params &p, int j, int field, unsi
 }
 
 // ----------------------------------------------------------- the kernel
-template <int MODE, class E, class IO>
+// With P the grid is made of 2-CTA clusters: both CTAs load their halves of
+// every stage (completion counted on the even CTA's barrier), the even CTA
+// issues the pair's MMAs and signals both CTAs' barriers, and each CTA's
+// epilogue drains its own 128 accumulator rows and reports to the even CTA.
+template <int MODE, class E, class IO, bool P>
 __global__ void __launch_bounds__(kTcThreads, 1)
     aft_tc_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtensorMap mapA,
                   const __grid_constant__ CUtensorMap mapB1,
@@ -434,7 +485,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                   const __grid_constant__ CUtensorMap mapA3,
                   const __grid_constant__ CUtensorMap mapA4)
 {
-    using C = TcCfg<MODE, E>;
+    using C = TcCfg<MODE, E, P>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -449,6 +500,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    const uint32_t rank = P ? cluster_rank() : 0;  // CTA of the pair (0 issues the MMAs)
+    const bool leader = rank == 0;
+    constexpr int RB = P ? 2 * BM : BM;  // accumulator rows of a tile
 
     if (threadIdx.x == 0) {
         *abort_flag = 0;
@@ -458,7 +512,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         for (int s = 0; s < 2; ++s) {
             mbar_init(smem_u32(&accf[s]), 1);
-            mbar_init(smem_u32(&acce[s]), kEpiWarps);
+            mbar_init(smem_u32(&acce[s]), P ? 2 * kEpiWarps : kEpiWarps);
         }
         mbar_init(smem_u32(drainb), 1);
         fence_mbar_init();
@@ -471,21 +525,42 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             tma_prefetch(&mapB3);
             tma_prefetch(&mapB4);
         }
-        if (C::NA == 4) {
+        if (C::W) {
             tma_prefetch(&mapA2);
             tma_prefetch(&mapA3);
             tma_prefetch(&mapA4);
         }
     }
     if (warp == kEpiWarps + 1) {
-        tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
-        tmem_relinquish();
+        if constexpr (P) {
+            tmem_alloc_pair(smem_u32(tmem_slot), C::TMEM_COLS);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+            tmem_relinquish();
+        }
     }
     tc_fence_before();
-    __syncthreads();
+    // a pair's barriers must be initialised before either CTA signals them
+    if constexpr (P)
+        cluster_sync_all();
+    else
+        __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     const int ntiles = p.n_tiles;
+    auto ld2 = [&](uint32_t dst, const CUtensorMap *m, uint32_t bar, int c0, int c1) {
+        if constexpr (P)
+            tma_load_2d_pair(dst, m, bar, c0, c1);
+        else
+            tma_load_2d(dst, m, bar, c0, c1);
+    };
+    auto ld3 = [&](uint32_t dst, const CUtensorMap *m, uint32_t bar, int c0, int c1, int c2) {
+        if constexpr (P)
+            tma_load_3d_pair(dst, m, bar, c0, c1, c2);
+        else
+            tma_load_3d(dst, m, bar, c0, c1, c2);
+    };
 
     if (warp == kEpiWarps) {
         // ------------------------------------------------ TMA producer
@@ -493,70 +568,72 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             uint32_t g = 0;
             bool stop = false;
             for (int jt = 0; !stop; ++jt) {
-                const int tile = sched_tile(jt, ntiles);
+                const int tile = sched_tile<P>(jt, ntiles);
                 if (tile < 0) break;
-                const Tile tl = decode_tile<MODE, C::BKe>(p, tile);
+                const Tile tl = decode_tile<MODE, C::BKe, P>(p, tile);
                 trace_at(p, jt, 0, global_timer());
-                for (int k = tl.k0; k < tl.k1; ++k, ++g) {
+                const int len = tl.k1 - tl.k0;
+                const int nsteps = len * tl.passes;
+                // this CTA's accumulator rows and its share of B's columns / rows
+                const int m0 = (P ? 2 * tl.mrow + (int)rank : tl.mrow) * BM;
+                const int bofs = (int)rank * C::BROWS;  // dW: this CTA's key rows
+                for (int js = 0; js < nsteps; ++js, ++g) {
+                    const int k = tl.k0 + (tl.passes > 1 ? js % len : js);
                     const int s = g % C::STAGES;
                     const uint32_t ph = (g / C::STAGES) & 1;
-                    if (!mbar_wait(smem_u32(&empty[s]), ph ^ 1, abort_flag, p.status,
+                    if (!mbar_wait<P>(smem_u32(&empty[s]), ph ^ 1, abort_flag, p.status,
                                    DC_DEVERR_TIMEOUT_EMPTY)) {
                         stop = true;
                         break;
                     }
-                    const uint32_t fb = smem_u32(&full[s]);
-                    // dW tiles past the first row block carry no low parts
-                    const bool w_lo = !C::W || tl.mrow * BM < p.lo_rows;
-                    mbar_arrive_expect_tx(fb, w_lo ? C::STAGE_BYTES
-                                                   : C::STAGE_BYTES - 2 * C::TILE_BYTES);
+                    // both CTAs' copies complete on the even CTA's barrier
+                    const uint32_t fb = P ? smem_in_cta(smem_u32(&full[s]), 0) : smem_u32(&full[s]);
+                    if (leader) mbar_arrive_expect_tx(smem_u32(&full[s]), (P ? 2 : 1) * C::STAGE_BYTES);
                     const uint32_t sa = smem_u32(smem + s * C::STAGE_BYTES);
                     const uint32_t sb = sa + C::NA * C::TILE_BYTES;
-                    if (MODE == FWD || MODE == BWD1) {
-                        // A: A'[t rows, i cols] K-major; B: PV/PE [i rows, d cols] MN-major
-                        tma_load_2d(sa, &mapA, fb, k * C::BKe, tl.mrow * BM);
+                    if (MODE == FWD || MODE == BWD1 || MODE == HGRAD) {
+                        if (MODE == HGRAD) {
+                            // A: A'[t rows (K), i cols (M)] MN-major
 #pragma unroll
-                        for (int j = 0; j < BN / C::BOX_MN; ++j) {
-                            const int x = tl.ncol * BN + j * C::BOX_MN;
-                            tma_load_3d(sb + j * C::MN_LBO, &mapB1, fb, x, k * C::BKe, tl.b);
-                            tma_load_3d(sb + C::TILE_BYTES + j * C::MN_LBO, &mapB2, fb, x,
-                                        k * C::BKe, tl.b);
+                            for (int j = 0; j < BM / C::BOX_MN; ++j)
+                                ld2(sa + j * C::MN_LBO, &mapA, fb, m0 + j * C::BOX_MN, k * C::BKe);
+                        } else {
+                            // A: A'[t rows, i cols] K-major
+                            ld2(sa, &mapA, fb, k * C::BKe, m0);
                         }
-                    } else if (MODE == HGRAD) {
-                        // A: A'[t rows (K), i cols (M)] MN-major; B: G/N [t rows, d cols] MN-major
-#pragma unroll
-                        for (int j = 0; j < BM / C::BOX_MN; ++j)
-                            tma_load_2d(sa + j * C::MN_LBO, &mapA, fb, tl.mrow * BM + j * C::BOX_MN,
-                                        k * C::BKe);
+                        // B: [PV | PE] or [G | N] (then [G lo | N lo]) [K rows, d cols]
+                        // MN-major, one BN-column tile each; a pair splits them
 #pragma unroll
                         for (int j = 0; j < BN / C::BOX_MN; ++j) {
                             const int x = tl.ncol * BN + j * C::BOX_MN;
-                            tma_load_3d(sb + j * C::MN_LBO, &mapB1, fb, x, k * C::BKe, tl.b);
-                            tma_load_3d(sb + C::TILE_BYTES + j * C::MN_LBO, &mapB2, fb, x,
-                                        k * C::BKe, tl.b);
-                            if (C::NB == 4) {
-                                tma_load_3d(sb + 2 * C::TILE_BYTES + j * C::MN_LBO, &mapB3, fb, x,
-                                            k * C::BKe, tl.b);
-                                tma_load_3d(sb + 3 * C::TILE_BYTES + j * C::MN_LBO, &mapB4, fb, x,
-                                            k * C::BKe, tl.b);
+                            const uint32_t o = sb + j * C::MN_LBO;
+                            if (P) {
+                                ld3(o, rank ? &mapB2 : &mapB1, fb, x, k * C::BKe, tl.b);
+                            } else {
+                                ld3(o, &mapB1, fb, x, k * C::BKe, tl.b);
+                                ld3(o + C::TILE_B, &mapB2, fb, x, k * C::BKe, tl.b);
+                                if (C::NB == 4) {
+                                    ld3(o + 2 * C::TILE_B, &mapB3, fb, x, k * C::BKe, tl.b);
+                                    ld3(o + 3 * C::TILE_B, &mapB4, fb, x, k * C::BKe, tl.b);
+                                }
                             }
                         }
                     } else {
-                        // A: G, N, G lo, N lo [t rows, d cols] K-major; B: PV, PE [i rows, d] K-major
+                        // A: G, N (first pass) or their low parts (second pass) [t rows, d]
+                        // K-major; B: PV, PE [256 i rows, d] K-major
                         const int bb = k / p.kpb, x = (k % p.kpb) * C::BKe;
-                        tma_load_3d(sa, &mapA, fb, x, tl.mrow * BM, bb);
-                        tma_load_3d(sa + C::TILE_BYTES, &mapA2, fb, x, tl.mrow * BM, bb);
-                        if (w_lo) {
-                            tma_load_3d(sa + 2 * C::TILE_BYTES, &mapA3, fb, x, tl.mrow * BM, bb);
-                            tma_load_3d(sa + 3 * C::TILE_BYTES, &mapA4, fb, x, tl.mrow * BM, bb);
-                        }
-                        tma_load_3d(sb, &mapB1, fb, x, tl.ncol * BN, bb);
-                        tma_load_3d(sb + C::TILE_BYTES, &mapB2, fb, x, tl.ncol * BN, bb);
+                        const bool lo = js >= len;
+                        ld3(sa, lo ? &mapA3 : &mapA, fb, x, m0, bb);
+                        ld3(sa + C::TILE_BYTES, lo ? &mapA4 : &mapA2, fb, x, m0, bb);
+                        ld3(sb, &mapB1, fb, x, tl.ncol * C::WN + bofs, bb);
+                        ld3(sb + C::TILE_B, &mapB2, fb, x, tl.ncol * C::WN + bofs, bb);
                     }
                 }
             }
-            if (*abort_flag) {
-                // let the copies already in flight land before the CTA exits
+            if (*abort_flag && leader) {
+                // let the copies already in flight land before the CTA exits (a
+                // pair's barriers live in the even CTA, which the odd one awaits
+                // at the final cluster barrier)
                 const uint32_t first = g > (uint32_t)C::STAGES ? g - C::STAGES : 0;
                 for (uint32_t q = first; q < g; ++q)
                     mbar_wait(smem_u32(&full[q % C::STAGES]), (q / C::STAGES) & 1, nullptr,
@@ -564,27 +641,40 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
         }
     } else if (warp == kEpiWarps + 1) {
-        // ------------------------------------------------ MMA issuer
-        if (lane == 0) {
+        // ------------------------------------------------ MMA issuer (even CTA of a pair)
+        auto mma = [&](uint32_t d, uint64_t a, uint64_t b, uint32_t acc_on) {
+            if constexpr (P)
+                umma_pair(d, a, b, C::IDESC, acc_on);
+            else
+                umma<C::TF32>(d, a, b, C::IDESC, acc_on);
+        };
+        auto commit = [&](uint32_t bar) {
+            if constexpr (P)
+                umma_commit_pair(bar);
+            else
+                umma_commit(bar);
+        };
+        if (lane == 0 && leader) {
             uint32_t g = 0, j = 0;
             bool stop = false;
             for (; !stop; ++j) {
-                const int tile = sched_tile(j, ntiles);
+                const int tile = sched_tile<P>(j, ntiles);
                 if (tile < 0) break;
-                const Tile tl = decode_tile<MODE, C::BKe>(p, tile);
+                const Tile tl = decode_tile<MODE, C::BKe, P>(p, tile);
                 const uint32_t buf = j & 1, use = j >> 1;
-                if (!mbar_wait(smem_u32(&acce[buf]), (use & 1) ^ 1, abort_flag, p.status,
-                               DC_DEVERR_TIMEOUT_ACC))
+                // both CTAs' epilogues report here (cluster-scope acquire)
+                if (!mbar_wait<P>(smem_u32(&acce[buf]), (use & 1) ^ 1, abort_flag, p.status,
+                                  DC_DEVERR_TIMEOUT_ACC))
                     break;
                 tc_fence_after();
                 trace_at(p, j, 1, global_timer());
                 trace_at(p, j, 5, tile);
                 trace_at(p, j, 6, tl.k1 - tl.k0);
                 const uint32_t acc = tmem + buf * C::ACC_COLS;
-                const bool w_lo = tl.mrow * BM < p.lo_rows;
-                for (int k = tl.k0; k < tl.k1; ++k, ++g) {
+                const int nsteps = (tl.k1 - tl.k0) * tl.passes;
+                for (int js = 0; js < nsteps; ++js, ++g) {
                     const int s = g % C::STAGES;
-                    if (!mbar_wait(smem_u32(&full[s]), (g / C::STAGES) & 1, abort_flag, p.status,
+                    if (!mbar_wait<P>(smem_u32(&full[s]), (g / C::STAGES) & 1, abort_flag, p.status,
                                    DC_DEVERR_TIMEOUT_FULL)) {
                         stop = true;
                         break;
@@ -594,52 +684,40 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     const uint32_t sb = sa + C::NA * C::TILE_BYTES;
 #pragma unroll
                     for (int u = 0; u < C::NSUB; ++u) {
-                        const uint32_t first = (k == tl.k0 && u == 0) ? 0u : 1u;
+                        const uint32_t first = (js == 0 && u == 0) ? 0u : 1u;
                         const uint32_t koff = u * C::UK * (int)sizeof(E);  // K-major step
                         const uint32_t moff = u * C::UK * 128;             // MN-major step
                         if (C::W) {
-                            const uint32_t T = C::TILE_BYTES;
+                            // acc[RB t, 256 i] += G . PV^T + N . PE^T (or their low parts)
                             const uint64_t b1 = sw128_desc(sb + koff, 16, C::K_SBO, C::K_LAYOUT);
-                            const uint64_t b2 = sw128_desc(sb + T + koff, 16, C::K_SBO, C::K_LAYOUT);
-                            umma<C::TF32>(acc, sw128_desc(sa + koff, 16, C::K_SBO, C::K_LAYOUT), b1,
-                                          C::IDESC, first);
-                            umma<C::TF32>(acc, sw128_desc(sa + T + koff, 16, C::K_SBO, C::K_LAYOUT),
-                                          b2, C::IDESC, 1u);
-                            if (!w_lo) continue;
-                            umma<C::TF32>(acc,
-                                          sw128_desc(sa + 2 * T + koff, 16, C::K_SBO, C::K_LAYOUT),
-                                          b1, C::IDESC, 1u);
-                            umma<C::TF32>(acc,
-                                          sw128_desc(sa + 3 * T + koff, 16, C::K_SBO, C::K_LAYOUT),
-                                          b2, C::IDESC, 1u);
+                            const uint64_t b2 =
+                                sw128_desc(sb + C::TILE_B + koff, 16, C::K_SBO, C::K_LAYOUT);
+                            mma(acc, sw128_desc(sa + koff, 16, C::K_SBO, C::K_LAYOUT), b1, first);
+                            mma(acc, sw128_desc(sa + C::TILE_BYTES + koff, 16, C::K_SBO, C::K_LAYOUT),
+                                b2, 1u);
                         } else {
                             const uint64_t a = C::H ? sw128_desc(sa + moff, C::MN_LBO, C::MN_SBO,
                                                                  C::MN_LAYOUT)
                                                     : sw128_desc(sa + koff, 16, C::K_SBO, C::K_LAYOUT);
-                            const uint64_t b1 =
-                                sw128_desc(sb + moff, C::MN_LBO, C::MN_SBO, C::MN_LAYOUT);
-                            const uint64_t b2 = sw128_desc(sb + C::TILE_BYTES + moff, C::MN_LBO,
-                                                           C::MN_SBO, C::MN_LAYOUT);
-                            umma<C::TF32>(acc, a, b1, C::IDESC, first);
-                            umma<C::TF32>(acc + BN, a, b2, C::IDESC, first);
+                            // acc[:, 0:2BN] = [num | den]: one N = 256 MMA over the
+                            // two adjacent B tiles (their MN blocks are MN_LBO apart)
+                            const uint64_t b = sw128_desc(sb + moff, C::MN_LBO, C::MN_SBO, C::MN_LAYOUT);
+                            mma(acc, a, b, first);
                             if (C::NB == 4) {
-                                const uint64_t b3 = sw128_desc(sb + 2 * C::TILE_BYTES + moff,
-                                                               C::MN_LBO, C::MN_SBO, C::MN_LAYOUT);
-                                const uint64_t b4 = sw128_desc(sb + 3 * C::TILE_BYTES + moff,
-                                                               C::MN_LBO, C::MN_SBO, C::MN_LAYOUT);
-                                umma<C::TF32>(acc, a, b3, C::IDESC, 1u);
-                                umma<C::TF32>(acc + BN, a, b4, C::IDESC, 1u);
+                                const uint64_t bl = sw128_desc(sb + 2 * C::TILE_B + moff, C::MN_LBO,
+                                                               C::MN_SBO, C::MN_LAYOUT);
+                                mma(acc, a, bl, 1u);
                             }
                         }
                     }
-                    umma_commit(smem_u32(&empty[s]));
+                    commit(smem_u32(&empty[s]));
                 }
                 if (stop) break;
-                umma_commit(smem_u32(&accf[buf]));
+                commit(smem_u32(&accf[buf]));
                 trace_at(p, j, 2, global_timer());
             }
             if (*abort_flag) {  // MMAs must finish before TMEM is released
-                umma_commit(smem_u32(drainb));
+                commit(smem_u32(drainb));
                 mbar_wait(smem_u32(drainb), 0, nullptr, p.status, DC_DEVERR_TIMEOUT_DRAIN);
             }
         }
@@ -649,26 +727,29 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int slice = warp >> 2;         // columns slice*32 .. slice*32+31
         const int row = quad * 32 + lane;
         for (uint32_t j = 0;; ++j) {
-            const int tile = sched_tile(j, ntiles);
+            const int tile = sched_tile<P>(j, ntiles);
             if (tile < 0) break;
-            const Tile tl = decode_tile<MODE, C::BKe>(p, tile);
+            const Tile tl = decode_tile<MODE, C::BKe, P>(p, tile);
             const uint32_t buf = j & 1, use = j >> 1;
             // warp-uniform, because the TMEM loads below are warp-collective
-            const bool ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&accf[buf]), use & 1,
-                                                              abort_flag, p.status,
-                                                              DC_DEVERR_TIMEOUT_ACC));
+            const bool ok = __all_sync(0xffffffffu, mbar_wait<P>(smem_u32(&accf[buf]), use & 1,
+                                                                 abort_flag, p.status,
+                                                                 DC_DEVERR_TIMEOUT_ACC));
             if (!ok) break;
             tc_fence_after();
             if (threadIdx.x == 0) trace_at(p, j, 3, global_timer());
+            // each warp owns a slice of WN/4 columns (32, or 64 for the dW tile)
+            constexpr int SLICE = C::WN / 4;
             const uint32_t lane_addr =
-                tmem + buf * C::ACC_COLS + ((uint32_t)(quad * 32) << 16) + slice * 32;
-            const int r = tl.mrow * BM + row;  // t (FWD, BWD1, WGRAD) or i (HGRAD)
+                tmem + buf * C::ACC_COLS + ((uint32_t)(quad * 32) << 16) + slice * SLICE;
+            // t (FWD, BWD1, WGRAD) or i (HGRAD): this CTA's 128 rows of the tile
+            const int r = (P ? 2 * tl.mrow + (int)rank : tl.mrow) * BM + row;
 #pragma unroll 1
-            for (int sb = 0; sb < 2; ++sb) {
+            for (int sb = 0; sb < SLICE / 16; ++sb) {
                 float v1[16], v2[16];
                 tmem_ld16(lane_addr + sb * 16, v1);
                 if (!C::W) tmem_ld16(lane_addr + BN + sb * 16, v2);
-                const int c0 = tl.ncol * BN + slice * 32 + sb * 16;  // d, or i for WGRAD
+                const int c0 = tl.ncol * C::WN + slice * SLICE + sb * 16;  // d, or i for WGRAD
                 if (MODE == FWD)
                     epi16_fwd<IO>(p, tl.b, r, c0, v1, v2);
                 else if (MODE == BWD1)
@@ -680,14 +761,26 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(&acce[buf]));
+            if (lane == 0) {
+                if constexpr (P)
+                    mbar_arrive_remote(smem_in_cta(smem_u32(&acce[buf]), 0));
+                else
+                    mbar_arrive(smem_u32(&acce[buf]));
+            }
             if (threadIdx.x == 0) trace_at(p, j, 4, global_timer());
         }
     }
-    __syncthreads();
+    // neither CTA of a pair leaves while the other may still signal its barriers
+    if constexpr (P)
+        cluster_sync_all();
+    else
+        __syncthreads();
     if (warp == kEpiWarps + 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, C::TMEM_COLS);
+        if constexpr (P)
+            tmem_dealloc_pair(tmem, C::TMEM_COLS);
+        else
+            tmem_dealloc(tmem, C::TMEM_COLS);
     }
 }
 

@@ -135,6 +135,14 @@ def test_bf16_ragged(ops, dev):
     assert_errs(run_case(ops, dev, 8, 3, 100, 100, 72, True, dtype=torch.bfloat16, wscale=0.5), 1e-2)
 
 
+@pytest.mark.parametrize("B,Tq,Tk,D,causal", [(2, 1024, 1024, 128, True), (1, 1100, 1100, 72, True),
+                                              (1, 1030, 1290, 136, False)])
+def test_bf16_cta_pairs(ops, dev, B, Tq, Tk, D, causal):
+    """Sequences from 1024 on run as 2-CTA clusters (M = 256 MMAs): full,
+    ragged (partial row pairs, partial d blocks) and non-causal cross."""
+    assert_errs(run_case(ops, dev, 30 + Tq, B, Tq, Tk, D, causal, dtype=torch.bfloat16, wscale=0.3), 1e-2)
+
+
 # ----------------------------------------------------------- semantics
 def test_accumulate_and_workspace_reuse(ops, dev):
     B, T, D = 2, 96, 64
