@@ -933,15 +933,16 @@ static int bwd_impl(const void *Q, const void *K, const void *V, const float *w,
     // split-K factor for dW: pick the split count whose tiles fill the
     // persistent workers (CTAs, or CTA pairs) in the least time, waves x time
     // per tile, where a tile costs at least its epilogue (the scaled atomic
-    // adds of a 128 x 256 block per CTA: measured at about 8 K steps of a
-    // single CTA's main loop, about 28 of a pair's), so splitting finer than
-    // that only adds atomics
+    // adds of a 128 x 256 block per CTA: measured at about 4 K steps of a
+    // single CTA's main loop; for pairs, whose epilogues contend for the same
+    // dW lines, splitting below ~40 steps measured slower), so splitting
+    // finer than that only adds atomics
     p.kpb = L.dp / TcCfg<WGRAD, E>::BKe;
     const int tiles = wgrad_tiles(L, causal);
     const int ktot = L.B * p.kpb;
     const bool pairs = use_pairs(L);
     const int workers = pairs ? sm_count() / 2 : sm_count();
-    const double kEpiSteps = pairs ? 28.0 : 8.0;
+    const double kEpiSteps = pairs ? 40.0 : 4.0;
     int best = 1;
     double best_cost = 1e30;
     for (int sp = 1; sp <= std::max(1, ktot / 8); ++sp) {
