@@ -195,6 +195,25 @@ DECODER_CONFIGS = {
 }
 
 
+def soak(step, barrier, seconds=0.5):
+    """Untimed steps for `seconds` of wall time (in rounds of 20 steps; every
+    rank runs the same number of rounds: rank 0 decides and broadcasts)."""
+    import torch
+    import torch.distributed as dist
+
+    t0 = time.perf_counter()
+    while True:
+        for _ in range(20):
+            step()
+        barrier()
+        go = torch.tensor([1 if time.perf_counter() - t0 < seconds else 0],
+                          device=torch.cuda.current_device())
+        if dist.is_available() and dist.is_initialized():
+            dist.broadcast(go, 0)
+        if not int(go):
+            break
+
+
 def _timed(torch, fn, steps, flush, stream):
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
@@ -278,6 +297,7 @@ def bench_train(args, dev, rank, world, dist):
         barrier()
     sampler = ClockSampler(int(os.environ.get("LOCAL_RANK", "0")))
     with sampler:
+        soak(step, barrier)
         barrier()
         total_ms = _timed(torch, step, args.steps, flush, stream)
         barrier()
@@ -593,6 +613,9 @@ def main():
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     sampler = ClockSampler(local)
     with sampler:
+        # untimed steps for half a second first, so the 200 ms clock samples
+        # see the GPU under this load when the timed region itself is short
+        soak(step, barrier)
         barrier()
         for i in range(args.steps):
             flush.zero_()

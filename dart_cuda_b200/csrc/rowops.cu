@@ -334,6 +334,68 @@ __global__ void bias_bwd_kernel(const float *__restrict__ dy, float *__restrict_
     }
 }
 
+// 16-byte variant (N % 4 == 0, aligned rows): a block covers 128 columns x 8
+// row lanes, each lane two rows per iteration so four loads are in flight.
+__global__ void bias_bwd_vec4(const float4 *__restrict__ dy, float4 *__restrict__ da,
+                              float *__restrict__ part, int M, int N4, int rows_per_cta,
+                              int accumulate)
+{
+    __shared__ float4 red[8][33];
+    const int col = blockIdx.x * 32 + threadIdx.x;
+    const int r0 = blockIdx.y * rows_per_cta, r1 = min(M, r0 + rows_per_cta);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (col < N4) {
+        int r = r0 + threadIdx.y;
+        for (; r + 8 < r1; r += 16) {
+            const size_t o0 = (size_t)r * N4 + col, o1 = o0 + (size_t)8 * N4;
+            const float4 g0 = __ldcs(dy + o0), g1 = __ldcs(dy + o1);
+            acc.x += g0.x + g1.x;
+            acc.y += g0.y + g1.y;
+            acc.z += g0.z + g1.z;
+            acc.w += g0.w + g1.w;
+            if (da) {
+                float4 a0 = g0, a1 = g1;
+                if (accumulate) {
+                    const float4 p0 = da[o0], p1 = da[o1];
+                    a0 = make_float4(p0.x + g0.x, p0.y + g0.y, p0.z + g0.z, p0.w + g0.w);
+                    a1 = make_float4(p1.x + g1.x, p1.y + g1.y, p1.z + g1.z, p1.w + g1.w);
+                }
+                da[o0] = a0;
+                da[o1] = a1;
+            }
+        }
+        for (; r < r1; r += 8) {
+            const size_t o = (size_t)r * N4 + col;
+            const float4 g = __ldcs(dy + o);
+            acc.x += g.x;
+            acc.y += g.y;
+            acc.z += g.z;
+            acc.w += g.w;
+            if (da) {
+                float4 a = g;
+                if (accumulate) {
+                    const float4 p = da[o];
+                    a = make_float4(p.x + g.x, p.y + g.y, p.z + g.z, p.w + g.w);
+                }
+                da[o] = a;
+            }
+        }
+    }
+    red[threadIdx.y][threadIdx.x] = acc;
+    __syncthreads();
+    if (threadIdx.y == 0 && col < N4) {
+        float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            s.x += red[k][threadIdx.x].x;
+            s.y += red[k][threadIdx.x].y;
+            s.z += red[k][threadIdx.x].z;
+            s.w += red[k][threadIdx.x].w;
+        }
+        reinterpret_cast<float4 *>(part)[(size_t)blockIdx.y * N4 + col] = s;
+    }
+}
+
 // ===================================================================== CE
 // One warp per row (V small) or one block per row; online max/sum-exp with a
 // single read of the row.  loss_row = (1-eps)(lse - x_y) + eps(lse - mean x),
@@ -419,6 +481,90 @@ __global__ void ce_fwd_block(const float *__restrict__ logits, const int32_t *__
             const float lse = m + logf(s + 1e-12f);
             const float xt = xr[tgt[row]];
             row_loss[row] = (1.0f - eps) * (lse - xt) + eps * (lse - sx / (float)V);
+        }
+    }
+}
+
+// Wide rows (1024 < V <= 1024*NV4, V % 4 == 0, 16-byte aligned): one block
+// of 256 threads per row holds the whole row in registers (NV4 float4 per
+// thread, all loads issued up front), so the forward reads each logit once
+// and the backward reads once and writes once.  Two block reductions: the
+// row maximum, then sum e^{x-max} and sum x.
+template <int NV4>
+__device__ __forceinline__ void ce_row_regs(const float *__restrict__ xr, int V, float4 (&x)[NV4],
+                                            float &mx, float &s, float &sx, float *red)
+{
+    const float4 *x4 = reinterpret_cast<const float4 *>(xr);
+    const int n4 = V >> 2;
+    float m = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < NV4; ++k) {
+        const int i = threadIdx.x + k * 256;
+        x[k] = i < n4 ? __ldcs(x4 + i) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+        m = fmaxf(m, fmaxf(fmaxf(x[k].x, x[k].y), fmaxf(x[k].z, x[k].w)));
+    }
+    mx = block_max(m, red);
+    float a = 0.f, b = 0.f;
+#pragma unroll
+    for (int k = 0; k < NV4; ++k) {
+        if (threadIdx.x + k * 256 < n4) {
+            a += __expf(x[k].x - mx) + __expf(x[k].y - mx) + __expf(x[k].z - mx) + __expf(x[k].w - mx);
+            b += (x[k].x + x[k].y) + (x[k].z + x[k].w);
+        }
+    }
+    s = block_sum(a, red);
+    sx = block_sum(b, red);
+}
+
+template <int NV4>
+__global__ void __launch_bounds__(256) ce_fwd_regs(const float *__restrict__ logits,
+                                                   const int32_t *__restrict__ tgt,
+                                                   float *__restrict__ row_loss, int T, int V,
+                                                   float eps)
+{
+    __shared__ float red[32];
+    const int row = blockIdx.x;
+    const float *xr = logits + (size_t)row * V;
+    float4 x[NV4];
+    float mx, s, sx;
+    ce_row_regs<NV4>(xr, V, x, mx, s, sx, red);
+    if (threadIdx.x == 0) {
+        const float lse = mx + logf(s + 1e-12f);
+        const float xt = xr[tgt[row]];
+        row_loss[row] = (1.0f - eps) * (lse - xt) + eps * (lse - sx / (float)V);
+    }
+}
+
+template <int NV4>
+__global__ void __launch_bounds__(256) ce_bwd_regs(const float *__restrict__ logits,
+                                                   const int32_t *__restrict__ tgt,
+                                                   const float *__restrict__ gscale,
+                                                   float *__restrict__ grad, int T, int V,
+                                                   float eps)
+{
+    __shared__ float red[32];
+    const int row = blockIdx.x;
+    const float *xr = logits + (size_t)row * V;
+    float4 x[NV4];
+    float mx, s, sx;
+    ce_row_regs<NV4>(xr, V, x, mx, s, sx, red);
+    const float inv = 1.0f / (s + 1e-12f);
+    const float scale = (gscale ? gscale[0] : 1.0f) / (float)T;
+    const int y = tgt[row];
+    const float off = eps / (float)V;
+    float4 *g4 = reinterpret_cast<float4 *>(grad + (size_t)row * V);
+    const int n4 = V >> 2;
+#pragma unroll
+    for (int k = 0; k < NV4; ++k) {
+        const int i = threadIdx.x + k * 256;
+        if (i < n4) {
+            const int v0 = 4 * i;
+            float4 g;
+            g.x = (__expf(x[k].x - mx) * inv - ((v0 == y ? 1.0f - eps : 0.f) + off)) * scale;
+            g.y = (__expf(x[k].y - mx) * inv - ((v0 + 1 == y ? 1.0f - eps : 0.f) + off)) * scale;
+            g.z = (__expf(x[k].z - mx) * inv - ((v0 + 2 == y ? 1.0f - eps : 0.f) + off)) * scale;
+            g.w = (__expf(x[k].w - mx) * inv - ((v0 + 3 == y ? 1.0f - eps : 0.f) + off)) * scale;
+            __stcs(g4 + i, g);
         }
     }
 }
@@ -530,6 +676,45 @@ using namespace dc;
 using namespace dc::rows;
 
 static bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// Cross-entropy rows: a warp per row up to V = 1024; wider rows held in
+// registers by a block per row when V % 4 == 0 (up to 16384); otherwise a
+// streaming block per row.
+static void ce_fwd_launch(const float *logits, const int32_t *targets, float *rows, int T, int V,
+                          float eps, cudaStream_t st)
+{
+    const bool regs = V > 1024 && V % 4 == 0 && V <= 16384 && aligned16(logits);
+    if (V <= 1024)
+        ce_fwd_warp<<<(T + 7) / 8, 256, 0, st>>>(logits, targets, rows, T, V, eps);
+    else if (regs && V <= 2048)
+        ce_fwd_regs<2><<<T, 256, 0, st>>>(logits, targets, rows, T, V, eps);
+    else if (regs && V <= 4096)
+        ce_fwd_regs<4><<<T, 256, 0, st>>>(logits, targets, rows, T, V, eps);
+    else if (regs && V <= 8192)
+        ce_fwd_regs<8><<<T, 256, 0, st>>>(logits, targets, rows, T, V, eps);
+    else if (regs)
+        ce_fwd_regs<16><<<T, 256, 0, st>>>(logits, targets, rows, T, V, eps);
+    else
+        ce_fwd_block<<<T, 256, 0, st>>>(logits, targets, rows, T, V, eps);
+}
+
+static void ce_bwd_launch(const float *logits, const int32_t *targets, const float *gscale,
+                          float *dlogits, int T, int V, float eps, cudaStream_t st)
+{
+    const bool regs = V > 1024 && V % 4 == 0 && V <= 16384 && aligned16(logits) && aligned16(dlogits);
+    if (V <= 1024)
+        ce_bwd_warp<<<(T + 7) / 8, 256, 0, st>>>(logits, targets, gscale, dlogits, T, V, eps);
+    else if (regs && V <= 2048)
+        ce_bwd_regs<2><<<T, 256, 0, st>>>(logits, targets, gscale, dlogits, T, V, eps);
+    else if (regs && V <= 4096)
+        ce_bwd_regs<4><<<T, 256, 0, st>>>(logits, targets, gscale, dlogits, T, V, eps);
+    else if (regs && V <= 8192)
+        ce_bwd_regs<8><<<T, 256, 0, st>>>(logits, targets, gscale, dlogits, T, V, eps);
+    else if (regs)
+        ce_bwd_regs<16><<<T, 256, 0, st>>>(logits, targets, gscale, dlogits, T, V, eps);
+    else
+        ce_bwd_block<<<T, 256, 0, st>>>(logits, targets, gscale, dlogits, T, V, eps);
+}
 
 extern "C" {
 
@@ -648,15 +833,21 @@ int dc_bias_bwd(const float *dy, float *da, float *db, int M, int N, int accumul
     if ((long long)M * N == 0) return DC_OK;
     if (!dy || !db) return fail(DC_ERR_INVALID, "null pointer");
     cudaStream_t st = as_stream(stream);
-    const int cblocks = (N + 31) / 32;
+    const bool vec = N % 4 == 0 && aligned16(dy) && (!da || aligned16(da));
+    const int cblocks = vec ? (N / 4 + 31) / 32 : (N + 31) / 32;
     const int target = std::max(1, sm_count() * 8 / cblocks);
-    const int rows_per_cta = std::max(8, (M + target - 1) / target);
+    const int rows_per_cta = std::max(16, (M + target - 1) / target);
     const int rblocks = (M + rows_per_cta - 1) / rows_per_cta;
     float *part = nullptr;
     DC_CUDA_TRY(cudaMallocAsync(&part, (size_t)rblocks * N * sizeof(float), st));
     KernelTimer kt("bias_bwd", st);
-    bias_bwd_kernel<<<dim3(cblocks, rblocks), dim3(32, 8), 0, st>>>(dy, da, part, M, N,
-                                                                     rows_per_cta, accumulate);
+    if (vec)
+        bias_bwd_vec4<<<dim3(cblocks, rblocks), dim3(32, 8), 0, st>>>(
+            reinterpret_cast<const float4 *>(dy), reinterpret_cast<float4 *>(da), part, M, N / 4,
+            rows_per_cta, accumulate);
+    else
+        bias_bwd_kernel<<<dim3(cblocks, rblocks), dim3(32, 8), 0, st>>>(dy, da, part, M, N,
+                                                                         rows_per_cta, accumulate);
     colsum_parts<<<(N + 255) / 256, 256, 0, st>>>(part, rblocks, N, db, db, N, accumulate);
     cudaError_t e = cudaGetLastError();
     cudaFreeAsync(part, st);
@@ -675,10 +866,7 @@ int dc_ce_fwd(const float *logits, const int32_t *targets, float *loss, float *r
     float *rows = row_loss;
     if (!rows) DC_CUDA_TRY(cudaMallocAsync(&rows, (size_t)T * sizeof(float), st));
     KernelTimer kt("ce_fwd", st);
-    if (V <= 1024)
-        ce_fwd_warp<<<(T + 7) / 8, 256, 0, st>>>(logits, targets, rows, T, V, eps);
-    else
-        ce_fwd_block<<<T, 256, 0, st>>>(logits, targets, rows, T, V, eps);
+    ce_fwd_launch(logits, targets, rows, T, V, eps, st);
     mean_kernel<<<1, 1024, 0, st>>>(rows, T, loss);
     cudaError_t e = cudaGetLastError();
     if (!row_loss) cudaFreeAsync(rows, st);
@@ -739,10 +927,7 @@ int dc_ce_fwd_noalloc(const float *logits, const int32_t *targets, float *loss, 
     float *rows = ce_noalloc_rows_ptr();
     if (!rows) return fail(DC_ERR_CUDA, "dc_ce_fwd_noalloc: cannot resolve the scratch array address");
     cudaStream_t st = as_stream(stream);
-    if (V <= 1024)
-        ce_fwd_warp<<<(T + 7) / 8, 256, 0, st>>>(logits, targets, rows, T, V, eps);
-    else
-        ce_fwd_block<<<T, 256, 0, st>>>(logits, targets, rows, T, V, eps);
+    ce_fwd_launch(logits, targets, rows, T, V, eps, st);
     mean_kernel<<<1, 1024, 0, st>>>(rows, T, loss);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fail(DC_ERR_CUDA, "ce fwd noalloc: %s", cudaGetErrorString(e));
@@ -758,10 +943,7 @@ int dc_ce_bwd(const float *logits, const int32_t *targets, const float *grad_sca
     if (!logits || !targets || !dlogits) return fail(DC_ERR_INVALID, "null pointer");
     cudaStream_t st = as_stream(stream);
     KernelTimer kt("ce_bwd", st);
-    if (V <= 1024)
-        ce_bwd_warp<<<(T + 7) / 8, 256, 0, st>>>(logits, targets, grad_scale, dlogits, T, V, eps);
-    else
-        ce_bwd_block<<<T, 256, 0, st>>>(logits, targets, grad_scale, dlogits, T, V, eps);
+    ce_bwd_launch(logits, targets, grad_scale, dlogits, T, V, eps, st);
     DC_CUDA_TRY(cudaGetLastError());
     return DC_OK;
 }

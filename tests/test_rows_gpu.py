@@ -53,7 +53,7 @@ def test_layernorm(ops, dev, R, C):
     torch.testing.assert_close(grads[2], 2 * db, rtol=1e-5, atol=1e-5)
 
 
-@pytest.mark.parametrize("M,N", [(16384, 1024), (64, 96), (5, 3), (1000, 65)])
+@pytest.mark.parametrize("M,N", [(16384, 1024), (64, 96), (5, 3), (1000, 65), (37, 260)])
 def test_bias(ops, dev, M, N):
     rng = np.random.default_rng(M * N)
     a = rng.standard_normal((M, N)).astype(np.float32)
@@ -67,7 +67,8 @@ def test_bias(ops, dev, M, N):
     assert relerr(db.cpu().numpy(), rb) < 1e-5
 
 
-@pytest.mark.parametrize("Tn,V", [(16384, 65), (64, 8192), (4, 2), (3, 50257)])
+@pytest.mark.parametrize("Tn,V", [(16384, 65), (64, 8192), (4, 2), (3, 50257), (33, 2052), (17, 16384),
+                                  (9, 1028)])
 def test_cross_entropy(ops, dev, Tn, V):
     rng = np.random.default_rng(Tn + V)
     x = (2 * rng.standard_normal((Tn, V))).astype(np.float32)
