@@ -515,11 +515,16 @@ def main():
                          "contraction costs more than the 16 bytes per element of saved statistics")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-rows", action="store_true", help="skip the LayerNorm/bias/CE bandwidth pass")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="override the configuration's sequences per GPU (small profiling cases)")
     args = ap.parse_args()
 
     if args.config in DECODER_CONFIGS:
         return main_decoder(args)
     B, T, d, dt, desc = CONFIGS[args.config]
+    if args.batch:
+        B = args.batch
+        desc = desc.replace(f"B={CONFIGS[args.config][0]}", f"B={B}")
     stats = args.backward == "stats" or (args.backward == "auto" and T >= 1024)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
