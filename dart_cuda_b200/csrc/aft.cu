@@ -521,7 +521,9 @@ __global__ void __launch_bounds__(256) bwd_stats_kernel(const Params p)
 #pragma unroll
         for (int j = 0; j < 16; ++j) r[j] = inv[j] = 0.f;
     }
-    epi16_grads<IO, E>(p, b, t, d0, r, inv);
+    EpiPre none;
+    none.ok = false;
+    epi16_grads<IO, E>(p, b, t, d0, r, inv, none);
 }
 
 // ------------------------------------------------------------ host side

@@ -200,9 +200,41 @@ __device__ __forceinline__ float fast_sigmoid(float q) { return __fdividef(1.0f,
 // `full` = the row and all 16 columns are inside the logical tensor and the
 // tensors allow 32-byte vector access; otherwise an element-wise path runs.
 
-template <class IO>
+// The epilogue's element-wise inputs (Q; Q and dZ; K and V) for bf16 tensors,
+// loaded before the accumulator is ready so their latency overlaps the main
+// loop.  ok = false: the epilogue loads them itself (other types, partial
+// columns or rows, accumulate mode).  Enabled for the forward only: for the
+// two-input epilogues the held registers spill under the 96-register budget
+// of 576 threads and measured slower.
+struct EpiPre {
+    uint32_t a[8], b[8];
+    bool ok;
+};
+
+template <int MODE, class IO>
+__device__ __forceinline__ void epi_prefetch(const Params &p, int bb, int r, int c0, EpiPre &pf)
+{
+    pf.ok = false;
+    if constexpr (sizeof(IO) == 2 && MODE == FWD) {
+        const int rows = MODE == HGRAD ? p.Tk : p.Tq;
+        if (!p.vec_io || p.accumulate || c0 + 16 > p.D || r >= rows) return;
+        const size_t o = ((size_t)bb * rows + r) * p.ldi + c0;
+        if (MODE == HGRAD) {
+            ld32B_nc((const IO *)p.K + o, pf.a);
+            ld32B_nc((const IO *)p.V + o, pf.b);
+        } else {
+            ld32B_nc((const IO *)p.Q + o, pf.a);
+            if (MODE == BWD1)
+                ld32B_nc((const IO *)p.dZ + ((size_t)bb * rows + r) * p.ldo + c0, pf.b);
+        }
+        pf.ok = true;
+    }
+}
+
+template <class IO, class E>
 __device__ __forceinline__ void epi16_fwd(const Params &p, int b, int t, int d0,
-                                          const float (&num)[16], const float (&den)[16])
+                                          const float (&num)[16], const float (&den)[16],
+                                          const EpiPre &pf)
 {
     if (t >= p.Tq) return;
     if (p.Rs) {  // r and 1/den for the backward, exactly as epi16_bwd1 forms them
@@ -220,7 +252,10 @@ __device__ __forceinline__ void epi16_fwd(const Params &p, int b, int t, int d0,
     const size_t o = row * p.ldi + d0, oz = row * p.ldo + d0;
     if (p.vec_io && d0 + 16 <= p.D) {
         float q[16], z[16];
-        ld16g((const IO *)p.Q + o, q);
+        if (pf.ok)
+            words_to_bf16(pf.a, q);
+        else
+            ld16g((const IO *)p.Q + o, q);
 #pragma unroll
         for (int j = 0; j < 16; ++j) z[j] = __fdividef(num[j], den[j] * (1.0f + __expf(-q[j])));
         st16((IO *)p.Z + oz, z);
@@ -238,7 +273,8 @@ __device__ __forceinline__ void epi16_fwd(const Params &p, int b, int t, int d0,
 // forward's r = num/den and inv = 1/den of 16 columns of row t.
 template <class IO, class E>
 __device__ __forceinline__ void epi16_grads(const Params &p, int b, int t, int d0,
-                                            const float (&rr)[16], const float (&iv)[16])
+                                            const float (&rr)[16], const float (&iv)[16],
+                                            const EpiPre &pf)
 {
     float g[16], n[16];
     const bool trow = t < p.Tq;
@@ -246,8 +282,13 @@ __device__ __forceinline__ void epi16_grads(const Params &p, int b, int t, int d
     const size_t o = row * p.ldi + d0, oz = row * p.ldo + d0;
     if (trow && p.vec_io && d0 + 16 <= p.D) {
         float q[16], dz[16], dq[16];
-        ld16g((const IO *)p.Q + o, q);
-        ld16g((const IO *)p.dZ + oz, dz);
+        if (pf.ok) {
+            words_to_bf16(pf.a, q);
+            words_to_bf16(pf.b, dz);
+        } else {
+            ld16g((const IO *)p.Q + o, q);
+            ld16g((const IO *)p.dZ + oz, dz);
+        }
         if (p.accumulate) ld16((const IO *)p.dQ + o, dq);
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
@@ -298,7 +339,8 @@ __device__ __forceinline__ void epi16_grads(const Params &p, int b, int t, int d
 
 template <class IO, class E>
 __device__ __forceinline__ void epi16_bwd1(const Params &p, int b, int t, int d0,
-                                           const float (&num)[16], const float (&den)[16])
+                                           const float (&num)[16], const float (&den)[16],
+                                           const EpiPre &pf)
 {
     float r[16], inv[16];
 #pragma unroll
@@ -306,20 +348,26 @@ __device__ __forceinline__ void epi16_bwd1(const Params &p, int b, int t, int d0
         inv[j] = __fdividef(1.0f, den[j]);
         r[j] = num[j] * inv[j];
     }
-    epi16_grads<IO, E>(p, b, t, d0, r, inv);
+    epi16_grads<IO, E>(p, b, t, d0, r, inv, pf);
 }
 
 template <class IO>
 __device__ __forceinline__ void epi16_hgrad(const Params &p, int b, int i, int d0,
-                                            const float (&h1)[16], const float (&h2)[16])
+                                            const float (&h1)[16], const float (&h2)[16],
+                                            const EpiPre &pf)
 {
     if (i >= p.Tk) return;
     const size_t o = ((size_t)b * p.Tk + i) * p.ldi + d0;
     const float *cb = p.c + (size_t)b * p.dp + d0;
     if (p.vec_io && d0 + 16 <= p.D) {
         float k[16], v[16], c[16], dk[16], dv[16];
-        ld16g((const IO *)p.K + o, k);
-        ld16g((const IO *)p.V + o, v);
+        if (pf.ok) {
+            words_to_bf16(pf.a, k);
+            words_to_bf16(pf.b, v);
+        } else {
+            ld16g((const IO *)p.K + o, k);
+            ld16g((const IO *)p.V + o, v);
+        }
         ld16g(cb, c);
         if (p.accumulate) {
             ld16((const IO *)p.dK + o, dk);
@@ -732,6 +780,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             if (tile < 0) break;
             const Tile tl = decode_tile<MODE, C::BKe, P>(p, tile);
             const uint32_t buf = j & 1, use = j >> 1;
+            // each warp owns a slice of WN/4 columns (32, or 64 for the dW tile)
+            constexpr int SLICE = C::WN / 4;
+            // t (FWD, BWD1, WGRAD) or i (HGRAD): this CTA's 128 rows of the tile
+            const int r = (P ? 2 * tl.mrow + (int)rank : tl.mrow) * BM + row;
+            const int cbase = tl.ncol * C::WN + slice * SLICE;  // d, or i for WGRAD
+            // element-wise inputs requested while the main loop still runs
+            EpiPre pf[2];
+            if constexpr (MODE == FWD) {
+#pragma unroll
+                for (int sb = 0; sb < 2; ++sb) epi_prefetch<MODE, IO>(p, tl.b, r, cbase + sb * 16, pf[sb]);
+            }
             // warp-uniform, because the TMEM loads below are warp-collective
             const bool ok = __all_sync(0xffffffffu, mbar_wait<P>(smem_u32(&accf[buf]), use & 1,
                                                                  abort_flag, p.status,
@@ -739,26 +798,37 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             if (!ok) break;
             tc_fence_after();
             if (threadIdx.x == 0) trace_at(p, j, 3, global_timer());
-            // each warp owns a slice of WN/4 columns (32, or 64 for the dW tile)
-            constexpr int SLICE = C::WN / 4;
             const uint32_t lane_addr =
                 tmem + buf * C::ACC_COLS + ((uint32_t)(quad * 32) << 16) + slice * SLICE;
-            // t (FWD, BWD1, WGRAD) or i (HGRAD): this CTA's 128 rows of the tile
-            const int r = (P ? 2 * tl.mrow + (int)rank : tl.mrow) * BM + row;
+            if constexpr (C::W) {
 #pragma unroll 1
-            for (int sb = 0; sb < SLICE / 16; ++sb) {
-                float v1[16], v2[16];
-                tmem_ld16(lane_addr + sb * 16, v1);
-                if (!C::W) tmem_ld16(lane_addr + BN + sb * 16, v2);
-                const int c0 = tl.ncol * C::WN + slice * SLICE + sb * 16;  // d, or i for WGRAD
-                if (MODE == FWD)
-                    epi16_fwd<IO>(p, tl.b, r, c0, v1, v2);
-                else if (MODE == BWD1)
-                    epi16_bwd1<IO, E>(p, tl.b, r, c0, v1, v2);
-                else if (MODE == HGRAD)
-                    epi16_hgrad<IO>(p, tl.b, r, c0, v1, v2);
-                else
-                    epi16_wgrad(p, r, c0, v1);
+                for (int sb = 0; sb < SLICE / 16; ++sb) {
+                    float v1[16];
+                    tmem_ld16(lane_addr + sb * 16, v1);
+                    epi16_wgrad(p, r, cbase + sb * 16, v1);
+                }
+            } else if constexpr (MODE == FWD) {
+#pragma unroll
+                for (int sb = 0; sb < 2; ++sb) {
+                    float v1[16], v2[16];
+                    tmem_ld16(lane_addr + sb * 16, v1);
+                    tmem_ld16(lane_addr + BN + sb * 16, v2);
+                    epi16_fwd<IO, E>(p, tl.b, r, cbase + sb * 16, v1, v2, pf[sb]);
+                }
+            } else {
+                EpiPre none;
+                none.ok = false;
+#pragma unroll 1
+                for (int sb = 0; sb < 2; ++sb) {
+                    float v1[16], v2[16];
+                    tmem_ld16(lane_addr + sb * 16, v1);
+                    tmem_ld16(lane_addr + BN + sb * 16, v2);
+                    const int c0 = cbase + sb * 16;
+                    if (MODE == BWD1)
+                        epi16_bwd1<IO, E>(p, tl.b, r, c0, v1, v2, none);
+                    else
+                        epi16_hgrad<IO>(p, tl.b, r, c0, v1, v2, none);
+                }
             }
             tc_fence_before();
             __syncwarp();
