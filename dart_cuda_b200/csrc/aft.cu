@@ -350,6 +350,8 @@ __global__ void __launch_bounds__(256)
                    int D, int ldk, int dp, int ncb, int nsplit, int rows_per_split, int vec,
                    float *__restrict__ cpart)
 {
+    grid_dep_wait();  // launched early (programmatic dependent launch)
+    grid_dep_launch();
     const int bid = blockIdx.x;
     const int Tqp = gridDim.x - ncb * nsplit * B;
     if (bid < Tqp) {
@@ -374,6 +376,8 @@ __global__ void __launch_bounds__(256)
                   int Tk, int D, int ldk, int Tkp, int dp, int rows_per_block, int vec,
                   E *__restrict__ PV, E *__restrict__ PE)
 {
+    grid_dep_wait();  // launched early (programmatic dependent launch)
+    grid_dep_launch();
     __shared__ __align__(16) float cs[128];
     const int b = blockIdx.z;
     const int dblk = blockIdx.x * 128;
@@ -505,6 +509,8 @@ namespace aft {
 template <class IO, class E>
 __global__ void __launch_bounds__(256) bwd_stats_kernel(const Params p)
 {
+    grid_dep_wait();  // launched early (programmatic dependent launch)
+    grid_dep_launch();
     const int groups = p.dp / 16;
     const size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= (size_t)p.B * p.Tqp * groups) return;
@@ -646,9 +652,9 @@ static int run_prep(const Layout &L, const IO *K, const IO *V, const float *w, i
         KernelTimer kt("aft_prep_w_colmax", st);
         const int ncb = (L.D + 255) / 256;
         const int grid = L.Tqp + ncb * L.nsplit * L.B;
-        prep_wc_kernel<IO, E><<<grid, 256, 0, st>>>(w, ldw, L.Tq, L.Tk, L.Tkp, causal, m, Ap, K,
-                                                    L.B, L.D, L.ldi, L.dp, ncb, L.nsplit,
-                                                    L.rows_per_split, vec, cpart);
+        DC_CUDA_TRY(launch_pdl(prep_wc_kernel<IO, E>, dim3(grid), dim3(256), 0, st, 1, w, ldw, L.Tq,
+                               L.Tk, L.Tkp, causal, m, Ap, K, L.B, L.D, L.ldi, L.dp, ncb,
+                               L.nsplit, L.rows_per_split, vec, cpart));
     }
     {
         KernelTimer kt("aft_prep_p", st);
@@ -658,9 +664,9 @@ static int run_prep(const Layout &L, const IO *K, const IO *V, const float *w, i
         rsplit = std::min(rsplit, std::max(1, L.Tkp / 16));
         const int rows_per_block = (L.Tkp + rsplit - 1) / rsplit;
         rsplit = (L.Tkp + rows_per_block - 1) / rows_per_block;
-        prep_p_kernel<IO, E><<<dim3(ndb, rsplit, L.B), 256, 0, st>>>(
-            K, V, cpart, L.nsplit, c, L.B, L.Tk, L.D, L.ldi, L.Tkp, L.dp, rows_per_block, vec, PV,
-            PE);
+        DC_CUDA_TRY(launch_pdl(prep_p_kernel<IO, E>, dim3(ndb, rsplit, L.B), dim3(256), 0, st, 1,
+                               K, V, cpart, L.nsplit, c, L.B, L.Tk, L.D, L.ldi, L.Tkp, L.dp,
+                               rows_per_block, vec, PV, PE));
     }
     DC_CUDA_TRY(cudaGetLastError());
     return DC_OK;
@@ -791,11 +797,11 @@ static int launch_tc(Params p, const Layout &L, char *ws, cudaStream_t st)
         max_clusters[dev] = std::max(1, n);
     }
     const int workers = P ? max_clusters[dev] : sm_count();
-    cfg.gridDim = dim3((P ? 2 : 1) * std::max(1, std::min(p.n_tiles, workers)));
+    const dim3 grid((P ? 2 : 1) * std::max(1, std::min(p.n_tiles, workers)));
     {
         KernelTimer kt(names[MODE], st);
-        DC_CUDA_TRY(cudaLaunchKernelEx(&cfg, aft_tc_kernel<MODE, E, IO, P>, p, mA, mB1, mB2, mB3,
-                                       mB4, mA2, mA3, mA4));
+        DC_CUDA_TRY(launch_pdl(aft_tc_kernel<MODE, E, IO, P>, grid, dim3(kTcThreads), C::SMEM_BYTES,
+                               st, P ? 2 : 1, p, mA, mB1, mB2, mB3, mB4, mA2, mA3, mA4));
     }
     DC_CUDA_TRY(cudaGetLastError());
     return DC_OK;
@@ -926,7 +932,8 @@ static int bwd_impl(const void *Q, const void *K, const void *V, const float *w,
     if ((flags & DC_AFT_WS_VALID) && saves_stats(flags)) {
         KernelTimer kt("aft_bwd_from_stats", st);
         const size_t n = (size_t)L.B * L.Tqp * (L.dp / 16);
-        bwd_stats_kernel<IO, E><<<(unsigned)((n + 255) / 256), 256, 0, st>>>(p);
+        DC_CUDA_TRY(launch_pdl(bwd_stats_kernel<IO, E>, dim3((unsigned)((n + 255) / 256)), dim3(256),
+                               0, st, 1, p));
         DC_CUDA_TRY(cudaGetLastError());
     } else {
         DC_TRY((launch<BWD1, E, IO>(p, L, ws, st, flags)));

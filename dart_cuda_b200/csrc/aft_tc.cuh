@@ -596,6 +596,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     else
         __syncthreads();
     tc_fence_after();
+    // the set-up above overlapped the previous kernel's tail; its results are
+    // visible from here on (programmatic dependent launch)
+    grid_dep_wait();
+    grid_dep_launch();
     const uint32_t tmem = *tmem_slot;
     const int ntiles = p.n_tiles;
     auto ld2 = [&](uint32_t dst, const CUtensorMap *m, uint32_t bar, int c0, int c1) {

@@ -256,6 +256,17 @@ __host__ __device__ constexpr uint32_t umma_idesc(uint32_t fmt, uint32_t M, uint
            ((N >> 3) << 17) | ((M >> 4) << 24);
 }
 
+// ------------------------------------------------- programmatic dependent launch
+// A kernel launched with programmatic stream serialisation may start while
+// the previous kernel of its stream is still finishing; it must pass
+// grid_dep_wait() before touching memory that kernel writes or reads.
+// grid_dep_launch() lets the next kernel of the stream be scheduled early.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch()
+{
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ------------------------------------------------- CTA pairs (cta_group::2)
 // Two CTAs of a cluster share one M = 256 MMA: each holds half of A (its
 // 128 rows) and half of B (its N/2) in shared memory and its 128 rows of the
