@@ -9,18 +9,21 @@
 //   HGRAD     : acc[i, d]  = sum_t A'[t,i] G[t,d]    and   sum_t A'[t,i] N[t,d]
 //   WGRAD     : acc[t, i]  = sum_{b,d} (G PV^T + N PE^T + G_lo PV^T + N_lo PE^T)
 //
-// Warp roles (576 threads): warps 0-15 epilogue (warp w reads TMEM lanes
-// 32*(w%4).. and the 32-column slice w/4), warp 16 TMA producer, warp 17
-// TMEM allocator + MMA issuer.  Sixteen epilogue warps (four per SM
-// sub-partition) hide the latency of the element-wise epilogue.  Each CTA
-// walks its tiles (sched_tile); the accumulator is double-buffered in TMEM
-// so the epilogue of one tile overlaps the main loop of the next.
+// Warp roles (448 threads): warps 0-11 epilogue (warp w reads TMEM lanes
+// 32*(w%4).. and, of each row's 16-column sub-blocks, every third one starting
+// at w/4), warp 12 TMA producer, warp 13 TMEM allocator + MMA issuer.  Each
+// CTA walks its tiles (sched_tile); the accumulator is double-buffered in
+// TMEM so the epilogue of one tile overlaps the main loop of the next.
 #pragma once
 
 namespace dc {
 namespace aft {
 
-constexpr int kEpiWarps = 16;
+// Epilogue warps, a multiple of 4 (a quarter per TMEM lane quadrant).  Twelve
+// give 14 warps a CTA, at most 4 per SM sub-partition, so each thread has 128
+// registers; sixteen (5 warps on some sub-partitions, 96 registers) measured
+// slower in the backward epilogues.
+constexpr int kEpiWarps = 12;
 constexpr int kTcThreads = (kEpiWarps + 2) * 32;
 constexpr int kSmemBudget = 227 * 1024;
 #ifndef DC_WGRAD_KROW
@@ -203,9 +206,9 @@ __device__ __forceinline__ float fast_sigmoid(float q) { return __fdividef(1.0f,
 // The epilogue's element-wise inputs (Q; Q and dZ; K and V) for bf16 tensors,
 // loaded before the accumulator is ready so their latency overlaps the main
 // loop.  ok = false: the epilogue loads them itself (other types, partial
-// columns or rows, accumulate mode).  Enabled for the forward only: for the
-// two-input epilogues the held registers spill under the 96-register budget
-// of 576 threads and measured slower.
+// columns or rows, accumulate mode).  Used by the forward only: holding the
+// two inputs of the backward epilogues this way spills under the 128-register
+// budget and measured slower.
 struct EpiPre {
     uint32_t a[8], b[8];
     bool ok;
@@ -775,25 +778,32 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
         }
     } else {
-        // ------------------------------------------------ epilogue (warps 0-15)
-        const int quad = warp & 3;           // TMEM lanes 32*quad .. 32*quad+31
-        const int slice = warp >> 2;         // columns slice*32 .. slice*32+31
+        // ------------------------------------------------ epilogue warps
+        // warp w reads TMEM lanes 32*(w%4).. (its quadrant's rows) and, of the
+        // row's 16-column sub-blocks, every QW-th starting at w/4
+        constexpr int QW = kEpiWarps / 4;          // warps per lane quadrant
+        constexpr int NSB = C::WN / 16;            // 16-column sub-blocks per row
+        constexpr int MAXK = (NSB + QW - 1) / QW;  // sub-blocks per warp, at most
+        const int quad = warp & 3;
+        const int slice = warp >> 2;
         const int row = quad * 32 + lane;
         for (uint32_t j = 0;; ++j) {
             const int tile = sched_tile<P>(j, ntiles);
             if (tile < 0) break;
             const Tile tl = decode_tile<MODE, C::BKe, P>(p, tile);
             const uint32_t buf = j & 1, use = j >> 1;
-            // each warp owns a slice of WN/4 columns (32, or 64 for the dW tile)
-            constexpr int SLICE = C::WN / 4;
             // t (FWD, BWD1, WGRAD) or i (HGRAD): this CTA's 128 rows of the tile
             const int r = (P ? 2 * tl.mrow + (int)rank : tl.mrow) * BM + row;
-            const int cbase = tl.ncol * C::WN + slice * SLICE;  // d, or i for WGRAD
+            const int cb0 = tl.ncol * C::WN;  // first column (d, or i for WGRAD)
             // element-wise inputs requested while the main loop still runs
-            EpiPre pf[2];
-            if constexpr (MODE == FWD) {
+            EpiPre pf[C::W ? 1 : MAXK];
+            if constexpr (!C::W) {
 #pragma unroll
-                for (int sb = 0; sb < 2; ++sb) epi_prefetch<MODE, IO>(p, tl.b, r, cbase + sb * 16, pf[sb]);
+                for (int k = 0; k < MAXK; ++k) {
+                    const int sb = slice + k * QW;
+                    pf[k].ok = false;
+                    if (sb < NSB) epi_prefetch<MODE, IO>(p, tl.b, r, cb0 + sb * 16, pf[k]);
+                }
             }
             // warp-uniform, because the TMEM loads below are warp-collective
             const bool ok = __all_sync(0xffffffffu, mbar_wait<P>(smem_u32(&accf[buf]), use & 1,
@@ -802,36 +812,29 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             if (!ok) break;
             tc_fence_after();
             if (threadIdx.x == 0) trace_at(p, j, 3, global_timer());
-            const uint32_t lane_addr =
-                tmem + buf * C::ACC_COLS + ((uint32_t)(quad * 32) << 16) + slice * SLICE;
+            const uint32_t lane_addr = tmem + buf * C::ACC_COLS + ((uint32_t)(quad * 32) << 16);
             if constexpr (C::W) {
 #pragma unroll 1
-                for (int sb = 0; sb < SLICE / 16; ++sb) {
+                for (int sb = slice; sb < NSB; sb += QW) {
                     float v1[16];
                     tmem_ld16(lane_addr + sb * 16, v1);
-                    epi16_wgrad(p, r, cbase + sb * 16, v1);
-                }
-            } else if constexpr (MODE == FWD) {
-#pragma unroll
-                for (int sb = 0; sb < 2; ++sb) {
-                    float v1[16], v2[16];
-                    tmem_ld16(lane_addr + sb * 16, v1);
-                    tmem_ld16(lane_addr + BN + sb * 16, v2);
-                    epi16_fwd<IO, E>(p, tl.b, r, cbase + sb * 16, v1, v2, pf[sb]);
+                    epi16_wgrad(p, r, cb0 + sb * 16, v1);
                 }
             } else {
-                EpiPre none;
-                none.ok = false;
-#pragma unroll 1
-                for (int sb = 0; sb < 2; ++sb) {
+#pragma unroll
+                for (int k = 0; k < MAXK; ++k) {
+                    const int sb = slice + k * QW;  // warp-uniform
+                    if (sb >= NSB) break;
                     float v1[16], v2[16];
                     tmem_ld16(lane_addr + sb * 16, v1);
                     tmem_ld16(lane_addr + BN + sb * 16, v2);
-                    const int c0 = cbase + sb * 16;
-                    if (MODE == BWD1)
-                        epi16_bwd1<IO, E>(p, tl.b, r, c0, v1, v2, none);
+                    const int c0 = cb0 + sb * 16;
+                    if (MODE == FWD)
+                        epi16_fwd<IO, E>(p, tl.b, r, c0, v1, v2, pf[k]);
+                    else if (MODE == BWD1)
+                        epi16_bwd1<IO, E>(p, tl.b, r, c0, v1, v2, pf[k]);
                     else
-                        epi16_hgrad<IO>(p, tl.b, r, c0, v1, v2, none);
+                        epi16_hgrad<IO>(p, tl.b, r, c0, v1, v2, pf[k]);
                 }
             }
             tc_fence_before();
