@@ -514,6 +514,10 @@ def main():
                          "repeats the forward contraction; auto: stats from T >= 1024, where the "
                          "contraction costs more than the 16 bytes per element of saved statistics")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
+    ap.add_argument("--no-overlap", action="store_true",
+                    help="N>1: all-reduce dW after the whole backward instead of beside dK/dV")
+    ap.add_argument("--spare-sms", type=int, default=32,
+                    help="N>1: SMs the dK/dV kernel leaves free for the overlapped all-reduce")
     ap.add_argument("--no-rows", action="store_true", help="skip the LayerNorm/bias/CE bandwidth pass")
     ap.add_argument("--batch", type=int, default=0,
                     help="override the configuration's sequences per GPU (small profiling cases)")
@@ -583,19 +587,49 @@ def main():
     ws = ops.AftWorkspace(B, T, T, d, tdt, flags=1, device=dev, save_stats=stats)
     flush = torch.empty(256 * 1024 * 1024 // 4, device=dev)
 
+    grads = (dQ, dK, dV, dW)
+    overlap = dist is not None and not args.no_overlap
+    config["dw_allreduce"] = ("none" if dist is None else "serial" if not overlap
+                              else f"beside dK/dV ({args.spare_sms} SMs left free)")
+
     def compute():
         ops.aft_fwd(Q, K_, V, w, causal=True, out=Z, workspace=ws)
-        ops.aft_bwd(Q, K_, V, w, dZ, causal=True, grads=(dQ, dK, dV, dW), workspace=ws, ws_valid=True)
+        ops.aft_bwd(Q, K_, V, w, dZ, causal=True, grads=grads, workspace=ws, ws_valid=True)
 
-    graph = None
+    # N > 1: forward, dQ and dW; then dW's all-reduce on a side stream while
+    # the dK/dV contraction runs with a few SMs left to the collective
+    def part_a():
+        ops.aft_fwd(Q, K_, V, w, causal=True, out=Z, workspace=ws)
+        ops.aft_bwd(Q, K_, V, w, dZ, causal=True, grads=grads, workspace=ws, ws_valid=True,
+                    part="dw")
+
+    def part_b():
+        ops.aft_bwd(Q, K_, V, w, dZ, causal=True, grads=grads, workspace=ws, ws_valid=True,
+                    part="dkdv", spare_sms=args.spare_sms)
+
+    graphs = None
+    comm = torch.cuda.Stream(device=dev)
+    dw_ready = torch.cuda.Event()
+
+    def run(i, fn):
+        if graphs is not None:
+            graphs[i].replay()
+        else:
+            fn()
 
     def step():
-        if graph is not None:
-            graph.replay()
-        else:
-            compute()
-        if dist is not None:
+        if not overlap:
+            run(0, compute)
+            if dist is not None:
+                dist.all_reduce(dW)
+            return
+        run(0, part_a)
+        dw_ready.record()
+        with torch.cuda.stream(comm):
+            comm.wait_event(dw_ready)
             dist.all_reduce(dW)
+        run(1, part_b)
+        torch.cuda.current_stream().wait_stream(comm)
 
     def barrier():
         if dist is not None:
@@ -606,10 +640,16 @@ def main():
         step()
     barrier()
     if not args.no_graph:
-        # the library's launches of one fwd+bwd, replayed as one CUDA graph
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            compute()
+        # the library's launches of one fwd+bwd replayed as CUDA graphs (two
+        # when the all-reduce runs between them)
+        parts = (part_a, part_b) if overlap else (compute,)
+        captured = []
+        for fn in parts:
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr):
+                fn()
+            captured.append(gr)
+        graphs = captured
         for _ in range(2):
             step()
         barrier()
@@ -639,12 +679,12 @@ def main():
 
     # ---- per-kernel timing pass (same steps, events around every launch)
     ops.profile_enable(True)  # eager launches: the events bracket each kernel
+    saved, graphs = graphs, None
     for i in range(args.steps):
         flush.zero_()
-        compute()
-        if dist is not None:
-            dist.all_reduce(dW)
+        step()
     torch.cuda.synchronize()
+    graphs = saved
     prof = ops.profile_read()
     ops.profile_enable(False)
     launches = sum(c for _, c in prof.values()) / args.steps

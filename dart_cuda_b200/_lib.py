@@ -22,6 +22,14 @@ DC_AFT_WS_VALID = 0x4
 DC_AFT_SIMT = 0x8
 DC_AFT_COMPUTE_BF16 = 0x10
 DC_AFT_SAVE_STATS = 0x20
+DC_AFT_BWD_NO_DKDV = 0x40
+DC_AFT_BWD_DKDV = 0x80
+
+
+def DC_AFT_SPARE_SMS(n):
+    return (n & 0xFF) << 16
+
+
 DC_GEMM_TRANS_A = 0x1
 DC_GEMM_TRANS_B = 0x2
 DC_GEMM_BIAS = 0x4

@@ -87,6 +87,7 @@ struct Params {
     int splits;       // WGRAD: split-K factor
     int vec_io;       // user tensors allow 32-byte vector access along D
     int vec_w;        // w / dW allow 32-byte vector access along a row
+    int spare_sms;    // host only: SMs the persistent launch leaves free
     const void *Q, *K, *V, *dZ;
     void *Z, *dQ, *dK, *dV;
     float *dW;
@@ -796,7 +797,8 @@ static int launch_tc(Params p, const Layout &L, char *ws, cudaStream_t st)
         DC_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, aft_tc_kernel<MODE, E, IO, P>, &cfg));
         max_clusters[dev] = std::max(1, n);
     }
-    const int workers = P ? max_clusters[dev] : sm_count();
+    const int workers = P ? std::max(1, max_clusters[dev] - (p.spare_sms + 1) / 2)
+                          : std::max(1, sm_count() - p.spare_sms);
     const dim3 grid((P ? 2 : 1) * std::max(1, std::min(p.n_tiles, workers)));
     {
         KernelTimer kt(names[MODE], st);
@@ -872,6 +874,7 @@ static Params make_params(const Layout &L, char *ws, int flags)
         p.Rs = reinterpret_cast<float *>(ws + L.off_rs);
         p.Is = reinterpret_cast<float *>(ws + L.off_is);
     }
+    p.spare_sms = (flags >> 16) & 0xff;
     p.status = device_status_word();
     return p;
 }
@@ -912,10 +915,6 @@ static int bwd_impl(const void *Q, const void *K, const void *V, const float *w,
                     int flags, char *ws, cudaStream_t st)
 {
     const int causal = (flags & DC_AFT_CAUSAL) ? 1 : 0;
-    if (!(flags & DC_AFT_WS_VALID))
-        DC_TRY(run_prep<IO, E>(L, (const IO *)K, (const IO *)V, w, ldw, causal, ws, st));
-    if (!(flags & DC_AFT_ACCUMULATE))
-        DC_CUDA_TRY(cudaMemset2DAsync(dW, (size_t)ldw * 4, 0, (size_t)L.Tk * 4, L.Tq, st));
     Params p = make_params(L, ws, flags);
     p.Q = Q;
     p.K = K;
@@ -929,41 +928,52 @@ static int bwd_impl(const void *Q, const void *K, const void *V, const float *w,
     p.ldw = ldw;
     p.vec_io = vec_ok<IO>(L, {Q, K, V, dZ, dQ, dK, dV});
     p.vec_w = (ldw % 8 == 0) && ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(dW)) & 31) == 0;
-    if ((flags & DC_AFT_WS_VALID) && saves_stats(flags)) {
-        KernelTimer kt("aft_bwd_from_stats", st);
-        const size_t n = (size_t)L.B * L.Tqp * (L.dp / 16);
-        DC_CUDA_TRY(launch_pdl(bwd_stats_kernel<IO, E>, dim3((unsigned)((n + 255) / 256)), dim3(256),
-                               0, st, 1, p));
-        DC_CUDA_TRY(cudaGetLastError());
-    } else {
-        DC_TRY((launch<BWD1, E, IO>(p, L, ws, st, flags)));
-    }
-    DC_TRY((launch<HGRAD, E, IO>(p, L, ws, st, flags)));
-    // split-K factor for dW: pick the split count whose tiles fill the
-    // persistent workers (CTAs, or CTA pairs) in the least time, waves x time
-    // per tile, where a tile costs at least its epilogue (the scaled atomic
-    // adds of a 128 x 256 block per CTA: measured at about 4 K steps of a
-    // single CTA's main loop; for pairs, whose epilogues contend for the same
-    // dW lines, splitting below ~40 steps measured slower), so splitting
-    // finer than that only adds atomics
-    p.kpb = L.dp / TcCfg<WGRAD, E>::BKe;
-    const int tiles = wgrad_tiles(L, causal);
-    const int ktot = L.B * p.kpb;
-    const bool pairs = use_pairs(L);
-    const int workers = pairs ? sm_count() / 2 : sm_count();
-    const double kEpiSteps = pairs ? 40.0 : 4.0;
-    int best = 1;
-    double best_cost = 1e30;
-    for (int sp = 1; sp <= std::max(1, ktot / 8); ++sp) {
-        const int waves = (tiles * sp + workers - 1) / workers;
-        const double cost = waves * std::max((double)ktot / sp, kEpiSteps);
-        if (cost < 0.97 * best_cost) {  // more splits only for a clear gain (atomics)
-            best_cost = cost;
-            best = sp;
+    // dQ, g and n, then dW (which needs only g, n and the prep panels), then
+    // dK and dV: a caller that splits the call can reduce dW across ranks
+    // while the last contraction runs
+    if (!(flags & DC_AFT_BWD_DKDV)) {
+        if (!(flags & DC_AFT_WS_VALID))
+            DC_TRY(run_prep<IO, E>(L, (const IO *)K, (const IO *)V, w, ldw, causal, ws, st));
+        if (!(flags & DC_AFT_ACCUMULATE))
+            DC_CUDA_TRY(cudaMemset2DAsync(dW, (size_t)ldw * 4, 0, (size_t)L.Tk * 4, L.Tq, st));
+        if ((flags & DC_AFT_WS_VALID) && saves_stats(flags)) {
+            KernelTimer kt("aft_bwd_from_stats", st);
+            const size_t n = (size_t)L.B * L.Tqp * (L.dp / 16);
+            DC_CUDA_TRY(launch_pdl(bwd_stats_kernel<IO, E>, dim3((unsigned)((n + 255) / 256)),
+                                   dim3(256), 0, st, 1, p));
+            DC_CUDA_TRY(cudaGetLastError());
+        } else {
+            DC_TRY((launch<BWD1, E, IO>(p, L, ws, st, flags)));
         }
+        // split-K factor for dW: pick the split count whose tiles fill the
+        // persistent workers (CTAs, or CTA pairs) in the least time, waves x
+        // time per tile, where a tile costs at least its epilogue (the scaled
+        // atomic adds of a 128 x 256 block per CTA: measured at about 4 K
+        // steps of a single CTA's main loop; for pairs, whose epilogues
+        // contend for the same dW lines, splitting below ~40 steps measured
+        // slower), so splitting finer than that only adds atomics
+        Params pw = p;
+        pw.kpb = L.dp / TcCfg<WGRAD, E>::BKe;
+        const int tiles = wgrad_tiles(L, causal);
+        const int ktot = L.B * pw.kpb;
+        const bool pairs = use_pairs(L);
+        const int workers = pairs ? sm_count() / 2 : sm_count();
+        const double kEpiSteps = pairs ? 40.0 : 4.0;
+        int best = 1;
+        double best_cost = 1e30;
+        for (int sp = 1; sp <= std::max(1, ktot / 8); ++sp) {
+            const int waves = (tiles * sp + workers - 1) / workers;
+            const double cost = waves * std::max((double)ktot / sp, kEpiSteps);
+            if (cost < 0.97 * best_cost) {  // more splits only for a clear gain (atomics)
+                best_cost = cost;
+                best = sp;
+            }
+        }
+        pw.splits = best;
+        DC_TRY((launch<WGRAD, E, IO>(pw, L, ws, st, flags)));
     }
-    p.splits = best;
-    return launch<WGRAD, E, IO>(p, L, ws, st, flags);
+    if (!(flags & DC_AFT_BWD_NO_DKDV)) DC_TRY((launch<HGRAD, E, IO>(p, L, ws, st, flags)));
+    return DC_OK;
 }
 
 }  // namespace aft
@@ -1040,7 +1050,13 @@ int dc_aft_bwd_strided(const void *Q, const void *K, const void *V, const float 
     clear_error();
     DC_TRY(validate(Q, K, V, w, ldw, B, Tq, Tk, D, dtype, flags));
     if ((long long)B * Tq * D == 0) return DC_OK;
-    if (!dZ || !dQ || !dK || !dV || !dW) return fail(DC_ERR_INVALID, "null gradient pointer");
+    const bool part1 = !(flags & DC_AFT_BWD_DKDV), part2 = !(flags & DC_AFT_BWD_NO_DKDV);
+    if (!part1 && !part2)
+        return fail(DC_ERR_INVALID, "DC_AFT_BWD_NO_DKDV and DC_AFT_BWD_DKDV together");
+    if (!part1 && !(flags & DC_AFT_WS_VALID))
+        return fail(DC_ERR_INVALID, "DC_AFT_BWD_DKDV needs DC_AFT_WS_VALID (g, n of an earlier call)");
+    if ((part1 && (!dZ || !dQ || !dW)) || (part2 && (!dK || !dV)))
+        return fail(DC_ERR_INVALID, "null gradient pointer");
     if (ldi < D || ldo < D) return fail(DC_ERR_INVALID, "row strides (%d, %d) < D (%d)", ldi, ldo, D);
     cudaStream_t st = as_stream(stream);
     Layout L = make_layout(B, Tq, Tk, D, dtype, flags);

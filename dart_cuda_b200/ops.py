@@ -16,10 +16,10 @@ from ctypes import byref, c_int, c_size_t
 
 import torch
 
-from ._lib import (DC_AFT_ACCUMULATE, DC_AFT_CAUSAL, DC_AFT_COMPUTE_BF16, DC_AFT_SAVE_STATS,
-                   DC_AFT_SIMT, DC_AFT_WS_VALID, DC_BF16, DC_F32, DC_GEMM_ACCUMULATE, DC_GEMM_BIAS,
-                   DC_GEMM_GELU, DC_GEMM_GELU_BWD, DC_GEMM_TRANS_A, DC_GEMM_TRANS_B, DcError, check,
-                   lib)
+from ._lib import (DC_AFT_ACCUMULATE, DC_AFT_BWD_DKDV, DC_AFT_BWD_NO_DKDV, DC_AFT_CAUSAL,
+                   DC_AFT_COMPUTE_BF16, DC_AFT_SAVE_STATS, DC_AFT_SIMT, DC_AFT_SPARE_SMS,
+                   DC_AFT_WS_VALID, DC_BF16, DC_F32, DC_GEMM_ACCUMULATE, DC_GEMM_BIAS, DC_GEMM_GELU,
+                   DC_GEMM_GELU_BWD, DC_GEMM_TRANS_A, DC_GEMM_TRANS_B, DcError, check, lib)
 
 
 def _stream() -> int:
@@ -112,26 +112,40 @@ def aft_fwd(Q, K, V, w, causal=True, out=None, workspace: AftWorkspace | None = 
 
 
 def aft_bwd(Q, K, V, w, dZ, causal=True, grads=None, accumulate=False,
-            workspace: AftWorkspace | None = None, ws_valid=False, simt=False, compute_bf16=False):
+            workspace: AftWorkspace | None = None, ws_valid=False, simt=False, compute_bf16=False,
+            part=None, spare_sms=0):
+    """dQ, dK, dV, dW of the AFT-full op.
+
+    part=None computes all four.  part="dw" computes dQ and dW only and leaves
+    g, n in `workspace`; part="dkdv" then computes dK and dV from them (same
+    workspace, ws_valid=True), so a data-parallel caller can all-reduce dW
+    while dK and dV run.  spare_sms leaves that many SMs free for such a
+    collective.  Entries of `grads` a part does not write may be None."""
     Q3, K3, V3, G3 = _as3d(Q), _as3d(K), _as3d(V), _as3d(dZ)
     for t, n in ((Q3, "Q"), (K3, "K"), (V3, "V"), (G3, "dZ")):
         _need(t, n)
     _need(w, "w", rows_strided=True)
     B, Tq, D = Q3.shape
     Tk = K3.shape[1]
+    if part not in (None, "dw", "dkdv"):
+        raise DcError(f"part must be None, 'dw' or 'dkdv' (got {part!r})")
     if grads is None:
         grads = (torch.empty_like(Q), torch.empty_like(K), torch.empty_like(V),
                  torch.empty(w.shape[0], w.stride(0), device=w.device)[:, : w.shape[1]])
     dQ, dK, dV, dW = grads
-    if dW.dtype != torch.float32 or dW.stride(0) != w.stride(0) or dW.stride(1) != 1:
+    if dW is not None and (dW.dtype != torch.float32 or dW.stride(0) != w.stride(0) or dW.stride(1) != 1):
         raise DcError("dW must be float32 with the row stride of w")
     ws = workspace.ptr if workspace is not None else None
     nb = workspace.nbytes if workspace is not None else 0
-    flags = _flags(causal, accumulate, ws_valid, simt, compute_bf16)
+    flags = _flags(causal, accumulate, ws_valid, simt, compute_bf16) | DC_AFT_SPARE_SMS(spare_sms)
     if workspace is not None and workspace.save_stats:
         flags |= DC_AFT_SAVE_STATS
+    if part == "dw":
+        flags |= DC_AFT_BWD_NO_DKDV
+    elif part == "dkdv":
+        flags |= DC_AFT_BWD_DKDV
     check(lib().dc_aft_bwd(Q3.data_ptr(), K3.data_ptr(), V3.data_ptr(), w.data_ptr(), w.stride(0),
-                           G3.data_ptr(), dQ.data_ptr(), dK.data_ptr(), dV.data_ptr(), dW.data_ptr(),
+                           G3.data_ptr(), _ptr(dQ), _ptr(dK), _ptr(dV), _ptr(dW),
                            B, Tq, Tk, D, _dtype_code(Q3), flags, ws, nb, _stream()),
           "dc_aft_bwd")
     return dQ, dK, dV, dW

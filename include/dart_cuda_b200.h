@@ -55,6 +55,16 @@ extern "C" {
                                     of HBM traffic per element of Z; pays off
                                     from Tk of about 1024 on.  Forward and
                                     backward must pass the same flags.        */
+/* The backward in two calls, so a data-parallel caller can all-reduce dW
+ * while dK and dV are still being computed: a DC_AFT_BWD_NO_DKDV call writes
+ * dQ and dW (dK, dV may be NULL) and leaves g and n in the workspace; a later
+ * DC_AFT_BWD_DKDV call on the same workspace (with DC_AFT_WS_VALID) writes dK
+ * and dV only (dZ, dQ, dW may be NULL). */
+#define DC_AFT_BWD_NO_DKDV 0x40
+#define DC_AFT_BWD_DKDV 0x80
+/* The persistent tensor-core kernels of this call leave n SMs (0..255) free,
+ * e.g. for a collective running beside them on another stream. */
+#define DC_AFT_SPARE_SMS(n) (((n)&0xff) << 16)
 
 /* Message of the last failing call on this host thread ("" if none). */
 const char *dc_last_error(void);

@@ -196,6 +196,48 @@ def test_saved_stats_match_recompute(ops, dev, dtype, B, T, D, accumulate):
     assert ops.device_status() == 0
 
 
+@pytest.mark.parametrize("dtype,B,T,D", [(torch.bfloat16, 4, 512, 256), (torch.bfloat16, 2, 1024, 128),
+                                         (torch.float32, 2, 130, 40)])
+@pytest.mark.parametrize("save", [False, True])
+def test_split_backward(ops, dev, dtype, B, T, D, save):
+    """The backward as two calls (dQ + dW, then dK + dV with SMs left free)
+    gives the one-call results: dQ, dK, dV bit for bit, dW up to the order of
+    its split-K additions."""
+    Q, K, V, W, dZ = make_inputs(23, B, T, T, D)
+    tq, tk, tv, tg = to_dev(dev, dtype, Q, K, V, dZ)
+    tw = torch.from_numpy(W).to(dev)
+    ws = ops.AftWorkspace(B, T, T, D, dtype, flags=1, save_stats=save)
+    ops.aft_fwd(tq, tk, tv, tw, causal=True, workspace=ws)
+    g0 = ops.aft_bwd(tq, tk, tv, tw, tg, causal=True, workspace=ws, ws_valid=True)
+    dQ, dK, dV = (torch.full_like(x, 7.0) for x in (tq, tk, tv))
+    dW = torch.full_like(tw, 7.0)
+    ops.aft_bwd(tq, tk, tv, tw, tg, causal=True, grads=(dQ, None, None, dW), workspace=ws,
+                ws_valid=True, part="dw")
+    assert float(dK[0, 0, 0]) == 7.0  # untouched by the first part
+    ops.aft_bwd(tq, tk, tv, tw, tg, causal=True, grads=(None, dK, dV, None), workspace=ws,
+                ws_valid=True, part="dkdv", spare_sms=20)
+    for a, b in zip(g0[:3], (dQ, dK, dV)):
+        assert torch.equal(a, b)
+    torch.testing.assert_close(dW, g0[3], rtol=1e-5, atol=1e-6)
+    assert ops.device_status() == 0
+
+
+def test_split_backward_rejects_misuse(ops, dev):
+    from dart_cuda_b200 import DcError
+
+    t = torch.zeros(1, 128, 64, device=dev, dtype=torch.bfloat16)
+    w = torch.zeros(128, 128, device=dev)
+    g = (torch.empty_like(t), torch.empty_like(t), torch.empty_like(t), torch.empty_like(w))
+    with pytest.raises(DcError):  # the second part needs the first part's workspace
+        ops.aft_bwd(t, t, t, w, t, grads=g, part="dkdv")
+    with pytest.raises(DcError):  # dK, dV missing for the second part
+        ws = ops.AftWorkspace(1, 128, 128, 64, torch.bfloat16, flags=1)
+        ops.aft_bwd(t, t, t, w, t, grads=g[:1] + (None, None) + g[3:], workspace=ws, ws_valid=True,
+                    part="dkdv")
+    with pytest.raises(DcError):
+        ops.aft_bwd(t, t, t, w, t, grads=g, part="both")
+
+
 def test_deterministic_forward(ops, dev):
     Q, K, V, W, _ = make_inputs(10, 2, 256, 256, 128)
     tq, tk, tv = to_dev(dev, torch.bfloat16, Q, K, V)
