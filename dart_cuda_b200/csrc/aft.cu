@@ -227,27 +227,21 @@ __device__ __forceinline__ void st8op(float *p, const float (&v)[8])
 }
 
 // Row maxima m_t over the visible set and A' = exp(w - m) (0 outside the
-// set and in the padding), one block per padded row t.
+// set and in the padding), one warp per padded row t.
 template <class E>
-__device__ __forceinline__ void prep_w_row(int t, const float *__restrict__ w, int ldw, int Tq,
-                                           int Tk, int Tkp, int causal, float *__restrict__ m,
-                                           E *__restrict__ Ap)
+__device__ __forceinline__ void prep_w_row(int t, int lane, const float *__restrict__ w, int ldw,
+                                           int Tq, int Tk, int Tkp, int causal,
+                                           float *__restrict__ m, E *__restrict__ Ap)
 {
-    __shared__ float red[32];
     E *row = Ap + (size_t)t * Tkp;
-    if (t >= Tq) {
-        for (int i = threadIdx.x; i < Tkp; i += blockDim.x) row[i] = to_op<E>(0.f);
-        if (threadIdx.x == 0) m[t] = 0.f;
-        return;
-    }
-    const int lim = causal ? min(t + 1, Tk) : Tk;
+    const int lim = t < Tq ? (causal ? min(t + 1, Tk) : Tk) : 0;
     const float *wr = w + (size_t)t * ldw;
     // 16-byte loads when a row starts on a 16-byte boundary (ldw % 4 == 0):
     // a float4 at a multiple of 4 below lim then stays inside the row
     const bool vec = (ldw % 4 == 0) && ((reinterpret_cast<uintptr_t>(w) & 15) == 0);
     float mx = -INFINITY;
     if (vec) {
-        for (int i = threadIdx.x * 4; i < lim; i += blockDim.x * 4) {
+        for (int i = lane * 4; i < lim; i += 128) {
             const float4 v = __ldg(reinterpret_cast<const float4 *>(wr + i));
             mx = fmaxf(mx, v.x);
             if (i + 1 < lim) mx = fmaxf(mx, v.y);
@@ -255,31 +249,33 @@ __device__ __forceinline__ void prep_w_row(int t, const float *__restrict__ w, i
             if (i + 3 < lim) mx = fmaxf(mx, v.w);
         }
     } else {
-        for (int i = threadIdx.x; i < lim; i += blockDim.x) mx = fmaxf(mx, wr[i]);
+        for (int i = lane; i < lim; i += 32) mx = fmaxf(mx, wr[i]);
     }
-    mx = block_max(mx, red);
-    if (threadIdx.x == 0) m[t] = mx;
-    if (vec) {
-        // eight A' entries per thread, one vector store (Tkp is a multiple of 8)
-        for (int i = threadIdx.x * 8; i < Tkp; i += blockDim.x * 8) {
-            float v[8];
 #pragma unroll
-            for (int k = 0; k < 8; ++k) v[k] = 0.f;
-            if (i < lim) {
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) m[t] = t < Tq ? mx : 0.f;
+    // eight A' entries per lane and step, one vector store (Tkp is a multiple of 8)
+    for (int i = lane * 8; i < Tkp; i += 256) {
+        float v[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[k] = 0.f;
+        if (i < lim) {
+            if (vec) {
                 const float4 a = __ldg(reinterpret_cast<const float4 *>(wr + i));
                 v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
                 if (i + 4 < lim) {
                     const float4 b = __ldg(reinterpret_cast<const float4 *>(wr + i + 4));
                     v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
                 }
+            } else {
 #pragma unroll
-                for (int k = 0; k < 8; ++k) v[k] = i + k < lim ? __expf(v[k] - mx) : 0.f;
+                for (int k = 0; k < 8; ++k)
+                    if (i + k < lim) v[k] = wr[i + k];
             }
-            st8op(row + i, v);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) v[k] = i + k < lim ? __expf(v[k] - mx) : 0.f;
         }
-    } else {
-        for (int i = threadIdx.x; i < Tkp; i += blockDim.x)
-            row[i] = to_op<E>(i < lim ? __expf(wr[i] - mx) : 0.f);
+        st8op(row + i, v);
     }
 }
 
@@ -341,7 +337,7 @@ __device__ __forceinline__ void prep_colmax_block(int bx, int s, int b, const IO
     if (d < D) cpart[((size_t)s * B + b) * dp + d] = m;
 }
 
-// First prep launch: blocks [0, Tqp) build the rows of A' and m; the
+// First prep launch: blocks [0, Tqp/8) build the rows of A' and m; the
 // remaining blocks compute the partial column maxima of K (ncb column blocks
 // of 256 x nsplit row slices x B).
 template <class IO, class E>
@@ -354,12 +350,13 @@ __global__ void __launch_bounds__(256)
     grid_dep_wait();  // launched early (programmatic dependent launch)
     grid_dep_launch();
     const int bid = blockIdx.x;
-    const int Tqp = gridDim.x - ncb * nsplit * B;
-    if (bid < Tqp) {
-        prep_w_row<E>(bid, w, ldw, Tq, Tk, Tkp, causal, m, Ap);
+    const int wblocks = gridDim.x - ncb * nsplit * B;  // eight rows of A' each
+    if (bid < wblocks) {
+        prep_w_row<E>(bid * 8 + (threadIdx.x >> 5), threadIdx.x & 31, w, ldw, Tq, Tk, Tkp, causal,
+                      m, Ap);
         return;
     }
-    const int q = bid - Tqp;
+    const int q = bid - wblocks;
     prep_colmax_block<IO>(q % ncb, (q / ncb) % nsplit, q / (ncb * nsplit), K, B, Tk, D, ldk, dp,
                           rows_per_split, vec, cpart);
 }
@@ -561,7 +558,7 @@ static Layout make_layout(int B, int Tq, int Tk, int D, int dtype, int flags)
     L.dp = (int)round_up(std::max(D, 1), D_ALIGN);
     L.esz = operand_size(dtype, flags);
     const int dblocks = (D + 255) / 256;
-    int want = (4 * 148 + dblocks * B - 1) / std::max(1, dblocks * B);
+    int want = (8 * 148 + dblocks * B - 1) / std::max(1, dblocks * B);
     L.nsplit = std::max(1, std::min(want, (Tk + 31) / 32));
     L.rows_per_split = (Tk + L.nsplit - 1) / L.nsplit;
     L.nsplit = std::max(1, (Tk + L.rows_per_split - 1) / L.rows_per_split);
@@ -652,7 +649,7 @@ static int run_prep(const Layout &L, const IO *K, const IO *V, const float *w, i
         // A' rows and the partial column maxima of K in one launch
         KernelTimer kt("aft_prep_w_colmax", st);
         const int ncb = (L.D + 255) / 256;
-        const int grid = L.Tqp + ncb * L.nsplit * L.B;
+        const int grid = L.Tqp / 8 + ncb * L.nsplit * L.B;
         DC_CUDA_TRY(launch_pdl(prep_wc_kernel<IO, E>, dim3(grid), dim3(256), 0, st, 1, w, ldw, L.Tq,
                                L.Tk, L.Tkp, causal, m, Ap, K, L.B, L.D, L.ldi, L.dp, ncb,
                                L.nsplit, L.rows_per_split, vec, cpart));

@@ -331,13 +331,17 @@ __device__ __forceinline__ void epi16_grads(const Params &p, int b, int t, int d
     const size_t go = ((size_t)b * p.Tqp + t) * p.dp + d0;
     float hi[16], lo[16];
     constexpr bool BF = sizeof(E) == 2;
-    const bool keep_lo = t < p.lo_rows;
-    round16(g, hi, lo, BF);
-    st16op((E *)p.G1 + go, hi);
-    if (keep_lo) st16op((E *)p.G1l + go, lo);
-    round16(n, hi, lo, BF);
-    st16op((E *)p.G2 + go, hi);
-    if (keep_lo) st16op((E *)p.G2l + go, lo);
+    if (t < p.lo_rows) {
+        round16(g, hi, lo, BF);
+        st16op((E *)p.G1 + go, hi);
+        st16op((E *)p.G1l + go, lo);
+        round16(n, hi, lo, BF);
+        st16op((E *)p.G2 + go, hi);
+        st16op((E *)p.G2l + go, lo);
+    } else {  // the operand-precision store rounds exactly as round16's hi
+        st16op((E *)p.G1 + go, g);
+        st16op((E *)p.G2 + go, n);
+    }
 }
 
 template <class IO, class E>
