@@ -456,26 +456,29 @@ __device__ __forceinline__ Tile decode_tile(const Params &p, int idx)
     constexpr int RB = P ? 2 * BM : BM;
     Tile t{};
     t.passes = 1;
-    if (MODE == FWD || MODE == BWD1) {
-        // rows t (heavy, late-t tiles first), columns d
+    if (MODE != WGRAD) {
+        // groups g = (b, column block d) in chunks of group_chunk; within a
+        // chunk, row levels heavy first (FWD/BWD1: late t; HGRAD: early i)
         const int nd = p.dp / BN;
-        const int per = nd * p.B;
-        t.mrow = p.Tqp / RB - 1 - idx / per;
-        const int rem = idx % per;
-        t.ncol = rem % nd;
-        t.b = rem / nd;
-        t.k0 = 0;
-        t.k1 = (p.causal ? min(p.Tkp, (t.mrow + 1) * RB) : p.Tkp) / BKe;
-    } else if (MODE == HGRAD) {
-        // rows i (heavy, early-i tiles first), columns d
-        const int nd = p.dp / BN;
-        const int per = nd * p.B;
-        t.mrow = idx / per;
-        const int rem = idx % per;
-        t.ncol = rem % nd;
-        t.b = rem / nd;
-        t.k0 = p.causal ? (t.mrow * RB) / BKe : 0;
-        t.k1 = p.Tqp / BKe;
+        const int G = nd * p.B;
+        const int nm = (MODE == HGRAD ? p.Tkp : p.Tqp) / RB;
+        const int GC = p.group_chunk;
+        const int g0 = idx / (GC * nm) * GC;
+        const int gcnt = min(GC, G - g0);
+        const int within = idx - g0 * nm;
+        const int level = within / gcnt;
+        const int g = g0 + within % gcnt;
+        t.ncol = g % nd;
+        t.b = g / nd;
+        if (MODE == HGRAD) {
+            t.mrow = level;
+            t.k0 = p.causal ? (t.mrow * RB) / BKe : 0;
+            t.k1 = p.Tqp / BKe;
+        } else {
+            t.mrow = nm - 1 - level;
+            t.k0 = 0;
+            t.k1 = (p.causal ? min(p.Tkp, (t.mrow + 1) * RB) : p.Tkp) / BKe;
+        }
     } else {
         // RB query rows x 256 keys (two 128-blocks); ncol counts the key pairs
         const int pair = idx / p.splits, s = idx % p.splits;
