@@ -88,7 +88,6 @@ struct Params {
     int vec_io;       // user tensors allow 32-byte vector access along D
     int vec_w;        // w / dW allow 32-byte vector access along a row
     int spare_sms;    // host only: SMs the persistent launch leaves free
-    int group_chunk;  // FWD/BWD1/HGRAD: (batch, column block) groups walked together
     const void *Q, *K, *V, *dZ;
     void *Z, *dQ, *dK, *dV;
     float *dW;
@@ -771,19 +770,6 @@ static int launch_tc(Params p, const Layout &L, char *ws, cudaStream_t st)
         DC_TRY(map_3d(&mB2, ws + L.off_pe, L, L.Tkp, BK, C::BROWS, false, kr));
         mB3 = mB4 = mB1;
         p.n_tiles = wgrad_tiles(L, p.causal) * p.splits;
-    }
-    // Tiles sharing a B panel (one batch element's column block) are walked
-    // in chunks of groups whose panels, with A', fit in about half of L2, so
-    // each panel is fetched from HBM once rather than once per row level.
-    if (MODE != WGRAD) {
-        const size_t groups = (size_t)(L.dp / BN) * L.B;
-        const size_t kdim = MODE == HGRAD ? L.Tqp : L.Tkp;
-        const size_t panels = P ? 2 : C::NB;  // B panels of a group (a pair splits them)
-        const size_t group_bytes = panels * kdim * BN * L.esz;
-        const size_t ap_bytes = (size_t)L.Tqp * L.Tkp * L.esz;
-        const size_t budget = (size_t)64 << 20;
-        const size_t fit = budget > ap_bytes ? (budget - ap_bytes) / std::max<size_t>(1, group_bytes) : 1;
-        p.group_chunk = (int)std::max<size_t>(1, std::min(groups, fit));
     }
     p.trace = (g_trace_modes >> MODE) & 1 ? g_trace_buf : nullptr;
     static const char *names[4] = {"aft_tc_fwd", "aft_tc_bwd_recompute", "aft_tc_dkdv",

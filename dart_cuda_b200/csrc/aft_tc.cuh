@@ -457,25 +457,33 @@ __device__ __forceinline__ Tile decode_tile(const Params &p, int idx)
     Tile t{};
     t.passes = 1;
     if (MODE != WGRAD) {
-        // groups g = (b, column block d) in chunks of group_chunk; within a
-        // chunk, row levels heavy first (FWD/BWD1: late t; HGRAD: early i)
+        // Tiles in bundles of two of one group g = (b, column block d): row
+        // levels q and nm-1-q, whose K lengths sum to the same total for every
+        // q (causal; all equal otherwise), heavy tile first.  Bundles run
+        // group-major; with nm odd the middle-level tiles of all groups follow,
+        // paired with each other.
         const int nd = p.dp / BN;
-        const int G = nd * p.B;
         const int nm = (MODE == HGRAD ? p.Tkp : p.Tqp) / RB;
-        const int GC = p.group_chunk;
-        const int g0 = idx / (GC * nm) * GC;
-        const int gcnt = min(GC, G - g0);
-        const int within = idx - g0 * nm;
-        const int level = within / gcnt;
-        const int g = g0 + within % gcnt;
+        const int nb = nm / 2;
+        const int bundles = nd * p.B * nb;
+        const int u = idx >> 1;
+        int g, level;  // level 0 = the lightest row level
+        if (u < bundles) {
+            g = u / nb;
+            const int q = u % nb;
+            level = (idx & 1) ? q : nm - 1 - q;
+        } else {
+            g = idx - 2 * bundles;
+            level = nm / 2;
+        }
         t.ncol = g % nd;
         t.b = g / nd;
-        if (MODE == HGRAD) {
-            t.mrow = level;
+        if (MODE == HGRAD) {  // early key rows see the most query rows
+            t.mrow = nm - 1 - level;
             t.k0 = p.causal ? (t.mrow * RB) / BKe : 0;
             t.k1 = p.Tqp / BKe;
         } else {
-            t.mrow = nm - 1 - level;
+            t.mrow = level;
             t.k0 = 0;
             t.k1 = (p.causal ? min(p.Tkp, (t.mrow + 1) * RB) : p.Tkp) / BKe;
         }
@@ -509,14 +517,18 @@ __device__ __forceinline__ Tile decode_tile(const Params &p, int idx)
     return t;
 }
 
-// Tile of this CTA's (or CTA pair's) j-th iteration: tiles are listed
-// heavy-first and dealt boustrophedon (round j even: c, odd: G-1-c) so each
-// worker pairs heavy and light tiles.  -1 once it has no more tiles.
-template <bool P = false>
+// Tile of this CTA's (or CTA pair's) j-th iteration, -1 once it has no more.
+// Units are dealt boustrophedon (round r even: worker c, odd: G-1-c): for
+// FWD/BWD1/HGRAD a unit is a bundle of two tiles with equal K sums
+// (decode_tile), so every worker gets the same main-loop work up to one
+// bundle; for WGRAD a unit is one tile of a heavy-first list.
+template <int MODE, bool P = false>
 __device__ __forceinline__ int sched_tile(int j, int ntiles)
 {
     const int G = P ? gridDim.x >> 1 : gridDim.x, c = P ? blockIdx.x >> 1 : blockIdx.x;
-    const int t = j * G + ((j & 1) ? (G - 1 - c) : c);
+    const int r = MODE != WGRAD ? j >> 1 : j;
+    const int unit = r * G + ((r & 1) ? (G - 1 - c) : c);
+    const int t = MODE != WGRAD ? 2 * unit + (j & 1) : unit;
     return t < ntiles ? t : -1;
 }
 
@@ -631,7 +643,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             uint32_t g = 0;
             bool stop = false;
             for (int jt = 0; !stop; ++jt) {
-                const int tile = sched_tile<P>(jt, ntiles);
+                const int tile = sched_tile<MODE, P>(jt, ntiles);
                 if (tile < 0) break;
                 const Tile tl = decode_tile<MODE, C::BKe, P>(p, tile);
                 trace_at(p, jt, 0, global_timer());
@@ -721,7 +733,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             uint32_t g = 0, j = 0;
             bool stop = false;
             for (; !stop; ++j) {
-                const int tile = sched_tile<P>(j, ntiles);
+                const int tile = sched_tile<MODE, P>(j, ntiles);
                 if (tile < 0) break;
                 const Tile tl = decode_tile<MODE, C::BKe, P>(p, tile);
                 const uint32_t buf = j & 1, use = j >> 1;
@@ -795,7 +807,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int slice = warp >> 2;
         const int row = quad * 32 + lane;
         for (uint32_t j = 0;; ++j) {
-            const int tile = sched_tile<P>(j, ntiles);
+            const int tile = sched_tile<MODE, P>(j, ntiles);
             if (tile < 0) break;
             const Tile tl = decode_tile<MODE, C::BKe, P>(p, tile);
             const uint32_t buf = j & 1, use = j >> 1;
