@@ -206,16 +206,11 @@ __device__ __forceinline__ float block_max(float v, float *red)
 // Eight operand-precision values, one 16-byte (bf16) or two (tf32) stores.
 __device__ __forceinline__ void st8op(__nv_bfloat16 *p, const float (&v)[8])
 {
-    uint4 x;
-    x.x = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v[0])) |
-          ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v[1])) << 16);
-    x.y = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v[2])) |
-          ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v[3])) << 16);
-    x.z = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v[4])) |
-          ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v[5])) << 16);
-    x.w = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v[6])) |
-          ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v[7])) << 16);
-    *reinterpret_cast<uint4 *>(p) = x;
+    uint32_t w[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k)  // paired conversions, v[2k] in the low half
+        asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(w[k]) : "f"(v[2 * k + 1]), "f"(v[2 * k]));
+    *reinterpret_cast<uint4 *>(p) = make_uint4(w[0], w[1], w[2], w[3]);
 }
 __device__ __forceinline__ void st8op(float *p, const float (&v)[8])
 {

@@ -89,10 +89,14 @@ struct TcCfg {
 
 // ----------------------------------------------------------- vector I/O
 // bf16 <-> fp32 by bit placement: a bf16 is the high half of an fp32.
+// One paired conversion (a in the low half): converting the two values one at
+// a time costs two instructions on the special-function pipe, which the
+// epilogues' exponentials and reciprocals already keep busy.
 __device__ __forceinline__ uint32_t pack2(float a, float b)
 {
-    return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(a)) |
-           ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(b)) << 16);
+    uint32_t r;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(b), "f"(a));
+    return r;
 }
 // 256-bit accesses: one full 32-byte sector per thread per instruction
 // (sm_100 global v8 loads/stores); callers guarantee 32-byte alignment.
@@ -190,9 +194,17 @@ __device__ __forceinline__ void round16(const float (&v)[16], float (&hi)[16], f
                                         bool bf16)
 {
 #pragma unroll
-    for (int k = 0; k < 16; ++k) {
-        hi[k] = bf16 ? __bfloat162float(__float2bfloat16_rn(v[k])) : to_op<float>(v[k]);
+    for (int k = 0; k < 16; k += 2) {
+        if (bf16) {
+            const uint32_t w = pack2(v[k], v[k + 1]);
+            hi[k] = __uint_as_float(w << 16);
+            hi[k + 1] = __uint_as_float(w & 0xFFFF0000u);
+        } else {
+            hi[k] = to_op<float>(v[k]);
+            hi[k + 1] = to_op<float>(v[k + 1]);
+        }
         lo[k] = v[k] - hi[k];
+        lo[k + 1] = v[k + 1] - hi[k + 1];
     }
 }
 
