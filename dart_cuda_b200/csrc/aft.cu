@@ -85,6 +85,8 @@ struct Params {
     int n_tiles;      // tensor-core path: number of output tiles of the launch
     int kpb;          // WGRAD: K steps per batch element (dp / BKe)
     int splits;       // WGRAD: split-K factor
+    int sk_tiles;     // WGRAD: dW tiles
+    int sk_lo;        // WGRAD: leading tiles that also run a low-part pass
     int vec_io;       // user tensors allow 32-byte vector access along D
     int vec_w;        // w / dW allow 32-byte vector access along a row
     int spare_sms;    // host only: SMs the persistent launch leaves free
@@ -764,7 +766,7 @@ static int launch_tc(Params p, const Layout &L, char *ws, cudaStream_t st)
         DC_TRY(map_3d(&mB1, ws + L.off_pv, L, L.Tkp, BK, C::BROWS, false, kr));
         DC_TRY(map_3d(&mB2, ws + L.off_pe, L, L.Tkp, BK, C::BROWS, false, kr));
         mB3 = mB4 = mB1;
-        p.n_tiles = wgrad_tiles(L, p.causal) * p.splits;
+        p.n_tiles = (p.sk_tiles + p.sk_lo) * p.splits;
     }
     p.trace = (g_trace_modes >> MODE) & 1 ? g_trace_buf : nullptr;
     static const char *names[4] = {"aft_tc_fwd", "aft_tc_bwd_recompute", "aft_tc_dkdv",
@@ -937,20 +939,29 @@ static int bwd_impl(const void *Q, const void *K, const void *V, const float *w,
         } else {
             DC_TRY((launch<BWD1, E, IO>(p, L, ws, st, flags)));
         }
-        // split-K factor for dW: pick the split count whose tiles fill the
-        // persistent workers (CTAs, or CTA pairs) in the least time, waves x
-        // time per tile, where a tile costs at least its epilogue (the scaled
-        // atomic adds of a 128 x 256 block per CTA: measured at about 4 K
-        // steps of a single CTA's main loop; for pairs, whose epilogues
-        // contend for the same dW lines, splitting below ~40 steps measured
-        // slower), so splitting finer than that only adds atomics
+        // dW: tiles, then the low-part passes of the first rows' tiles as
+        // tiles of their own, each split into `splits` K ranges.  The split
+        // count is the one whose units fill the persistent workers (CTAs, or
+        // CTA pairs) in the least time, waves x time per unit, where a unit
+        // costs at least its epilogue (the scaled atomic adds of a 128 x 256
+        // block per CTA: measured at about 4 K steps of 128 B, 8 of the 64 B
+        // steps a single CTA runs, of its main loop; for pairs, whose
+        // epilogues contend for the same dW lines, splitting below ~40 steps
+        // measured slower), so splitting finer than that only adds atomics.
+        // All units then have one K length and the workers walk K together,
+        // which keeps the operand slices they read in L2.
         Params pw = p;
-        pw.kpb = L.dp / TcCfg<WGRAD, E>::BKe;
-        const int tiles = wgrad_tiles(L, causal);
-        const int ktot = L.B * pw.kpb;
         const bool pairs = use_pairs(L);
+        pw.kpb = L.dp / (pairs ? TcCfg<WGRAD, E, sizeof(E) == 2>::BKe : TcCfg<WGRAD, E, false>::BKe);
+        const int rb = pairs ? 2 * BM : BM;
+        const int lo_blocks = std::min((p.lo_rows + rb - 1) / rb, L.Tqp / rb);
+        pw.sk_tiles = wgrad_tiles(L, causal);
+        pw.sk_lo = !causal ? lo_blocks * ((L.Tkp / BN + 1) / 2)
+                   : pairs ? lo_blocks * (lo_blocks + 1) / 2 : wgrad_pairs_before(lo_blocks);
+        const int tiles = pw.sk_tiles + pw.sk_lo;
+        const int ktot = L.B * pw.kpb;
         const int workers = pairs ? sm_count() / 2 : sm_count();
-        const double kEpiSteps = pairs ? 40.0 : 4.0;
+        const double kEpiSteps = pairs ? 40.0 : 8.0;  // in K steps of the launched tile
         int best = 1;
         double best_cost = 1e30;
         for (int sp = 1; sp <= std::max(1, ktot / 8); ++sp) {

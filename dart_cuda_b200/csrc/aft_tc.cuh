@@ -26,9 +26,6 @@ namespace aft {
 constexpr int kEpiWarps = 12;
 constexpr int kTcThreads = (kEpiWarps + 2) * 32;
 constexpr int kSmemBudget = 227 * 1024;
-#ifndef DC_WGRAD_KROW
-#define DC_WGRAD_KROW 128
-#endif
 
 // P: the launch runs CTA pairs (cta_group::2): every MMA is M = 256 over the
 // pair, each CTA loading its 128 rows of A and half of B.  bf16 operands.
@@ -39,10 +36,12 @@ struct TcCfg {
     static constexpr bool W = MODE == WGRAD;
     static constexpr bool H = MODE == HGRAD;
     // bytes of K per operand row and stage.  dW's four K-major tiles per stage
-    // take 128 B rows (two or three stages): TMA moves whole 128 B row segments
-    // at a markedly higher rate than 64 B ones, which outweighs the shallower
-    // pipeline (measured at T = 4096: 354 -> 228 us).
-    static constexpr int KROW = W ? DC_WGRAD_KROW : 128;
+    // take 128 B rows with CTA pairs (two stages): TMA moves whole 128 B row
+    // segments at a markedly higher rate than 64 B ones, which outweighs the
+    // shallower pipeline (dW at T = 4096: 354 -> 228 us); single CTAs (short
+    // sequences) measured faster with 64 B rows and four stages (T = 512:
+    // 32.6 -> 30.3 us).
+    static constexpr int KROW = W ? (P ? 128 : 64) : 128;
     static constexpr int BKe = KROW / (int)sizeof(E);  // K elements per stage
     static constexpr int UK = TF32 ? 8 : 16;           // K per MMA instruction
     static constexpr int NSUB = BKe / UK;              // MMAs per stage and operand pair
@@ -448,8 +447,9 @@ __device__ __forceinline__ void epi16_wgrad(const Params &p, int t, int i0, cons
 
 // ----------------------------------------------------------- tile schedule
 struct Tile {
-    int b, mrow, ncol, k0, k1;  // mrow/ncol: 128-row block of the accumulator / column block
-    int passes;                 // WGRAD: 2 when the low parts of g, n add a second pass over K
+    int b, mrow, ncol;  // mrow/ncol: 128-row block of the accumulator / column block
+    int k0, k1;         // K steps [k0, k1); WGRAD: of the tile's passes laid end to end
+    int kt;             // WGRAD: K steps of one pass (steps from kt on read the low parts)
 };
 
 // dW tiles of a causal launch: row block r holds r/2 + 1 column pairs, so
@@ -467,7 +467,7 @@ __device__ __forceinline__ Tile decode_tile(const Params &p, int idx)
 {
     constexpr int RB = P ? 2 * BM : BM;
     Tile t{};
-    t.passes = 1;
+    t.kt = 0x7fffffff;
     if (MODE != WGRAD) {
         // Tiles in bundles of two of one group g = (b, column block d): row
         // levels q and nm-1-q, whose K lengths sum to the same total for every
@@ -500,8 +500,13 @@ __device__ __forceinline__ Tile decode_tile(const Params &p, int idx)
             t.k1 = (p.causal ? min(p.Tkp, (t.mrow + 1) * RB) : p.Tkp) / BKe;
         }
     } else {
-        // RB query rows x 256 keys (two 128-blocks); ncol counts the key pairs
-        const int pair = idx / p.splits, s = idx % p.splits;
+        // RB query rows x 256 keys (two 128-blocks); ncol counts the key pairs.
+        // Units: split s of tile u, where tiles sk_tiles.. are the low-part
+        // passes of the first sk_lo tiles (kept separate so that every unit
+        // has the same K length and all workers walk K together)
+        const int u = idx / p.splits, s = idx % p.splits;
+        const bool lo = u >= p.sk_tiles;
+        const int pair = lo ? u - p.sk_tiles : u;
         if (!p.causal) {
             const int np = (p.Tkp / BN + 1) / 2;
             t.mrow = pair / np;
@@ -521,10 +526,10 @@ __device__ __forceinline__ Tile decode_tile(const Params &p, int idx)
             t.mrow = r;
             t.ncol = pair - wgrad_pairs_before(r);
         }
-        const int total = p.B * p.kpb;
-        t.k0 = (int)(((long long)s * total) / p.splits);
-        t.k1 = (int)(((long long)(s + 1) * total) / p.splits);
-        t.passes = t.mrow * RB < p.lo_rows ? 2 : 1;
+        const int kt = p.kpb * p.B;
+        t.kt = kt;
+        t.k0 = (int)(((long long)s * kt) / p.splits) + (lo ? kt : 0);
+        t.k1 = (int)(((long long)(s + 1) * kt) / p.splits) + (lo ? kt : 0);
     }
     return t;
 }
@@ -533,7 +538,7 @@ __device__ __forceinline__ Tile decode_tile(const Params &p, int idx)
 // Units are dealt boustrophedon (round r even: worker c, odd: G-1-c): for
 // FWD/BWD1/HGRAD a unit is a bundle of two tiles with equal K sums
 // (decode_tile), so every worker gets the same main-loop work up to one
-// bundle; for WGRAD a unit is one tile of a heavy-first list.
+// bundle; for WGRAD a unit is one split of one tile or low-part pass.
 template <int MODE, bool P = false>
 __device__ __forceinline__ int sched_tile(int j, int ntiles)
 {
@@ -585,7 +590,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int lane = threadIdx.x & 31;
     const uint32_t rank = P ? cluster_rank() : 0;  // CTA of the pair (0 issues the MMAs)
     const bool leader = rank == 0;
-    constexpr int RB = P ? 2 * BM : BM;  // accumulator rows of a tile
 
     if (threadIdx.x == 0) {
         *abort_flag = 0;
@@ -659,13 +663,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 if (tile < 0) break;
                 const Tile tl = decode_tile<MODE, C::BKe, P>(p, tile);
                 trace_at(p, jt, 0, global_timer());
-                const int len = tl.k1 - tl.k0;
-                const int nsteps = len * tl.passes;
                 // this CTA's accumulator rows and its share of B's columns / rows
                 const int m0 = (P ? 2 * tl.mrow + (int)rank : tl.mrow) * BM;
                 const int bofs = (int)rank * C::BROWS;  // dW: this CTA's key rows
-                for (int js = 0; js < nsteps; ++js, ++g) {
-                    const int k = tl.k0 + (tl.passes > 1 ? js % len : js);
+                for (int e = tl.k0; e < tl.k1; ++e, ++g) {
+                    const bool lo = e >= tl.kt;  // dW: the low-part pass
+                    const int k = lo ? e - tl.kt : e;
                     const int s = g % C::STAGES;
                     const uint32_t ph = (g / C::STAGES) & 1;
                     if (!mbar_wait<P>(smem_u32(&empty[s]), ph ^ 1, abort_flag, p.status,
@@ -709,7 +712,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         // A: G, N (first pass) or their low parts (second pass) [t rows, d]
                         // K-major; B: PV, PE [256 i rows, d] K-major
                         const int bb = k / p.kpb, x = (k % p.kpb) * C::BKe;
-                        const bool lo = js >= len;
                         ld3(sa, lo ? &mapA3 : &mapA, fb, x, m0, bb);
                         ld3(sa + C::TILE_BYTES, lo ? &mapA4 : &mapA2, fb, x, m0, bb);
                         ld3(sb, &mapB1, fb, x, tl.ncol * C::WN + bofs, bb);
@@ -758,7 +760,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 trace_at(p, j, 5, tile);
                 trace_at(p, j, 6, tl.k1 - tl.k0);
                 const uint32_t acc = tmem + buf * C::ACC_COLS;
-                const int nsteps = (tl.k1 - tl.k0) * tl.passes;
+                const int nsteps = tl.k1 - tl.k0;
                 for (int js = 0; js < nsteps; ++js, ++g) {
                     const int s = g % C::STAGES;
                     if (!mbar_wait<P>(smem_u32(&full[s]), (g / C::STAGES) & 1, abort_flag, p.status,
@@ -775,7 +777,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         const uint32_t koff = u * C::UK * (int)sizeof(E);  // K-major step
                         const uint32_t moff = u * C::UK * 128;             // MN-major step
                         if (C::W) {
-                            // acc[RB t, 256 i] += G . PV^T + N . PE^T (or their low parts)
+                            // acc[128 or 256 t, 256 i] += G . PV^T + N . PE^T (or their low parts)
                             const uint64_t b1 = sw128_desc(sb + koff, 16, C::K_SBO, C::K_LAYOUT);
                             const uint64_t b2 =
                                 sw128_desc(sb + C::TILE_B + koff, 16, C::K_SBO, C::K_LAYOUT);
