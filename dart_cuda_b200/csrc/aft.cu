@@ -84,6 +84,7 @@ struct Params {
     int ldo;          // row stride of Z and dZ (elements, >= D)
     int n_tiles;      // tensor-core path: number of output tiles of the launch
     int kpb;          // WGRAD: K steps per batch element (dp / BKe)
+    int bundled;      // FWD/BWD1/HGRAD: tiles dealt in equal-work bundles of two
     int splits;       // WGRAD: split-K factor
     int sk_tiles;     // WGRAD: dW tiles
     int sk_lo;        // WGRAD: leading tiles that also run a low-part pass
@@ -793,6 +794,9 @@ static int launch_tc(Params p, const Layout &L, char *ws, cudaStream_t st)
     }
     const int workers = P ? std::max(1, max_clusters[dev] - (p.spare_sms + 1) / 2)
                           : std::max(1, sm_count() - p.spare_sms);
+    // bundles only pay with at least two tiles a worker: with fewer they
+    // would leave workers idle (decode_tile)
+    p.bundled = MODE != WGRAD && p.n_tiles >= 2 * workers;
     const dim3 grid((P ? 2 : 1) * std::max(1, std::min(p.n_tiles, workers)));
     {
         KernelTimer kt(names[MODE], st);

@@ -474,13 +474,18 @@ __device__ __forceinline__ Tile decode_tile(const Params &p, int idx)
         // q (causal; all equal otherwise), heavy tile first.  Bundles run
         // group-major; with nm odd the middle-level tiles of all groups follow,
         // paired with each other.
+        // Without bundles (fewer than two tiles a worker) the tiles come
+        // heavy level first, one per unit.
         const int nd = p.dp / BN;
         const int nm = (MODE == HGRAD ? p.Tkp : p.Tqp) / RB;
         const int nb = nm / 2;
         const int bundles = nd * p.B * nb;
         const int u = idx >> 1;
         int g, level;  // level 0 = the lightest row level
-        if (u < bundles) {
+        if (!p.bundled) {
+            g = idx % (nd * p.B);
+            level = nm - 1 - idx / (nd * p.B);
+        } else if (u < bundles) {
             g = u / nb;
             const int q = u % nb;
             level = (idx & 1) ? q : nm - 1 - q;
@@ -536,16 +541,18 @@ __device__ __forceinline__ Tile decode_tile(const Params &p, int idx)
 
 // Tile of this CTA's (or CTA pair's) j-th iteration, -1 once it has no more.
 // Units are dealt boustrophedon (round r even: worker c, odd: G-1-c): for
-// FWD/BWD1/HGRAD a unit is a bundle of two tiles with equal K sums
-// (decode_tile), so every worker gets the same main-loop work up to one
-// bundle; for WGRAD a unit is one split of one tile or low-part pass.
+// FWD/BWD1/HGRAD with at least two tiles a worker (p.bundled) a unit is a
+// bundle of two tiles with equal K sums (decode_tile), so every worker gets
+// the same main-loop work up to one bundle; otherwise, and for WGRAD, a unit
+// is one tile (WGRAD: one split of one tile or low-part pass).
 template <int MODE, bool P = false>
-__device__ __forceinline__ int sched_tile(int j, int ntiles)
+__device__ __forceinline__ int sched_tile(const Params &p, int j, int ntiles)
 {
     const int G = P ? gridDim.x >> 1 : gridDim.x, c = P ? blockIdx.x >> 1 : blockIdx.x;
-    const int r = MODE != WGRAD ? j >> 1 : j;
+    const bool bundles = MODE != WGRAD && p.bundled;
+    const int r = bundles ? j >> 1 : j;
     const int unit = r * G + ((r & 1) ? (G - 1 - c) : c);
-    const int t = MODE != WGRAD ? 2 * unit + (j & 1) : unit;
+    const int t = bundles ? 2 * unit + (j & 1) : unit;
     return t < ntiles ? t : -1;
 }
 
@@ -659,7 +666,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             uint32_t g = 0;
             bool stop = false;
             for (int jt = 0; !stop; ++jt) {
-                const int tile = sched_tile<MODE, P>(jt, ntiles);
+                const int tile = sched_tile<MODE, P>(p, jt, ntiles);
                 if (tile < 0) break;
                 const Tile tl = decode_tile<MODE, C::BKe, P>(p, tile);
                 trace_at(p, jt, 0, global_timer());
@@ -747,7 +754,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             uint32_t g = 0, j = 0;
             bool stop = false;
             for (; !stop; ++j) {
-                const int tile = sched_tile<MODE, P>(j, ntiles);
+                const int tile = sched_tile<MODE, P>(p, j, ntiles);
                 if (tile < 0) break;
                 const Tile tl = decode_tile<MODE, C::BKe, P>(p, tile);
                 const uint32_t buf = j & 1, use = j >> 1;
@@ -821,7 +828,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int slice = warp >> 2;
         const int row = quad * 32 + lane;
         for (uint32_t j = 0;; ++j) {
-            const int tile = sched_tile<MODE, P>(j, ntiles);
+            const int tile = sched_tile<MODE, P>(p, j, ntiles);
             if (tile < 0) break;
             const Tile tl = decode_tile<MODE, C::BKe, P>(p, tile);
             const uint32_t buf = j & 1, use = j >> 1;

@@ -63,6 +63,8 @@ __device__ __forceinline__ float sigm(float q) { return 1.0f / (1.0f + __expf(-q
 
 __global__ void __launch_bounds__(kThreads) aft_decode_kernel(Params p)
 {
+    grid_dep_wait();  // programmatic dependent launch: inputs are ready
+    grid_dep_launch();
     // the grid covers Tmax rows; blocks past the history of position t leave
     p.t = *p.pos;
     if (p.t < 0 || p.t >= p.Tmax) {
@@ -225,6 +227,8 @@ __global__ void __launch_bounds__(kThreads) aft_decode_kernel(Params p)
 __global__ void cache_fill_kernel(const float *__restrict__ qkv, int ldq, int B, int T, int D,
                                   float *__restrict__ cache)
 {
+    grid_dep_wait();  // programmatic dependent launch: inputs are ready
+    grid_dep_launch();
     const size_t g = (size_t)blockIdx.x * blockDim.x + threadIdx.x;  // 4-column group
     const size_t groups = (size_t)B * D / 4;
     if (g >= groups * T) return;
@@ -304,7 +308,7 @@ int dc_aft_decode(const float *qkv, int ldq, const float *w, int ldw, long long 
     p.part = reinterpret_cast<float *>(ws + round_up((int64_t)(slabs * sizeof(int)), 256));
     cudaStream_t st = as_stream(stream);
     KernelTimer kt("aft_decode", st);
-    aft_decode_kernel<<<dim3(slabs, max_chunks), kThreads, 0, st>>>(p);
+    (void)launch_pdl(aft_decode_kernel, dim3(slabs, max_chunks), dim3(kThreads), 0, st, 1, p);
     DC_CUDA_TRY(cudaGetLastError());
     return DC_OK;
 }
@@ -317,7 +321,8 @@ int dc_kv_cache_fill(const float *qkv, int ldq, int B, int T, int D, float *cach
     if (n == 0) return DC_OK;
     cudaStream_t st = as_stream(stream);
     KernelTimer kt("kv_cache_fill", st);
-    dec::cache_fill_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(qkv, ldq, B, T, D, cache);
+    (void)launch_pdl(dec::cache_fill_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, st,
+                     1, qkv, ldq, B, T, D, cache);
     DC_CUDA_TRY(cudaGetLastError());
     return DC_OK;
 }

@@ -238,6 +238,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     tc_fence_before();
     __syncthreads();
+    // programmatic dependent launch: the set-up above overlapped the previous
+    // kernel's tail; its outputs are visible from here on
+    grid_dep_wait();
+    grid_dep_launch();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     const int ntiles = p.n_tiles;
@@ -421,7 +425,8 @@ static int launch(Params p, const void *A, int lda, const void *B, int ldb, cuda
     const int grid = std::max(1, std::min(p.n_tiles, sm_count()));
     {
         KernelTimer kt("gemm_tc", st);
-        gemm_tc_kernel<E, A_MN, B_MN><<<grid, kThreads, C::SMEM_BYTES, st>>>(p, mA, mB);
+        DC_CUDA_TRY(launch_pdl(gemm_tc_kernel<E, A_MN, B_MN>, dim3(grid), dim3(kThreads),
+                               C::SMEM_BYTES, st, 1, p, mA, mB));
     }
     DC_CUDA_TRY(cudaGetLastError());
     return DC_OK;

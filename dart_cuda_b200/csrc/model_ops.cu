@@ -29,6 +29,8 @@ __global__ void embed_fwd_kernel(const int32_t *__restrict__ idx, const float *_
                                  const float *__restrict__ wpe, float *__restrict__ out, int T,
                                  int D, int V, int *status)
 {
+    grid_dep_wait();  // programmatic dependent launch: inputs are ready
+    grid_dep_launch();
     const int row = blockIdx.x;  // b*T + t
     const int t = row % T;
     const int tok = idx[row];
@@ -45,6 +47,8 @@ __global__ void embed_fwd_kernel(const int32_t *__restrict__ idx, const float *_
 __global__ void embed_bwd_tok_kernel(const int32_t *__restrict__ idx, const float *__restrict__ dx,
                                      float *__restrict__ dwte, int D, int V)
 {
+    grid_dep_wait();  // programmatic dependent launch: inputs are ready
+    grid_dep_launch();
     const int row = blockIdx.x;
     const int tok = idx[row];
     if (tok < 0 || tok >= V) return;
@@ -56,6 +60,8 @@ __global__ void embed_bwd_tok_kernel(const int32_t *__restrict__ idx, const floa
 __global__ void embed_bwd_pos_kernel(const float *__restrict__ dx, float *__restrict__ dwpe, int B,
                                      int T, int D)
 {
+    grid_dep_wait();  // programmatic dependent launch: inputs are ready
+    grid_dep_launch();
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (size_t)T * D) return;
     const int t = (int)(i / D), d = (int)(i % D);
@@ -69,6 +75,8 @@ __device__ __forceinline__ float sigm(float q) { return 1.0f / (1.0f + __expf(-q
 __global__ void gate_fwd_kernel(const float *__restrict__ q, int ldq, const float *__restrict__ v0,
                                 float *__restrict__ out, int ldo, int M, int N)
 {
+    grid_dep_wait();  // programmatic dependent launch: inputs are ready
+    grid_dep_launch();
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (size_t)M * N) return;
     const int m = (int)(i / N), n = (int)(i % N);
@@ -81,6 +89,8 @@ __global__ void gate_bwd_kernel(const float *__restrict__ q, int ldq, const floa
                                 const float *__restrict__ dz, int ldz, float *__restrict__ dq,
                                 int lddq, float *__restrict__ dv0, int M, int N, int rows_per_block)
 {
+    grid_dep_wait();  // programmatic dependent launch: inputs are ready
+    grid_dep_launch();
     __shared__ float part[8][33];
     const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
     const int n = blockIdx.x * 32 + tx;
@@ -115,6 +125,8 @@ __global__ void greedy_embed_kernel(const float *__restrict__ logits, int ldl, i
                                     const int *pos_dev, int D, int32_t *__restrict__ tokens, int ldt,
                                     float *__restrict__ x)
 {
+    grid_dep_wait();  // programmatic dependent launch: inputs are ready
+    grid_dep_launch();
     __shared__ float sv[32];
     __shared__ int si[32];
     const int pos = *pos_dev + 1;
@@ -187,6 +199,8 @@ constexpr int DC_DEVERR_FULL = 0x40;  // decode ran past the sequence capacity
 
 __global__ void advance_kernel(int *pos, int cap, int *status)
 {
+    grid_dep_wait();  // programmatic dependent launch: inputs are ready
+    grid_dep_launch();
     if (*pos + 1 >= cap) {
         atomicOr(status, DC_DEVERR_FULL);
         return;
@@ -211,7 +225,8 @@ int dc_embedding_fwd(const int32_t *idx, const float *wte, const float *wpe, flo
     if (!idx || !wte || !wpe || !out) return fail(DC_ERR_INVALID, "null pointer");
     cudaStream_t st = as_stream(stream);
     KernelTimer kt("embedding_fwd", st);
-    embed_fwd_kernel<<<B * T, 128, 0, st>>>(idx, wte, wpe, out, T, D, V, device_status_word());
+    (void)launch_pdl(embed_fwd_kernel, dim3(B * T), dim3(128), 0, st, 1, idx, wte, wpe, out, T, D,
+                     V, device_status_word());
     DC_CUDA_TRY(cudaGetLastError());
     return DC_OK;
 }
@@ -224,10 +239,12 @@ int dc_embedding_bwd(const int32_t *idx, const float *dx, float *dwte, float *dw
     if ((long long)B * T * D == 0) return DC_OK;
     cudaStream_t st = as_stream(stream);
     KernelTimer kt("embedding_bwd", st);
-    if (dwte) embed_bwd_tok_kernel<<<B * T, 128, 0, st>>>(idx, dx, dwte, D, V);
+    if (dwte) (void)launch_pdl(embed_bwd_tok_kernel, dim3(B * T), dim3(128), 0, st, 1, idx, dx,
+                               dwte, D, V);
     if (dwpe) {
         const size_t n = (size_t)T * D;
-        embed_bwd_pos_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(dx, dwpe, B, T, D);
+        (void)launch_pdl(embed_bwd_pos_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0,
+                         st, 1, dx, dwpe, B, T, D);
     }
     DC_CUDA_TRY(cudaGetLastError());
     return DC_OK;
@@ -242,7 +259,8 @@ int dc_gate_fwd(const float *q, int ldq, const float *v0, float *out, int ldo, i
     cudaStream_t st = as_stream(stream);
     const size_t n = (size_t)M * N;
     KernelTimer kt("gate_fwd", st);
-    gate_fwd_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(q, ldq, v0, out, ldo, M, N);
+    (void)launch_pdl(gate_fwd_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, st, 1, q,
+                     ldq, v0, out, ldo, M, N);
     DC_CUDA_TRY(cudaGetLastError());
     return DC_OK;
 }
@@ -259,7 +277,9 @@ int dc_gate_bwd(const float *q, int ldq, const float *v0, const float *dz, int l
     const int rows = (M + rsplit - 1) / rsplit;
     rsplit = (M + rows - 1) / rows;
     KernelTimer kt("gate_bwd", st);
-    gate_bwd_kernel<<<dim3(cb, rsplit), 256, 0, st>>>(q, ldq, v0, dz, ldz, dq, lddq, dv0, M, N,
+    (void)launch_pdl(gate_bwd_kernel, dim3(cb, rsplit), dim3(256), 0, st, 1, q, ldq, v0, dz, ldz,
+                     dq, lddq,
+                     dv0, M, N,
                                                       rows);
     DC_CUDA_TRY(cudaGetLastError());
     return DC_OK;
@@ -275,8 +295,9 @@ int dc_greedy_embed(const float *logits, int ldl, int B, int V, const float *wte
     if (x && (!wte || !wpe || D <= 0)) return fail(DC_ERR_INVALID, "embedding tables needed");
     cudaStream_t st = as_stream(stream);
     KernelTimer kt("greedy_embed", st);
-    greedy_embed_kernel<<<B, 256, 0, st>>>(logits, ldl, V, wte, wpe, pos, D, tokens, ldt, x);
-    advance_kernel<<<1, 1, 0, st>>>(pos, ldt, device_status_word());
+    (void)launch_pdl(greedy_embed_kernel, dim3(B), dim3(256), 0, st, 1, logits, ldl, V, wte, wpe,
+                     pos, D, tokens, ldt, x);
+    (void)launch_pdl(advance_kernel, dim3(1), dim3(1), 0, st, 1, pos, ldt, device_status_word());
     DC_CUDA_TRY(cudaGetLastError());
     return DC_OK;
 }

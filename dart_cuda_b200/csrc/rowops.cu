@@ -11,6 +11,7 @@
 #include <mutex>
 
 #include "dc_internal.h"
+#include "dc_ptx.cuh"
 
 namespace dc {
 namespace rows {
@@ -61,6 +62,8 @@ __global__ void ln_fwd_warp(const float *__restrict__ x, const float *__restrict
                             const float *__restrict__ beta, float *__restrict__ y, int R, int C,
                             float eps)
 {
+    grid_dep_wait();  // programmatic dependent launch: inputs are ready
+    grid_dep_launch();
     const int lane = threadIdx.x & 31;
     const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (row >= R) return;
@@ -108,6 +111,8 @@ __global__ void ln_fwd_block(const float *__restrict__ x, const float *__restric
                              const float *__restrict__ beta, float *__restrict__ y, int R, int C,
                              float eps)
 {
+    grid_dep_wait();  // programmatic dependent launch: inputs are ready
+    grid_dep_launch();
     __shared__ float red[32];
     const int row = blockIdx.x;
     const float *xr = x + (size_t)row * C;
@@ -134,6 +139,8 @@ __global__ void ln_bwd_warp(const float *__restrict__ x, const float *__restrict
                             float *__restrict__ part, int R, int C, float eps, int accumulate,
                             int rows_per_cta)
 {
+    grid_dep_wait();  // programmatic dependent launch: inputs are ready
+    grid_dep_launch();
     extern __shared__ float sh[];  // [nwarps][2C]
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
     const int C4 = C >> 2;
@@ -243,6 +250,8 @@ __global__ void ln_bwd_block(const float *__restrict__ x, const float *__restric
                              const float *__restrict__ dy, float *__restrict__ dx,
                              float *__restrict__ part, int R, int C, float eps, int accumulate)
 {
+    grid_dep_wait();  // programmatic dependent launch: inputs are ready
+    grid_dep_launch();
     __shared__ float red[32];
     const int row = blockIdx.x;
     const float *xr = x + (size_t)row * C;
@@ -281,6 +290,8 @@ __global__ void colsum_parts(const float *__restrict__ part, int nparts, int W,
                              float *out0, float *out1, int split,
                              int accumulate)
 {
+    grid_dep_wait();  // programmatic dependent launch: inputs are ready
+    grid_dep_launch();
     const int j = blockIdx.x * blockDim.x + threadIdx.x;
     if (j >= W) return;
     float acc = 0.f;
@@ -293,6 +304,8 @@ __global__ void colsum_parts(const float *__restrict__ part, int nparts, int W,
 __global__ void bias_fwd_vec(const float4 *__restrict__ a, const float4 *__restrict__ b,
                              float4 *__restrict__ out, size_t n4, int N4)
 {
+    grid_dep_wait();  // programmatic dependent launch: inputs are ready
+    grid_dep_launch();
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4;
          i += (size_t)gridDim.x * blockDim.x) {
         const float4 x = a[i], y = b[i % N4];
@@ -302,6 +315,8 @@ __global__ void bias_fwd_vec(const float4 *__restrict__ a, const float4 *__restr
 __global__ void bias_fwd_scalar(const float *__restrict__ a, const float *__restrict__ b,
                                 float *__restrict__ out, size_t n, int N)
 {
+    grid_dep_wait();  // programmatic dependent launch: inputs are ready
+    grid_dep_launch();
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
          i += (size_t)gridDim.x * blockDim.x)
         out[i] = a[i] + b[i % N];
@@ -312,6 +327,8 @@ __global__ void bias_bwd_kernel(const float *__restrict__ dy, float *__restrict_
                                 float *__restrict__ part, int M, int N, int rows_per_cta,
                                 int accumulate)
 {
+    grid_dep_wait();  // programmatic dependent launch: inputs are ready
+    grid_dep_launch();
     __shared__ float red[8][33];
     const int col = blockIdx.x * 32 + threadIdx.x;
     const int r0 = blockIdx.y * rows_per_cta, r1 = min(M, r0 + rows_per_cta);
@@ -340,6 +357,8 @@ __global__ void bias_bwd_vec4(const float4 *__restrict__ dy, float4 *__restrict_
                               float *__restrict__ part, int M, int N4, int rows_per_cta,
                               int accumulate)
 {
+    grid_dep_wait();  // programmatic dependent launch: inputs are ready
+    grid_dep_launch();
     __shared__ float4 red[8][33];
     const int col = blockIdx.x * 32 + threadIdx.x;
     const int r0 = blockIdx.y * rows_per_cta, r1 = min(M, r0 + rows_per_cta);
@@ -420,6 +439,8 @@ __device__ __forceinline__ void online_merge(float &m, float &s, float m2, float
 __global__ void ce_fwd_warp(const float *__restrict__ logits, const int32_t *__restrict__ tgt,
                             float *__restrict__ row_loss, int T, int V, float eps)
 {
+    grid_dep_wait();  // programmatic dependent launch: inputs are ready
+    grid_dep_launch();
     const int lane = threadIdx.x & 31;
     const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (row >= T) return;
@@ -447,6 +468,8 @@ __global__ void ce_fwd_warp(const float *__restrict__ logits, const int32_t *__r
 __global__ void ce_fwd_block(const float *__restrict__ logits, const int32_t *__restrict__ tgt,
                              float *__restrict__ row_loss, int T, int V, float eps)
 {
+    grid_dep_wait();  // programmatic dependent launch: inputs are ready
+    grid_dep_launch();
     __shared__ float rm[32], rs[32], red[32];
     const int row = blockIdx.x;
     const float *xr = logits + (size_t)row * V;
@@ -522,6 +545,8 @@ __global__ void __launch_bounds__(256) ce_fwd_regs(const float *__restrict__ log
                                                    float *__restrict__ row_loss, int T, int V,
                                                    float eps)
 {
+    grid_dep_wait();  // programmatic dependent launch: inputs are ready
+    grid_dep_launch();
     __shared__ float red[32];
     const int row = blockIdx.x;
     const float *xr = logits + (size_t)row * V;
@@ -542,6 +567,8 @@ __global__ void __launch_bounds__(256) ce_bwd_regs(const float *__restrict__ log
                                                    float *__restrict__ grad, int T, int V,
                                                    float eps)
 {
+    grid_dep_wait();  // programmatic dependent launch: inputs are ready
+    grid_dep_launch();
     __shared__ float red[32];
     const int row = blockIdx.x;
     const float *xr = logits + (size_t)row * V;
@@ -572,6 +599,8 @@ __global__ void __launch_bounds__(256) ce_bwd_regs(const float *__restrict__ log
 // mean of the row losses (ce_mean_reduce, engine.cu:829-837), deterministic
 __global__ void mean_kernel(const float *__restrict__ v, int n, float *__restrict__ out)
 {
+    grid_dep_wait();  // programmatic dependent launch: inputs are ready
+    grid_dep_launch();
     __shared__ float red[32];
     float s = 0.f;
     for (int i = threadIdx.x; i < n; i += blockDim.x) s += v[i];
@@ -585,6 +614,8 @@ __global__ void ce_bwd_warp(const float *__restrict__ logits, const int32_t *__r
                             const float *__restrict__ gscale, float *__restrict__ grad, int T,
                             int V, float eps)
 {
+    grid_dep_wait();  // programmatic dependent launch: inputs are ready
+    grid_dep_launch();
     const int lane = threadIdx.x & 31;
     const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (row >= T) return;
@@ -613,6 +644,8 @@ __global__ void ce_bwd_block(const float *__restrict__ logits, const int32_t *__
                              const float *__restrict__ gscale, float *__restrict__ grad, int T,
                              int V, float eps)
 {
+    grid_dep_wait();  // programmatic dependent launch: inputs are ready
+    grid_dep_launch();
     __shared__ float rm[32], rs[32];
     const int row = blockIdx.x;
     const float *xr = logits + (size_t)row * V;
@@ -656,6 +689,8 @@ __global__ void adam_kernel(float *__restrict__ p, const float *__restrict__ g,
                             float *__restrict__ m, float *__restrict__ v, int64_t n, float lr,
                             float b1, float b2, float eps, float wd, float c1, float c2)
 {
+    grid_dep_wait();  // programmatic dependent launch: inputs are ready
+    grid_dep_launch();
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
          i += (int64_t)gridDim.x * blockDim.x) {
         const float gr = g[i];
@@ -685,17 +720,23 @@ static void ce_fwd_launch(const float *logits, const int32_t *targets, float *ro
 {
     const bool regs = V > 1024 && V % 4 == 0 && V <= 16384 && aligned16(logits);
     if (V <= 1024)
-        ce_fwd_warp<<<(T + 7) / 8, 256, 0, st>>>(logits, targets, rows, T, V, eps);
+        (void)launch_pdl(ce_fwd_warp, dim3((T + 7) / 8), dim3(256), 0, st, 1, logits, targets,
+                         rows, T, V, eps);
     else if (regs && V <= 2048)
-        ce_fwd_regs<2><<<T, 256, 0, st>>>(logits, targets, rows, T, V, eps);
+        (void)launch_pdl(ce_fwd_regs<2>, dim3(T), dim3(256), 0, st, 1, logits, targets, rows, T,
+                         V, eps);
     else if (regs && V <= 4096)
-        ce_fwd_regs<4><<<T, 256, 0, st>>>(logits, targets, rows, T, V, eps);
+        (void)launch_pdl(ce_fwd_regs<4>, dim3(T), dim3(256), 0, st, 1, logits, targets, rows, T,
+                         V, eps);
     else if (regs && V <= 8192)
-        ce_fwd_regs<8><<<T, 256, 0, st>>>(logits, targets, rows, T, V, eps);
+        (void)launch_pdl(ce_fwd_regs<8>, dim3(T), dim3(256), 0, st, 1, logits, targets, rows, T,
+                         V, eps);
     else if (regs)
-        ce_fwd_regs<16><<<T, 256, 0, st>>>(logits, targets, rows, T, V, eps);
+        (void)launch_pdl(ce_fwd_regs<16>, dim3(T), dim3(256), 0, st, 1, logits, targets, rows, T,
+                         V, eps);
     else
-        ce_fwd_block<<<T, 256, 0, st>>>(logits, targets, rows, T, V, eps);
+        (void)launch_pdl(ce_fwd_block, dim3(T), dim3(256), 0, st, 1, logits, targets, rows, T, V,
+                         eps);
 }
 
 static void ce_bwd_launch(const float *logits, const int32_t *targets, const float *gscale,
@@ -703,17 +744,23 @@ static void ce_bwd_launch(const float *logits, const int32_t *targets, const flo
 {
     const bool regs = V > 1024 && V % 4 == 0 && V <= 16384 && aligned16(logits) && aligned16(dlogits);
     if (V <= 1024)
-        ce_bwd_warp<<<(T + 7) / 8, 256, 0, st>>>(logits, targets, gscale, dlogits, T, V, eps);
+        (void)launch_pdl(ce_bwd_warp, dim3((T + 7) / 8), dim3(256), 0, st, 1, logits, targets,
+                         gscale, dlogits, T, V, eps);
     else if (regs && V <= 2048)
-        ce_bwd_regs<2><<<T, 256, 0, st>>>(logits, targets, gscale, dlogits, T, V, eps);
+        (void)launch_pdl(ce_bwd_regs<2>, dim3(T), dim3(256), 0, st, 1, logits, targets, gscale,
+                         dlogits, T, V, eps);
     else if (regs && V <= 4096)
-        ce_bwd_regs<4><<<T, 256, 0, st>>>(logits, targets, gscale, dlogits, T, V, eps);
+        (void)launch_pdl(ce_bwd_regs<4>, dim3(T), dim3(256), 0, st, 1, logits, targets, gscale,
+                         dlogits, T, V, eps);
     else if (regs && V <= 8192)
-        ce_bwd_regs<8><<<T, 256, 0, st>>>(logits, targets, gscale, dlogits, T, V, eps);
+        (void)launch_pdl(ce_bwd_regs<8>, dim3(T), dim3(256), 0, st, 1, logits, targets, gscale,
+                         dlogits, T, V, eps);
     else if (regs)
-        ce_bwd_regs<16><<<T, 256, 0, st>>>(logits, targets, gscale, dlogits, T, V, eps);
+        (void)launch_pdl(ce_bwd_regs<16>, dim3(T), dim3(256), 0, st, 1, logits, targets, gscale,
+                         dlogits, T, V, eps);
     else
-        ce_bwd_block<<<T, 256, 0, st>>>(logits, targets, gscale, dlogits, T, V, eps);
+        (void)launch_pdl(ce_bwd_block, dim3(T), dim3(256), 0, st, 1, logits, targets, gscale,
+                         dlogits, T, V, eps);
 }
 
 extern "C" {
@@ -732,15 +779,19 @@ int dc_layernorm_fwd(const float *x, const float *gamma, const float *beta, floa
     const unsigned grid = (unsigned)((R + wpb - 1) / wpb);
     KernelTimer kt("layernorm_fwd", st);
     if (vec && C <= 128)
-        ln_fwd_warp<1><<<grid, 32 * wpb, 0, st>>>(x, gamma, beta, y, R, C, eps);
+        (void)launch_pdl(ln_fwd_warp<1>, dim3(grid), dim3(32 * wpb), 0, st, 1, x, gamma, beta, y,
+                         R, C, eps);
     else if (vec && C <= 256)
-        ln_fwd_warp<2><<<grid, 32 * wpb, 0, st>>>(x, gamma, beta, y, R, C, eps);
+        (void)launch_pdl(ln_fwd_warp<2>, dim3(grid), dim3(32 * wpb), 0, st, 1, x, gamma, beta, y,
+                         R, C, eps);
     else if (vec && C <= 512)
-        ln_fwd_warp<4><<<grid, 32 * wpb, 0, st>>>(x, gamma, beta, y, R, C, eps);
+        (void)launch_pdl(ln_fwd_warp<4>, dim3(grid), dim3(32 * wpb), 0, st, 1, x, gamma, beta, y,
+                         R, C, eps);
     else if (vec && C <= 1024)
-        ln_fwd_warp<8><<<grid, 32 * wpb, 0, st>>>(x, gamma, beta, y, R, C, eps);
+        (void)launch_pdl(ln_fwd_warp<8>, dim3(grid), dim3(32 * wpb), 0, st, 1, x, gamma, beta, y,
+                         R, C, eps);
     else
-        ln_fwd_block<<<R, 256, 0, st>>>(x, gamma, beta, y, R, C, eps);
+        (void)launch_pdl(ln_fwd_block, dim3(R), dim3(256), 0, st, 1, x, gamma, beta, y, R, C, eps);
     DC_CUDA_TRY(cudaGetLastError());
     return DC_OK;
 }
@@ -774,13 +825,16 @@ int dc_layernorm_bwd(const float *x, const float *gamma, const float *dy, float 
     KernelTimer kt("layernorm_bwd", st);
     if (vec) {
         if (C <= 128)
-            ln_bwd_warp<1><<<nparts, 32 * wpb, shbytes, st>>>(x, gamma, dy, dx, part, R, C, eps,
+            (void)launch_pdl(ln_bwd_warp<1>, dim3(nparts), dim3(32 * wpb), shbytes, st, 1, x,
+                             gamma, dy, dx, part, R, C, eps,
                                                               accumulate, rows_per_cta);
         else if (C <= 256)
-            ln_bwd_warp<2><<<nparts, 32 * wpb, shbytes, st>>>(x, gamma, dy, dx, part, R, C, eps,
+            (void)launch_pdl(ln_bwd_warp<2>, dim3(nparts), dim3(32 * wpb), shbytes, st, 1, x,
+                             gamma, dy, dx, part, R, C, eps,
                                                               accumulate, rows_per_cta);
         else if (C <= 512)
-            ln_bwd_warp<4><<<nparts, 32 * wpb, shbytes, st>>>(x, gamma, dy, dx, part, R, C, eps,
+            (void)launch_pdl(ln_bwd_warp<4>, dim3(nparts), dim3(32 * wpb), shbytes, st, 1, x,
+                             gamma, dy, dx, part, R, C, eps,
                                                               accumulate, rows_per_cta);
         else {
             static bool attr = false;
@@ -789,15 +843,18 @@ int dc_layernorm_bwd(const float *x, const float *gamma, const float *dy, float 
                                      (int)shbytes);
                 attr = true;
             }
-            ln_bwd_warp<8><<<nparts, 32 * wpb, shbytes, st>>>(x, gamma, dy, dx, part, R, C, eps,
+            (void)launch_pdl(ln_bwd_warp<8>, dim3(nparts), dim3(32 * wpb), shbytes, st, 1, x,
+                             gamma, dy, dx, part, R, C, eps,
                                                               accumulate, rows_per_cta);
         }
     } else {
-        ln_bwd_block<<<R, 256, 0, st>>>(x, gamma, dy, dx, part, R, C, eps, accumulate);
+        (void)launch_pdl(ln_bwd_block, dim3(R), dim3(256), 0, st, 1, x, gamma, dy, dx, part, R, C,
+                         eps, accumulate);
     }
     if (cudaGetLastError() != cudaSuccess) rc = fail(DC_ERR_CUDA, "layernorm bwd launch failed");
     if (rc == DC_OK) {
-        colsum_parts<<<(2 * C + 255) / 256, 256, 0, st>>>(part, nparts, 2 * C, dgamma, dbeta, C,
+        (void)launch_pdl(colsum_parts, dim3((2 * C + 255) / 256), dim3(256), 0, st, 1, part,
+                         nparts, 2 * C, dgamma, dbeta, C,
                                                           accumulate);
         if (cudaGetLastError() != cudaSuccess)
             rc = fail(DC_ERR_CUDA, "layernorm colsum launch failed");
@@ -817,10 +874,11 @@ int dc_bias_fwd(const float *a, const float *b, float *out, int M, int N, void *
     const int blocks = (int)std::min<size_t>((n + 1023) / 1024, (size_t)sm_count() * 8);
     KernelTimer kt("bias_fwd", st);
     if (N % 4 == 0 && aligned16(a) && aligned16(b) && aligned16(out))
-        bias_fwd_vec<<<blocks, 256, 0, st>>>((const float4 *)a, (const float4 *)b, (float4 *)out,
+        (void)launch_pdl(bias_fwd_vec, dim3(blocks), dim3(256), 0, st, 1, (const float4 *)a,
+                         (const float4 *)b, (float4 *)out,
                                               n / 4, N / 4);
     else
-        bias_fwd_scalar<<<blocks, 256, 0, st>>>(a, b, out, n, N);
+        (void)launch_pdl(bias_fwd_scalar, dim3(blocks), dim3(256), 0, st, 1, a, b, out, n, N);
     DC_CUDA_TRY(cudaGetLastError());
     return DC_OK;
 }
@@ -842,13 +900,16 @@ int dc_bias_bwd(const float *dy, float *da, float *db, int M, int N, int accumul
     DC_CUDA_TRY(cudaMallocAsync(&part, (size_t)rblocks * N * sizeof(float), st));
     KernelTimer kt("bias_bwd", st);
     if (vec)
-        bias_bwd_vec4<<<dim3(cblocks, rblocks), dim3(32, 8), 0, st>>>(
+        (void)launch_pdl(bias_bwd_vec4, dim3(cblocks, rblocks), dim3(32, 8), 0, st, 1,
             reinterpret_cast<const float4 *>(dy), reinterpret_cast<float4 *>(da), part, M, N / 4,
             rows_per_cta, accumulate);
     else
-        bias_bwd_kernel<<<dim3(cblocks, rblocks), dim3(32, 8), 0, st>>>(dy, da, part, M, N,
+        (void)launch_pdl(bias_bwd_kernel, dim3(cblocks, rblocks), dim3(32, 8), 0, st, 1, dy, da,
+                         part, M,
+                         N,
                                                                          rows_per_cta, accumulate);
-    colsum_parts<<<(N + 255) / 256, 256, 0, st>>>(part, rblocks, N, db, db, N, accumulate);
+    (void)launch_pdl(colsum_parts, dim3((N + 255) / 256), dim3(256), 0, st, 1, part, rblocks, N,
+                     db, db, N, accumulate);
     cudaError_t e = cudaGetLastError();
     cudaFreeAsync(part, st);
     if (e != cudaSuccess) return fail(DC_ERR_CUDA, "bias bwd: %s", cudaGetErrorString(e));
@@ -867,7 +928,7 @@ int dc_ce_fwd(const float *logits, const int32_t *targets, float *loss, float *r
     if (!rows) DC_CUDA_TRY(cudaMallocAsync(&rows, (size_t)T * sizeof(float), st));
     KernelTimer kt("ce_fwd", st);
     ce_fwd_launch(logits, targets, rows, T, V, eps, st);
-    mean_kernel<<<1, 1024, 0, st>>>(rows, T, loss);
+    (void)launch_pdl(mean_kernel, dim3(1), dim3(1024), 0, st, 1, rows, T, loss);
     cudaError_t e = cudaGetLastError();
     if (!row_loss) cudaFreeAsync(rows, st);
     if (e != cudaSuccess) return fail(DC_ERR_CUDA, "ce fwd: %s", cudaGetErrorString(e));
@@ -928,7 +989,7 @@ int dc_ce_fwd_noalloc(const float *logits, const int32_t *targets, float *loss, 
     if (!rows) return fail(DC_ERR_CUDA, "dc_ce_fwd_noalloc: cannot resolve the scratch array address");
     cudaStream_t st = as_stream(stream);
     ce_fwd_launch(logits, targets, rows, T, V, eps, st);
-    mean_kernel<<<1, 1024, 0, st>>>(rows, T, loss);
+    (void)launch_pdl(mean_kernel, dim3(1), dim3(1024), 0, st, 1, rows, T, loss);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fail(DC_ERR_CUDA, "ce fwd noalloc: %s", cudaGetErrorString(e));
     return DC_OK;
@@ -959,7 +1020,8 @@ int dc_adam_step(float *p, const float *g, float *m, float *v, int64_t n, int t,
     const float c1 = 1.0f - powf(b1, step), c2 = 1.0f - powf(b2, step);
     const int blocks = (int)std::min<int64_t>((n + 255) / 256, (int64_t)sm_count() * 8);
     KernelTimer kt("adam", as_stream(stream));
-    adam_kernel<<<blocks, 256, 0, as_stream(stream)>>>(p, g, m, v, n, lr, b1, b2, eps,
+    (void)launch_pdl(adam_kernel, dim3(blocks), dim3(256), 0, as_stream(stream), 1, p, g, m, v, n,
+                     lr, b1, b2, eps,
                                                        weight_decay, c1, c2);
     DC_CUDA_TRY(cudaGetLastError());
     return DC_OK;

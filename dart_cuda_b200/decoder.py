@@ -378,7 +378,7 @@ class AftDecoder:
         z = lambda *s: torch.zeros(*s, device=dev)
         s = {"B": B}
         s["cache"] = [z(Tm, B * d * 2) for _ in range(c.n_layers)]
-        s["x"], s["a"], s["x1"], s["x2"], s["zd"], s["qc"], s["cg"] = (z(B, d) for _ in range(7))
+        s["x"], s["a"], s["zd"], s["qc"], s["cg"] = (z(B, d) for _ in range(5))
         s["qkv"], s["h"] = z(B, 3 * d), z(B, F)
         s["logits"] = z(B, c.vocab)
         s["v0"] = [self.P[f"{l}.bcv"] for l in range(c.n_layers)]
@@ -431,14 +431,16 @@ class AftDecoder:
             check(lib().dc_aft_decode(s["qkv"].data_ptr(), 3 * d, P[f"{l}.pos"].data_ptr(), Tm, Tm * Tm,
                                       s["cache"][l].data_ptr(), B, c.n_heads, hs, s["pos"].data_ptr(), Tm,
                                       s["zd"].data_ptr(), d, s["ws"].data_ptr(), s["ws_bytes"], st), "dc_aft_decode")
-            ops.gemm(s["zd"], P[f"{l}.wo"], out=s["x1"], bias=P[f"{l}.bo"], residual=x)
-            ops.layernorm_fwd(s["x1"], P[f"{l}.ln2g"], P[f"{l}.ln2b"], out=s["a"])
+            # residual adds in place on x (the step keeps no activations), so a
+            # split-K GEMM starts from x itself rather than from a copy
+            ops.gemm(s["zd"], P[f"{l}.wo"], out=x, bias=P[f"{l}.bo"], residual=x)
+            ops.layernorm_fwd(x, P[f"{l}.ln2g"], P[f"{l}.ln2b"], out=s["a"])
             ops.gemm(s["a"], P[f"{l}.wcq"], out=s["qc"], bias=P[f"{l}.bcq"])
             self._gate(s["qc"], s["v0"][l], s["cg"])
-            ops.gemm(s["cg"], P[f"{l}.wco"], out=s["x2"], bias=P[f"{l}.bco"], residual=s["x1"])
-            ops.layernorm_fwd(s["x2"], P[f"{l}.ln3g"], P[f"{l}.ln3b"], out=s["a"])
+            ops.gemm(s["cg"], P[f"{l}.wco"], out=x, bias=P[f"{l}.bco"], residual=x)
+            ops.layernorm_fwd(x, P[f"{l}.ln3g"], P[f"{l}.ln3b"], out=s["a"])
             ops.gemm(s["a"], P[f"{l}.w1"], out=s["h"], bias=P[f"{l}.b1"], gelu=True)
-            ops.gemm(s["h"], P[f"{l}.w2"], out=x, bias=P[f"{l}.b2"], residual=s["x2"])
+            ops.gemm(s["h"], P[f"{l}.w2"], out=x, bias=P[f"{l}.b2"], residual=x)
         ops.layernorm_fwd(x, P["lnfg"], P["lnfb"], out=s["a"])
         ops.gemm(s["a"], P["wlm"][:, : c.vocab], out=s["logits"], bias=P["blm"])
         self._greedy(s)
