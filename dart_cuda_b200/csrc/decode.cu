@@ -50,7 +50,7 @@ struct Params {
     float *cache;      // [Tmax][B*D/4][8]
     int B, H, hs, D, Tmax;
     const int *pos;    // device: the position t being decoded
-    int rows;          // history rows per chunk (multiple of kGroup)
+    int rows;          // history rows per chunk (multiple of kGroup), set on the device
     int *status;
     int t, chunks;     // set on the device from *pos
     float *Z;
@@ -71,6 +71,9 @@ __global__ void __launch_bounds__(kThreads) aft_decode_kernel(Params p)
         if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) atomicOr(p.status, 0x40);
         return;
     }
+    // the t+1 history rows split evenly over the grid's chunks, so every
+    // block streams about the same number of rows whatever t is
+    p.rows = ((p.t + (int)gridDim.y) / (int)gridDim.y + kGroup - 1) / kGroup * kGroup;
     p.chunks = p.t / p.rows + 1;
     if ((int)blockIdx.y >= p.chunks) return;
     const int cols = p.B * p.D;
@@ -279,13 +282,14 @@ int dc_aft_decode(const float *qkv, int ldq, const float *w, int ldw, long long 
         return fail(DC_ERR_UNSUPPORTED, "more than %d heads per %d-column slab", kMaxHeads, kSlab);
     const int cols = B * D;
     const int slabs = (cols + kSlab - 1) / kSlab;
-    // history chunks: about two blocks per SM at full length, at most
-    // kMaxChunks per slab, a multiple of kGroup rows each
-    const int want = std::min(kMaxChunks, std::max(1, (2 * sm_count() + slabs - 1) / slabs));
-    int rows = std::max(kGroup, (Tmax + want - 1) / want);
-    rows = (rows + kGroup - 1) / kGroup * kGroup;
-    if (rows > kMaxRows) return fail(DC_ERR_UNSUPPORTED, "Tmax %d above %d", Tmax, kMaxRows * kMaxChunks);
-    const int max_chunks = (Tmax + rows - 1) / rows;
+    // history chunks: the grid holds about two blocks per SM (slabs x
+    // chunks); the kernel splits the t+1 rows of each step over them, at
+    // most kMaxRows rows a chunk
+    const int min_chunks = (Tmax + kMaxRows - 1) / kMaxRows;
+    if (min_chunks > kMaxChunks)
+        return fail(DC_ERR_UNSUPPORTED, "Tmax %d above %d", Tmax, kMaxRows * kMaxChunks);
+    const int max_chunks =
+        std::min(kMaxChunks, std::max(min_chunks, std::max(1, 2 * sm_count() / slabs)));
     Params p{};
     p.qkv = qkv;
     p.ldq = ldq;
@@ -299,7 +303,6 @@ int dc_aft_decode(const float *qkv, int ldq, const float *w, int ldw, long long 
     p.D = D;
     p.Tmax = Tmax;
     p.pos = pos;
-    p.rows = rows;
     p.status = device_status_word();
     p.Z = Z;
     p.ldz = ldz;
