@@ -85,6 +85,7 @@ struct Params {
     int n_tiles;      // tensor-core path: number of output tiles of the launch
     int kpb;          // WGRAD: K steps per batch element (dp / BKe)
     int bundled;      // FWD/BWD1/HGRAD: tiles dealt in equal-work bundles of two
+    int n_full;       // FWD/BWD1/HGRAD without bundles: units before the half tiles
     int splits;       // WGRAD: split-K factor
     int sk_tiles;     // WGRAD: dW tiles
     int sk_lo;        // WGRAD: leading tiles that also run a low-part pass
@@ -794,9 +795,25 @@ static int launch_tc(Params p, const Layout &L, char *ws, cudaStream_t st)
     }
     const int workers = P ? std::max(1, max_clusters[dev] - (p.spare_sms + 1) / 2)
                           : std::max(1, sm_count() - p.spare_sms);
-    // bundles only pay with at least two tiles a worker: with fewer they
-    // would leave workers idle (decode_tile)
-    p.bundled = MODE != WGRAD && p.n_tiles >= 2 * workers;
+    // Schedule (decode_tile): bundles only pay with at least two tiles a
+    // worker (with fewer they would leave workers idle).  Where whole rounds
+    // leave a partial last one, its tiles can run as halves spread over all
+    // workers instead, when that shortens the schedule (counting a half as
+    // half a tile; single CTAs with two B tiles a stage).
+    p.bundled = 0;
+    p.n_full = p.n_tiles;
+    if (MODE != WGRAD) {
+        const int U = p.n_tiles;
+        const double rounds = (double)((U + workers - 1) / workers);
+        const int F = U / workers * workers, R = U - F;
+        const double with_halves = (double)(U / workers) + 0.5 * ((2 * R + workers - 1) / workers);
+        if (C::HALF_OK && R > 0 && with_halves < 0.95 * rounds) {
+            p.n_full = F;
+            p.n_tiles = F + 2 * R;
+        } else {
+            p.bundled = U >= 2 * workers;
+        }
+    }
     const dim3 grid((P ? 2 : 1) * std::max(1, std::min(p.n_tiles, workers)));
     {
         KernelTimer kt(names[MODE], st);

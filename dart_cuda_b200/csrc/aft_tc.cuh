@@ -75,6 +75,10 @@ struct TcCfg {
     static constexpr uint32_t A_MN = H ? 1 : 0;
     static constexpr uint32_t B_MN = W ? 0 : 1;
     static constexpr uint32_t IDESC = umma_idesc(TF32 ? 2u : 1u, P ? 2 * BM : BM, MMA_N, A_MN, B_MN);
+    // half tiles: 64 of a tile's BN columns, one N = 128 MMA over [num | den]
+    // (single CTAs with the two B tiles of a stage; see decode_tile)
+    static constexpr bool HALF_OK = !W && !P && NB == 2;
+    static constexpr uint32_t IDESC_HALF = umma_idesc(TF32 ? 2u : 1u, BM, BN, A_MN, B_MN);
     static_assert(!P || !TF32, "CTA pairs run bf16 operands");
     static constexpr uint32_t MN_LBO = BKe * 128;      // bytes between 128 B MN blocks
     static constexpr uint32_t MN_LAYOUT = TF32 ? 1u : 2u;
@@ -450,6 +454,7 @@ struct Tile {
     int b, mrow, ncol;  // mrow/ncol: 128-row block of the accumulator / column block
     int k0, k1;         // K steps [k0, k1); WGRAD: of the tile's passes laid end to end
     int kt;             // WGRAD: K steps of one pass (steps from kt on read the low parts)
+    int half;           // -1: all BN columns; 0 or 1: that half of them (N = 128 MMA)
 };
 
 // dW tiles of a causal launch: row block r holds r/2 + 1 column pairs, so
@@ -468,14 +473,16 @@ __device__ __forceinline__ Tile decode_tile(const Params &p, int idx)
     constexpr int RB = P ? 2 * BM : BM;
     Tile t{};
     t.kt = 0x7fffffff;
+    t.half = -1;
     if (MODE != WGRAD) {
         // Tiles in bundles of two of one group g = (b, column block d): row
         // levels q and nm-1-q, whose K lengths sum to the same total for every
         // q (causal; all equal otherwise), heavy tile first.  Bundles run
         // group-major; with nm odd the middle-level tiles of all groups follow,
         // paired with each other.
-        // Without bundles (fewer than two tiles a worker) the tiles come
-        // heavy level first, one per unit.
+        // Without bundles the tiles come heavy level first, one per unit;
+        // units from n_full on are halves of the remaining (lightest) tiles,
+        // which spread a last, partial round over all workers.
         const int nd = p.dp / BN;
         const int nm = (MODE == HGRAD ? p.Tkp : p.Tqp) / RB;
         const int nb = nm / 2;
@@ -483,8 +490,13 @@ __device__ __forceinline__ Tile decode_tile(const Params &p, int idx)
         const int u = idx >> 1;
         int g, level;  // level 0 = the lightest row level
         if (!p.bundled) {
-            g = idx % (nd * p.B);
-            level = nm - 1 - idx / (nd * p.B);
+            int tt = idx;
+            if (idx >= p.n_full) {
+                tt = p.n_full + ((idx - p.n_full) >> 1);
+                t.half = (idx - p.n_full) & 1;
+            }
+            g = tt % (nd * p.B);
+            level = nm - 1 - tt / (nd * p.B);
         } else if (u < bundles) {
             g = u / nb;
             const int q = u % nb;
@@ -685,7 +697,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     }
                     // both CTAs' copies complete on the even CTA's barrier
                     const uint32_t fb = P ? smem_in_cta(smem_u32(&full[s]), 0) : smem_u32(&full[s]);
-                    if (leader) mbar_arrive_expect_tx(smem_u32(&full[s]), (P ? 2 : 1) * C::STAGE_BYTES);
+                    // a half tile loads half of each B tile
+                    const int bytes = C::STAGE_BYTES - (tl.half >= 0 ? C::TILE_B : 0);
+                    if (leader) mbar_arrive_expect_tx(smem_u32(&full[s]), (P ? 2 : 1) * bytes);
                     const uint32_t sa = smem_u32(smem + s * C::STAGE_BYTES);
                     const uint32_t sb = sa + C::NA * C::TILE_BYTES;
                     if (MODE == FWD || MODE == BWD1 || MODE == HGRAD) {
@@ -699,16 +713,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                             ld2(sa, &mapA, fb, k * C::BKe, m0);
                         }
                         // B: [PV | PE] or [G | N] (then [G lo | N lo]) [K rows, d cols]
-                        // MN-major, one BN-column tile each; a pair splits them
+                        // MN-major, one BN-column tile each; a pair splits them.
+                        // A half tile loads its half of both, the second right
+                        // after the first (one N = 128 operand).
+                        const int nbx = (tl.half >= 0 ? BN / 2 : BN) / C::BOX_MN;
+                        const int x0 = tl.ncol * BN + (tl.half > 0 ? BN / 2 : 0);
 #pragma unroll
                         for (int j = 0; j < BN / C::BOX_MN; ++j) {
-                            const int x = tl.ncol * BN + j * C::BOX_MN;
+                            if (j >= nbx) break;
+                            const int x = x0 + j * C::BOX_MN;
                             const uint32_t o = sb + j * C::MN_LBO;
                             if (P) {
                                 ld3(o, rank ? &mapB2 : &mapB1, fb, x, k * C::BKe, tl.b);
                             } else {
                                 ld3(o, &mapB1, fb, x, k * C::BKe, tl.b);
-                                ld3(o + C::TILE_B, &mapB2, fb, x, k * C::BKe, tl.b);
+                                ld3(o + nbx * C::MN_LBO, &mapB2, fb, x, k * C::BKe, tl.b);
                                 if (C::NB == 4) {
                                     ld3(o + 2 * C::TILE_B, &mapB3, fb, x, k * C::BKe, tl.b);
                                     ld3(o + 3 * C::TILE_B, &mapB4, fb, x, k * C::BKe, tl.b);
@@ -738,11 +757,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
     } else if (warp == kEpiWarps + 1) {
         // ------------------------------------------------ MMA issuer (even CTA of a pair)
-        auto mma = [&](uint32_t d, uint64_t a, uint64_t b, uint32_t acc_on) {
+        auto mma = [&](uint32_t d, uint64_t a, uint64_t b, uint32_t acc_on,
+                       uint32_t idesc = C::IDESC) {
             if constexpr (P)
-                umma_pair(d, a, b, C::IDESC, acc_on);
+                umma_pair(d, a, b, idesc, acc_on);
             else
-                umma<C::TF32>(d, a, b, C::IDESC, acc_on);
+                umma<C::TF32>(d, a, b, idesc, acc_on);
         };
         auto commit = [&](uint32_t bar) {
             if constexpr (P)
@@ -798,7 +818,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                             // acc[:, 0:2BN] = [num | den]: one N = 256 MMA over the
                             // two adjacent B tiles (their MN blocks are MN_LBO apart)
                             const uint64_t b = sw128_desc(sb + moff, C::MN_LBO, C::MN_SBO, C::MN_LAYOUT);
-                            mma(acc, a, b, first);
+                            mma(acc, a, b, first, tl.half >= 0 ? C::IDESC_HALF : C::IDESC);
                             if (C::NB == 4) {
                                 const uint64_t bl = sw128_desc(sb + 2 * C::TILE_B + moff, C::MN_LBO,
                                                                C::MN_SBO, C::MN_LAYOUT);
@@ -834,7 +854,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const uint32_t buf = j & 1, use = j >> 1;
             // t (FWD, BWD1, WGRAD) or i (HGRAD): this CTA's 128 rows of the tile
             const int r = (P ? 2 * tl.mrow + (int)rank : tl.mrow) * BM + row;
-            const int cb0 = tl.ncol * C::WN;  // first column (d, or i for WGRAD)
+            // first column (d, or i for WGRAD); a half tile's 64 columns hold
+            // num and den at accumulator columns 0 and 64 (else 0 and BN)
+            const int cb0 = tl.ncol * C::WN + (tl.half > 0 ? BN / 2 : 0);
+            const int nsb = tl.half >= 0 ? NSB / 2 : NSB;
+            const uint32_t dofs = tl.half >= 0 ? BN / 2 : BN;
             // element-wise inputs requested while the main loop still runs
             EpiPre pf[C::W ? 1 : MAXK];
             if constexpr (!C::W) {
@@ -842,7 +866,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 for (int k = 0; k < MAXK; ++k) {
                     const int sb = slice + k * QW;
                     pf[k].ok = false;
-                    if (sb < NSB) epi_prefetch<MODE, IO>(p, tl.b, r, cb0 + sb * 16, pf[k]);
+                    if (sb < nsb) epi_prefetch<MODE, IO>(p, tl.b, r, cb0 + sb * 16, pf[k]);
                 }
             }
             // warp-uniform, because the TMEM loads below are warp-collective
@@ -864,10 +888,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
                 for (int k = 0; k < MAXK; ++k) {
                     const int sb = slice + k * QW;  // warp-uniform
-                    if (sb >= NSB) break;
+                    if (sb >= nsb) break;
                     float v1[16], v2[16];
                     tmem_ld16(lane_addr + sb * 16, v1);
-                    tmem_ld16(lane_addr + BN + sb * 16, v2);
+                    tmem_ld16(lane_addr + dofs + sb * 16, v2);
                     const int c0 = cb0 + sb * 16;
                     if (MODE == FWD)
                         epi16_fwd<IO, E>(p, tl.b, r, c0, v1, v2, pf[k]);

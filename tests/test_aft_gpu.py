@@ -222,6 +222,24 @@ def test_split_backward(ops, dev, dtype, B, T, D, save):
     assert ops.device_status() == 0
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_half_tiles(ops, dev, dtype):
+    """160 tiles of 128 rows on 148 workers: the 12 left after a full round
+    run as 24 half tiles (64 columns each); the results still meet the
+    oracle."""
+    B, T, D = 40, 512, 128
+    Q, K, V, W, dZ = make_inputs(24, B, T, T, D)
+    tq, tk, tv, tg = to_dev(dev, dtype, Q, K, V, dZ)
+    tw = torch.from_numpy(W).to(dev)
+    Z = ops.aft_fwd(tq, tk, tv, tw, causal=True)
+    g = ops.aft_bwd(tq, tk, tv, tw, tg, causal=True)
+    Qr, Kr, Vr, dZr = rounded(dtype, Q, K, V, dZ)
+    ref = oracle_ref(Qr, Kr, Vr, W, dZr, True)
+    errs = {n: relerr(x.float().cpu().numpy(), r) for n, x, r in zip(("Z", "dQ", "dK", "dV", "dW"), (Z,) + tuple(g), ref)}
+    assert_errs(errs, TOL[dtype])
+    assert ops.device_status() == 0
+
+
 def test_split_backward_rejects_misuse(ops, dev):
     from dart_cuda_b200 import DcError
 
