@@ -77,6 +77,20 @@ def test_skinny_split_k(ops, M, N, K):
     assert rel(acc, A.double().cpu() @ ref_B + R.double().cpu()) < TOL[torch.float32]
 
 
+@pytest.mark.parametrize("M,N,K", [(64, 2048, 512), (1, 100, 40), (3, 36, 1000)])
+def test_skinny_gelu_alpha(ops, M, N, K):
+    """Few rows (the decode step's layers): GELU with the pre-activation
+    kept, a bias and alpha, in one pass (GELU is never split along K)."""
+    A = torch.randn(M, K).cuda()
+    B = torch.randn(K, N).cuda()
+    bias = torch.randn(N).cuda()
+    aux = torch.empty(M, N).cuda()
+    C = ops.gemm(A, B, bias=bias, gelu=True, gelu_aux=aux, alpha=0.5)
+    pre = 0.5 * (A.double().cpu() @ B.double().cpu()) + bias.double().cpu()
+    assert rel(aux, pre) < TOL[torch.float32]
+    assert rel(C, gelu64(pre)) < TOL[torch.float32]
+
+
 def test_gelu_and_its_backward(ops):
     M, N, K = 512, 1024, 256
     A, B, ref = operands(M, N, K, False, False, torch.float32, seed=3)
