@@ -278,9 +278,7 @@ int dc_gate_bwd(const float *q, int ldq, const float *v0, const float *dz, int l
     rsplit = (M + rows - 1) / rows;
     KernelTimer kt("gate_bwd", st);
     (void)launch_pdl(gate_bwd_kernel, dim3(cb, rsplit), dim3(256), 0, st, 1, q, ldq, v0, dz, ldz,
-                     dq, lddq,
-                     dv0, M, N,
-                                                      rows);
+                     dq, lddq, dv0, M, N, rows);
     DC_CUDA_TRY(cudaGetLastError());
     return DC_OK;
 }

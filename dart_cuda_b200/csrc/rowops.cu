@@ -826,16 +826,13 @@ int dc_layernorm_bwd(const float *x, const float *gamma, const float *dy, float 
     if (vec) {
         if (C <= 128)
             (void)launch_pdl(ln_bwd_warp<1>, dim3(nparts), dim3(32 * wpb), shbytes, st, 1, x,
-                             gamma, dy, dx, part, R, C, eps,
-                                                              accumulate, rows_per_cta);
+                             gamma, dy, dx, part, R, C, eps, accumulate, rows_per_cta);
         else if (C <= 256)
             (void)launch_pdl(ln_bwd_warp<2>, dim3(nparts), dim3(32 * wpb), shbytes, st, 1, x,
-                             gamma, dy, dx, part, R, C, eps,
-                                                              accumulate, rows_per_cta);
+                             gamma, dy, dx, part, R, C, eps, accumulate, rows_per_cta);
         else if (C <= 512)
             (void)launch_pdl(ln_bwd_warp<4>, dim3(nparts), dim3(32 * wpb), shbytes, st, 1, x,
-                             gamma, dy, dx, part, R, C, eps,
-                                                              accumulate, rows_per_cta);
+                             gamma, dy, dx, part, R, C, eps, accumulate, rows_per_cta);
         else {
             static bool attr = false;
             if (!attr) {
@@ -844,8 +841,7 @@ int dc_layernorm_bwd(const float *x, const float *gamma, const float *dy, float 
                 attr = true;
             }
             (void)launch_pdl(ln_bwd_warp<8>, dim3(nparts), dim3(32 * wpb), shbytes, st, 1, x,
-                             gamma, dy, dx, part, R, C, eps,
-                                                              accumulate, rows_per_cta);
+                             gamma, dy, dx, part, R, C, eps, accumulate, rows_per_cta);
         }
     } else {
         (void)launch_pdl(ln_bwd_block, dim3(R), dim3(256), 0, st, 1, x, gamma, dy, dx, part, R, C,
@@ -854,8 +850,7 @@ int dc_layernorm_bwd(const float *x, const float *gamma, const float *dy, float 
     if (cudaGetLastError() != cudaSuccess) rc = fail(DC_ERR_CUDA, "layernorm bwd launch failed");
     if (rc == DC_OK) {
         (void)launch_pdl(colsum_parts, dim3((2 * C + 255) / 256), dim3(256), 0, st, 1, part,
-                         nparts, 2 * C, dgamma, dbeta, C,
-                                                          accumulate);
+                         nparts, 2 * C, dgamma, dbeta, C, accumulate);
         if (cudaGetLastError() != cudaSuccess)
             rc = fail(DC_ERR_CUDA, "layernorm colsum launch failed");
     }
@@ -875,8 +870,7 @@ int dc_bias_fwd(const float *a, const float *b, float *out, int M, int N, void *
     KernelTimer kt("bias_fwd", st);
     if (N % 4 == 0 && aligned16(a) && aligned16(b) && aligned16(out))
         (void)launch_pdl(bias_fwd_vec, dim3(blocks), dim3(256), 0, st, 1, (const float4 *)a,
-                         (const float4 *)b, (float4 *)out,
-                                              n / 4, N / 4);
+                         (const float4 *)b, (float4 *)out, n / 4, N / 4);
     else
         (void)launch_pdl(bias_fwd_scalar, dim3(blocks), dim3(256), 0, st, 1, a, b, out, n, N);
     DC_CUDA_TRY(cudaGetLastError());
@@ -901,13 +895,11 @@ int dc_bias_bwd(const float *dy, float *da, float *db, int M, int N, int accumul
     KernelTimer kt("bias_bwd", st);
     if (vec)
         (void)launch_pdl(bias_bwd_vec4, dim3(cblocks, rblocks), dim3(32, 8), 0, st, 1,
-            reinterpret_cast<const float4 *>(dy), reinterpret_cast<float4 *>(da), part, M, N / 4,
-            rows_per_cta, accumulate);
+                         reinterpret_cast<const float4 *>(dy), reinterpret_cast<float4 *>(da),
+                         part, M, N / 4, rows_per_cta, accumulate);
     else
         (void)launch_pdl(bias_bwd_kernel, dim3(cblocks, rblocks), dim3(32, 8), 0, st, 1, dy, da,
-                         part, M,
-                         N,
-                                                                         rows_per_cta, accumulate);
+                         part, M, N, rows_per_cta, accumulate);
     (void)launch_pdl(colsum_parts, dim3((N + 255) / 256), dim3(256), 0, st, 1, part, rblocks, N,
                      db, db, N, accumulate);
     cudaError_t e = cudaGetLastError();
@@ -1021,8 +1013,7 @@ int dc_adam_step(float *p, const float *g, float *m, float *v, int64_t n, int t,
     const int blocks = (int)std::min<int64_t>((n + 255) / 256, (int64_t)sm_count() * 8);
     KernelTimer kt("adam", as_stream(stream));
     (void)launch_pdl(adam_kernel, dim3(blocks), dim3(256), 0, as_stream(stream), 1, p, g, m, v, n,
-                     lr, b1, b2, eps,
-                                                       weight_decay, c1, c2);
+                     lr, b1, b2, eps, weight_decay, c1, c2);
     DC_CUDA_TRY(cudaGetLastError());
     return DC_OK;
 }
