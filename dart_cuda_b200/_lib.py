@@ -14,6 +14,7 @@ PKG = Path(__file__).resolve().parent
 LIB_PATH = Path(os.environ.get("DART_CUDA_B200_LIB", PKG / "lib" / "libmat_mul.so"))
 
 DC_OK = 0
+DC_ERR_INVALID = 1
 DC_F32 = 0
 DC_BF16 = 1
 DC_AFT_CAUSAL = 0x1

@@ -72,3 +72,27 @@ def test_exports_reference_symbol_union():
     missing = [n for n in REFERENCE_UNION if not hasattr(lib, n)]
     assert not missing, missing
     assert set(REFERENCE_UNION) <= set(declared_functions())
+
+
+def test_split_backward_flags_are_validated_on_the_host():
+    """The two-part backward's flag rules are checked before any CUDA call,
+    so misuse fails the same way on a machine without a GPU."""
+    from dart_cuda_b200 import _lib
+
+    lib = _lib.lib()
+    fake = 0x1000  # never dereferenced: validation returns first
+    base = _lib.DC_AFT_CAUSAL
+
+    def bwd(flags, dQ=fake, dK=fake, dV=fake, dW=fake):
+        return lib.dc_aft_bwd(fake, fake, fake, fake, 128, fake, dQ, dK, dV, dW, 1, 128, 128, 64,
+                              _lib.DC_BF16, flags, None, 0, None)
+
+    both = base | _lib.DC_AFT_BWD_NO_DKDV | _lib.DC_AFT_BWD_DKDV | _lib.DC_AFT_WS_VALID
+    assert bwd(both) == _lib.DC_ERR_INVALID
+    assert b"together" in lib.dc_last_error()
+    assert bwd(base | _lib.DC_AFT_BWD_DKDV) == _lib.DC_ERR_INVALID  # needs the first part's workspace
+    assert b"WS_VALID" in lib.dc_last_error()
+    dkdv = base | _lib.DC_AFT_BWD_DKDV | _lib.DC_AFT_WS_VALID
+    assert bwd(dkdv, dK=None) == _lib.DC_ERR_INVALID
+    assert bwd(base | _lib.DC_AFT_BWD_NO_DKDV, dW=None) == _lib.DC_ERR_INVALID
+    assert _lib.DC_AFT_SPARE_SMS(48) == 48 << 16 and _lib.DC_AFT_SPARE_SMS(300) == (300 & 0xFF) << 16
