@@ -86,6 +86,7 @@ struct Params {
     int kpb;          // WGRAD: K steps per batch element (dp / BKe)
     int bundled;      // FWD/BWD1/HGRAD: tiles dealt in equal-work bundles of two
     int n_full;       // FWD/BWD1/HGRAD without bundles: units before the half tiles
+    int zero_dw;      // BWD1 / saved-statistics kernel: also zero dW[Tq][Tk] (stride ldw)
     int splits;       // WGRAD: split-K factor
     int sk_tiles;     // WGRAD: dW tiles
     int sk_lo;        // WGRAD: leading tiles that also run a low-part pass
@@ -508,6 +509,8 @@ __global__ void __launch_bounds__(256) bwd_stats_kernel(const Params p)
 {
     grid_dep_wait();  // launched early (programmatic dependent launch)
     grid_dep_launch();
+    if (p.zero_dw)
+        zero_dw(p, (size_t)blockIdx.x * blockDim.x + threadIdx.x, (size_t)gridDim.x * blockDim.x);
     const int groups = p.dp / 16;
     const size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= (size_t)p.B * p.Tqp * groups) return;
@@ -949,8 +952,15 @@ static int bwd_impl(const void *Q, const void *K, const void *V, const float *w,
     if (!(flags & DC_AFT_BWD_DKDV)) {
         if (!(flags & DC_AFT_WS_VALID))
             DC_TRY(run_prep<IO, E>(L, (const IO *)K, (const IO *)V, w, ldw, causal, ws, st));
-        if (!(flags & DC_AFT_ACCUMULATE))
-            DC_CUDA_TRY(cudaMemset2DAsync(dW, (size_t)ldw * 4, 0, (size_t)L.Tk * 4, L.Tq, st));
+        // dW starts at zero for the split-K atomics: the tensor-core and
+        // statistics kernels clear it themselves (no memset node between
+        // them and the dW launch); the CUDA-core cross-check path does not
+        if (!(flags & DC_AFT_ACCUMULATE)) {
+            if (flags & DC_AFT_SIMT)
+                DC_CUDA_TRY(cudaMemset2DAsync(dW, (size_t)ldw * 4, 0, (size_t)L.Tk * 4, L.Tq, st));
+            else
+                p.zero_dw = 1;
+        }
         if ((flags & DC_AFT_WS_VALID) && saves_stats(flags)) {
             KernelTimer kt("aft_bwd_from_stats", st);
             const size_t n = (size_t)L.B * L.Tqp * (L.dp / 16);
@@ -972,6 +982,7 @@ static int bwd_impl(const void *Q, const void *K, const void *V, const float *w,
         // All units then have one K length and the workers walk K together,
         // which keeps the operand slices they read in L2.
         Params pw = p;
+        pw.zero_dw = 0;
         const bool pairs = use_pairs(L);
         pw.kpb = L.dp / (pairs ? TcCfg<WGRAD, E, sizeof(E) == 2>::BKe : TcCfg<WGRAD, E, false>::BKe);
         const int rb = pairs ? 2 * BM : BM;

@@ -449,6 +449,28 @@ __device__ __forceinline__ void epi16_wgrad(const Params &p, int t, int i0, cons
     }
 }
 
+// dW[Tq][Tk] (row stride ldw) set to zero by `count` threads, this one being
+// thread `i` of them: the first backward kernel clears it for dW's split-K
+// atomics (the dW launch waits for that kernel to complete).
+__device__ __forceinline__ void zero_dw(const Params &p, size_t i, size_t count)
+{
+    if (p.vec_w) {  // rows of whole float4s (ldw % 8 == 0, 32-byte aligned base)
+        const size_t per = (size_t)(p.Tk + 3) / 4, n = per * p.Tq;
+        for (size_t e = i; e < n; e += count) {
+            const size_t t = e / per, c = (e % per) * 4;
+            float *row = p.dW + t * p.ldw;
+            if (c + 3 < (size_t)p.Tk) {
+                *reinterpret_cast<float4 *>(row + c) = make_float4(0.f, 0.f, 0.f, 0.f);
+            } else {
+                for (size_t k = c; k < (size_t)p.Tk; ++k) row[k] = 0.f;
+            }
+        }
+    } else {
+        const size_t n = (size_t)p.Tq * p.Tk;
+        for (size_t e = i; e < n; e += count) p.dW[(e / p.Tk) * p.ldw + e % p.Tk] = 0.f;
+    }
+}
+
 // ----------------------------------------------------------- tile schedule
 struct Tile {
     int b, mrow, ncol;  // mrow/ncol: 128-row block of the accumulator / column block
@@ -911,6 +933,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
             if (threadIdx.x == 0) trace_at(p, j, 4, global_timer());
         }
+        if constexpr (MODE == BWD1)
+            if (p.zero_dw)
+                zero_dw(p, (size_t)blockIdx.x * (kEpiWarps * 32) + threadIdx.x,
+                        (size_t)gridDim.x * (kEpiWarps * 32));
     }
     // neither CTA of a pair leaves while the other may still signal its barriers
     if constexpr (P)
