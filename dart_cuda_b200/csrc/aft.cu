@@ -25,7 +25,7 @@
 //   HGRAD : acc[i, d] = sum_t A'[t,i] G[t,d]   (and N)   -> dK, dV
 //   WGRAD : acc[t, i] = sum_{b,d} G[b,t,d] P[b,i,d]      -> dW (split-K, atomics)
 // Operands are staged by TMA into 128-byte-swizzled shared memory; one thread
-// issues the MMAs into double-buffered TMEM accumulators; eight warps read
+// issues the MMAs into double-buffered TMEM accumulators; twelve warps read
 // TMEM back and apply the element-wise epilogue with 32-byte accesses.
 #include <cuda_bf16.h>
 #include <math.h>
