@@ -43,7 +43,7 @@ constexpr int BM = 128;        // accumulator rows = TMEM lanes
 constexpr int BN = 128;        // accumulator columns (one accumulator)
 constexpr int T_ALIGN = 128;   // workspace padding of Tq and Tk (tf32 operands)
 constexpr int T_ALIGN2 = 256;  // ... with bf16 operands: CTA pairs cover 256 rows
-constexpr int D_ALIGN = 128;   // workspace padding of D
+constexpr int D_ALIGN = 128;   // workspace padding of D (64 for narrow heads, make_layout)
 
 enum Mode { FWD = 0, BWD1 = 1, HGRAD = 2, WGRAD = 3 };
 
@@ -84,6 +84,7 @@ struct Params {
     int ldo;          // row stride of Z and dZ (elements, >= D)
     int n_tiles;      // tensor-core path: number of output tiles of the launch
     int kpb;          // WGRAD: K steps per batch element (dp / BKe)
+    int narrow;       // dp = 64 < BN: every FWD/BWD1/HGRAD tile is a half tile (half 0)
     int bundled;      // FWD/BWD1/HGRAD: tiles dealt in equal-work bundles of two
     int n_full;       // FWD/BWD1/HGRAD without bundles: units before the half tiles
     int zero_dw;      // BWD1 / saved-statistics kernel: also zero dW[Tq][Tk] (stride ldw)
@@ -387,11 +388,12 @@ __global__ void __launch_bounds__(256)
             for (int s = 0; s < nsplit; ++s) mx = fmaxf(mx, cpart[((size_t)s * B + b) * dp + d]);
         }
         cs[threadIdx.x] = mx;
-        if (blockIdx.y == 0) c[(size_t)b * dp + d] = mx;
+        if (blockIdx.y == 0 && d < dp) c[(size_t)b * dp + d] = mx;
     }
     __syncthreads();
     const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
     const int d0 = dblk + tx * 8;
+    if (d0 >= dp) return;  // narrow panels: 64 columns
     float cc[8];
 #pragma unroll
     for (int k = 0; k < 8; ++k) cc[k] = cs[tx * 8 + k];
@@ -546,6 +548,12 @@ static int operand_size(int dtype, int flags)
     return (dtype == DC_F32 && !(flags & DC_AFT_COMPUTE_BF16)) ? 4 : 2;
 }
 
+// Long sequences with bf16 operands run as CTA pairs (M = 256 per MMA, each
+// CTA loading half of B): the main loops dominate there.  Short ones keep one
+// CTA per tile: their element-wise epilogues dominate, and twice as many
+// independent workers drain them faster.
+static bool use_pairs(const Layout &L) { return L.esz == 2 && std::max(L.Tqp, L.Tkp) >= 1024; }
+
 static Layout make_layout(int B, int Tq, int Tk, int D, int dtype, int flags)
 {
     Layout L{};
@@ -557,8 +565,13 @@ static Layout make_layout(int B, int Tq, int Tk, int D, int dtype, int flags)
     const int talign = operand_size(dtype, flags) == 2 ? T_ALIGN2 : T_ALIGN;
     L.Tqp = (int)round_up(std::max(Tq, 1), talign);
     L.Tkp = (int)round_up(std::max(Tk, 1), talign);
-    L.dp = (int)round_up(std::max(D, 1), D_ALIGN);
     L.esz = operand_size(dtype, flags);
+    // Narrow heads (D <= 64, e.g. the reference's 4 x 64-channel heads) pad
+    // D to 64 rather than 128 where every tile can be a 64-column half tile
+    // (single CTAs: not the CTA-pair regime of long bf16 sequences, whose
+    // tiles span 128 columns): half the operand panels, B loads, MMA work and
+    // dW's K range.
+    L.dp = D <= 64 && !use_pairs(L) ? 64 : (int)round_up(std::max(D, 1), D_ALIGN);
     const int dblocks = (D + 255) / 256;
     int want = (8 * 148 + dblocks * B - 1) / std::max(1, dblocks * B);
     L.nsplit = std::max(1, std::min(want, (Tk + 31) / 32));
@@ -658,7 +671,7 @@ static int run_prep(const Layout &L, const IO *K, const IO *V, const float *w, i
     }
     {
         KernelTimer kt("aft_prep_p", st);
-        const int ndb = L.dp / 128;
+        const int ndb = (L.dp + 127) / 128;
         const int target = sm_count() * 4;
         int rsplit = std::max(1, (target + ndb * L.B - 1) / (ndb * L.B));
         rsplit = std::min(rsplit, std::max(1, L.Tkp / 16));
@@ -674,12 +687,6 @@ static int run_prep(const Layout &L, const IO *K, const IO *V, const float *w, i
 
 // dW output tiles (128 query rows x 256 keys) before split-K; causal
 // launches skip the pairs above the diagonal.
-// Long sequences with bf16 operands run as CTA pairs (M = 256 per MMA, each
-// CTA loading half of B): the main loops dominate there.  Short ones keep one
-// CTA per tile: their element-wise epilogues dominate, and twice as many
-// independent workers drain them faster.
-static bool use_pairs(const Layout &L) { return L.esz == 2 && std::max(L.Tqp, L.Tkp) >= 1024; }
-
 static int wgrad_tiles(const Layout &L, int causal)
 {
     if (use_pairs(L)) {  // CTA pairs: 256 query rows x 256 keys
@@ -747,7 +754,7 @@ static int launch_tc(Params p, const Layout &L, char *ws, cudaStream_t st)
     // tensor maps: A, B1..B4 (B3/B4 only for the tf32 dK/dV low parts), A2..A4 (dW)
     CUtensorMap mA, mB1, mB2, mB3, mB4, mA2, mA3, mA4;
     const uint32_t BK = C::BKe, BOX = C::BOX_MN;
-    const int nd = L.dp / BN;
+    const int nd = (L.dp + BN - 1) / BN;
     if (MODE == FWD || MODE == BWD1) {
         DC_TRY(map_ap(&mA, ws + L.off_ap, L, BK, BM, false));
         DC_TRY(map_3d(&mB1, ws + L.off_pv, L, L.Tkp, BOX, BK, true));
@@ -805,7 +812,12 @@ static int launch_tc(Params p, const Layout &L, char *ws, cudaStream_t st)
     // half a tile; single CTAs with two B tiles a stage).
     p.bundled = 0;
     p.n_full = p.n_tiles;
-    if (MODE != WGRAD) {
+    p.narrow = MODE != WGRAD && L.dp < BN;
+    if (p.narrow && !C::HALF_OK && MODE != HGRAD)
+        return fail(DC_ERR_UNSUPPORTED, "narrow panels need half tiles");  // excluded by make_layout
+    if (p.narrow) {
+        p.bundled = p.n_tiles >= 2 * workers;
+    } else if (MODE != WGRAD) {
         const int U = p.n_tiles;
         const double rounds = (double)((U + workers - 1) / workers);
         const int F = U / workers * workers, R = U - F;

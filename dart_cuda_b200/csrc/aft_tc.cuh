@@ -505,7 +505,7 @@ __device__ __forceinline__ Tile decode_tile(const Params &p, int idx)
         // Without bundles the tiles come heavy level first, one per unit;
         // units from n_full on are halves of the remaining (lightest) tiles,
         // which spread a last, partial round over all workers.
-        const int nd = p.dp / BN;
+        const int nd = (p.dp + BN - 1) / BN;
         const int nm = (MODE == HGRAD ? p.Tkp : p.Tqp) / RB;
         const int nb = nm / 2;
         const int bundles = nd * p.B * nb;
@@ -529,6 +529,10 @@ __device__ __forceinline__ Tile decode_tile(const Params &p, int idx)
         }
         t.ncol = g % nd;
         t.b = g / nd;
+        // narrow panels (64 columns): every tile is the first half of one
+        // (HGRAD at tf32 keeps whole tiles: its loads past column 64 read the
+        // tensor maps' zero fill and its epilogue stops at D)
+        if (p.narrow && !(MODE == HGRAD && BKe == 32)) t.half = 0;
         if (MODE == HGRAD) {  // early key rows see the most query rows
             t.mrow = nm - 1 - level;
             t.k0 = p.causal ? (t.mrow * RB) / BKe : 0;

@@ -161,7 +161,7 @@ def test_accumulate_and_workspace_reuse(ops, dev):
 
 
 @pytest.mark.parametrize("dtype,B,T,D", [(torch.bfloat16, 4, 512, 256), (torch.bfloat16, 2, 200, 72),
-                                         (torch.bfloat16, 1, 1100, 136),
+                                         (torch.bfloat16, 1, 1100, 136), (torch.bfloat16, 8, 256, 64),
                                          (torch.float32, 2, 130, 40), (torch.float32, 3, 256, 128)])
 @pytest.mark.parametrize("accumulate", [False, True])
 def test_saved_stats_match_recompute(ops, dev, dtype, B, T, D, accumulate):
@@ -197,7 +197,7 @@ def test_saved_stats_match_recompute(ops, dev, dtype, B, T, D, accumulate):
 
 
 @pytest.mark.parametrize("dtype,B,T,D", [(torch.bfloat16, 4, 512, 256), (torch.bfloat16, 2, 1024, 128),
-                                         (torch.float32, 2, 130, 40)])
+                                         (torch.float32, 2, 130, 40), (torch.bfloat16, 16, 256, 64)])
 @pytest.mark.parametrize("save", [False, True])
 def test_split_backward(ops, dev, dtype, B, T, D, save):
     """The backward as two calls (dQ + dW, then dK + dV with SMs left free)
@@ -235,6 +235,27 @@ def test_half_tiles(ops, dev, dtype):
     g = ops.aft_bwd(tq, tk, tv, tw, tg, causal=True)
     Qr, Kr, Vr, dZr = rounded(dtype, Q, K, V, dZ)
     ref = oracle_ref(Qr, Kr, Vr, W, dZr, True)
+    errs = {n: relerr(x.float().cpu().numpy(), r) for n, x, r in zip(("Z", "dQ", "dK", "dV", "dW"), (Z,) + tuple(g), ref)}
+    assert_errs(errs, TOL[dtype])
+    assert ops.device_status() == 0
+
+
+@pytest.mark.parametrize("dtype,B,T,D,causal", [(torch.bfloat16, 80, 512, 64, True),
+                                                (torch.float32, 80, 512, 64, True),
+                                                (torch.bfloat16, 3, 300, 40, False),
+                                                (torch.bfloat16, 2, 1024, 64, True)])
+def test_narrow_heads(ops, dev, dtype, B, T, D, causal):
+    """Heads of at most 64 channels (multi-head layers) keep 64-column
+    panels and run every tile as a half tile; B = 80 at T = 512 has enough
+    tiles to deal them in bundles, and T = 1024 with bf16 is the CTA-pair
+    regime, which keeps 128-column panels."""
+    Q, K, V, W, dZ = make_inputs(25, B, T, T, D)
+    tq, tk, tv, tg = to_dev(dev, dtype, Q, K, V, dZ)
+    tw = torch.from_numpy(W).to(dev)
+    Z = ops.aft_fwd(tq, tk, tv, tw, causal=causal)
+    g = ops.aft_bwd(tq, tk, tv, tw, tg, causal=causal)
+    Qr, Kr, Vr, dZr = rounded(dtype, Q, K, V, dZ)
+    ref = oracle_ref(Qr, Kr, Vr, W, dZr, causal)
     errs = {n: relerr(x.float().cpu().numpy(), r) for n, x, r in zip(("Z", "dQ", "dK", "dV", "dW"), (Z,) + tuple(g), ref)}
     assert_errs(errs, TOL[dtype])
     assert ops.device_status() == 0
