@@ -57,6 +57,8 @@ struct KernelTimer {
 };
 bool profiling_enabled();
 
+inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
 // Launch with programmatic stream serialisation (the kernel calls
 // grid_dep_wait() before its first dependent memory access) and, when
 // cluster > 1, as clusters of `cluster` CTAs along x.

@@ -286,6 +286,15 @@ __device__ __forceinline__ uint32_t smem_in_cta(uint32_t saddr, uint32_t rank)
     return r;
 }
 
+// 32-bit load from the shared memory of another CTA of the cluster
+// (addr: shared::cluster, from smem_in_cta).
+__device__ __forceinline__ float ld_dsmem_f32(uint32_t addr)
+{
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+    return v;
+}
+
 __device__ __forceinline__ void cluster_sync_all()
 {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\t"

@@ -83,6 +83,94 @@ __global__ void gate_fwd_kernel(const float *__restrict__ q, int ldq, const floa
     out[(size_t)m * ldo + n] = sigm(q[(size_t)m * ldq + n]) * v0[n];
 }
 
+// 16-byte form (N, ldq, ldo multiples of 4, aligned bases): 32 float4
+// columns x 8 row lanes a block, four rows in flight per thread.
+__device__ __forceinline__ float4 sigm4(float4 q)
+{
+    return make_float4(sigm(q.x), sigm(q.y), sigm(q.z), sigm(q.w));
+}
+
+__global__ void gate_fwd_vec(const float4 *__restrict__ q, int ldq4, const float4 *__restrict__ v0,
+                             float4 *__restrict__ out, int ldo4, int M, int N4)
+{
+    grid_dep_wait();  // programmatic dependent launch: inputs are ready
+    grid_dep_launch();
+    const int c = blockIdx.x * 32 + (threadIdx.x & 31);
+    if (c >= N4) return;
+    const float4 v = v0[c];
+    const int step = gridDim.y * 8;
+    int m = blockIdx.y * 8 + (threadIdx.x >> 5);
+    for (; m + 3 * step < M; m += 4 * step) {
+        float4 x[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) x[k] = __ldcs(q + (size_t)(m + k * step) * ldq4 + c);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float4 s = sigm4(x[k]);
+            out[(size_t)(m + k * step) * ldo4 + c] = make_float4(s.x * v.x, s.y * v.y, s.z * v.z, s.w * v.w);
+        }
+    }
+    for (; m < M; m += step) {
+        const float4 s = sigm4(__ldcs(q + (size_t)m * ldq4 + c));
+        out[(size_t)m * ldo4 + c] = make_float4(s.x * v.x, s.y * v.y, s.z * v.z, s.w * v.w);
+    }
+}
+
+__global__ void gate_bwd_vec(const float4 *__restrict__ q, int ldq4, const float4 *__restrict__ v0,
+                             const float4 *__restrict__ dz, int ldz4, float4 *__restrict__ dq,
+                             int lddq4, float *__restrict__ dv0, int M, int N4)
+{
+    grid_dep_wait();  // programmatic dependent launch: inputs are ready
+    grid_dep_launch();
+    __shared__ float4 part[8][33];
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+    const int c = blockIdx.x * 32 + tx;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (c < N4) {
+        const float4 v = v0[c];
+        const int step = gridDim.y * 8;
+        int m = blockIdx.y * 8 + ty;
+        auto one = [&](const float4 x, const float4 g, size_t o) {
+            const float4 s = sigm4(x);
+            dq[o] = make_float4(g.x * v.x * s.x * (1.0f - s.x), g.y * v.y * s.y * (1.0f - s.y),
+                                g.z * v.z * s.z * (1.0f - s.z), g.w * v.w * s.w * (1.0f - s.w));
+            acc.x += g.x * s.x;
+            acc.y += g.y * s.y;
+            acc.z += g.z * s.z;
+            acc.w += g.w * s.w;
+        };
+        for (; m + 3 * step < M; m += 4 * step) {
+            float4 x[4], g[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                x[k] = __ldcs(q + (size_t)(m + k * step) * ldq4 + c);
+                g[k] = __ldcs(dz + (size_t)(m + k * step) * ldz4 + c);
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) one(x[k], g[k], (size_t)(m + k * step) * lddq4 + c);
+        }
+        for (; m < M; m += step)
+            one(__ldcs(q + (size_t)m * ldq4 + c), __ldcs(dz + (size_t)m * ldz4 + c),
+                (size_t)m * lddq4 + c);
+    }
+    part[ty][tx] = acc;
+    __syncthreads();
+    if (ty == 0 && c < N4) {
+        float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+            s.x += part[r][tx].x;
+            s.y += part[r][tx].y;
+            s.z += part[r][tx].z;
+            s.w += part[r][tx].w;
+        }
+        atomicAdd(dv0 + 4 * c, s.x);
+        atomicAdd(dv0 + 4 * c + 1, s.y);
+        atomicAdd(dv0 + 4 * c + 2, s.z);
+        atomicAdd(dv0 + 4 * c + 3, s.w);
+    }
+}
+
 // dq = dz * v0 * s (1 - s); dv0 += sum_m dz * s.  Block: 32 columns x 8 row
 // lanes; partial column sums meet in shared memory, one atomic per column.
 __global__ void gate_bwd_kernel(const float *__restrict__ q, int ldq, const float *__restrict__ v0,
@@ -259,6 +347,13 @@ int dc_gate_fwd(const float *q, int ldq, const float *v0, float *out, int ldo, i
     cudaStream_t st = as_stream(stream);
     const size_t n = (size_t)M * N;
     KernelTimer kt("gate_fwd", st);
+    if (N % 4 == 0 && ldq % 4 == 0 && ldo % 4 == 0 && aligned16(q) && aligned16(v0) && aligned16(out)) {
+        const int cb = (N / 4 + 31) / 32;
+        const int rb = std::max(1, std::min((M + 31) / 32, (8 * sm_count() + cb - 1) / cb));
+        DC_CUDA_TRY(launch_pdl(gate_fwd_vec, dim3(cb, rb), dim3(256), 0, st, 1, (const float4 *)q,
+                               ldq / 4, (const float4 *)v0, (float4 *)out, ldo / 4, M, N / 4));
+        return DC_OK;
+    }
     (void)launch_pdl(gate_fwd_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, st, 1, q,
                      ldq, v0, out, ldo, M, N);
     DC_CUDA_TRY(cudaGetLastError());
@@ -272,11 +367,22 @@ int dc_gate_bwd(const float *q, int ldq, const float *v0, const float *dz, int l
     if (M < 0 || N < 0 || ldq < N || ldz < N || lddq < N) return fail(DC_ERR_INVALID, "bad shape");
     if ((long long)M * N == 0) return DC_OK;
     cudaStream_t st = as_stream(stream);
+    KernelTimer kt("gate_bwd", st);
+    if (N % 4 == 0 && ldq % 4 == 0 && ldz % 4 == 0 && lddq % 4 == 0 && aligned16(q) &&
+        aligned16(v0) && aligned16(dz) && aligned16(dq)) {
+        // two blocks an SM: eight 16-byte loads in flight per thread suffice,
+        // and fewer blocks mean fewer atomics on each dv0 column
+        const int cb4 = (N / 4 + 31) / 32;
+        const int rb = std::max(1, std::min((M + 31) / 32, (2 * sm_count() + cb4 - 1) / cb4));
+        DC_CUDA_TRY(launch_pdl(gate_bwd_vec, dim3(cb4, rb), dim3(256), 0, st, 1, (const float4 *)q,
+                               ldq / 4, (const float4 *)v0, (const float4 *)dz, ldz / 4,
+                               (float4 *)dq, lddq / 4, dv0, M, N / 4));
+        return DC_OK;
+    }
     const int cb = (N + 31) / 32;
     int rsplit = std::max(1, std::min((M + 63) / 64, (4 * sm_count() + cb - 1) / cb));
     const int rows = (M + rsplit - 1) / rsplit;
     rsplit = (M + rows - 1) / rows;
-    KernelTimer kt("gate_bwd", st);
     (void)launch_pdl(gate_bwd_kernel, dim3(cb, rsplit), dim3(256), 0, st, 1, q, ldq, v0, dz, ldz,
                      dq, lddq, dv0, M, N, rows);
     DC_CUDA_TRY(cudaGetLastError());

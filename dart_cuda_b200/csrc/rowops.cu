@@ -285,19 +285,41 @@ __global__ void ln_bwd_block(const float *__restrict__ x, const float *__restric
     }
 }
 
-// Sum `nparts` partial rows of width W into out (+= when accumulate).
-__global__ void colsum_parts(const float *__restrict__ part, int nparts, int W,
-                             float *out0, float *out1, int split,
-                             int accumulate)
+// Sum `nparts` partial rows of width W into out (+= when accumulate).  A
+// block (32 x kColLanes) covers 32 columns; lane y adds partials y, y +
+// kColLanes, ... with four loads in flight, and the lanes' sums are added in
+// a fixed order (deterministic).  One thread per column walking all partials
+// was latency-bound: hundreds of dependent L2 round trips on a handful of SMs.
+constexpr int kColLanes = 16;
+__global__ void __launch_bounds__(32 * kColLanes)
+    colsum_parts(const float *__restrict__ part, int nparts, int W, float *out0, float *out1,
+                 int split, int accumulate)
 {
     grid_dep_wait();  // programmatic dependent launch: inputs are ready
     grid_dep_launch();
-    const int j = blockIdx.x * blockDim.x + threadIdx.x;
-    if (j >= W) return;
-    float acc = 0.f;
-    for (int p = 0; p < nparts; ++p) acc += part[(size_t)p * W + j];
-    float *o = (j < split) ? out0 + j : out1 + (j - split);
-    *o = accumulate ? *o + acc : acc;
+    __shared__ float red[kColLanes][33];
+    const int j = blockIdx.x * 32 + threadIdx.x;
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    if (j < W) {
+        int p = threadIdx.y;
+        for (; p + 3 * kColLanes < nparts; p += 4 * kColLanes) {
+            const float *q = part + (size_t)p * W + j;
+            a0 += q[0];
+            a1 += q[(size_t)kColLanes * W];
+            a2 += q[(size_t)2 * kColLanes * W];
+            a3 += q[(size_t)3 * kColLanes * W];
+        }
+        for (; p < nparts; p += kColLanes) a0 += part[(size_t)p * W + j];
+    }
+    red[threadIdx.y][threadIdx.x] = (a0 + a1) + (a2 + a3);
+    __syncthreads();
+    if (threadIdx.y == 0 && j < W) {
+        float acc = 0.f;
+#pragma unroll
+        for (int k = 0; k < kColLanes; ++k) acc += red[k][threadIdx.x];
+        float *o = (j < split) ? out0 + j : out1 + (j - split);
+        *o = accumulate ? *o + acc : acc;
+    }
 }
 
 // ==================================================================== bias
@@ -413,6 +435,94 @@ __global__ void bias_bwd_vec4(const float4 *__restrict__ dy, float4 *__restrict_
         }
         reinterpret_cast<float4 *>(part)[(size_t)blockIdx.y * N4 + col] = s;
     }
+}
+
+// Column sums on clusters, one launch: the kSumCluster CTAs of a cluster
+// (grid x) split the rows of one 16-column block (grid y).  A CTA's 512
+// threads are 128 row lanes x 4 float4 column lanes with four rows in flight
+// each; lanes of a column meet by shuffles and shared memory, and rank 0 adds
+// the cluster's CTA sums, read from distributed shared memory in rank order.
+// The sums are deterministic and no partial rows go through global memory
+// (the two-pass form spent a second launch and an L2 round trip on them).
+constexpr int kSumCluster = 8;
+constexpr int kSumThreads = 512;
+constexpr int kSumRowLanes = kSumThreads / 4;
+
+__device__ __forceinline__ void add4(float4 &a, const float4 &b)
+{
+    a.x += b.x;
+    a.y += b.y;
+    a.z += b.z;
+    a.w += b.w;
+}
+
+__global__ void __launch_bounds__(kSumThreads)
+    bias_bwd_cluster(const float4 *__restrict__ dy, float4 *__restrict__ da,
+                     float *__restrict__ db, int M, int N4, int accumulate)
+{
+    grid_dep_wait();  // programmatic dependent launch: inputs are ready
+    grid_dep_launch();
+    __shared__ float4 wsum[kSumThreads / 32][4];
+    __shared__ float csum[16];
+    const int q = threadIdx.x & 3, rl = threadIdx.x >> 2;
+    const int c4 = blockIdx.y * 4 + q;
+    const int rpc = (M + kSumCluster - 1) / kSumCluster;
+    const int r0 = (int)cluster_rank() * rpc, r1 = min(M, r0 + rpc);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (c4 < N4) {
+        int r = r0 + rl;
+        for (; r + 3 * kSumRowLanes < r1; r += 4 * kSumRowLanes) {
+            float4 g[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) g[k] = __ldcs(dy + (size_t)(r + k * kSumRowLanes) * N4 + c4);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                add4(acc, g[k]);
+                if (da) {
+                    const size_t o = (size_t)(r + k * kSumRowLanes) * N4 + c4;
+                    float4 a = g[k];
+                    if (accumulate) add4(a, da[o]);
+                    da[o] = a;
+                }
+            }
+        }
+        for (; r < r1; r += kSumRowLanes) {
+            const size_t o = (size_t)r * N4 + c4;
+            const float4 g = __ldcs(dy + o);
+            add4(acc, g);
+            if (da) {
+                float4 a = g;
+                if (accumulate) add4(a, da[o]);
+                da[o] = a;
+            }
+        }
+    }
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) {
+        acc.x += __shfl_xor_sync(0xffffffffu, acc.x, off);
+        acc.y += __shfl_xor_sync(0xffffffffu, acc.y, off);
+        acc.z += __shfl_xor_sync(0xffffffffu, acc.z, off);
+        acc.w += __shfl_xor_sync(0xffffffffu, acc.w, off);
+    }
+    if ((threadIdx.x & 31) < 4) wsum[threadIdx.x >> 5][q] = acc;
+    __syncthreads();
+    if (threadIdx.x < 16) {
+        float v = 0.f;
+#pragma unroll
+        for (int w = 0; w < kSumThreads / 32; ++w)
+            v += reinterpret_cast<const float *>(&wsum[w][0])[threadIdx.x];
+        csum[threadIdx.x] = v;
+    }
+    cluster_sync_all();
+    if (cluster_rank() == 0 && threadIdx.x < 16) {
+        const int j = blockIdx.y * 16 + threadIdx.x;
+        const uint32_t mine = (uint32_t)__cvta_generic_to_shared(&csum[threadIdx.x]);
+        float v = 0.f;
+#pragma unroll
+        for (int r = 0; r < kSumCluster; ++r) v += ld_dsmem_f32(smem_in_cta(mine, r));
+        if (j < 4 * N4) db[j] = accumulate ? db[j] + v : v;
+    }
+    cluster_sync_all();  // the CTA sums stay readable until rank 0 has added them
 }
 
 // ===================================================================== CE
@@ -710,7 +820,6 @@ __global__ void adam_kernel(float *__restrict__ p, const float *__restrict__ g,
 using namespace dc;
 using namespace dc::rows;
 
-static bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 // Cross-entropy rows: a warp per row up to V = 1024; wider rows held in
 // registers by a block per row when V % 4 == 0 (up to 16384); otherwise a
@@ -849,7 +958,7 @@ int dc_layernorm_bwd(const float *x, const float *gamma, const float *dy, float 
     }
     if (cudaGetLastError() != cudaSuccess) rc = fail(DC_ERR_CUDA, "layernorm bwd launch failed");
     if (rc == DC_OK) {
-        (void)launch_pdl(colsum_parts, dim3((2 * C + 255) / 256), dim3(256), 0, st, 1, part,
+        (void)launch_pdl(colsum_parts, dim3((2 * C + 31) / 32), dim3(32, kColLanes), 0, st, 1, part,
                          nparts, 2 * C, dgamma, dbeta, C, accumulate);
         if (cudaGetLastError() != cudaSuccess)
             rc = fail(DC_ERR_CUDA, "layernorm colsum launch failed");
@@ -886,6 +995,16 @@ int dc_bias_bwd(const float *dy, float *da, float *db, int M, int N, int accumul
     if (!dy || !db) return fail(DC_ERR_INVALID, "null pointer");
     cudaStream_t st = as_stream(stream);
     const bool vec = N % 4 == 0 && aligned16(dy) && (!da || aligned16(da));
+    // one-launch cluster form when its CTAs (a cluster per 16 columns) fill
+    // at least half the SMs
+    const int nb16 = (N + 15) / 16;
+    if (vec && 2 * nb16 * kSumCluster >= sm_count() && nb16 <= 65535) {
+        KernelTimer kt("bias_bwd", st);
+        DC_CUDA_TRY(launch_pdl(bias_bwd_cluster, dim3(kSumCluster, nb16), dim3(kSumThreads), 0, st,
+                               kSumCluster, reinterpret_cast<const float4 *>(dy),
+                               reinterpret_cast<float4 *>(da), db, M, N / 4, accumulate));
+        return DC_OK;
+    }
     const int cblocks = vec ? (N / 4 + 31) / 32 : (N + 31) / 32;
     const int target = std::max(1, sm_count() * 8 / cblocks);
     const int rows_per_cta = std::max(16, (M + target - 1) / target);
@@ -900,7 +1019,7 @@ int dc_bias_bwd(const float *dy, float *da, float *db, int M, int N, int accumul
     else
         (void)launch_pdl(bias_bwd_kernel, dim3(cblocks, rblocks), dim3(32, 8), 0, st, 1, dy, da,
                          part, M, N, rows_per_cta, accumulate);
-    (void)launch_pdl(colsum_parts, dim3((N + 255) / 256), dim3(256), 0, st, 1, part, rblocks, N,
+    (void)launch_pdl(colsum_parts, dim3((N + 31) / 32), dim3(32, kColLanes), 0, st, 1, part, rblocks, N,
                      db, db, N, accumulate);
     cudaError_t e = cudaGetLastError();
     cudaFreeAsync(part, st);

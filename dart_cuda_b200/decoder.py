@@ -111,6 +111,11 @@ class AftDecoder:
         self._init(seed, std)
         self._bufs = None
         self._dec = None
+        # heads 1.. of each AFT layer run on their own streams (head 0 on the
+        # caller's): one head's launches leave most SMs idle at these sizes
+        # (B*T/128 row tiles of 64 columns), so the heads run side by side
+        self._head_streams = [torch.cuda.Stream(self.device) for _ in range(cfg.n_heads - 1)] \
+            if self.device.type == "cuda" else []
 
     def _view(self, flat, name):
         off, shape = self._offsets[name]
@@ -235,20 +240,32 @@ class AftDecoder:
         d, hs, Tm = c.d_model, c.head, c.block_size
         pos, dpos = self.P[f"{l}.pos"], self.G[f"{l}.pos"]
         q0 = qkv.data_ptr()
+        main = torch.cuda.current_stream()
+        side = self._head_streams
+        if side:  # fork: the head streams start after what the caller queued
+            fork = torch.cuda.Event()
+            fork.record(main)
+            for s in side:
+                s.wait_event(fork)
         for h in range(c.n_heads):
+            st = (main if h == 0 else side[h - 1]).cuda_stream
             Q, K, Vv = (q0 + 4 * (j * d + h * hs) for j in range(3))
             w = pos[h].data_ptr()
             if not backward:
                 check(lib().dc_aft_fwd_strided(Q, K, Vv, w, Tm, z.data_ptr() + 4 * h * hs, B, T, T, hs,
                                                3 * d, d, DC_F32, self._aft_flags, self._ws(l, h),
-                                               self._ws_bytes, ops._stream()), "dc_aft_fwd_strided")
+                                               self._ws_bytes, st), "dc_aft_fwd_strided")
             else:
                 g0 = dqkv.data_ptr()
                 dQ, dK, dV = (g0 + 4 * (j * d + h * hs) for j in range(3))
                 check(lib().dc_aft_bwd_strided(Q, K, Vv, w, Tm, dz.data_ptr() + 4 * h * hs, dQ, dK, dV,
                                                dpos[h].data_ptr(), B, T, T, hs, 3 * d, d, DC_F32,
                                                self._aft_flags | DC_AFT_WS_VALID, self._ws(l, h),
-                                               self._ws_bytes, ops._stream()), "dc_aft_bwd_strided")
+                                               self._ws_bytes, st), "dc_aft_bwd_strided")
+        for s in side:  # join
+            done = torch.cuda.Event()
+            done.record(s)
+            main.wait_event(done)
 
     def _gate(self, q, v0, out):
         M, N = q.shape

@@ -67,6 +67,50 @@ def test_bias(ops, dev, M, N):
     assert relerr(db.cpu().numpy(), rb) < 1e-5
 
 
+@pytest.mark.parametrize("M,N", [(16384, 256), (3000, 768), (9, 160)])
+def test_bias_grad_only(ops, dev, M, N):
+    """db alone (no da), overwritten and then accumulated: the one-launch
+    cluster reduction, deterministic from call to call."""
+    rng = np.random.default_rng(M + N)
+    dy = rng.standard_normal((M, N)).astype(np.float32)
+    rb = oracle.bias_bwd(dy)[1]
+    tdy = T(dev, dy)
+    db = torch.full((N,), 3.0, device=dev)
+    ops.bias_bwd(tdy, grads=(None, db))
+    assert relerr(db.cpu().numpy(), rb) < 1e-5
+    db2 = torch.zeros(N, device=dev)
+    ops.bias_bwd(tdy, grads=(None, db2))
+    assert torch.equal(db, db2)
+    ops.bias_bwd(tdy, grads=(None, db), accumulate=True)
+    assert relerr(db.cpu().numpy(), 2 * rb) < 1e-5
+
+
+@pytest.mark.parametrize("M,N,ld", [(16384, 256, 256), (300, 96, 100), (7, 6, 6)])
+def test_gate(ops, dev, M, N, ld):
+    """z = sigmoid(q) * v0 and its backward (dq, dv0 accumulated) against
+    float64 on the host, row strides wider than N included."""
+    from dart_cuda_b200._lib import lib
+
+    rng = np.random.default_rng(M * N)
+    q = rng.standard_normal((M, ld)).astype(np.float32)
+    v0 = rng.standard_normal(N).astype(np.float32)
+    dz = rng.standard_normal((M, ld)).astype(np.float32)
+    tq, tv, tdz = T(dev, q), T(dev, v0), T(dev, dz)
+    z = torch.zeros(M, ld, device=dev)
+    dq = torch.zeros(M, ld, device=dev)
+    dv = torch.ones(N, device=dev)
+    st = torch.cuda.current_stream().cuda_stream
+    assert lib().dc_gate_fwd(tq.data_ptr(), ld, tv.data_ptr(), z.data_ptr(), ld, M, N, st) == 0
+    assert lib().dc_gate_bwd(tq.data_ptr(), ld, tv.data_ptr(), tdz.data_ptr(), ld, dq.data_ptr(), ld,
+                             dv.data_ptr(), M, N, st) == 0
+    s = 1.0 / (1.0 + np.exp(-q[:, :N].astype(np.float64)))
+    g = dz[:, :N].astype(np.float64)
+    assert relerr(z[:, :N].cpu().numpy(), s * v0) < 1e-5
+    assert relerr(dq[:, :N].cpu().numpy(), g * v0 * s * (1 - s)) < 1e-5
+    assert relerr(dv.cpu().numpy(), 1.0 + (g * s).sum(0)) < 1e-5
+    assert float(z[:, N:].abs().sum()) == 0.0 and float(dq[:, N:].abs().sum()) == 0.0
+
+
 @pytest.mark.parametrize("Tn,V", [(16384, 65), (64, 8192), (4, 2), (3, 50257), (33, 2052), (17, 16384),
                                   (9, 1028)])
 def test_cross_entropy(ops, dev, Tn, V):
