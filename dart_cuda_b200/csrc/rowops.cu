@@ -153,10 +153,14 @@ __global__ void ln_bwd_warp(const float *__restrict__ x, const float *__restrict
     const float4 *g4 = reinterpret_cast<const float4 *>(gamma);
     const int r0 = blockIdx.x * rows_per_cta;
     const int r1 = min(R, r0 + rows_per_cta);
+    // with accumulate, rows of up to 512 columns also load the old dx with
+    // x and dy (one memory round trip a row instead of two)
+    constexpr bool kEarlyOld = NV <= 4;
     for (int row = r0 + wid; row < r1; row += nw) {
         const float4 *xr = reinterpret_cast<const float4 *>(x + (size_t)row * C);
         const float4 *gr = reinterpret_cast<const float4 *>(dy + (size_t)row * C);
-        float4 v[NV], g[NV];
+        float4 *dr = reinterpret_cast<float4 *>(dx + (size_t)row * C);
+        float4 v[NV], g[NV], old[kEarlyOld ? NV : 1];
         float s = 0.f;
 #pragma unroll
         for (int k = 0; k < NV; ++k) {
@@ -164,8 +168,10 @@ __global__ void ln_bwd_warp(const float *__restrict__ x, const float *__restrict
             const bool in = j < C4;
             v[k] = in ? xr[j] : make_float4(0.f, 0.f, 0.f, 0.f);
             g[k] = in ? gr[j] : make_float4(0.f, 0.f, 0.f, 0.f);
-            s += (v[k].x + v[k].y) + (v[k].z + v[k].w);
+            if (kEarlyOld) old[kEarlyOld ? k : 0] = in && accumulate ? dr[j] : make_float4(0.f, 0.f, 0.f, 0.f);
         }
+#pragma unroll
+        for (int k = 0; k < NV; ++k) s += (v[k].x + v[k].y) + (v[k].z + v[k].w);
         const float mean = warp_sum(s) / (float)C;
         float q = 0.f;
 #pragma unroll
@@ -204,7 +210,6 @@ __global__ void ln_bwd_warp(const float *__restrict__ x, const float *__restrict
         }
         const float invC = 1.0f / (float)C;
         const float m1 = warp_sum(s1) * invC, m2 = warp_sum(s2) * invC;
-        float4 *dr = reinterpret_cast<float4 *>(dx + (size_t)row * C);
 #pragma unroll
         for (int k = 0; k < NV; ++k) {
             const int j = lane + 32 * k;
@@ -216,11 +221,11 @@ __global__ void ln_bwd_warp(const float *__restrict__ x, const float *__restrict
                 o.z = inv_std * (g[k].z * ga.z - m1 - v[k].z * m2);
                 o.w = inv_std * (g[k].w * ga.w - m1 - v[k].w * m2);
                 if (accumulate) {
-                    const float4 old = dr[j];
-                    o.x += old.x;
-                    o.y += old.y;
-                    o.z += old.z;
-                    o.w += old.w;
+                    const float4 a = kEarlyOld ? old[kEarlyOld ? k : 0] : dr[j];
+                    o.x += a.x;
+                    o.y += a.y;
+                    o.z += a.z;
+                    o.w += a.w;
                 }
                 dr[j] = o;
             }

@@ -116,6 +116,9 @@ class AftDecoder:
         # (B*T/128 row tiles of 64 columns), so the heads run side by side
         self._head_streams = [torch.cuda.Stream(self.device) for _ in range(cfg.n_heads - 1)] \
             if self.device.type == "cuda" else []
+        # the backward's weight and bias gradients (off the input-gradient
+        # chain) run on a second stream beside it
+        self._wgrad_stream = torch.cuda.Stream(self.device) if self.device.type == "cuda" else None
 
     def _view(self, flat, name):
         off, shape = self._offsets[name]
@@ -324,40 +327,74 @@ class AftDecoder:
         ops.ce_bwd(b["logits"], b["targets"], grad_scale=b["scale"], out=b["dlog"])
         check(lib().dc_copy2d(b["dlog_pad"].data_ptr(), self.Vp * 4, b["dlog"].data_ptr(), V * 4, V * 4,
                               B * T, st), "dc_copy2d")
+        main, side = torch.cuda.current_stream(), self._wgrad_stream
+
+        def fork():
+            """Side work queued after this point sees what main has queued so far."""
+            ev = torch.cuda.Event()
+            ev.record(main)
+            side.wait_event(ev)
+
+        def join():
+            """Main waits for all side work queued so far: called before main
+            overwrites a buffer the side work reads (dX by the LayerNorm
+            backward's accumulation; dh, da and dqkv are rewritten only after
+            a later join)."""
+            ev = torch.cuda.Event()
+            ev.record(side)
+            main.wait_event(ev)
+
+        fork()
+        with torch.cuda.stream(side):
+            ops.gemm(b["af"], b["dlog_pad"], trans_a=True, out=G["wlm"])
+            ops.bias_bwd(b["dlog"], grads=(None, G["blm"]))
         ops.gemm(b["dlog_pad"], P["wlm"], trans_b=True, out=b["da"])
-        ops.gemm(b["af"], b["dlog_pad"], trans_a=True, out=G["wlm"])
-        ops.bias_bwd(b["dlog"], grads=(None, G["blm"]))
         dX = b["dX"]
         ops.layernorm_bwd(b["x"][c.n_layers], P["lnfg"], b["da"], grads=(dX, G["lnfg"], G["lnfb"]))
         for l in reversed(range(c.n_layers)):
             # FFN: x3 = x2 + gelu(a3 W1 + b1) W2 + b2
+            fork()
+            with torch.cuda.stream(side):
+                ops.gemm(b["h"][l], dX, trans_a=True, out=G[f"{l}.w2"])
+                ops.bias_bwd(dX, grads=(None, G[f"{l}.b2"]))
             ops.gemm(dX, P[f"{l}.w2"], trans_b=True, out=b["dh"], gelu_bwd_aux=b["u"][l])
-            ops.gemm(b["h"][l], dX, trans_a=True, out=G[f"{l}.w2"])
-            ops.bias_bwd(dX, grads=(None, G[f"{l}.b2"]))
+            fork()
+            with torch.cuda.stream(side):
+                ops.gemm(b["a3"][l], b["dh"], trans_a=True, out=G[f"{l}.w1"])
+                ops.bias_bwd(b["dh"], grads=(None, G[f"{l}.b1"]))
             ops.gemm(b["dh"], P[f"{l}.w1"], trans_b=True, out=b["da"])
-            ops.gemm(b["a3"][l], b["dh"], trans_a=True, out=G[f"{l}.w1"])
-            ops.bias_bwd(b["dh"], grads=(None, G[f"{l}.b1"]))
+            join()
             ops.layernorm_bwd(b["x2"][l], P[f"{l}.ln3g"], b["da"], grads=(dX, G[f"{l}.ln3g"], G[f"{l}.ln3b"]),
                               accumulate=True)
             # cross: x2 = x1 + (sigmoid(qc) * v0) Wco + bco, qc = a2 Wcq + bcq
+            fork()
+            with torch.cuda.stream(side):
+                ops.gemm(b["cg"][l], dX, trans_a=True, out=G[f"{l}.wco"])
+                ops.bias_bwd(dX, grads=(None, G[f"{l}.bco"]))
             ops.gemm(dX, P[f"{l}.wco"], trans_b=True, out=b["dz"])
-            ops.gemm(b["cg"][l], dX, trans_a=True, out=G[f"{l}.wco"])
-            ops.bias_bwd(dX, grads=(None, G[f"{l}.bco"]))
             check(lib().dc_gate_bwd(b["qc"][l].data_ptr(), d, self._v0(l).data_ptr(), b["dz"].data_ptr(), d,
                                     b["da"].data_ptr(), d, G[f"{l}.bcv"].data_ptr(), B * T, d, st), "dc_gate_bwd")
+            fork()
+            with torch.cuda.stream(side):
+                ops.gemm(b["a2"][l], b["da"], trans_a=True, out=G[f"{l}.wcq"])
+                ops.bias_bwd(b["da"], grads=(None, G[f"{l}.bcq"]))
             ops.gemm(b["da"], P[f"{l}.wcq"], trans_b=True, out=b["dz"])
-            ops.gemm(b["a2"][l], b["da"], trans_a=True, out=G[f"{l}.wcq"])
-            ops.bias_bwd(b["da"], grads=(None, G[f"{l}.bcq"]))
+            join()
             ops.layernorm_bwd(b["x1"][l], P[f"{l}.ln2g"], b["dz"], grads=(dX, G[f"{l}.ln2g"], G[f"{l}.ln2b"]),
                               accumulate=True)
             # self: x1 = x + AFT(a1 Wqkv + bqkv) Wo + bo
+            fork()
+            with torch.cuda.stream(side):
+                ops.gemm(b["z"][l], dX, trans_a=True, out=G[f"{l}.wo"])
+                ops.bias_bwd(dX, grads=(None, G[f"{l}.bo"]))
             ops.gemm(dX, P[f"{l}.wo"], trans_b=True, out=b["dz"])
-            ops.gemm(b["z"][l], dX, trans_a=True, out=G[f"{l}.wo"])
-            ops.bias_bwd(dX, grads=(None, G[f"{l}.bo"]))
             self._aft(l, b["qkv"][l], None, B, T, backward=True, dz=b["dz"], dqkv=b["dqkv"])
+            fork()
+            with torch.cuda.stream(side):
+                ops.gemm(b["a1"][l], b["dqkv"], trans_a=True, out=G[f"{l}.wqkv"])
+                ops.bias_bwd(b["dqkv"], grads=(None, G[f"{l}.bqkv"]))
             ops.gemm(b["dqkv"], P[f"{l}.wqkv"], trans_b=True, out=b["da"])
-            ops.gemm(b["a1"][l], b["dqkv"], trans_a=True, out=G[f"{l}.wqkv"])
-            ops.bias_bwd(b["dqkv"], grads=(None, G[f"{l}.bqkv"]))
+            join()
             ops.layernorm_bwd(b["x"][l], P[f"{l}.ln1g"], b["da"], grads=(dX, G[f"{l}.ln1g"], G[f"{l}.ln1b"]),
                               accumulate=True)
         check(lib().dc_embedding_bwd(b["idx"].data_ptr(), dX.data_ptr(), G["wte"].data_ptr(), G["wpe"].data_ptr(),
