@@ -305,8 +305,10 @@ def bench_train(args, dev, rank, world, dist):
     ms = total_ms / args.steps
     value = B * T * world / (ms / 1e3)
 
-    # per-kernel pass (eager, events around every library launch)
+    # per-kernel pass (eager, events around every library launch; all on one
+    # stream so that no kernel's events also span another stream's work)
     ops.profile_enable(True)
+    m.concurrent = False
     for _ in range(args.steps):
         flush.zero_()
         fwd_bwd()
@@ -314,6 +316,7 @@ def bench_train(args, dev, rank, world, dist):
             dist.all_reduce(m.grad)
         m.optimizer_step(lr=3e-4)
     torch.cuda.synchronize()
+    m.concurrent = True
     prof = ops.profile_read()
     ops.profile_enable(False)
     d, F, V, M, L = cfg.d_model, 4 * cfg.d_model, cfg.vocab, B * T, cfg.n_layers

@@ -14,10 +14,14 @@
 // residual adds): bias, GELU (keeping the pre-activation for the backward),
 // the GELU derivative, and a residual / accumulate input.
 //
-// One persistent CTA per SM walks 128x128 output tiles (split along K when
+// One persistent CTA per SM walks 128 x BN output tiles (split along K when
 // the tiles alone cannot fill the SMs and the epilogue is linear): warp 16
-// issues TMA loads into a 6-deep ring of 32 KB stages, warp 17 owns TMEM and
-// issues the MMAs into a double-buffered accumulator, warps 0-15 drain it.
+// issues TMA loads into a ring of stages (six of 32 KB with BN = 128, four of
+// 48 KB with BN = 256), warp 17 owns TMEM and issues the MMAs into a
+// double-buffered accumulator, warps 0-15 drain it.  BN = 256 (one N = 256
+// MMA a K slice) serves products with enough 128 x 256 tiles to fill the SMs
+// unsplit: each A tile then feeds twice the outputs from shared memory, and
+// the tall, short-K layers of the decoder take half as many rounds.
 #include <cuda_bf16.h>
 
 #include "dc_internal.h"
@@ -26,7 +30,7 @@
 namespace dc {
 namespace gemm {
 
-constexpr int BM = 128, BN = 128;
+constexpr int BM = 128, BN = 128;  // BN: the narrow tile; Cfg::TBN the launched one
 constexpr int kEpiWarps = 16;
 constexpr int kThreads = (kEpiWarps + 2) * 32;
 
@@ -38,21 +42,23 @@ enum : int {
     EPI_ATOMIC = 16,   // split-K: C += value with atomics (C pre-initialised)
 };
 
-template <class E, bool A_MN, bool B_MN>
+template <class E, bool A_MN, bool B_MN, int TBN_ = BN>
 struct Cfg {
+    static constexpr int TBN = TBN_;
     static constexpr bool TF32 = sizeof(E) == 4;
     static constexpr int BKe = 128 / (int)sizeof(E);     // K elements per stage (128 B rows)
     static constexpr int UK = TF32 ? 8 : 16;             // K per MMA instruction
     static constexpr int NSUB = BKe / UK;
     static constexpr int BOX_MN = 128 / (int)sizeof(E);  // MN elements in one 128 B block
-    static constexpr int TILE_BYTES = 128 * 128;
-    static constexpr int STAGE_BYTES = 2 * TILE_BYTES;
-    static constexpr int STAGES = 6;
-    static constexpr uint32_t IDESC = umma_idesc(TF32 ? 2u : 1u, BM, BN, A_MN, B_MN);
+    static constexpr int TILE_BYTES = 128 * 128;        // A: 128 rows x 128 B of K
+    static constexpr int B_BYTES = TBN * 128;           // B: TBN columns x 128 B of K
+    static constexpr int STAGE_BYTES = TILE_BYTES + B_BYTES;
+    static constexpr int STAGES = TBN == 128 ? 6 : 4;
+    static constexpr uint32_t IDESC = umma_idesc(TF32 ? 2u : 1u, BM, TBN, A_MN, B_MN);
     static constexpr uint32_t MN_LBO = BKe * 128;
     static constexpr uint32_t MN_LAYOUT = TF32 ? 1u : 2u;
     static constexpr uint32_t MN_SBO = TF32 ? 512u : 1024u;
-    static constexpr uint32_t TMEM_COLS = 2 * BN;
+    static constexpr uint32_t TMEM_COLS = 2 * TBN;
     static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 512;
     static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 };
@@ -175,6 +181,7 @@ struct Tile {
     int m0, n0, k0, k1, split;
 };
 
+template <int TBN>
 __device__ __forceinline__ Tile decode_tile(const Params &p, int idx)
 {
     Tile t;
@@ -182,7 +189,7 @@ __device__ __forceinline__ Tile decode_tile(const Params &p, int idx)
     t.split = idx / per;
     const int rem = idx % per;
     t.m0 = (rem / p.tiles_n) * BM;
-    t.n0 = (rem % p.tiles_n) * BN;
+    t.n0 = (rem % p.tiles_n) * TBN;
     t.k0 = (int)(((long long)t.split * p.ksteps) / p.splits);
     t.k1 = (int)(((long long)(t.split + 1) * p.ksteps) / p.splits);
     return t;
@@ -194,12 +201,12 @@ __device__ __forceinline__ int sched_tile(int j, int ntiles)
     return t < ntiles ? t : -1;
 }
 
-template <class E, bool A_MN, bool B_MN>
+template <class E, bool A_MN, bool B_MN, int TBN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtensorMap mapA,
                    const __grid_constant__ CUtensorMap mapB)
 {
-    using C = Cfg<E, A_MN, B_MN>;
+    using C = Cfg<E, A_MN, B_MN, TBN>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -254,7 +261,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int jt = 0; !stop; ++jt) {
                 const int tile = sched_tile(jt, ntiles);
                 if (tile < 0) break;
-                const Tile tl = decode_tile(p, tile);
+                const Tile tl = decode_tile<TBN>(p, tile);
                 for (int k = tl.k0; k < tl.k1; ++k, ++g) {
                     const int s = g % C::STAGES;
                     if (!mbar_wait(smem_u32(&empty[s]), ((g / C::STAGES) & 1) ^ 1, abort_flag,
@@ -276,10 +283,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     if (B_MN) {
 #pragma unroll
-                        for (int j = 0; j < BN / C::BOX_MN; ++j)
+                        for (int j = 0; j < TBN / C::BOX_MN; ++j)
                             tma_load_2d(sb + j * C::MN_LBO, &mapB, fb, tl.n0 + j * C::BOX_MN, kx);
                     } else {
-                        tma_load_2d(sb, &mapB, fb, kx, tl.n0);
+                        // K-major rows in 128-row boxes; the 8-row swizzle
+                        // atoms of the second continue those of the first
+#pragma unroll
+                        for (int j = 0; j < TBN / 128; ++j)
+                            tma_load_2d(sb + j * C::TILE_BYTES, &mapB, fb, kx, tl.n0 + 128 * j);
                     }
                 }
             }
@@ -298,13 +309,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (uint32_t j = 0; !stop; ++j) {
                 const int tile = sched_tile(j, ntiles);
                 if (tile < 0) break;
-                const Tile tl = decode_tile(p, tile);
+                const Tile tl = decode_tile<TBN>(p, tile);
                 const uint32_t buf = j & 1, use = j >> 1;
                 if (!mbar_wait(smem_u32(&acce[buf]), (use & 1) ^ 1, abort_flag, p.status,
                                DC_DEVERR_TIMEOUT_ACC))
                     break;
                 tc_fence_after();
-                const uint32_t acc = tmem + buf * BN;
+                const uint32_t acc = tmem + buf * TBN;
                 for (int k = tl.k0; k < tl.k1; ++k, ++g) {
                     const int s = g % C::STAGES;
                     if (!mbar_wait(smem_u32(&full[s]), (g / C::STAGES) & 1, abort_flag, p.status,
@@ -345,19 +356,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (uint32_t j = 0;; ++j) {
             const int tile = sched_tile(j, ntiles);
             if (tile < 0) break;
-            const Tile tl = decode_tile(p, tile);
+            const Tile tl = decode_tile<TBN>(p, tile);
             const uint32_t buf = j & 1, use = j >> 1;
             const bool ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&accf[buf]), use & 1,
                                                               abort_flag, p.status,
                                                               DC_DEVERR_TIMEOUT_ACC));
             if (!ok) break;
             tc_fence_after();
-            const uint32_t lane_addr = tmem + buf * BN + ((uint32_t)(quad * 32) << 16) + slice * 32;
+            // a quarter of the tile's columns per warp of a lane quadrant
+            constexpr int QC = TBN / 4;
+            const uint32_t lane_addr = tmem + buf * TBN + ((uint32_t)(quad * 32) << 16) + slice * QC;
 #pragma unroll 1
-            for (int sb = 0; sb < 2; ++sb) {
+            for (int sb = 0; sb < QC / 16; ++sb) {
                 float v[16];
                 tmem_ld16(lane_addr + sb * 16, v);
-                epilogue16(p, tl.m0 + row, tl.n0 + slice * 32 + sb * 16, tl.split, v);
+                epilogue16(p, tl.m0 + row, tl.n0 + slice * QC + sb * 16, tl.split, v);
             }
             tc_fence_before();
             __syncwarp();
@@ -400,16 +413,16 @@ static int map_operand(CUtensorMap *m, const void *base, int esz, int rows, int 
     return encode_tmap(m, tmap_type(esz), 2, base, dims, strides, box, sw);
 }
 
-template <class E, bool A_MN, bool B_MN>
+template <class E, bool A_MN, bool B_MN, int TBN>
 static int launch(Params p, const void *A, int lda, const void *B, int ldb, cudaStream_t st)
 {
-    using C = Cfg<E, A_MN, B_MN>;
+    using C = Cfg<E, A_MN, B_MN, TBN>;
     static bool attr_set[64] = {false};
     int dev = 0;
     DC_CUDA_TRY(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64) return fail(DC_ERR_UNSUPPORTED, "device ordinal %d", dev);
     if (!attr_set[dev]) {
-        DC_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel<E, A_MN, B_MN>,
+        DC_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel<E, A_MN, B_MN, TBN>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          C::SMEM_BYTES));
         attr_set[dev] = true;
@@ -425,22 +438,22 @@ static int launch(Params p, const void *A, int lda, const void *B, int ldb, cuda
     const int grid = std::max(1, std::min(p.n_tiles, sm_count()));
     {
         KernelTimer kt("gemm_tc", st);
-        DC_CUDA_TRY(launch_pdl(gemm_tc_kernel<E, A_MN, B_MN>, dim3(grid), dim3(kThreads),
+        DC_CUDA_TRY(launch_pdl(gemm_tc_kernel<E, A_MN, B_MN, TBN>, dim3(grid), dim3(kThreads),
                                C::SMEM_BYTES, st, 1, p, mA, mB));
     }
     DC_CUDA_TRY(cudaGetLastError());
     return DC_OK;
 }
 
-template <class E>
+template <class E, int TBN>
 static int dispatch(const Params &p, bool ta, bool tb, const void *A, int lda, const void *B,
                     int ldb, cudaStream_t st)
 {
     // op(B) = B   -> B stored [K,N] -> MN-major;  op(B) = B^T -> K-major
-    if (!ta && !tb) return launch<E, false, true>(p, A, lda, B, ldb, st);
-    if (!ta && tb) return launch<E, false, false>(p, A, lda, B, ldb, st);
-    if (ta && !tb) return launch<E, true, true>(p, A, lda, B, ldb, st);
-    return launch<E, true, false>(p, A, lda, B, ldb, st);
+    if (!ta && !tb) return launch<E, false, true, TBN>(p, A, lda, B, ldb, st);
+    if (!ta && tb) return launch<E, false, false, TBN>(p, A, lda, B, ldb, st);
+    if (ta && !tb) return launch<E, true, true, TBN>(p, A, lda, B, ldb, st);
+    return launch<E, true, false, TBN>(p, A, lda, B, ldb, st);
 }
 
 static bool aligned(const void *q, int bytes)
@@ -497,14 +510,18 @@ extern "C" int dc_gemm(const void *A, int lda, const void *B, int ldb, float *C,
     p.epi = ((flags & DC_GEMM_BIAS) ? EPI_BIAS : 0) | (gelu ? EPI_GELU : 0) |
             (gelu_bwd ? EPI_GELU_BWD : 0) | (R ? EPI_RESID : 0);
     p.tiles_m = (M + BM - 1) / BM;
-    p.tiles_n = (N + BN - 1) / BN;
+    const int sms = sm_count();
+    // 128 x 256 tiles where they fill at least half the SMs unsplit
+    const int wide_tiles = p.tiles_m * ((N + 255) / 256);
+    const int tbn = N >= 256 && 2 * wide_tiles >= sms ? 256 : BN;
+    p.tiles_n = (N + tbn - 1) / tbn;
     const int bke = 128 / esz;
     p.ksteps = (K + bke - 1) / bke;
     // split K when the tiles leave SMs idle and the epilogue is linear, down
     // to one K step a split: the decode step's 64-row products are latency
     // bound, and more, shorter splits measured faster (C5: 121k -> 126k
     // tokens/s with at least 4 / 1 K steps a split)
-    const int tiles = p.tiles_m * p.tiles_n, sms = sm_count();
+    const int tiles = p.tiles_m * p.tiles_n;
     int splits = 1;
     if (!gelu && !gelu_bwd && tiles * 2 <= sms)
         splits = std::max(1, std::min(sms / tiles, p.ksteps));
@@ -523,6 +540,10 @@ extern "C" int dc_gemm(const void *A, int lda, const void *B, int ldb, float *C,
                                           cudaMemcpyDeviceToDevice, st));
         p.epi = (p.epi & EPI_BIAS) | EPI_ATOMIC;
     }
-    if (dtype == DC_F32) return dispatch<float>(p, ta, tb, A, lda, B, ldb, st);
-    return dispatch<__nv_bfloat16>(p, ta, tb, A, lda, B, ldb, st);
+    if (tbn == 256) {
+        if (dtype == DC_F32) return dispatch<float, 256>(p, ta, tb, A, lda, B, ldb, st);
+        return dispatch<__nv_bfloat16, 256>(p, ta, tb, A, lda, B, ldb, st);
+    }
+    if (dtype == DC_F32) return dispatch<float, BN>(p, ta, tb, A, lda, B, ldb, st);
+    return dispatch<__nv_bfloat16, BN>(p, ta, tb, A, lda, B, ldb, st);
 }

@@ -348,8 +348,10 @@ int dc_gate_fwd(const float *q, int ldq, const float *v0, float *out, int ldo, i
     const size_t n = (size_t)M * N;
     KernelTimer kt("gate_fwd", st);
     if (N % 4 == 0 && ldq % 4 == 0 && ldo % 4 == 0 && aligned16(q) && aligned16(v0) && aligned16(out)) {
+        // one row a thread for short inputs (the decode step's 64 rows are
+        // latency-bound), up to eight blocks an SM for long ones
         const int cb = (N / 4 + 31) / 32;
-        const int rb = std::max(1, std::min((M + 31) / 32, (8 * sm_count() + cb - 1) / cb));
+        const int rb = std::max(1, std::min((M + 7) / 8, (8 * sm_count() + cb - 1) / cb));
         DC_CUDA_TRY(launch_pdl(gate_fwd_vec, dim3(cb, rb), dim3(256), 0, st, 1, (const float4 *)q,
                                ldq / 4, (const float4 *)v0, (float4 *)out, ldo / 4, M, N / 4));
         return DC_OK;

@@ -119,6 +119,8 @@ class AftDecoder:
         # the backward's weight and bias gradients (off the input-gradient
         # chain) run on a second stream beside it
         self._wgrad_stream = torch.cuda.Stream(self.device) if self.device.type == "cuda" else None
+        # False: every launch on the caller's stream (per-kernel timing)
+        self.concurrent = True
 
     def _view(self, flat, name):
         off, shape = self._offsets[name]
@@ -244,14 +246,14 @@ class AftDecoder:
         pos, dpos = self.P[f"{l}.pos"], self.G[f"{l}.pos"]
         q0 = qkv.data_ptr()
         main = torch.cuda.current_stream()
-        side = self._head_streams
+        side = self._head_streams if self.concurrent else []
         if side:  # fork: the head streams start after what the caller queued
             fork = torch.cuda.Event()
             fork.record(main)
             for s in side:
                 s.wait_event(fork)
         for h in range(c.n_heads):
-            st = (main if h == 0 else side[h - 1]).cuda_stream
+            st = (side[h - 1] if h and side else main).cuda_stream
             Q, K, Vv = (q0 + 4 * (j * d + h * hs) for j in range(3))
             w = pos[h].data_ptr()
             if not backward:
@@ -327,7 +329,8 @@ class AftDecoder:
         ops.ce_bwd(b["logits"], b["targets"], grad_scale=b["scale"], out=b["dlog"])
         check(lib().dc_copy2d(b["dlog_pad"].data_ptr(), self.Vp * 4, b["dlog"].data_ptr(), V * 4, V * 4,
                               B * T, st), "dc_copy2d")
-        main, side = torch.cuda.current_stream(), self._wgrad_stream
+        main = torch.cuda.current_stream()
+        side = self._wgrad_stream if self.concurrent else main
 
         def fork():
             """Side work queued after this point sees what main has queued so far."""

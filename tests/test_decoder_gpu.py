@@ -101,6 +101,55 @@ def test_train_step_matches_float64(mods):
     assert ops.device_status() == 0
 
 
+def test_concurrent_streams_match_serial(mods):
+    """Heads on their own streams and the weight gradients beside the
+    input-gradient chain give the gradients of the all-on-one-stream step, in
+    a captured CUDA graph too (up to the order of split-K atomics)."""
+    decoder, ops, _, _ = mods
+    cfg = tiny_cfg(decoder, vocab=29, d_model=128, n_heads=4, block_size=64)
+    m = decoder.AftDecoder(cfg, seed=7, std=0.1)
+    g = torch.Generator().manual_seed(8)
+    idx = torch.randint(0, cfg.vocab, (16, 64), generator=g, dtype=torch.int32).cuda()
+    tgt = torch.randint(0, cfg.vocab, (16, 64), generator=g, dtype=torch.int32).cuda()
+
+    def step():
+        m.forward(idx, tgt)
+        m.backward()
+
+    def close(a, b):
+        # per parameter, normwise.  Two all-on-one-stream steps already differ
+        # by up to 5e-4 here (split-K atomics add in a different order every
+        # run, and the differences travel down the input-gradient chain); a
+        # stream race would hand a kernel a stale or half-written buffer.
+        for k in m.G:
+            off, shape = m._offsets[k]
+            n = int(np.prod(shape))
+            x, y = a[off:off + n].double(), b[off:off + n].double()
+            assert float((x - y).norm()) <= 2e-3 * float(y.norm()) + 1e-9, k
+
+    m.concurrent = False
+    step()
+    serial = m.grad.clone()
+    m.concurrent = True
+    step()
+    torch.cuda.synchronize()
+    close(m.grad, serial)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        step()  # warm the graph's allocations on the capture stream
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    m.grad.zero_()
+    graph.replay()
+    torch.cuda.synchronize()
+    close(m.grad, serial)
+    del graph
+    assert ops.device_status() == 0
+
+
 def test_loss_decreases(mods):
     decoder, _, _, _ = mods
     cfg = tiny_cfg(decoder, vocab=13, d_model=64, n_heads=4, block_size=32)

@@ -56,6 +56,40 @@ def test_layouts(ops, ta, tb, dtype, M, N, K):
     assert rel(C, ref) < TOL[dtype]
 
 
+@pytest.mark.parametrize("ta,tb", [(False, False), (False, True), (True, False), (True, True)])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("M,N,K", [(4736, 512, 256), (4700, 300, 72)])
+def test_wide_tiles(ops, ta, tb, dtype, M, N, K):
+    """Enough rows for 128 x 256 tiles (one N = 256 MMA a K slice): the
+    K-major B operand in two 128-row boxes, the MN-major one in eight or
+    four 128-byte blocks; N = 300 leaves a partly empty last tile."""
+    if dtype == torch.bfloat16 and (M % 8 or N % 8 or K % 8):
+        pytest.skip("bf16 rows must be 16-byte multiples")
+    A, B, ref = operands(M, N, K, ta, tb, dtype, seed=5)
+    C = ops.gemm(A, B, trans_a=ta, trans_b=tb)
+    torch.cuda.synchronize()
+    assert rel(C, ref) < TOL[dtype]
+
+
+def test_wide_tiles_fused_epilogues(ops):
+    """Bias, GELU with the pre-activation kept, and a residual on 128 x 256
+    tiles (the decoder's feed-forward shapes)."""
+    M, N, K = 4736, 1024, 256
+    A, B, ref = operands(M, N, K, False, False, torch.float32, seed=6)
+    A, ref = A * 0.2, ref * 0.2
+    bias = torch.randn(N).cuda()
+    pre = torch.empty(M, N, device="cuda")
+    H = ops.gemm(A, B, bias=bias, gelu=True, gelu_aux=pre)
+    pre_ref = ref + bias.double().cpu()
+    assert rel(pre, pre_ref) < TOL[torch.float32]
+    assert rel(H, gelu64(pre_ref)) < TOL[torch.float32]
+    W = torch.randn(N, 256).cuda() * 0.05
+    R = torch.randn(M, 256).cuda()
+    Y = ops.gemm(H, W, residual=R)
+    yref = H.double().cpu() @ W.double().cpu() + R.double().cpu()
+    assert rel(Y, yref) < TOL[torch.float32]
+
+
 @pytest.mark.parametrize("M,N,K", [(64, 512, 512), (64, 2048, 512), (64, 512, 2048), (7, 65, 256)])
 def test_skinny_split_k(ops, M, N, K):
     """Few output tiles: K is split across CTAs (bias once, residual kept)."""
