@@ -437,9 +437,17 @@ def bench_decode(args, dev, rank, world, dist):
     roof = None
     if "aft_decode" in kern:
         k = kern["aft_decode"]
+        algo = dec_bytes / max(prof["aft_decode"][1], 1)
+        # measured DRAM traffic at one position, scaled to the mean launch by
+        # the algorithmic bytes (both grow with the history length t)
+        traffic = None
+        tf = ROOT / "profiles" / "decoder_c5_traffic.json"
+        if tf.exists():
+            t = json.loads(tf.read_text())
+            traffic = algo * t["dram_bytes_per_launch_at_t"] / t["algorithmic_bytes_per_launch_at_t"]
         roof = {"bound": "hbm", "achieved": k["GB/s"], "peak": P["hbm_gbs"], "unit": "GB/s",
-                "frac": k["hbm_frac"], "traffic": None, "kernel": "aft_decode", "peak_source": P["source"],
-                "algorithmic_bytes": dec_bytes / max(prof["aft_decode"][1], 1)}
+                "frac": k["hbm_frac"], "traffic": traffic, "kernel": "aft_decode", "peak_source": P["source"],
+                "algorithmic_bytes": algo}
     toks = m._dec["tokens"]
     h_prompt = prompt.cpu().pin_memory()
     h_toks = torch.empty(B, T0 + new, dtype=torch.int32).pin_memory()
