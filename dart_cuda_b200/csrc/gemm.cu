@@ -54,6 +54,7 @@ struct Cfg {
     static constexpr int B_BYTES = TBN * 128;           // B: TBN columns x 128 B of K
     static constexpr int STAGE_BYTES = TILE_BYTES + B_BYTES;
     static constexpr int STAGES = TBN == 128 ? 6 : 4;
+    static_assert(kEpiWarps * 2048 <= STAGES * STAGE_BYTES, "epilogue staging fits the stages");
     static constexpr uint32_t IDESC = umma_idesc(TF32 ? 2u : 1u, BM, TBN, A_MN, B_MN);
     static constexpr uint32_t MN_LBO = BKe * 128;
     static constexpr uint32_t MN_LAYOUT = TF32 ? 1u : 2u;
@@ -181,6 +182,81 @@ struct Tile {
     int m0, n0, k0, k1, split;
 };
 
+__device__ __forceinline__ void st_shared4(uint32_t a, float x, float y, float z, float w)
+{
+    asm volatile("st.shared.v4.f32 [%0], {%1,%2,%3,%4};" ::"r"(a), "f"(x), "f"(y), "f"(z), "f"(w)
+                 : "memory");
+}
+__device__ __forceinline__ float4 ld_shared4(uint32_t a)
+{
+    float4 x;
+    asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(x.x), "=f"(x.y), "=f"(x.z), "=f"(x.w)
+                 : "r"(a)
+                 : "memory");
+    return x;
+}
+
+// Epilogue of 16 accumulator columns of a warp's 32 rows (whole tiles,
+// 16-byte path, no split-K atomics).  The tcgen05 load gives lane i row i;
+// writing every lane's 64 bytes to global memory directly puts 32 rows, 32
+// sectors of 32 different lines, behind each store instruction.  Instead
+// the block goes through 2 KB of shared memory (16-byte chunk k of row i at
+// chunk k ^ ((i >> 1) & 3), conflict-free both ways) and comes back as four
+// lanes per row: every instruction then covers 8 rows x 64 contiguous bytes.
+// The streamed inputs (residual, GELU pre-activation) of all 4 passes are
+// loaded before the first store (R may alias C: same elements, read first).
+__device__ __forceinline__ void epilogue16_staged(const Params &p, int row0, int c0, int split,
+                                                  const float (&v)[16], uint32_t sbase, int lane)
+{
+    const int epi = p.epi;
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+        st_shared4(sbase + lane * 64 + ((k ^ ((lane >> 1) & 3)) << 4), v[4 * k], v[4 * k + 1],
+                   v[4 * k + 2], v[4 * k + 3]);
+    __syncwarp();
+    const int c = lane & 3;
+    const int gc = c0 + 4 * c;
+    float4 bb = make_float4(0.f, 0.f, 0.f, 0.f);
+    if ((epi & EPI_BIAS) && split == 0) bb = *reinterpret_cast<const float4 *>(p.bias + gc);
+    float4 in[4];
+    if (epi & (EPI_RESID | EPI_GELU_BWD)) {
+        const float *src = (epi & EPI_RESID) ? p.R : p.aux;
+        const int ld = (epi & EPI_RESID) ? p.ldr : p.ldx;
+#pragma unroll
+        for (int it = 0; it < 4; ++it)
+            in[it] = *reinterpret_cast<const float4 *>(
+                src + (size_t)(row0 + it * 8 + (lane >> 2)) * ld + gc);
+    }
+#pragma unroll
+    for (int it = 0; it < 4; ++it) {
+        const int r = it * 8 + (lane >> 2);
+        float4 x = ld_shared4(sbase + r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
+        x.x = x.x * p.alpha + bb.x;
+        x.y = x.y * p.alpha + bb.y;
+        x.z = x.z * p.alpha + bb.z;
+        x.w = x.w * p.alpha + bb.w;
+        const size_t grow = (size_t)(row0 + r);
+        if (epi & EPI_RESID) {
+            x.x += in[it].x;
+            x.y += in[it].y;
+            x.z += in[it].z;
+            x.w += in[it].w;
+        }
+        if (epi & EPI_GELU) {
+            if (p.aux) *reinterpret_cast<float4 *>(p.aux + grow * p.ldx + gc) = x;
+            x = make_float4(gelu_f(x.x), gelu_f(x.y), gelu_f(x.z), gelu_f(x.w));
+        } else if (epi & EPI_GELU_BWD) {
+            x.x *= gelu_d(in[it].x);
+            x.y *= gelu_d(in[it].y);
+            x.z *= gelu_d(in[it].z);
+            x.w *= gelu_d(in[it].w);
+        }
+        *reinterpret_cast<float4 *>(p.C + grow * p.ldc + gc) = x;
+    }
+    __syncwarp();  // the staging block is rewritten by the next pass
+}
+
 template <int TBN>
 __device__ __forceinline__ Tile decode_tile(const Params &p, int idx)
 {
@@ -210,6 +286,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    // the staged epilogue's 2 KB a warp: the pipeline stages, free once a
+    // CTA's last tile is in TMEM (its MMAs have read every stage, no load follows)
+    const uint32_t stg = smem_u32(smem);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::STAGES * C::STAGE_BYTES);
     uint64_t *full = bars;
     uint64_t *empty = bars + C::STAGES;
@@ -366,11 +445,24 @@ __global__ void __launch_bounds__(kThreads, 1)
             // a quarter of the tile's columns per warp of a lane quadrant
             constexpr int QC = TBN / 4;
             const uint32_t lane_addr = tmem + buf * TBN + ((uint32_t)(quad * 32) << 16) + slice * QC;
+            // a CTA's last tile, when whole and on the 16-byte path, goes
+            // through the staged form (its shared memory is then free; split-K
+            // atomics, and a residual together with GELU', keep the
+            // row-per-lane form).  Staging through memory of its own instead
+            // (32 KB more a CTA) sped the GEMMs up alone but slowed the
+            // decoder step: fewer other kernels' CTAs could share the SM.
+            const bool staged = sched_tile(j + 1, ntiles) < 0 && p.vec && !(p.epi & EPI_ATOMIC) &&
+                                (p.epi & (EPI_RESID | EPI_GELU_BWD)) != (EPI_RESID | EPI_GELU_BWD) &&
+                                tl.m0 + BM <= p.M && tl.n0 + TBN <= p.N;
 #pragma unroll 1
             for (int sb = 0; sb < QC / 16; ++sb) {
                 float v[16];
                 tmem_ld16(lane_addr + sb * 16, v);
-                epilogue16(p, tl.m0 + row, tl.n0 + slice * QC + sb * 16, tl.split, v);
+                if (staged)
+                    epilogue16_staged(p, tl.m0 + quad * 32, tl.n0 + slice * QC + sb * 16, tl.split, v,
+                                      stg + warp * 2048, lane);
+                else
+                    epilogue16(p, tl.m0 + row, tl.n0 + slice * QC + sb * 16, tl.split, v);
             }
             tc_fence_before();
             __syncwarp();
