@@ -197,8 +197,8 @@ __device__ __forceinline__ float4 ld_shared4(uint32_t a)
     return x;
 }
 
-// Epilogue of 16 accumulator columns of a warp's 32 rows (whole tiles,
-// 16-byte path, no split-K atomics).  The tcgen05 load gives lane i row i;
+// Epilogue of 16 accumulator columns of a warp's 32 rows (all in bounds,
+// 16-byte path; split-K partial sums are added with 16-byte atomics).  The tcgen05 load gives lane i row i;
 // writing every lane's 64 bytes to global memory directly puts 32 rows, 32
 // sectors of 32 different lines, behind each store instruction.  Instead
 // the block goes through 2 KB of shared memory (16-byte chunk k of row i at
@@ -237,6 +237,10 @@ __device__ __forceinline__ void epilogue16_staged(const Params &p, int row0, int
         x.z = x.z * p.alpha + bb.z;
         x.w = x.w * p.alpha + bb.w;
         const size_t grow = (size_t)(row0 + r);
+        if (epi & EPI_ATOMIC) {
+            atomicAdd(reinterpret_cast<float4 *>(p.C + grow * p.ldc + gc), x);
+            continue;
+        }
         if (epi & EPI_RESID) {
             x.x += in[it].x;
             x.y += in[it].y;
@@ -445,15 +449,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             // a quarter of the tile's columns per warp of a lane quadrant
             constexpr int QC = TBN / 4;
             const uint32_t lane_addr = tmem + buf * TBN + ((uint32_t)(quad * 32) << 16) + slice * QC;
-            // a CTA's last tile, when whole and on the 16-byte path, goes
-            // through the staged form (its shared memory is then free; split-K
-            // atomics, and a residual together with GELU', keep the
-            // row-per-lane form).  Staging through memory of its own instead
-            // (32 KB more a CTA) sped the GEMMs up alone but slowed the
-            // decoder step: fewer other kernels' CTAs could share the SM.
-            const bool staged = sched_tile(j + 1, ntiles) < 0 && p.vec && !(p.epi & EPI_ATOMIC) &&
+            // a CTA's last tile (under split-K its only one) goes through the
+            // staged form where the warp's 32 rows and the tile's columns are
+            // in bounds on the 16-byte path: its shared memory is then free (a
+            // residual together with GELU' keeps the row-per-lane form).
+            // Staging through memory of its own instead (32 KB more a CTA)
+            // sped the GEMMs up alone but slowed the decoder step: fewer other
+            // kernels' CTAs could share the SM.
+            const bool staged = sched_tile(j + 1, ntiles) < 0 && p.vec &&
                                 (p.epi & (EPI_RESID | EPI_GELU_BWD)) != (EPI_RESID | EPI_GELU_BWD) &&
-                                tl.m0 + BM <= p.M && tl.n0 + TBN <= p.N;
+                                tl.m0 + quad * 32 + 32 <= p.M && tl.n0 + TBN <= p.N;
 #pragma unroll 1
             for (int sb = 0; sb < QC / 16; ++sb) {
                 float v[16];
