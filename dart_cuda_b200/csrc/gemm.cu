@@ -608,12 +608,15 @@ extern "C" int dc_gemm(const void *A, int lda, const void *B, int ldb, float *C,
             (gelu_bwd ? EPI_GELU_BWD : 0) | (R ? EPI_RESID : 0);
     p.tiles_m = (M + BM - 1) / BM;
     const int sms = sm_count();
-    // 128 x 256 tiles where they fill at least half the SMs unsplit
+    // 128 x 256 tiles where they fill at least half the SMs unsplit, or
+    // where K is long enough to be split into many long units (the weight
+    // gradients' K = B*T): each A tile then feeds twice the outputs
     const int wide_tiles = p.tiles_m * ((N + 255) / 256);
-    const int tbn = N >= 256 && 2 * wide_tiles >= sms ? 256 : BN;
-    p.tiles_n = (N + tbn - 1) / tbn;
     const int bke = 128 / esz;
     p.ksteps = (K + bke - 1) / bke;
+    const bool long_k = !gelu && !gelu_bwd && p.ksteps >= 128 && 2 * wide_tiles <= sms;
+    const int tbn = N >= 256 && (2 * wide_tiles >= sms || long_k) ? 256 : BN;
+    p.tiles_n = (N + tbn - 1) / tbn;
     // split K when the tiles leave SMs idle and the epilogue is linear, down
     // to one K step a split: the decode step's 64-row products are latency
     // bound, and more, shorter splits measured faster (C5: 121k -> 126k

@@ -71,6 +71,20 @@ def test_wide_tiles(ops, ta, tb, dtype, M, N, K):
     assert rel(C, ref) < TOL[dtype]
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("M,N,K", [(256, 768, 8192), (200, 300, 8200)])
+def test_long_k_split(ops, dtype, M, N, K):
+    """Weight-gradient shapes (X^T dY over a long K): 128 x 256 tiles split
+    along K, partial sums added by 16-byte atomics from the staged epilogue;
+    M = 200 leaves half-empty row quadrants, N = 300 a ragged last tile."""
+    if dtype == torch.bfloat16 and (M % 8 or N % 8 or K % 8):
+        pytest.skip("bf16 rows must be 16-byte multiples")
+    A, B, ref = operands(M, N, K, True, False, dtype, seed=9)
+    C = ops.gemm(A, B, trans_a=True)
+    torch.cuda.synchronize()
+    assert rel(C, ref) < TOL[dtype] * (4 if dtype == torch.bfloat16 else 1)
+
+
 def test_wide_tiles_fused_epilogues(ops):
     """Bias, GELU with the pre-activation kept, and a residual on 128 x 256
     tiles (the decoder's feed-forward shapes)."""
