@@ -1,21 +1,27 @@
 """AFT-full fwd+bwd benchmark (tokens/s) on 1..N B200s.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2|c1|c4]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c4|c2|c1|c3|c5]
+                    [--scaling weak|strong]
     python bench.py --impl reference ...      # CPU oracle on the host cores
 
 One step = forward + backward of the causal AFT-full operator over one batch
 of synthetic sequences (seeded N(0,1) Q, K, V, dZ; w ~ N(0, 0.02)), the
-backward reusing the forward's operand panels.  Default workload: B=32, T=512,
-d=512, bf16 tensors, fp32 accumulation, per GPU (weak scaling); with N > 1
-GPUs every rank runs its own batch shard and the shared bias gradient dW is
-summed across ranks with one NCCL all-reduce inside the step.
+backward reusing the forward's operand panels.  Default workload: the
+long-context configuration B=8, T=4096, d=1024, bf16 tensors, fp32
+accumulation (tensor-core bound); c2 is B=32, T=512, d=512 (HBM bound).
+With N > 1 GPUs every rank runs its own batch shard (weak scaling: the
+configuration's B per rank; strong: B split over the ranks) and the shared
+bias gradient dW is summed across ranks with one NCCL all-reduce inside the
+step.
 
 `value`  : tokens/s of the whole job, inputs resident in HBM, device-timed
            with CUDA events, L2 flushed between steps (outside the events).
 `e2e`    : the same through the C ABI with host (pinned) buffers: each step
            copies Q, K, V, dZ host->device and Z, dQ, dK, dV, dW back.
-`roofline`: the dominant kernel's achieved bytes or FLOPs per launch over its
-           CUDA-event time, against the measured peaks.
+`roofline`: the dominant kernel's algorithmic FLOPs (or user-tensor bytes)
+           per launch over its CUDA-event time against the measured peaks,
+           and under `step` the whole step against t_roof = max(F / tensor
+           peak, user bytes / HBM bandwidth).
 """
 from __future__ import annotations
 
@@ -107,28 +113,58 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------ CPU
-def cpu_baseline(B, T, d, dtype_name, budget_s=10.0):
-    """Oracle port (fp32 C restatement, OpenMP over query rows) on the host
-    cores, on a bounded sample of the workload: as many of the B sequences as
-    fit the time budget.  Returns (tokens/s, cores, sample description)."""
-    import oracle
+class CpuSample:
+    """The oracle port (fp32 C restatement of the reference loops, OpenMP over
+    query rows) on the host cores, over a bounded sample of the workload.
 
-    cores = os.cpu_count() or 1
-    oracle.set_threads(cores)
-    rng = np.random.default_rng(0)
-    W = (0.02 * rng.standard_normal((T, T))).astype(np.float32)
+    In the reference algorithm every channel d of every sequence is
+    independent (only dW sums over them), so a sample of `dsub` channels of
+    `nseq` sequences costs nseq/B * dsub/d of a full step; its rate in
+    tokens/s is nseq * T * (dsub / d) / seconds."""
 
-    def one(nseq):
-        Q, K, V, dZ = (rng.standard_normal((nseq, T, d)).astype(np.float32) for _ in range(4))
+    def __init__(self, B, T, d, budget_s):
+        import oracle
+
+        self.oracle = oracle
+        self.cores = os.cpu_count() or 1
+        oracle.set_threads(self.cores)
+        self.B, self.T, self.d = B, T, d
+        rng = np.random.default_rng(0)
+        self.W = (0.02 * rng.standard_normal((T, T))).astype(np.float32)
+        self.rng = rng
+        # size the sample from a probe of a few channels of one sequence
+        dprobe = min(d, 8)
+        t = self._run(1, dprobe)
+        per_chan = t / dprobe  # seconds per channel of one sequence
+        if per_chan * d <= budget_s:
+            self.nseq, self.dsub = int(max(1, min(B, budget_s // (per_chan * d)))), d
+        else:
+            self.nseq, self.dsub = 1, int(max(1, min(d, budget_s // per_chan)))
+
+    def _run(self, nseq, dsub):
+        T = self.T
+        Q, K, V, dZ = (self.rng.standard_normal((nseq, T, dsub)).astype(np.float32) for _ in range(4))
         t0 = time.perf_counter()
-        oracle.aft_full_fwd(Q, K, V, W, True)
-        oracle.aft_full_bwd(Q, K, V, W, dZ, True)
+        self.oracle.aft_full_fwd(Q, K, V, self.W, True)
+        self.oracle.aft_full_bwd(Q, K, V, self.W, dZ, True)
         return time.perf_counter() - t0
 
-    t1 = one(1)
-    n = int(max(1, min(B, budget_s / max(t1, 1e-6))))
-    tn = one(n) if n > 1 else t1
-    return n * T / tn, cores, f"{n} of {B} sequences (T={T}, d={d}) fwd+bwd, fp32, {cores} threads, {tn:.2f} s"
+    def step(self):
+        """One timed sample: (seconds, tokens/s of the whole workload's rate)."""
+        t = self._run(self.nseq, self.dsub)
+        return t, self.nseq * self.T * (self.dsub / self.d) / t
+
+    def describe(self):
+        return (f"{self.nseq} of {self.B} sequences x {self.dsub} of {self.d} channels (T={self.T}) "
+                f"fwd+bwd per sample, fp32, {self.cores} threads; channels are independent in the "
+                f"reference algorithm, so the rate scales to the whole workload by d/{self.dsub}")
+
+
+def cpu_baseline(B, T, d, dtype_name, budget_s=10.0):
+    """Returns (tokens/s, cores, sample description) of one bounded sample."""
+    cs = CpuSample(B, T, d, budget_s)
+    secs, rate = cs.step()
+    return rate, cs.cores, cs.describe() + f", {secs:.2f} s"
 
 
 # ------------------------------------------------------------------ row ops
@@ -516,7 +552,10 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", default="c2", choices=sorted(CONFIGS) + sorted(DECODER_CONFIGS))
+    ap.add_argument("--config", default="c4", choices=sorted(CONFIGS) + sorted(DECODER_CONFIGS))
+    ap.add_argument("--scaling", default="weak", choices=["weak", "strong"],
+                    help="weak: every rank runs the configuration's B sequences; strong: the B "
+                         "sequences are split over the ranks (B divisible by N)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of a CUDA graph")
@@ -546,27 +585,43 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.scaling == "strong":
+        if B % world:
+            raise SystemExit(f"--scaling strong needs B ({B}) divisible by the rank count ({world})")
+        B //= world  # this rank's share of the configuration's sequences
     config = {"workload": desc, "B_per_gpu": B, "T": T, "d": d, "causal": True,
               "global_batch": B * world, "seq_len": T, "parallelism": f"batch-shard x{world}",
-              "l2": "flushed between steps (256 MiB write)",
+              "scaling": args.scaling,
+              "l2": "flushed between steps (256 MiB write); inputs larger than L2 at T=4096",
               "cuda_graph": not args.no_graph,
               "backward": "reads the forward's r, 1/den" if stats else "recomputes num/den"}
 
     if args.impl == "reference":
+        # The reference's CPU path (the oracle port) on the host cores: W
+        # untimed and K timed steps, each one bounded sample of this
+        # workload; ms_per_step is the measured time of a sample, so
+        # steps x ms_per_step is the arm's own timed wall time.
         if rank != 0:
             return
         K = max(1, args.steps)
-        vals = []
-        for _ in range(max(0, args.warmup)):
-            pass  # the oracle has no warm-up state; W is honoured by not timing it
-        tok_s, cores, sample = cpu_baseline(B, T, d, dt, budget_s=min(args.cpu_budget, 60.0 / K))
-        vals.append(tok_s)
+        W_ = max(0, args.warmup)
+        per_step = max(0.2, min(args.cpu_budget, 100.0 / (K + W_)))
+        cs = CpuSample(B * world, T, d, per_step)
+        for _ in range(W_):
+            cs.step()
+        secs, rates = [], []
+        for _ in range(K):
+            t, r = cs.step()
+            secs.append(t)
+            rates.append(r)
+        tok_s = len(secs) * cs.nseq * T * (cs.dsub / d) / sum(secs)
         line = {"metric": METRIC, "value": tok_s, "unit": "tokens/s", "impl": "reference", "n_gpus": args.gpus,
-                "steps": K, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+                "steps": K, "warmup": W_, "higher_is_better": True, "scaling": config["scaling"],
                 "dtype": "f32", "data": "synthetic", "config": config, "vs_baseline": None,
-                "ms_per_step": 1e3 * B * T / tok_s,
-                "cpu_baseline": {"value": tok_s, "unit": "tokens/s", "cores": cores, "kind": "port",
-                                 "sample": sample},
+                "ms_per_step": 1e3 * sum(secs) / K,
+                "step": "one bounded sample of the workload: " + cs.describe(),
+                "cpu_baseline": {"value": tok_s, "unit": "tokens/s", "cores": cs.cores, "kind": "port",
+                                 "sample": cs.describe()},
                 "e2e": {"value": tok_s, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
         return
@@ -771,61 +826,81 @@ def main():
     h2d = 4 * B * T * d * esz
     d2h = 4 * B * T * d * esz + T * T * 4
 
-    # ---- roofline of the dominant kernel
+    # ---- roofline.  Algorithmic work of one fwd+bwd step (per rank):
+    # F = 6 B d T(T+1) tensor-core FLOPs (three causal [num|den]-shaped
+    # contractions) and the user tensors' bytes: Q, K, V, dZ read and Z, dQ,
+    # dK, dV written (esz each), w read and dW written (fp32).
     P = peaks()
-    Tp = (T + 127) // 128 * 128
-    dp_ = (d + 127) // 128 * 128
-    io = B * T * d * esz           # one user tensor
-    pan = B * Tp * dp_ * esz        # one operand panel (E'V, E', g or n)
-    ap_ = Tp * Tp * esz
-    stat = B * Tp * dp_ * 4 if stats else 0  # one saved statistic (r or 1/den)
-    bytes_per = {
-        "aft_prep_w_colmax": T * T * 4 + ap_ + io,
-        "aft_prep_p": 2 * io + 2 * pan,
-        "aft_tc_fwd": 2 * pan + ap_ + 2 * io + 2 * stat,
-        "aft_tc_bwd_recompute": 2 * pan + ap_ + 3 * io + 2 * pan,
-        "aft_bwd_from_stats": 3 * io + 2 * stat + 2 * pan,
-        "aft_tc_dkdv": 2 * pan + ap_ + 4 * io,
-        "aft_tc_dw": 4 * pan + 2 * T * T * 4,
+    capped = "sw_power_cap" in sampler.summary()["reasons"]
+    p_tc = P["bf16_tflops_sustained"] if capped else P["bf16_tflops"]
+    io = B * T * d * esz            # one user tensor
+    wbytes = T * T * 4
+    step_flops = causal_flops(B, T, d)
+    step_bytes = 8 * io + 2 * wbytes
+    t_tc = step_flops / (p_tc * 1e12)
+    t_tc_burst = step_flops / (P["bf16_tflops"] * 1e12)
+    t_hbm = step_bytes / (P["hbm_gbs"] * 1e9)
+    t_roof = max(t_tc, t_hbm)
+    # per kernel: the user-tensor bytes each kernel must move (intermediate
+    # panels are not credited) and the FLOPs of its contraction
+    user_bytes = {
+        "aft_prep_w_colmax": wbytes + io,     # w, K
+        "aft_prep_p": 2 * io,                 # K, V
+        "aft_tc_fwd": 2 * io,                 # Q in, Z out
+        "aft_tc_bwd_recompute": 3 * io,       # Q, dZ in, dQ out
+        "aft_bwd_from_stats": 3 * io + wbytes,  # Q, dZ in, dQ out; clears dW
+        "aft_tc_dkdv": 4 * io,                # K, V in, dK, dV out
+        "aft_tc_dw": 2 * wbytes,              # w in, dW out
     }
     gemm = 2.0 * B * d * T * (T + 1)  # one [num|den] contraction, causal half
     flops_per = {"aft_tc_fwd": gemm, "aft_tc_bwd_recompute": gemm, "aft_tc_dkdv": gemm, "aft_tc_dw": gemm}
+    tot_ms = max(sum(m for m, _ in prof.values()), 1e-9)
     kern = {}
     for name, (ms, cnt) in prof.items():
         per_ms = ms / max(cnt, 1)
-        gbs = bytes_per.get(name, 0) / (per_ms / 1e3) / 1e9
+        gbs = user_bytes.get(name, 0) / (per_ms / 1e3) / 1e9
         tfs = flops_per.get(name, 0) / (per_ms / 1e3) / 1e12
-        kern[name] = {"ms_per_launch": per_ms, "launches": cnt, "share": ms / max(sum(m for m, _ in prof.values()), 1e-9),
-                      "GB/s": gbs, "TFLOP/s": tfs,
-                      "hbm_frac": gbs / P["hbm_gbs"], "tensor_frac": tfs / P["bf16_tflops"]}
+        kern[name] = {"ms_per_launch": per_ms, "launches": cnt, "share": ms / tot_ms,
+                      "user_GB/s": gbs, "TFLOP/s": tfs,
+                      "hbm_frac": gbs / P["hbm_gbs"], "tensor_frac": tfs / p_tc}
     dom = max(prof, key=lambda k: prof[k][0]) if prof else None
-    # measured DRAM traffic per launch (ncu capture summarised under profiles/)
+    # measured DRAM traffic per launch (ncu summaries under profiles/)
     traffic = None
+    traffic_step = None
     tf = ROOT / "profiles" / f"aft_{args.config}_traffic.json"
-    if dom and tf.exists():
-        traffic = json.loads(tf.read_text())["dram_bytes_per_launch"].get(dom)
+    if tf.exists():
+        tj = json.loads(tf.read_text())
+        per = tj["dram_bytes_per_launch"]
+        if dom:
+            traffic = per.get(dom)
+        if tj.get("B") == B and all(k in per for k in prof):
+            traffic_step = sum(per[k] * cnt for k, (_, cnt) in prof.items()) / max(args.steps, 1)
     roof = None
     if dom:
         k = kern[dom]
-        bound = "tensor" if k["tensor_frac"] > k["hbm_frac"] else "hbm"
-        if bound == "tensor":
-            # a run held at the power cap is compared with the sustained
-            # (power-capped) GEMM rate, a short one with the burst rate
-            capped = "sw_power_cap" in sampler.summary()["reasons"]
-            peak = P["bf16_tflops_sustained"] if capped else P["bf16_tflops"]
-            roof = {"bound": "tensor", "achieved": k["TFLOP/s"], "peak": peak, "unit": "TFLOP/s",
-                    "frac": k["TFLOP/s"] / peak, "traffic": traffic, "kernel": dom,
+        step = {"t_roof_ms": t_roof * 1e3, "t_measured_ms": ms_per_step, "frac": t_roof * 1e3 / ms_per_step,
+                "frac_vs_burst": max(t_tc_burst, t_hbm) * 1e3 / ms_per_step,
+                "bound": "tensor" if t_tc >= t_hbm else "hbm",
+                "flops": step_flops, "user_bytes": step_bytes,
+                "t_tensor_ms": t_tc * 1e3, "t_hbm_ms": t_hbm * 1e3,
+                "dram_traffic_bytes": traffic_step,
+                "traffic_over_user_bytes": traffic_step / step_bytes if traffic_step else None}
+        if dom in flops_per:
+            roof = {"bound": "tensor", "achieved": k["TFLOP/s"], "peak": p_tc, "unit": "TFLOP/s",
+                    "frac": k["TFLOP/s"] / p_tc, "traffic": traffic, "kernel": dom,
+                    "algorithmic_flops_per_launch": flops_per[dom],
                     "peak_source": P["source"] + (" bf16 sustained (sw_power_cap seen)" if capped
                                                   else " bf16 burst")}
         else:
-            roof = {"bound": "hbm", "achieved": k["GB/s"], "peak": P["hbm_gbs"], "unit": "GB/s",
+            roof = {"bound": "hbm", "achieved": k["user_GB/s"], "peak": P["hbm_gbs"], "unit": "GB/s",
                     "frac": k["hbm_frac"], "traffic": traffic, "kernel": dom, "peak_source": P["source"],
-                    "algorithmic_bytes": bytes_per.get(dom)}
+                    "algorithmic_bytes_per_launch": user_bytes.get(dom)}
+        roof["step"] = step
 
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": max(3, args.warmup), "ms_per_step": ms_per_step, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": dt, "data": "synthetic", "config": config,
+        "scaling": args.scaling, "vs_baseline": None, "dtype": dt, "data": "synthetic", "config": config,
         "tflops": causal_flops(B, T, d) * world / (ms_per_step / 1e3) / 1e12,
         "e2e": {"value": e2e_val, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "copies": "pinned host buffers; uploads, library calls and read-backs on three "

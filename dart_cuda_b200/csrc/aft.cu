@@ -31,6 +31,7 @@
 #include <math.h>
 
 #include <algorithm>
+#include <atomic>
 #include <initializer_list>
 
 #include "dc_internal.h"
@@ -125,6 +126,7 @@ __device__ __forceinline__ void epi_fwd(const Params &p, int b, int t, int d, fl
         const size_t row = (size_t)b * p.Tq + t;
         float s = sigmoidf_(ld_io((const IO *)p.Q, row * p.ldi + d));
         st_io((IO *)p.Z, row * p.ldo + d, s * (num / den));
+        if (p.status && (!(den >= 0x1p-100f) || !(fabsf(num) <= 3.0e38f))) atomicOr(p.status, DC_DEVERR_RANGE);
     }
 }
 
@@ -139,6 +141,7 @@ __device__ __forceinline__ void epi_bwd1(const Params &p, int b, int t, int d, f
         float s = sigmoidf_(ld_io((const IO *)p.Q, o));
         float dz = ld_io((const IO *)p.dZ, row * p.ldo + d);
         float r = num / den;
+        if (p.status && (!(den >= 0x1p-100f) || !(fabsf(num) <= 3.0e38f))) atomicOr(p.status, DC_DEVERR_RANGE);
         float dq = dz * r * s * (1.0f - s);
         if (p.accumulate) dq += ld_io((const IO *)p.dQ, o);
         st_io((IO *)p.dQ, o, dq);
@@ -525,6 +528,11 @@ __global__ void __launch_bounds__(256) bwd_stats_kernel(const Params p)
         const size_t so = ((size_t)b * p.Tqp + t) * p.dp + d0;
         ld16g(p.Rs + so, r);
         ld16g(p.Is + so, inv);
+        bool bad = false;  // the forward's range guard, on 1/den' and r
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+            bad |= d0 + j < p.D && (!(inv[j] <= 0x1p100f) || !(fabsf(r[j]) <= 3.0e38f));
+        if (bad) report_range(p);
     } else {
 #pragma unroll
         for (int j = 0; j < 16; ++j) r[j] = inv[j] = 0.f;
@@ -741,15 +749,17 @@ static int launch_tc(Params p, const Layout &L, char *ws, cudaStream_t st)
     static_assert(!P || sizeof(E) == 2, "CTA pairs run bf16 operands");
     using C = TcCfg<MODE, E, P>;
     constexpr int RB = P ? 2 * BM : BM;
-    static bool attr_set[64] = {false};  // per instantiation and device
+    // per instantiation and device; host threads may race to set them (the
+    // attribute call is idempotent), the flags themselves are atomic
+    static std::atomic<bool> attr_set[64];
     int dev = 0;
     DC_CUDA_TRY(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64) return fail(DC_ERR_UNSUPPORTED, "device ordinal %d", dev);
-    if (!attr_set[dev]) {
+    if (!attr_set[dev].load(std::memory_order_acquire)) {
         DC_CUDA_TRY(cudaFuncSetAttribute(aft_tc_kernel<MODE, E, IO, P>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          C::SMEM_BYTES));
-        attr_set[dev] = true;
+        attr_set[dev].store(true, std::memory_order_release);
     }
     // tensor maps: A, B1..B4 (B3/B4 only for the tf32 dK/dV low parts), A2..A4 (dW)
     CUtensorMap mA, mB1, mB2, mB3, mB4, mA2, mA3, mA4;
@@ -796,14 +806,15 @@ static int launch_tc(Params p, const Layout &L, char *ws, cudaStream_t st)
     cfg.numAttrs = 1;
     // persistent: one CTA (or CTA pair) per SM (pair); shared memory admits one.
     // Pairs need two SMs of one GPC: ask how many clusters fit at once.
-    static int max_clusters[64] = {0};
-    if (P && max_clusters[dev] == 0) {
+    static std::atomic<int> max_clusters[64];
+    if (P && max_clusters[dev].load(std::memory_order_acquire) == 0) {
         cfg.gridDim = dim3(2 * (sm_count() / 2));
         int n = 0;
         DC_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, aft_tc_kernel<MODE, E, IO, P>, &cfg));
-        max_clusters[dev] = std::max(1, n);
+        max_clusters[dev].store(std::max(1, n), std::memory_order_release);
     }
-    const int workers = P ? std::max(1, max_clusters[dev] - (p.spare_sms + 1) / 2)
+    const int workers = P ? std::max(1, max_clusters[dev].load(std::memory_order_acquire) -
+                                            (p.spare_sms + 1) / 2)
                           : std::max(1, sm_count() - p.spare_sms);
     // Schedule (decode_tile): bundles only pay with at least two tiles a
     // worker (with fewer they would leave workers idle).  Where whole rounds

@@ -249,12 +249,34 @@ __device__ __forceinline__ void epi_prefetch(const Params &p, int bb, int r, int
     }
 }
 
+// Range guard of the factorised stabilisation: an output whose denominator
+// den' (the sum of e^{w-m_t} e^{K-c_d} over the visible keys) is below 2^-100,
+// or whose numerator is not finite, is outside the range the factorisation
+// resolves (the reference's joint maximum never is); the call then reports
+// DC_DEVERR_RANGE in the device status word instead of passing inf or NaN on
+// silently.  Terms below 2^-126 that the operands or products lose are then
+// at most 2^-26 of den'.
+__device__ __forceinline__ bool out_of_range(float num, float den)
+{
+    return !(den >= 0x1p-100f) || !(fabsf(num) <= 3.0e38f);
+}
+__device__ __forceinline__ void report_range(const Params &p)
+{
+    if (p.status) atomicOr(p.status, DC_DEVERR_RANGE);
+}
+
 template <class IO, class E>
 __device__ __forceinline__ void epi16_fwd(const Params &p, int b, int t, int d0,
                                           const float (&num)[16], const float (&den)[16],
                                           const EpiPre &pf)
 {
     if (t >= p.Tq) return;
+    {
+        bool bad = false;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) bad |= d0 + j < p.D && out_of_range(num[j], den[j]);
+        if (bad) report_range(p);
+    }
     if (p.Rs) {  // r and 1/den for the backward, exactly as epi16_bwd1 forms them
         const size_t so = ((size_t)b * p.Tqp + t) * p.dp + d0;
         float r[16], inv[16];
@@ -364,6 +386,12 @@ __device__ __forceinline__ void epi16_bwd1(const Params &p, int b, int t, int d0
                                            const float (&num)[16], const float (&den)[16],
                                            const EpiPre &pf)
 {
+    if (t < p.Tq) {  // the range guard of epi16_fwd
+        bool bad = false;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) bad |= d0 + j < p.D && out_of_range(num[j], den[j]);
+        if (bad) report_range(p);
+    }
     float r[16], inv[16];
 #pragma unroll
     for (int j = 0; j < 16; ++j) {

@@ -2,6 +2,7 @@
 #include <stdarg.h>
 #include <string.h>
 
+#include <atomic>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -25,7 +26,7 @@ void clear_error() { g_last_error[0] = '\0'; }
 
 static constexpr int kMaxDevices = 64;
 static int *g_status[kMaxDevices] = {nullptr};
-static int g_sms[kMaxDevices] = {0};
+static std::atomic<int> g_sms[kMaxDevices];
 static std::mutex g_dev_mutex;
 
 int *device_status_word()
@@ -46,12 +47,13 @@ int sm_count()
 {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 148;
-    if (!g_sms[dev]) {
-        int n = 0;
+    int n = g_sms[dev].load(std::memory_order_relaxed);
+    if (!n) {
         cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-        g_sms[dev] = n > 0 ? n : 148;
+        n = n > 0 ? n : 148;
+        g_sms[dev].store(n, std::memory_order_relaxed);
     }
-    return g_sms[dev];
+    return n;
 }
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
@@ -193,7 +195,9 @@ int dc_device_status(void *stream, int *bits)
     if (bits) *bits = h;
     if (h) {
         DC_CUDA_TRY(cudaMemset(w, 0, sizeof(int)));
-        return dc::fail(DC_ERR_DEVICE, "device status bits 0x%x (bounded wait gave up)", h);
+        return dc::fail(DC_ERR_DEVICE, "device status bits 0x%x (0x1-0x10: a bounded wait gave up; "
+                        "0x20: token id out of range; 0x40: decode past capacity; "
+                        "0x80: AFT input outside the factorised range)", h);
     }
     return DC_OK;
 }

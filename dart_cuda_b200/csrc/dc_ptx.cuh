@@ -19,6 +19,7 @@
 #define DC_DEVERR_TIMEOUT_ACC   0x4   // epilogue waited too long for the accumulator
 #define DC_DEVERR_TIMEOUT_DRAIN 0x8   // drain after an abort did not finish
 #define DC_DEVERR_TMEM          0x10  // TMEM allocation returned an unusable address
+#define DC_DEVERR_RANGE         0x80  // AFT: a denominator below 2^-100 (factorised range)
 
 namespace dc {
 

@@ -24,6 +24,8 @@
 // the tall, short-K layers of the decoder take half as many rounds.
 #include <cuda_bf16.h>
 
+#include <atomic>
+
 #include "dc_internal.h"
 #include "dc_ptx.cuh"
 
@@ -514,15 +516,17 @@ template <class E, bool A_MN, bool B_MN, int TBN>
 static int launch(Params p, const void *A, int lda, const void *B, int ldb, cudaStream_t st)
 {
     using C = Cfg<E, A_MN, B_MN, TBN>;
-    static bool attr_set[64] = {false};
+    // per instantiation and device; host threads may race to set them (the
+    // attribute call is idempotent), the flags themselves are atomic
+    static std::atomic<bool> attr_set[64];
     int dev = 0;
     DC_CUDA_TRY(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64) return fail(DC_ERR_UNSUPPORTED, "device ordinal %d", dev);
-    if (!attr_set[dev]) {
+    if (!attr_set[dev].load(std::memory_order_acquire)) {
         DC_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel<E, A_MN, B_MN, TBN>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          C::SMEM_BYTES));
-        attr_set[dev] = true;
+        attr_set[dev].store(true, std::memory_order_release);
     }
     const int esz = (int)sizeof(E);
     CUtensorMap mA, mB;

@@ -948,12 +948,9 @@ int dc_layernorm_bwd(const float *x, const float *gamma, const float *dy, float 
             (void)launch_pdl(ln_bwd_warp<4>, dim3(nparts), dim3(32 * wpb), shbytes, st, 1, x,
                              gamma, dy, dx, part, R, C, eps, accumulate, rows_per_cta);
         else {
-            static bool attr = false;
-            if (!attr) {
-                cudaFuncSetAttribute(ln_bwd_warp<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)shbytes);
-                attr = true;
-            }
+            // idempotent: concurrent first calls may both set it
+            cudaFuncSetAttribute(ln_bwd_warp<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)shbytes);
             (void)launch_pdl(ln_bwd_warp<8>, dim3(nparts), dim3(32 * wpb), shbytes, st, 1, x,
                              gamma, dy, dx, part, R, C, eps, accumulate, rows_per_cta);
         }
@@ -1067,10 +1064,14 @@ int dc_ce_fwd(const float *logits, const int32_t *targets, float *loss, float *r
 // process exits.  It is shared by every call on a device and holds the last
 // call's row losses; each call overwrites all T entries it reads, so nothing
 // needs clearing, but calls that overlap on the GPU (other streams, other
-// host threads) race on it and must be serialised by the caller.
+// host threads) race on it and must be serialised by the caller.  Calls
+// queued back to back on one stream are ordered: every kernel of a call waits
+// for the previous kernel on the stream to finish before it touches memory.
 // The first call on each device looks the array's device address up (the
-// host-side symbol is only a stand-in for it); make that first call before
-// any stream capture.
+// host-side symbol is only a stand-in for it) and caches it; make that first
+// call before any stream capture.  The cache does not survive a device reset:
+// after cudaDeviceReset the module is loaded again and the array may move, so
+// a process that resets a device must not call this entry point afterwards.
 // ---------------------------------------------------------------------------
 #define DC_CE_NOALLOC_MAX_ROWS 65536
 

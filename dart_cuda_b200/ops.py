@@ -151,11 +151,26 @@ def aft_bwd(Q, K, V, w, dZ, causal=True, grads=None, accumulate=False,
     return dQ, dK, dV, dW
 
 
+DC_STATUS_AFT_RANGE = 0x80  # an AFT-full input outside the factorised range
+
+
 def device_status(sync_stream=True) -> int:
-    """Synchronise and return the device status bits (0 = no kernel gave up a
-    bounded wait); raises DcError when bits are set."""
+    """Synchronise and return the device status bits (0 = no kernel reported
+    anything); raises DcError when bits are set."""
     bits = c_int(0)
     check(lib().dc_device_status(_stream(), byref(bits)), "dc_device_status")
+    return bits.value
+
+
+def read_status() -> int:
+    """Synchronise, read and clear the device status bits without raising:
+    0x1-0x10 a bounded wait gave up, 0x20 token id out of range, 0x40 decode
+    past capacity, 0x80 (DC_STATUS_AFT_RANGE) an AFT-full input outside the
+    range of the factorised stabilisation."""
+    bits = c_int(0)
+    rc = lib().dc_device_status(_stream(), byref(bits))
+    if rc not in (0, 5):  # DC_OK, DC_ERR_DEVICE
+        check(rc, "dc_device_status")
     return bits.value
 
 

@@ -70,8 +70,23 @@ extern "C" {
 const char *dc_last_error(void);
 
 /* Synchronise `stream`, read and clear the device status word of the current
- * device.  Returns DC_OK, DC_ERR_DEVICE (a kernel gave up a bounded wait; the
- * bits are stored in *bits when non-NULL) or DC_ERR_CUDA. */
+ * device.  Returns DC_OK, DC_ERR_DEVICE (some kernel since the last read
+ * reported a condition; the bits are stored in *bits when non-NULL) or
+ * DC_ERR_CUDA.  Bits:
+ *   0x01-0x10  a bounded wait of a tensor-core kernel gave up (the kernel
+ *              stopped early; its outputs are incomplete)
+ *   0x20       dc_embedding_fwd saw a token id outside [0, V)
+ *   0x40       dc_greedy_embed ran past the token buffer's capacity
+ *   0x80       DC_STATUS_AFT_RANGE: an AFT-full call met inputs outside the
+ *              range of its factorised stabilisation.  The kernels scale by
+ *              the row maxima of w and the column maxima of K separately
+ *              (the reference takes one joint maximum per (t, d)); when, for
+ *              some (t, d), every visible term e^{w[t,i]-m_t} e^{K[i,d]-c_d}
+ *              is below 2^-100 (e.g. a row's w and a column's K rising in
+ *              opposite directions over a combined spread of about 70 or
+ *              more), that output and its gradients are not reliable and this
+ *              bit is set instead of the error passing silently. */
+#define DC_STATUS_AFT_RANGE 0x80
 int dc_device_status(void *stream, int *bits);
 
 /* Library version string. */
@@ -167,8 +182,11 @@ int dc_ce_bwd(const float *logits, const int32_t *targets, const float *grad_sca
  * call.  The per-row losses live in a fixed array inside the library, so
  * T <= 65536; larger T returns DC_ERR_INVALID.  The array is shared by all
  * calls on a device: calls that overlap on the GPU race and must be
- * serialised by the caller.  The first call on each device resolves the
- * array's device address; make it before any stream capture. */
+ * serialised by the caller (calls queued on one stream are ordered).  The
+ * first call on each device resolves the array's device address and caches
+ * it; make it before any stream capture.  The cached address does not
+ * survive cudaDeviceReset: do not call this entry point on a device after
+ * resetting it. */
 int dc_ce_fwd_noalloc(const float *logits, const int32_t *targets, float *loss, int T, int V,
                       float eps, void *stream);
 

@@ -67,23 +67,40 @@ void oracle_set_threads(int n)
  * ---------------------------------------------------------------------- */
 static void aft_full_fwd_row(const float *Q, const float *K, const float *V,
                              const float *WB, float *out, int T, int D,
-                             int masked, int ldw, int t)
+                             int masked, int ldw, int t, float *scratch)
 {
+    /* The reference's per-(t,d) loops over tp, evaluated for all d of row t
+     * at once (d innermost, so K and V rows are read contiguously).  Every
+     * (t,d) sees exactly the reference's sequence of operations: the max over
+     * tp in increasing tp, then num and den summed in increasing tp. */
+    float *max_val = scratch, *numerator = scratch + D, *denominator = scratch + 2 * D;
+    int limit = masked ? (t + 1) : T;
+    const float *wrow = WB + (size_t)t * ldw;
     for (int d = 0; d < D; d++) {
-        int limit = masked ? (t + 1) : T;
-        float max_val = -1e20f;
-        for (int tp = 0; tp < limit; tp++) {
-            float val = K[tp * D + d] + WB[(size_t)t * ldw + tp];
-            if (val > max_val) max_val = val;
+        max_val[d] = -1e20f;
+        numerator[d] = 0.0f;
+        denominator[d] = 0.0f;
+    }
+    for (int tp = 0; tp < limit; tp++) {
+        const float wv = wrow[tp];
+        const float *k = K + (size_t)tp * D;
+        for (int d = 0; d < D; d++) {
+            float val = k[d] + wv;
+            if (val > max_val[d]) max_val[d] = val;
         }
-        float numerator = 0.0f, denominator = 0.0f;
-        for (int tp = 0; tp < limit; tp++) {
-            float w = expf(K[tp * D + d] + WB[(size_t)t * ldw + tp] - max_val);
-            numerator += w * V[tp * D + d];
-            denominator += w;
+    }
+    for (int tp = 0; tp < limit; tp++) {
+        const float wv = wrow[tp];
+        const float *k = K + (size_t)tp * D, *v = V + (size_t)tp * D;
+        for (int d = 0; d < D; d++) {
+            float w = expf(k[d] + wv - max_val[d]);
+            numerator[d] += w * v[d];
+            denominator[d] += w;
         }
-        float sigQ = 1.0f / (1.0f + expf(-Q[t * D + d]));
-        out[t * D + d] = sigQ * (numerator / (denominator + 1e-6f));
+    }
+    for (int d = 0; d < D; d++) {
+        float sigQ = 1.0f / (1.0f + expf(-Q[(size_t)t * D + d]));
+        out[(size_t)t * D + d] = sigQ * (numerator[d] / (denominator[d] + 1e-6f));
     }
 }
 
@@ -94,51 +111,82 @@ void oracle_aft_full_fwd(const float *Q, const float *K, const float *V,
 {
     size_t sd = (size_t)T * D;
     long total = (long)B * T;
-#pragma omp parallel for schedule(dynamic, 1)
-    for (long bt = total - 1; bt >= 0; bt--) {
-        int b = (int)(bt / T), t = (int)(bt % T);
-        aft_full_fwd_row(Q + b * sd, K + b * sd, V + b * sd, WB, out + b * sd,
-                         T, D, masked, ldw, t);
+#pragma omp parallel
+    {
+        float *scratch = (float *)malloc((size_t)3 * D * sizeof(float));
+#pragma omp for schedule(dynamic, 1)
+        for (long bt = total - 1; bt >= 0; bt--) {
+            int b = (int)(bt / T), t = (int)(bt % T);
+            if (scratch)
+                aft_full_fwd_row(Q + b * sd, K + b * sd, V + b * sd, WB, out + b * sd,
+                                 T, D, masked, ldw, t, scratch);
+        }
+        free(scratch);
     }
 }
 
 /* ------------------------------------------------------------------------
  * AFT-full backward, one query row t of one sequence.  engine.cu:522-590.
  * dQ, dK, dV, dWB accumulate (+=), as the reference's atomicAdd does.
- * gK/gV/gWB here are the calling thread's private accumulators.
+ * gK/gV here are the calling thread's private accumulators; row t of gWB is
+ * written by this call alone (one thread owns each query row), and its
+ * entries receive their d contributions in increasing d, as the reference's
+ * loop nest (d outer, tp inner) adds them.
  * ---------------------------------------------------------------------- */
 static void aft_full_bwd_row(const float *Q, const float *K, const float *V,
                              const float *WB, const float *gout, float *gQ,
                              float *gK, float *gV, float *gWB, int T, int D,
-                             int masked, int ldw, int t)
+                             int masked, int ldw, int t, float *scratch)
 {
+    float *max_val = scratch, *num = scratch + D, *den = scratch + 2 * D;
+    float *den_inv = scratch + 3 * D, *ratio = scratch + 4 * D, *gs = scratch + 5 * D;
+    int limit = masked ? (t + 1) : T;
+    const float *wrow = WB + (size_t)t * ldw;
     for (int d = 0; d < D; d++) {
-        int limit = masked ? (t + 1) : T;
-        float max_val = -1e20f;
-        for (int tp = 0; tp < limit; tp++) {
-            float v = K[tp * D + d] + WB[(size_t)t * ldw + tp];
-            if (v > max_val) max_val = v;
+        max_val[d] = -1e20f;
+        num[d] = 0.0f;
+        den[d] = 0.0f;
+    }
+    for (int tp = 0; tp < limit; tp++) {
+        const float wv = wrow[tp];
+        const float *k = K + (size_t)tp * D;
+        for (int d = 0; d < D; d++) {
+            float v = k[d] + wv;
+            if (v > max_val[d]) max_val[d] = v;
         }
-        float num = 0.0f, den = 0.0f;
-        for (int tp = 0; tp < limit; tp++) {
-            float w = expf(K[tp * D + d] + WB[(size_t)t * ldw + tp] - max_val);
-            num += w * V[tp * D + d];
-            den += w;
+    }
+    for (int tp = 0; tp < limit; tp++) {
+        const float wv = wrow[tp];
+        const float *k = K + (size_t)tp * D, *vv = V + (size_t)tp * D;
+        for (int d = 0; d < D; d++) {
+            float w = expf(k[d] + wv - max_val[d]);
+            num[d] += w * vv[d];
+            den[d] += w;
         }
-        float den_inv = 1.0f / (den + 1e-9f);
-        float ratio = num * den_inv;
-        float sigQ = 1.0f / (1.0f + expf(-Q[t * D + d]));
+    }
+    for (int d = 0; d < D; d++) {
+        den_inv[d] = 1.0f / (den[d] + 1e-9f);
+        ratio[d] = num[d] * den_inv[d];
+        float sigQ = 1.0f / (1.0f + expf(-Q[(size_t)t * D + d]));
         float dSigQ = sigQ * (1.0f - sigQ);
-        float gO = gout[t * D + d];
-        gQ[t * D + d] += gO * ratio * dSigQ;
-        for (int tp = 0; tp < limit; tp++) {
-            float w = expf(K[tp * D + d] + WB[(size_t)t * ldw + tp] - max_val);
-            float dV = gO * sigQ * (w * den_inv);
-            gV[tp * D + d] += dV;
-            float dW = gO * sigQ * w * (V[tp * D + d] - ratio) * den_inv;
-            gK[tp * D + d] += dW;
-            gWB[(size_t)t * ldw + tp] += dW;
+        float gO = gout[(size_t)t * D + d];
+        gQ[(size_t)t * D + d] += gO * ratio[d] * dSigQ;
+        gs[d] = gO * sigQ;
+    }
+    for (int tp = 0; tp < limit; tp++) {
+        const float wv = wrow[tp];
+        const float *k = K + (size_t)tp * D, *vv = V + (size_t)tp * D;
+        float *gk = gK + (size_t)tp * D, *gv = gV + (size_t)tp * D;
+        float acc = gWB[(size_t)t * ldw + tp];
+        for (int d = 0; d < D; d++) {
+            float w = expf(k[d] + wv - max_val[d]);
+            float dV = gs[d] * (w * den_inv[d]);
+            gv[d] += dV;
+            float dW = gs[d] * w * (vv[d] - ratio[d]) * den_inv[d];
+            gk[d] += dW;
+            acc += dW;
         }
+        gWB[(size_t)t * ldw + tp] = acc;
     }
 }
 
@@ -151,39 +199,37 @@ void oracle_aft_full_bwd(const float *Q, const float *K, const float *V,
                          int masked, int ldw)
 {
     size_t sd = (size_t)T * D;
-    size_t wsz = (size_t)T * ldw;
     int nth = oracle_threads();
-    /* private dK/dV per thread per sequence would be B*T*D*nth; instead
-     * process one sequence at a time with private dK, dV and dWB. */
-    float *priv = (float *)calloc((size_t)nth * (2 * sd + wsz), sizeof(float));
+    /* private dK/dV per thread for one sequence at a time; dWB rows belong
+     * to the thread that owns the query row */
+    float *priv = (float *)calloc((size_t)nth * 2 * sd, sizeof(float));
     if (!priv) return;
     for (int b = 0; b < B; b++) {
-        memset(priv, 0, (size_t)nth * (2 * sd + wsz) * sizeof(float));
-#pragma omp parallel for schedule(dynamic, 1)
-        for (int t = T - 1; t >= 0; t--) {
-            float *mine = priv + (size_t)oracle_thread_id() * (2 * sd + wsz);
-            aft_full_bwd_row(Q + b * sd, K + b * sd, V + b * sd, WB,
-                             gout + b * sd, gQ + b * sd, mine, mine + sd,
-                             mine + 2 * sd, T, D, masked, ldw, t);
+        memset(priv, 0, (size_t)nth * 2 * sd * sizeof(float));
+#pragma omp parallel
+        {
+            float *scratch = (float *)malloc((size_t)6 * D * sizeof(float));
+            float *mine = priv + (size_t)oracle_thread_id() * 2 * sd;
+#pragma omp for schedule(dynamic, 1)
+            for (int t = T - 1; t >= 0; t--) {
+                if (scratch)
+                    aft_full_bwd_row(Q + b * sd, K + b * sd, V + b * sd, WB,
+                                     gout + b * sd, gQ + b * sd, mine, mine + sd,
+                                     gWB, T, D, masked, ldw, t, scratch);
+            }
+            free(scratch);
         }
         /* reduce the private accumulators */
 #pragma omp parallel for schedule(static)
         for (long j = 0; j < (long)sd; j++) {
             float sk = 0.0f, sv = 0.0f;
             for (int h = 0; h < nth; h++) {
-                float *mine = priv + (size_t)h * (2 * sd + wsz);
+                float *mine = priv + (size_t)h * 2 * sd;
                 sk += mine[j];
                 sv += mine[sd + j];
             }
             gK[b * sd + j] += sk;
             gV[b * sd + j] += sv;
-        }
-#pragma omp parallel for schedule(static)
-        for (long j = 0; j < (long)wsz; j++) {
-            float s = 0.0f;
-            for (int h = 0; h < nth; h++)
-                s += priv[(size_t)h * (2 * sd + wsz) + 2 * sd + j];
-            gWB[j] += s;
         }
     }
     free(priv);

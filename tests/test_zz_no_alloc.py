@@ -50,6 +50,32 @@ def test_ce_fwd_noalloc_matches_allocating_entry_point():
         assert abs(g - r) <= 1e-5 * abs(r), (T, V, g, r)
 
 
+def test_ce_fwd_noalloc_queued_calls_and_max_rows():
+    """Three calls queued back to back on one stream with no synchronisation
+    between them (each call's row-loss kernel must wait until the previous
+    call's mean has read the shared array), the first at the maximum row
+    count so the array's last entries are used, then compared one by one."""
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    L, noalloc = _bind()
+    stream = torch.cuda.current_stream().cuda_stream
+    rng = np.random.default_rng(6)
+    cases = []
+    for T, V in ((MAX_ROWS, 8), (1000, 512), (MAX_ROWS - 3, 16)):
+        x = torch.from_numpy((3 * rng.standard_normal((T, V))).astype(np.float32)).cuda()
+        y = torch.from_numpy(rng.integers(0, V, T).astype(np.int32)).cuda()
+        cases.append((T, V, x, y, torch.empty(1, device="cuda")))
+    torch.cuda.synchronize()
+    for T, V, x, y, out in cases:
+        assert noalloc(x.data_ptr(), y.data_ptr(), out.data_ptr(), T, V, 0.1, stream) == 0
+    torch.cuda.synchronize()
+    for T, V, x, y, out in cases:
+        ref = torch.empty(1, device="cuda")
+        assert L.dc_ce_fwd(x.data_ptr(), y.data_ptr(), ref.data_ptr(), None, T, V, 0.1, stream) == 0
+        torch.cuda.synchronize()
+        g, r = float(out), float(ref)
+        assert abs(g - r) <= 1e-5 * abs(r), (T, V, g, r)
+
+
 def test_ce_fwd_noalloc_rejects_too_many_rows():
     L, noalloc = _bind()
     stream = torch.cuda.current_stream().cuda_stream
