@@ -105,7 +105,13 @@ struct Params {
     void *G1, *G2;    // g and n = -g*r, [B][Tqp][dp] operand precision
     void *G1l, *G2l;  // their rounding residuals (g - G1, n - G2), same layout
     int lo_rows;      // the residuals exist for query rows t < lo_rows (multiple of 128)
-    float *Rs, *Is;   // forward statistics r = num/den and 1/den, [B][Tqp][dp] (nullptr: not kept)
+    // forward statistics r = num/den and 1/den (Rs == nullptr: not kept):
+    // fp32 [B][stat_lo][dp] for query rows t < stat_lo (= lo_rows, where the
+    // backward keeps g and n to better than operand precision), operand
+    // precision [B][Tqp][dp] (Rb, Ib; rows from stat_lo on) for the rest
+    float *Rs, *Is;
+    void *Rb, *Ib;
+    int stat_lo;
     int *status;
     unsigned long long *trace;  // optional per-tile timeline (nullptr: off)
 };
@@ -525,9 +531,15 @@ __global__ void __launch_bounds__(256) bwd_stats_kernel(const Params p)
     const int b = (int)(bt / p.Tqp);
     float r[16], inv[16];
     if (t < p.Tq) {
-        const size_t so = ((size_t)b * p.Tqp + t) * p.dp + d0;
-        ld16g(p.Rs + so, r);
-        ld16g(p.Is + so, inv);
+        if (t < p.stat_lo) {
+            const size_t so = ((size_t)b * p.stat_lo + t) * p.dp + d0;
+            ld16g(p.Rs + so, r);
+            ld16g(p.Is + so, inv);
+        } else {
+            const size_t so = ((size_t)b * p.Tqp + t) * p.dp + d0;
+            ld16g((const E *)p.Rb + so, r);
+            ld16g((const E *)p.Ib + so, inv);
+        }
         bool bad = false;  // the forward's range guard, on 1/den' and r
 #pragma unroll
         for (int j = 0; j < 16; ++j)
@@ -547,7 +559,9 @@ struct Layout {
     int B, Tq, Tk, D, Tqp, Tkp, dp, esz, nsplit, rows_per_split;
     int ldi, ldo;  // row strides of the user tensors (Q, K, V and grads; Z and dZ)
     size_t off_m, off_c, off_cpart, off_ap, off_pv, off_pe, off_g1, off_g2, off_g1l, off_g2l;
-    size_t off_rs, off_is;  // saved forward statistics (DC_AFT_SAVE_STATS only)
+    size_t off_rs, off_is;  // saved forward statistics, fp32 rows t < stat_lo (DC_AFT_SAVE_STATS)
+    size_t off_rb, off_ib;  // the same in operand precision, rows t >= stat_lo
+    int stat_lo;
     size_t total;
 };
 
@@ -561,6 +575,19 @@ static int operand_size(int dtype, int flags)
 // CTA per tile: their element-wise epilogues dominate, and twice as many
 // independent workers drain them faster.
 static bool use_pairs(const Layout &L) { return L.esz == 2 && std::max(L.Tqp, L.Tkp) >= 1024; }
+
+// Query rows whose g and n keep their rounding residuals (g - G1, n - G2):
+// dW's terms g*E'V + n*E' cancel most (and g = dZ*sigmoid(Q)/den' is largest)
+// in the first query rows, where den' sums few terms; with bf16 operands the
+// residuals of rows t < 128 (256 when CTA-pair tiles span two 128-row blocks)
+// bring dW to the accuracy of keeping them all.  tf32 keeps them everywhere
+// (they also enter dK/dV there).  The saved statistics of these rows stay
+// fp32, those of the others take the operand precision (their g and n are
+// rounded to it anyway).
+static int lo_rows_of(const Layout &L)
+{
+    return L.esz == 4 ? L.Tqp : std::min(L.Tqp, use_pairs(L) ? 2 * BM : BM);
+}
 
 static Layout make_layout(int B, int Tq, int Tk, int D, int dtype, int flags)
 {
@@ -601,9 +628,16 @@ static Layout make_layout(int B, int Tq, int Tk, int D, int dtype, int flags)
     L.off_g2 = take((size_t)B * L.Tqp * L.dp * L.esz);
     L.off_g1l = take((size_t)B * L.Tqp * L.dp * L.esz);
     L.off_g2l = take((size_t)B * L.Tqp * L.dp * L.esz);
-    const size_t nstat = (flags & DC_AFT_SAVE_STATS) ? (size_t)B * L.Tqp * L.dp * 4 : 0;
-    L.off_rs = take(nstat);
-    L.off_is = take(nstat);
+    // saved statistics: fp32 for the rows whose g and n keep their rounding
+    // residuals (lo_rows_of), operand precision for the rest
+    L.stat_lo = lo_rows_of(L);
+    const bool keep = (flags & DC_AFT_SAVE_STATS) != 0;
+    const size_t nlo = keep ? (size_t)B * L.stat_lo * L.dp * 4 : 0;
+    const size_t nhi = keep && L.stat_lo < L.Tqp ? (size_t)B * L.Tqp * L.dp * L.esz : 0;
+    L.off_rs = take(nlo);
+    L.off_is = take(nlo);
+    L.off_rb = take(nhi);
+    L.off_ib = take(nhi);
     L.total = off;
     return L;
 }
@@ -903,17 +937,13 @@ static Params make_params(const Layout &L, char *ws, int flags)
     p.G2 = ws + L.off_g2;
     p.G1l = ws + L.off_g1l;
     p.G2l = ws + L.off_g2l;
-    // Where the rounding residuals of g and n are kept.  dW's terms
-    // g*E'V + n*E' cancel most (and g = dZ*sigmoid(Q)/den' is largest) in the
-    // first query rows, where den' sums few terms; with bf16 operands the
-    // residuals of rows t < 128 bring dW to the accuracy of keeping them all.
-    // tf32 keeps them everywhere (they also enter dK/dV there).
-    // (CTA-pair tiles span two 128-row blocks, so there the first 256 rows
-    // carry them)
-    p.lo_rows = L.esz == 4 ? L.Tqp : std::min(L.Tqp, use_pairs(L) ? 2 * BM : BM);
+    p.lo_rows = lo_rows_of(L);
     if (saves_stats(flags)) {
         p.Rs = reinterpret_cast<float *>(ws + L.off_rs);
         p.Is = reinterpret_cast<float *>(ws + L.off_is);
+        p.Rb = ws + L.off_rb;
+        p.Ib = ws + L.off_ib;
+        p.stat_lo = L.stat_lo;
     }
     p.spare_sms = (flags >> 16) & 0xff;
     p.status = device_status_word();

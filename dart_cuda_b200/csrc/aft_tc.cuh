@@ -278,15 +278,21 @@ __device__ __forceinline__ void epi16_fwd(const Params &p, int b, int t, int d0,
         if (bad) report_range(p);
     }
     if (p.Rs) {  // r and 1/den for the backward, exactly as epi16_bwd1 forms them
-        const size_t so = ((size_t)b * p.Tqp + t) * p.dp + d0;
         float r[16], inv[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
             inv[j] = __fdividef(1.0f, den[j]);
             r[j] = num[j] * inv[j];
         }
-        st16(p.Rs + so, r);
-        st16(p.Is + so, inv);
+        if (t < p.stat_lo) {  // fp32 (rows whose g and n keep residuals)
+            const size_t so = ((size_t)b * p.stat_lo + t) * p.dp + d0;
+            st16(p.Rs + so, r);
+            st16(p.Is + so, inv);
+        } else {              // operand precision
+            const size_t so = ((size_t)b * p.Tqp + t) * p.dp + d0;
+            st16op((E *)p.Rb + so, r);
+            st16op((E *)p.Ib + so, inv);
+        }
     }
     const size_t row = (size_t)b * p.Tq + t;
     const size_t o = row * p.ldi + d0, oz = row * p.ldo + d0;
