@@ -104,6 +104,9 @@ SIGNATURES = {
     "mul_tensors": (_VP, [_VP, _VP]),
     "sum_tensor": (_VP, [_VP]),
     "mean_tensor": (_VP, [_VP]),
+    "matmul_tensors": (_VP, [_VP, _VP]),
+    "gelu_tensor": (_VP, [_VP]),
+    "embedding_forward": (_VP, [_IP, _VP, _VP, c_int32, c_int32]),
 }
 
 

@@ -143,12 +143,13 @@ class AftDecoder:
             self.P[name].copy_(val)
 
     # ------------------------------------------------------------ checkpoint
-    def reference_parameters(self):
+    def reference_parameters(self, grads: bool = False):
         """[(name, view)] in the reference's parameters() order, each view in
         the reference's shape (lib/core/transformers/aft/transformer_decoder.dart:90-97,
         transformer_decoder_block.dart:101-108, aft.dart:71-76,
-        aft_cross_attention.dart:39-45, aft_multi_head_*.dart, nn.dart:55)."""
-        c, P = self.cfg, self.P
+        aft_cross_attention.dart:39-45, aft_multi_head_*.dart, nn.dart:55).
+        grads=True gives the same views of the gradient buffer."""
+        c, P = self.cfg, (self.G if grads else self.P)
         d, hs = c.d_model, c.head
         out = [("wte", P["wte"]), ("wpe", P["wpe"])]
         for l in range(c.n_layers):

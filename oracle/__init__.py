@@ -290,6 +290,18 @@ class RefEngine:
         L.mul_tensors.argtypes = [VP, VP]
         L.sum_tensor.restype = VP
         L.sum_tensor.argtypes = [VP]
+        L.matmul_tensors.restype = VP
+        L.matmul_tensors.argtypes = [VP, VP]
+        L.gelu_tensor.restype = VP
+        L.gelu_tensor.argtypes = [VP]
+        L.add_tensors.restype = VP
+        L.add_tensors.argtypes = [VP, VP]
+        L.embedding_forward.restype = VP
+        L.embedding_forward.argtypes = [_IP, VP, VP, c_int, c_int]
+        L.adam_step.restype = None
+        L.adam_step.argtypes = [VP, VP, VP, c_int, c_float, c_float, c_float, c_float]
+        L.concat_tensors_gpu.restype = VP
+        L.concat_tensors_gpu.argtypes = [POINTER(VP), c_int]
         self.L = L
 
     def tensor(self, a: np.ndarray):

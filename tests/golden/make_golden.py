@@ -20,6 +20,7 @@ Inputs are seeded (numpy ``default_rng``) and stored next to the outputs.
 from __future__ import annotations
 
 import argparse
+import ctypes
 import sys
 from pathlib import Path
 
@@ -120,10 +121,171 @@ def ce_case(E: oracle.RefEngine, seed: int, T: int, V: int):
     return out
 
 
+def matmul_case(E: oracle.RefEngine, seed: int, M: int, K: int, N: int):
+    """matmul_tensors (native/src/engine.cu:480-507, matmul.cuh:27-131) and
+    its two backward products."""
+    rng = np.random.default_rng(seed)
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    B = rng.standard_normal((K, N)).astype(np.float32)
+    dC = rng.standard_normal((M, N)).astype(np.float32)
+    ha, _ = E.tensor(A); hb, _ = E.tensor(B)
+    hc = E.L.matmul_tensors(ha, hb)
+    C = E.data(hc, (M, N))
+    s, extra = E.weighted_sum(hc, (M, N), dC)
+    E.L.backward(s)
+    out = dict(A=A, B=B, dC=dC, C=C, dA=E.grad(ha, A.shape), dB=E.grad(hb, B.shape), seed=np.int32(seed))
+    E.free(s, *extra, hc, ha, hb)
+    return out
+
+
+def gelu_case(E: oracle.RefEngine, seed: int, R: int, C: int):
+    """gelu_tensor (native/src/engine.cu:445-458, elementwise.cuh gelu_fwd/bwd)."""
+    rng = np.random.default_rng(seed)
+    x = (2 * rng.standard_normal((R, C))).astype(np.float32)
+    dy = rng.standard_normal((R, C)).astype(np.float32)
+    hx, _ = E.tensor(x)
+    hy = E.L.gelu_tensor(hx)
+    y = E.data(hy, x.shape)
+    s, extra = E.weighted_sum(hy, x.shape, dy)
+    E.L.backward(s)
+    out = dict(x=x, dy=dy, y=y, dx=E.grad(hx, x.shape), seed=np.int32(seed))
+    E.free(s, *extra, hy, hx)
+    return out
+
+
+def embedding_case(E: oracle.RefEngine, seed: int, V: int, Tmax: int, T: int, D: int):
+    """embedding_forward (native/src/engine.cu:794-822): out[t] = wte[idx[t]] +
+    wpe[t]; the backward scatters into wte's rows (repeated ids add up) and
+    wpe's first T rows."""
+    rng = np.random.default_rng(seed)
+    wte = rng.standard_normal((V, D)).astype(np.float32)
+    wpe = rng.standard_normal((Tmax, D)).astype(np.float32)
+    idx = rng.integers(0, V, T).astype(np.int32)
+    idx[: min(3, T)] = idx[0]  # repeated ids
+    dy = rng.standard_normal((T, D)).astype(np.float32)
+    hte, _ = E.tensor(wte); hpe, _ = E.tensor(wpe)
+    hy = E.L.embedding_forward(idx.ctypes.data_as(oracle._IP), hte, hpe, T, D)
+    y = E.data(hy, (T, D))
+    s, extra = E.weighted_sum(hy, (T, D), dy)
+    E.L.backward(s)
+    out = dict(wte=wte, wpe=wpe, idx=idx, dy=dy, y=y, dwte=E.grad(hte, wte.shape),
+               dwpe=E.grad(hpe, wpe.shape), seed=np.int32(seed))
+    E.free(s, *extra, hy, hte, hpe)
+    return out
+
+
+def adam_case(E: oracle.RefEngine, seed: int, R: int, C: int, steps: int, lr: float):
+    """adam_step (native/src/engine.cu:887-905, loss_optim.cuh:255-298) for
+    `steps` consecutive steps t = 1..steps (the value the front end passes,
+    lib/core/optimizers/adam.dart:603-637); p's gradient of step k is set by
+    back-propagating sum(p * G_k) after zero_grad."""
+    rng = np.random.default_rng(seed)
+    p = rng.standard_normal((R, C)).astype(np.float32)
+    Gs = (0.5 * rng.standard_normal((steps, R, C))).astype(np.float32)
+    hp, _ = E.tensor(p)
+    hm, _ = E.tensor(np.zeros((R, C), np.float32))
+    hv, _ = E.tensor(np.zeros((R, C), np.float32))
+    ps, ms, vs = [], [], []
+    for k in range(steps):
+        E.L.zero_grad(hp)
+        s, extra = E.weighted_sum(hp, (R, C), Gs[k])
+        E.L.backward(s)
+        E.L.adam_step(hp, hm, hv, k + 1, lr, 0.9, 0.999, 1e-8)
+        ps.append(E.data(hp, (R, C)))
+        ms.append(E.data(hm, (R, C)))
+        vs.append(E.data(hv, (R, C)))
+        E.free(s, *extra)
+    E.free(hp, hm, hv)
+    return dict(p0=p, G=Gs, p=np.stack(ps), m=np.stack(ms), v=np.stack(vs), lr=np.float32(lr),
+                seed=np.int32(seed))
+
+
+def decoder_case(E: oracle.RefEngine, seed: int, vocab: int, d: int, n_layers: int, n_heads: int, T: int):
+    """One sequence through a TransformerDecoder built from the reference
+    engine's own handle ops, composed as the reference's layers compose them
+    (lib/core/transformers/aft/transformer_decoder.dart, transformer_decoder_block.dart:
+    pre-LN blocks; MultiHeadAFT: per-head Q/K/V Layers, aft_forward on the
+    head's posBias, concat, projection; MultiHeadAFTCross against the dummy
+    [1, d] zero encoder with aft_cross_forward; FeedForward with gelu_tensor;
+    residual add_tensors; final LayerNorm; LM head; cross_entropy_loss),
+    then backward from the loss.  A Layer is matmul_tensors followed by
+    add_tensor_row_broadcast of its [1, out] bias.  Parameters are N(0, 0.2)
+    (LayerNorm gains 1 + N(0, 0.1)) in the reference's parameters() order;
+    names and shapes come from the decoder's reference-order view."""
+    from dart_cuda_b200.decoder import AftDecoder, DecoderConfig
+
+    cfg = DecoderConfig(vocab=vocab, d_model=d, n_layers=n_layers, n_heads=n_heads, block_size=T)
+    names = [(n, tuple(v.shape)) for n, v in AftDecoder(cfg, device="cpu").reference_parameters()]
+    rng = np.random.default_rng(seed)
+    P = {}
+    for n, shp in names:
+        if n.endswith("gamma"):
+            P[n] = (1 + 0.1 * rng.standard_normal(shp)).astype(np.float32)
+        else:
+            P[n] = (0.2 * rng.standard_normal(shp)).astype(np.float32)
+    idx = rng.integers(0, vocab, T).astype(np.int32)
+    tgt = rng.integers(0, vocab, T).astype(np.int32)
+    L = E.L
+    H = {n: E.tensor(a)[0] for n, a in P.items()}
+    keep = []
+
+    def k(h):
+        keep.append(h)
+        return h
+
+    def layer(x, pre):
+        return k(L.add_tensor_row_broadcast(k(L.matmul_tensors(x, H[pre + ".w"])), H[pre + ".b"]))
+
+    def concat(hs):
+        arr = (ctypes.c_void_p * len(hs))(*hs)
+        return k(L.concat_tensors_gpu(ctypes.cast(arr, ctypes.POINTER(ctypes.c_void_p)), len(hs)))
+
+    def ln(x, pre):
+        return k(L.layernorm_forward(x, H[pre + ".gamma"], H[pre + ".beta"], 1e-5))
+
+    x = k(L.embedding_forward(idx.ctypes.data_as(oracle._IP), H["wte"], H["wpe"], T, d))
+    enc = k(E.tensor(np.zeros((1, cfg.enc), np.float32))[0])
+    for l in range(n_layers):
+        pre = f"blocks[{l}]"
+        a1 = ln(x, pre + ".ln1")
+        zs = []
+        for h in range(n_heads):
+            hp = f"{pre}.self.heads[{h}]"
+            q, kk, v = (layer(a1, f"{hp}.{nm}") for nm in "qkv")
+            zs.append(k(L.aft_forward(q, kk, v, H[hp + ".posBias"], True)))
+        x1 = k(L.add_tensors(x, layer(concat(zs), pre + ".self.proj")))
+        a2 = ln(x1, pre + ".ln2")
+        cs = []
+        for h in range(n_heads):
+            hp = f"{pre}.cross.heads[{h}]"
+            q = layer(a2, hp + ".q")
+            kk, v = layer(enc, hp + ".k"), layer(enc, hp + ".v")
+            cs.append(k(L.aft_cross_forward(q, kk, v, H[hp + ".posBias"])))
+        x2 = k(L.add_tensors(x1, layer(concat(cs), pre + ".cross.proj")))
+        a3 = ln(x2, pre + ".ln3")
+        f = k(L.gelu_tensor(layer(a3, pre + ".ffn.w1")))
+        x = k(L.add_tensors(x2, layer(f, pre + ".ffn.w2")))
+    af = ln(x, "finalLayerNorm")
+    logits = layer(af, "lmHead")
+    hl = k(L.cross_entropy_loss(logits, tgt.ctypes.data_as(oracle._IP), T, vocab))
+    loss = E.data(hl, (1, 1))
+    lg = E.data(logits, (T, vocab))
+    L.backward(hl)
+    out = {"idx": idx, "targets": tgt, "loss": loss, "logits": lg, "seed": np.int32(seed),
+           "dims": np.array([vocab, d, n_layers, n_heads, T], np.int32),
+           "names": np.array([n for n, _ in names])}
+    for n, _ in names:
+        out["p:" + n] = P[n]
+        out["g:" + n] = E.grad(H[n], P[n].shape)
+    E.free(*keep, *H.values())
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--out", default=str(Path(__file__).resolve().parent))
     ap.add_argument("--lib", default=str(oracle.REF_LIB_PATH))
+    ap.add_argument("--only", default="", help="comma-separated fixture names to (re)write")
     args = ap.parse_args()
     out = Path(args.out)
     out.mkdir(parents=True, exist_ok=True)
@@ -146,7 +308,15 @@ def main():
         "bias_m5_n3": bias_case(E, 112, 5, 3),
         "ce_t64_v65": ce_case(E, 113, 64, 65),
         "ce_t4_v8192": ce_case(E, 114, 4, 8192),
+        "matmul_m37_k50_n29": matmul_case(E, 115, 37, 50, 29),
+        "matmul_m128_k256_n65": matmul_case(E, 116, 128, 256, 65),
+        "gelu_r64_c96": gelu_case(E, 117, 64, 96),
+        "embedding_v65_t13_d16": embedding_case(E, 118, 65, 20, 13, 16),
+        "adam_r50_c7_s3": adam_case(E, 119, 50, 7, 3, 1e-2),
+        "decoder_v11_d32_l2_h2_t16": decoder_case(E, 120, 11, 32, 2, 2, 16),
     }
+    only = set(args.only.split(",")) if args.only else None
+    cases = {k: v for k, v in cases.items() if only is None or k in only}
     for name, arrs in cases.items():
         np.savez_compressed(out / f"{name}.npz", **arrs)
         print("wrote", name, {k: v.shape for k, v in arrs.items()})
