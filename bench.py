@@ -167,6 +167,75 @@ def cpu_baseline(B, T, d, dtype_name, budget_s=10.0):
     return rate, cs.cores, cs.describe() + f", {secs:.2f} s"
 
 
+# ------------------------------------------------------------------ host link
+def _numa_of_gpu(torch, dev):
+    try:
+        bus = torch.cuda.get_device_properties(dev).pci_bus_id.lower()  # dddddddd:bb:dd.f
+        dom, rest = bus.split(":", 1)
+        for name in (bus, f"{int(dom, 16):04x}:{rest}"):  # sysfs uses a 4-digit domain
+            f = Path(f"/sys/bus/pci/devices/{name}/numa_node")
+            if f.exists():
+                return int(f.read_text().strip())
+        return -2
+    except Exception:
+        return -2
+
+
+def _numa_of_cpus():
+    """NUMA nodes of the CPUs this process may run on."""
+    try:
+        cpus = os.sched_getaffinity(0)
+        nodes = set()
+        for nd in Path("/sys/devices/system/node").glob("node[0-9]*"):
+            for part in (nd / "cpulist").read_text().strip().split(","):
+                lo, _, hi = part.partition("-")
+                rng = range(int(lo), int(hi or lo) + 1)
+                if any(c in cpus for c in rng):
+                    nodes.add(int(nd.name[4:]))
+        return sorted(nodes)
+    except Exception:
+        return []
+
+
+def host_link(torch, dist, dev, bufset, host_inputs, h2d, d2h, e2e_step_ms, world, reps=3):
+    """Achieved host<->device copy rates of this rank's step copies, each
+    direction timed alone (pinned buffers, CUDA events on the copy stream),
+    and where the GPU and this process's CPUs sit (NUMA nodes), gathered over
+    the ranks: what bounds the end-to-end rate when every rank copies at once."""
+    s = torch.cuda.Stream(device=dev)
+    e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    with torch.cuda.stream(s):
+        e[0].record(s)
+        for _ in range(reps):
+            for dst, src in zip(bufset.inp, host_inputs):
+                dst.copy_(src, non_blocking=True)
+        e[1].record(s)
+        for _ in range(reps):
+            for dst, src in zip(bufset.host, bufset.out):
+                dst.copy_(src, non_blocking=True)
+        e[2].record(s)
+    torch.cuda.synchronize()
+    mine = [h2d * reps / (e[0].elapsed_time(e[1]) / 1e3) / 1e9, d2h * reps / (e[1].elapsed_time(e[2]) / 1e3) / 1e9,
+            (h2d + d2h) / (e2e_step_ms / 1e3) / 1e9, float(_numa_of_gpu(torch, dev))]
+    cpu_nodes = _numa_of_cpus()
+    mine.append(float(cpu_nodes[0]) if len(cpu_nodes) == 1 else -1.0)
+    t = torch.tensor(mine, device=dev, dtype=torch.float64)
+    if dist is not None:
+        allt = [torch.empty_like(t) for _ in range(world)]
+        dist.all_gather(allt, t)
+    else:
+        allt = [t]
+    rows = [[float(x) for x in a.cpu()] for a in allt]
+    return {"per_rank": [{"h2d_GB/s_alone": r[0], "d2h_GB/s_alone": r[1], "both_ways_GB/s_in_e2e": r[2],
+                          "gpu_numa": int(r[3]), "cpu_numa": int(r[4])} for r in rows],
+            "note": "alone: one direction of this rank's copies while the other ranks do the same; "
+                    "in_e2e: the step's copy bytes over the e2e step time; cpu_numa -1: the process "
+                    "may run on several NUMA nodes (pinned pages land where they are first touched)"}
+
+
 # ------------------------------------------------------------------ row ops
 def row_kernels(dev, P, reps=10):
     """HBM bandwidth of the training step's row kernels on tensors larger than
@@ -302,18 +371,40 @@ def bench_train(args, dev, rank, world, dist):
     tgt = torch.randint(0, cfg.vocab, (B, T), device=dev, generator=g, dtype=torch.int32)
     flush = torch.empty(256 * 1024 * 1024 // 4, device=dev)
     stream = torch.cuda.current_stream()
-    graph = None
+    graphs = None
+    # N > 1: the gradient all-reduce in buckets (the LM head with the last
+    # block, then one per block, then the embeddings), each started on a comm
+    # stream as soon as the backward has completed it, so the reductions
+    # overlap the rest of the backward; the CUDA graph of forward + backward
+    # is captured as one graph per bucket, replayed with the bucket's
+    # all-reduce queued between replays
+    overlap = dist is not None and not args.no_overlap
+    buckets = m.grad_buckets()
+    comm = torch.cuda.Stream(device=dev) if overlap else None
 
-    def fwd_bwd():
+    def reduce_bucket(k):
+        a, b = buckets[k]
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream())
+        comm.wait_event(ev)
+        with torch.cuda.stream(comm):
+            dist.all_reduce(m.grad[a:b])
+
+    def fwd_bwd(bucket_done=None):
         m.forward(idx, tgt)
-        m.backward(grad_scale=1.0 / world)
+        m.backward(grad_scale=1.0 / world, bucket_done=bucket_done)
 
     def step():
-        if graph is not None:
-            graph.replay()
+        if graphs is not None:
+            for k, gr in enumerate(graphs):
+                gr.replay()
+                if overlap:
+                    reduce_bucket(k)
         else:
-            fwd_bwd()
-        if dist is not None:
+            fwd_bwd(reduce_bucket if overlap else None)
+        if overlap:
+            torch.cuda.current_stream().wait_stream(comm)
+        elif dist is not None:
             dist.all_reduce(m.grad)
         m.optimizer_step(lr=3e-4)
 
@@ -326,9 +417,25 @@ def bench_train(args, dev, rank, world, dist):
         step()
     barrier()
     if not args.no_graph:
-        graph = torch.cuda.CUDAGraph()  # forward + backward; AdamW stays eager (its step count moves)
-        with torch.cuda.graph(graph):
-            fwd_bwd()
+        # forward + backward as CUDA graphs (AdamW stays eager: its step count
+        # moves); with the overlapped all-reduce, one graph per bucket
+        pool = torch.cuda.graph_pool_handle()
+        cap = torch.cuda.Stream(device=dev)
+        cap.wait_stream(torch.cuda.current_stream())
+        n = len(buckets) if overlap else 1
+        segs = [torch.cuda.CUDAGraph() for _ in range(n)]
+        with torch.cuda.stream(cap):
+            segs[0].capture_begin(pool=pool)
+
+            def boundary(k):
+                if k + 1 < n:
+                    segs[k].capture_end()
+                    segs[k + 1].capture_begin(pool=pool)
+
+            fwd_bwd(boundary if overlap else None)
+            segs[-1].capture_end()
+        torch.cuda.current_stream().wait_stream(cap)
+        graphs = segs
         step()
         barrier()
     sampler = ClockSampler(int(os.environ.get("LOCAL_RANK", "0")))
@@ -386,7 +493,10 @@ def bench_train(args, dev, rank, world, dist):
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": c["desc"], "B_per_gpu": B, "seq_len": T, "global_batch": B * world,
                    "parallelism": f"dp{world}", "l2": "flushed between steps (256 MiB write)",
-                   "cuda_graph": not args.no_graph},
+                   "cuda_graph": not args.no_graph,
+                   "grad_allreduce": ("none" if dist is None else
+                                      f"{len(buckets)} buckets overlapped with the backward" if overlap
+                                      else "one all-reduce after the backward")},
         "tflops": (gemm_flops + aft_flops) * world / (ms / 1e3) / 1e12,
         "e2e": {"value": B * T * world / (e2e_ms / args.steps / 1e3), "unit": "tokens/s",
                 "h2d_bytes_per_step": 2 * B * T * 4, "d2h_bytes_per_step": 4},
@@ -570,6 +680,9 @@ def main():
                     help="N>1: SMs the dK/dV kernel leaves free for the overlapped all-reduce "
                          "(default: 32 at N=2, 48 from N=4, where NCCL's all-reduce runs more CTAs; "
                          "measured at C2: N=8 6.6x with 16-32, 7.4x with 48)")
+    ap.add_argument("--nccl-max-ctas", type=int, default=0,
+                    help="N>1: cap NCCL's CTAs per collective (communicator config max_ctas); the "
+                         "dK/dV kernel then leaves that many SMs free unless --spare-sms is given")
     ap.add_argument("--no-rows", action="store_true", help="skip the LayerNorm/bias/CE bandwidth pass")
     ap.add_argument("--batch", type=int, default=0,
                     help="override the configuration's sequences per GPU (small profiling cases)")
@@ -636,8 +749,13 @@ def main():
 
         import torch.distributed as dist
 
+        opts = dist.ProcessGroupNCCL.Options()
+        if args.nccl_max_ctas > 0:
+            # cap the SMs NCCL's kernels take, so the dK/dV kernel running
+            # beside the dW all-reduce can leave exactly that many free
+            opts.config.max_ctas = args.nccl_max_ctas
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=dev)
+                                device_id=dev, pg_options=opts)
 
     from dart_cuda_b200 import ops
 
@@ -658,7 +776,10 @@ def main():
     grads = (dQ, dK, dV, dW)
     overlap = dist is not None and not args.no_overlap
     if args.spare_sms < 0:
-        args.spare_sms = 32 if world <= 2 else 48
+        if args.nccl_max_ctas > 0:
+            args.spare_sms = args.nccl_max_ctas
+        else:
+            args.spare_sms = 32 if world <= 2 else 48
     config["dw_allreduce"] = ("none" if dist is None else "serial" if not overlap
                               else f"beside dK/dV ({args.spare_sms} SMs left free)")
 
@@ -825,6 +946,7 @@ def main():
     e2e_val = B * T * world / (e2e_ms / args.steps / 1e3)
     h2d = 4 * B * T * d * esz
     d2h = 4 * B * T * d * esz + T * T * 4
+    link = host_link(torch, dist, dev, sets[0], (hQ, hK, hV, hdZ), h2d, d2h, e2e_ms / args.steps, world)
 
     # ---- roofline.  Algorithmic work of one fwd+bwd step (per rank):
     # F = 6 B d T(T+1) tensor-core FLOPs (three causal [num|den]-shaped
@@ -904,7 +1026,7 @@ def main():
         "tflops": causal_flops(B, T, d) * world / (ms_per_step / 1e3) / 1e12,
         "e2e": {"value": e2e_val, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "copies": "pinned host buffers; uploads, library calls and read-backs on three "
-                          "streams over two device buffer sets"},
+                          "streams over two device buffer sets", "host_link": link},
         "roofline": roof, "kernels": kern, "gpu_launches": launches * args.steps,
         "clocks": sampler.summary(),
     }

@@ -50,8 +50,17 @@ def _stale(target: Path, deps) -> bool:
     return any(d.stat().st_mtime > t for d in deps)
 
 
-def _compile(src: Path, verbose: bool, extra) -> Path:
-    obj = OBJ_DIR / (src.stem + ".o")
+# Test-only library for the bounded-wait test (tests/test_bounded_wait_gpu.py):
+# the AFT kernels and the runtime helpers built with a short wait limit and
+# DC_TEST_WITHHOLD, which adds dc_test_withhold_next(); never loaded by the
+# product.
+WAITTEST_LIB = OUT_DIR / "libmat_mul_waittest.so"
+WAITTEST_SOURCES = ("aft.cu", "dc_common.cu")
+WAITTEST_DEFINES = ["-DDC_TEST_WITHHOLD", "-DDC_WAIT_NS=50000000ull"]
+
+
+def _compile(src: Path, verbose: bool, extra, obj_dir: Path = OBJ_DIR) -> Path:
+    obj = obj_dir / (src.stem + ".o")
     if _stale(obj, [src, *_headers()]):
         cmd = [nvcc(), *NVCC_FLAGS, *extra, "-c", str(src), "-o", str(obj)]
         if verbose:
@@ -69,19 +78,30 @@ def build(force: bool = False, verbose: bool = False, extra=()) -> Path:
     OUT_DIR.mkdir(exist_ok=True)
     srcs = _sources()
     if force:
-        for o in OBJ_DIR.glob("*.o"):
+        for o in OBJ_DIR.glob("**/*.o"):
             o.unlink()
     with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as ex:
         objs = list(ex.map(lambda s: _compile(s, verbose, list(extra)), srcs))
-    if force or _stale(LIB, objs):
-        cmd = [nvcc(), *ARCH, "--shared", "-o", str(LIB), *map(str, objs), "-lcudart_static",
+    _link(LIB, objs, force, verbose)
+    # the bounded-wait test library
+    wdir = OBJ_DIR / "waittest"
+    wdir.mkdir(exist_ok=True)
+    wsrcs = [CSRC / n for n in WAITTEST_SOURCES]
+    with cf.ThreadPoolExecutor(max_workers=2) as ex:
+        wobjs = list(ex.map(lambda s: _compile(s, verbose, list(extra) + WAITTEST_DEFINES, wdir), wsrcs))
+    _link(WAITTEST_LIB, wobjs, force, verbose)
+    return LIB
+
+
+def _link(lib: Path, objs, force: bool, verbose: bool):
+    if force or _stale(lib, objs):
+        cmd = [nvcc(), *ARCH, "--shared", "-o", str(lib), *map(str, objs), "-lcudart_static",
                "-ldl", "-lrt", "-lpthread"]
         if verbose:
             print(" ".join(cmd), flush=True)
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
-    return LIB
 
 
 def main(argv=None):

@@ -114,7 +114,19 @@ struct Params {
     int stat_lo;
     int *status;
     unsigned long long *trace;  // optional per-tile timeline (nullptr: off)
+#ifdef DC_TEST_WITHHOLD
+    int test_withhold;  // test build only: CTA 0 skips its first stage's load
+#endif
 };
+
+#ifdef DC_TEST_WITHHOLD
+// Test build only (the library built with -DDC_TEST_WITHHOLD and a short
+// DC_WAIT_NS, never the product library): dc_test_withhold_next(1) makes the
+// next tensor-core launch's CTA 0 skip the TMA load and the arrival of its
+// first pipeline stage, so the MMA issuer's bounded wait for that stage runs
+// out and the abort path (status bit, drains, TMEM release) is exercised.
+static int g_test_withhold = 0;
+#endif
 
 // Per-tile timeline of the tensor-core launches whose mode bit is set in
 // g_trace_modes (bit MODE); see trace_at() in aft_tc.cuh.
@@ -825,6 +837,10 @@ static int launch_tc(Params p, const Layout &L, char *ws, cudaStream_t st)
         p.n_tiles = (p.sk_tiles + p.sk_lo) * p.splits;
     }
     p.trace = (g_trace_modes >> MODE) & 1 ? g_trace_buf : nullptr;
+#ifdef DC_TEST_WITHHOLD
+    p.test_withhold = g_test_withhold;
+    g_test_withhold = 0;
+#endif
     static const char *names[4] = {"aft_tc_fwd", "aft_tc_bwd_recompute", "aft_tc_dkdv",
                                    "aft_tc_dw"};
     cudaLaunchConfig_t cfg = {};
@@ -1071,6 +1087,14 @@ using namespace dc;
 using namespace dc::aft;
 
 extern "C" {
+
+#ifdef DC_TEST_WITHHOLD
+int dc_test_withhold_next(int on)
+{
+    g_test_withhold = on ? 1 : 0;
+    return DC_OK;
+}
+#endif
 
 int dc_aft_trace(void *device_buffer, size_t bytes, int mode_mask)
 {

@@ -755,6 +755,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         stop = true;
                         break;
                     }
+#ifdef DC_TEST_WITHHOLD
+                    // test build: CTA 0 withholds its first stage (no arrival,
+                    // no copy), so the consumer's bounded wait runs out
+                    if (p.test_withhold && blockIdx.x == 0 && jt == 0 && e == tl.k0) continue;
+#endif
                     // both CTAs' copies complete on the even CTA's barrier
                     const uint32_t fb = P ? smem_in_cta(smem_u32(&full[s]), 0) : smem_u32(&full[s]);
                     // a half tile loads half of each B tile

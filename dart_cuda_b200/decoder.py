@@ -317,9 +317,26 @@ class AftDecoder:
         b["idx"], b["targets"] = idx, targets.view(-1)
         return b["logits"], ops.ce_fwd(b["logits"], b["targets"], out=b["loss"])
 
-    def backward(self, grad_scale: float = 1.0):
+    def grad_buckets(self):
+        """[(start, end)] ranges of ``self.grad`` in the order the backward
+        completes them: the LM head, final LayerNorm and last block together,
+        then one per earlier block, then the embeddings.  Each range is
+        contiguous in the flat buffer."""
+        c = self.cfg
+        start = [self._offsets[f"{l}.wqkv"][0] for l in range(c.n_layers)] + [self._offsets["lnfg"][0]]
+        out = [(start[c.n_layers - 1], self.numel)]
+        for l in reversed(range(c.n_layers - 1)):
+            out.append((start[l], start[l + 1]))
+        out.append((0, start[0]))
+        return out
+
+    def backward(self, grad_scale: float = 1.0, bucket_done=None):
         """Gradients of the last forward's loss (times grad_scale) into
-        ``self.grad`` (overwritten)."""
+        ``self.grad`` (overwritten).  ``bucket_done(k)``, when given, is called
+        once the launches that complete bucket k of grad_buckets() have all
+        been queued on the caller's stream (every side stream joined back), so
+        a data-parallel caller can start that bucket's reduction while the
+        rest of the backward runs."""
         c, P, G = self.cfg, self.P, self.G
         b = self._bufs
         B, T = b["shape"]
@@ -401,8 +418,12 @@ class AftDecoder:
             join()
             ops.layernorm_bwd(b["x"][l], P[f"{l}.ln1g"], b["da"], grads=(dX, G[f"{l}.ln1g"], G[f"{l}.ln1b"]),
                               accumulate=True)
+            if bucket_done is not None:  # block l (and, for the last, the LM head) complete
+                bucket_done(c.n_layers - 1 - l)
         check(lib().dc_embedding_bwd(b["idx"].data_ptr(), dX.data_ptr(), G["wte"].data_ptr(), G["wpe"].data_ptr(),
                                      B, T, d, V, st), "dc_embedding_bwd")
+        if bucket_done is not None:
+            bucket_done(c.n_layers)
 
     def optimizer_step(self, lr=3e-4, b1=0.9, b2=0.999, eps=1e-8, weight_decay=0.001):
         """AdamW over every parameter in one launch, with the reference's step
@@ -411,19 +432,40 @@ class AftDecoder:
         self.t += 1
         ops.adam_step(self.flat, self.grad, self.adam_m, self.adam_v, self.t, lr, b1, b2, eps, weight_decay)
 
-    def train_step(self, idx, targets, lr=3e-4, process_group=None):
+    def train_step(self, idx, targets, lr=3e-4, process_group=None, overlap=True):
         """One data-parallel step: the loss is the mean over this rank's B*T
-        tokens; with a process group the gradients are averaged over ranks
-        with one all-reduce of the flat gradient buffer."""
+        tokens; with a process group the gradients are averaged over ranks.
+        overlap=True all-reduces them bucket by bucket (grad_buckets()) on a
+        comm stream while the rest of the backward runs; otherwise with one
+        all-reduce of the flat gradient buffer after it."""
         world = 1
         if process_group is not None:
             import torch.distributed as dist
             world = dist.get_world_size(process_group)
         _, loss = self.forward(idx, targets)
-        self.backward(grad_scale=1.0 / world)
-        if world > 1:
+        if world > 1 and overlap:
             import torch.distributed as dist
-            dist.all_reduce(self.grad, group=process_group)
+            main = torch.cuda.current_stream()
+            if getattr(self, "_comm_stream", None) is None:
+                self._comm_stream = torch.cuda.Stream(self.device)
+            comm = self._comm_stream
+            buckets = self.grad_buckets()
+
+            def done(k):
+                a, b = buckets[k]
+                ev = torch.cuda.Event()
+                ev.record(main)
+                comm.wait_event(ev)
+                with torch.cuda.stream(comm):
+                    dist.all_reduce(self.grad[a:b], group=process_group)
+
+            self.backward(grad_scale=1.0 / world, bucket_done=done)
+            main.wait_stream(comm)
+        else:
+            self.backward(grad_scale=1.0 / world)
+            if world > 1:
+                import torch.distributed as dist
+                dist.all_reduce(self.grad, group=process_group)
         self.optimizer_step(lr)
         return loss
 

@@ -61,3 +61,18 @@ def test_load_rejects_wrong_size(tmp_path):
     np.zeros(10, dtype="<f4").tofile(f)
     with pytest.raises(ValueError, match="expects"):
         a.load(f)
+
+
+def test_grad_buckets_cover_the_gradient_buffer():
+    """The data-parallel reduction buckets are disjoint, contiguous and cover
+    the whole flat gradient buffer, in the order the backward completes them
+    (LM head with the last block first, embeddings last)."""
+    m = make(n_layers=3)
+    bk = m.grad_buckets()
+    assert len(bk) == m.cfg.n_layers + 1
+    assert bk[0][1] == m.numel and bk[-1][0] == 0
+    for (a0, b0), (a1, b1) in zip(bk, bk[1:]):
+        assert b1 == a0 and a1 < b1
+    off = {n: o for n, (o, _) in m._offsets.items()}
+    assert bk[0][0] == off["2.wqkv"] and bk[1] == (off["1.wqkv"], off["2.wqkv"])
+    assert bk[-1] == (0, off["0.wqkv"])

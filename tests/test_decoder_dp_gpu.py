@@ -33,8 +33,20 @@ def _rank(rank, world, port, out_dir):
         shard = slice(2 * rank, 2 * rank + 2)
         m = decoder.AftDecoder(cfg, seed=5, std=0.2)
         m.forward(idx[shard].contiguous(), tgt[shard].contiguous())
-        m.backward(grad_scale=1.0 / world)
-        dist.all_reduce(m.grad)
+        # the gradients reduced bucket by bucket at the points the backward
+        # reports them complete (on the caller's stream, so each reduction
+        # sees exactly the work queued before it): a bucket reported too early
+        # would reduce partial gradients and miss the single-process result
+        buckets = m.grad_buckets()
+        seen = []
+
+        def done(k):
+            seen.append(k)
+            a, b = buckets[k]
+            dist.all_reduce(m.grad[a:b])
+
+        m.backward(grad_scale=1.0 / world, bucket_done=done)
+        assert seen == list(range(len(buckets))), seen
         m.optimizer_step(lr=1e-2)
         flat = [torch.empty_like(m.flat) for _ in range(world)]
         dist.all_gather(flat, m.flat)
