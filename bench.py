@@ -680,6 +680,8 @@ def main():
                     help="N>1: SMs the dK/dV kernel leaves free for the overlapped all-reduce "
                          "(default: 32 at N=2, 48 from N=4, where NCCL's all-reduce runs more CTAs; "
                          "measured at C2: N=8 6.6x with 16-32, 7.4x with 48)")
+    ap.add_argument("--no-dw-pack", action="store_true",
+                    help="N>1: all-reduce the full T x T dW instead of its block-packed causal part")
     ap.add_argument("--nccl-max-ctas", type=int, default=0,
                     help="N>1: cap NCCL's CTAs per collective (communicator config max_ctas); the "
                          "dK/dV kernel then leaves that many SMs free unless --spare-sms is given")
@@ -775,24 +777,32 @@ def main():
 
     grads = (dQ, dK, dV, dW)
     overlap = dist is not None and not args.no_overlap
+    # N > 1: dW in the block-packed causal layout for the all-reduce (the
+    # upper triangle, zero on every rank, is not moved), expanded after it
+    pack = dist is not None and not args.no_dw_pack
+    dWp = torch.empty(ops.aft_dw_packed_size(T, T), device=dev) if pack else None
+    red = dWp if pack else dW
     if args.spare_sms < 0:
         if args.nccl_max_ctas > 0:
             args.spare_sms = args.nccl_max_ctas
         else:
             args.spare_sms = 32 if world <= 2 else 48
-    config["dw_allreduce"] = ("none" if dist is None else "serial" if not overlap
+    config["dw_allreduce"] = ("none" if dist is None else ("serial" if not overlap
                               else f"beside dK/dV ({args.spare_sms} SMs left free)")
+                              + (", block-packed causal dW (53% of T^2 at T=4096), expanded after"
+                                 if pack else ", full T x T"))
 
     def compute():
         ops.aft_fwd(Q, K_, V, w, causal=True, out=Z, workspace=ws)
-        ops.aft_bwd(Q, K_, V, w, dZ, causal=True, grads=grads, workspace=ws, ws_valid=True)
+        ops.aft_bwd(Q, K_, V, w, dZ, causal=True, grads=(dQ, dK, dV, red), workspace=ws, ws_valid=True,
+                    dw_packed=pack)
 
     # N > 1: forward, dQ and dW; then dW's all-reduce on a side stream while
     # the dK/dV contraction runs with a few SMs left to the collective
     def part_a():
         ops.aft_fwd(Q, K_, V, w, causal=True, out=Z, workspace=ws)
-        ops.aft_bwd(Q, K_, V, w, dZ, causal=True, grads=grads, workspace=ws, ws_valid=True,
-                    part="dw")
+        ops.aft_bwd(Q, K_, V, w, dZ, causal=True, grads=(dQ, None, None, red), workspace=ws, ws_valid=True,
+                    part="dw", dw_packed=pack)
 
     def part_b():
         ops.aft_bwd(Q, K_, V, w, dZ, causal=True, grads=grads, workspace=ws, ws_valid=True,
@@ -812,15 +822,17 @@ def main():
         if not overlap:
             run(0, compute)
             if dist is not None:
-                dist.all_reduce(dW)
-            return
-        run(0, part_a)
-        dw_ready.record()
-        with torch.cuda.stream(comm):
-            comm.wait_event(dw_ready)
-            dist.all_reduce(dW)
-        run(1, part_b)
-        torch.cuda.current_stream().wait_stream(comm)
+                dist.all_reduce(red)
+        else:
+            run(0, part_a)
+            dw_ready.record()
+            with torch.cuda.stream(comm):
+                comm.wait_event(dw_ready)
+                dist.all_reduce(red)
+            run(1, part_b)
+            torch.cuda.current_stream().wait_stream(comm)
+        if pack:
+            ops.aft_dw_unpack(dWp, dW)
 
     def barrier():
         if dist is not None:
@@ -912,9 +924,12 @@ def main():
         stream.wait_event(bs.out_free)  # its previous outputs have been read back
         q, k, v, g = bs.inp
         ops.aft_fwd(q, k, v, w, causal=True, out=bs.out[0], workspace=ws)
-        ops.aft_bwd(q, k, v, w, g, causal=True, grads=bs.out[1:], workspace=ws, ws_valid=True)
+        ops.aft_bwd(q, k, v, w, g, causal=True, grads=bs.out[1:4] + (red,), workspace=ws, ws_valid=True,
+                    dw_packed=pack)
         if dist is not None:
-            dist.all_reduce(bs.out[4])
+            dist.all_reduce(red)
+        if pack:
+            ops.aft_dw_unpack(dWp, bs.out[4])
         bs.done.record(stream)
         with torch.cuda.stream(d2h_s):
             d2h_s.wait_event(bs.done)
@@ -973,6 +988,7 @@ def main():
         "aft_bwd_from_stats": 3 * io + wbytes,  # Q, dZ in, dQ out; clears dW
         "aft_tc_dkdv": 4 * io,                # K, V in, dK, dV out
         "aft_tc_dw": 2 * wbytes,              # w in, dW out
+        "aft_dw_unpack": wbytes,              # dW out (N > 1)
     }
     gemm = 2.0 * B * d * T * (T + 1)  # one [num|den] contraction, causal half
     flops_per = {"aft_tc_fwd": gemm, "aft_tc_bwd_recompute": gemm, "aft_tc_dkdv": gemm, "aft_tc_dw": gemm}

@@ -25,6 +25,7 @@ DC_AFT_COMPUTE_BF16 = 0x10
 DC_AFT_SAVE_STATS = 0x20
 DC_AFT_BWD_NO_DKDV = 0x40
 DC_AFT_BWD_DKDV = 0x80
+DC_AFT_DW_PACKED = 0x100
 
 
 def DC_AFT_SPARE_SMS(n):
@@ -52,6 +53,8 @@ SIGNATURES = {
     "dc_last_error": (ctypes.c_char_p, []),
     "dc_version": (ctypes.c_char_p, []),
     "dc_device_status": (c_int, [_VP, POINTER(c_int)]),
+    "dc_aft_dw_packed_size": (c_int, [c_int, c_int, POINTER(c_size_t)]),
+    "dc_aft_dw_unpack": (c_int, [_VP, _VP, c_int, c_int, c_int, _VP]),
     "dc_profile_enable": (c_int, [c_int]),
     "dc_profile_read": (c_int, [ctypes.c_char_p, _FP, POINTER(c_int), c_int]),
     "dc_aft_trace": (c_int, [_VP, c_size_t, c_int]),

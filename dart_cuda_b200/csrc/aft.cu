@@ -112,6 +112,7 @@ struct Params {
     float *Rs, *Is;
     void *Rb, *Ib;
     int stat_lo;
+    int dw_packed;    // dW in the block-packed causal layout (dw_packed_row)
     int *status;
     unsigned long long *trace;  // optional per-tile timeline (nullptr: off)
 #ifdef DC_TEST_WITHHOLD
@@ -132,6 +133,40 @@ static int g_test_withhold = 0;
 // g_trace_modes (bit MODE); see trace_at() in aft_tc.cuh.
 static unsigned long long *g_trace_buf = nullptr;
 static int g_trace_modes = 0;
+
+// ------------------------------------------------------------ packed dW
+// Block-packed causal dW (DC_AFT_DW_PACKED): query rows in blocks of 256;
+// block k holds its rows' causal extent only, min(Tk8, 256 (k + 1)) columns
+// (Tk8 = Tk rounded up to 8), row after row, so every row starts 32-byte
+// aligned and the blocks before k (all of full width) take 256^2 k(k+1)/2
+// floats.  At T = 4096 that is 53% of the full matrix: the data-parallel
+// all-reduce of dW moves half the bytes (the upper triangle is zero on every
+// rank).
+constexpr int kDwBlock = 256;
+
+__host__ __device__ __forceinline__ size_t dw_packed_width(int t, int Tk)
+{
+    const size_t k = (size_t)t / kDwBlock, tk8 = ((size_t)Tk + 7) & ~(size_t)7;
+    const size_t full = (k + 1) * kDwBlock;
+    return full < tk8 ? full : tk8;
+}
+
+__host__ __device__ __forceinline__ size_t dw_packed_row(int t, int Tk)
+{
+    const size_t k = (size_t)t / kDwBlock;
+    return (size_t)kDwBlock * kDwBlock * k * (k + 1) / 2 + ((size_t)t - k * kDwBlock) * dw_packed_width(t, Tk);
+}
+
+__host__ __device__ __forceinline__ size_t dw_packed_floats(int Tq, int Tk)
+{
+    return Tq > 0 ? dw_packed_row(Tq - 1, Tk) + dw_packed_width(Tq - 1, Tk) : 0;
+}
+
+// start of dW's row t in the caller's layout
+__device__ __forceinline__ float *dw_row(const Params &p, int t)
+{
+    return p.dW + (p.dw_packed ? dw_packed_row(t, p.Tk) : (size_t)t * p.ldw);
+}
 
 // ------------------------------------------------------------ epilogues
 // Shared by the tensor-core and CUDA-core paths so both apply identical
@@ -199,9 +234,8 @@ __device__ __forceinline__ void epi_hgrad(const Params &p, int b, int i, int d, 
 __device__ __forceinline__ void epi_wgrad(const Params &p, int t, int i, float acc)
 {
     if (t < p.Tq && i < p.Tk && (!p.causal || i <= t)) {
-        size_t o = (size_t)t * p.ldw + i;
-        float a = __expf(p.w[o] - p.m[t]);
-        atomicAdd(p.dW + o, a * acc);
+        float a = __expf(p.w[(size_t)t * p.ldw + i] - p.m[t]);
+        atomicAdd(dw_row(p, t) + i, a * acc);
     }
 }
 
@@ -564,6 +598,21 @@ __global__ void __launch_bounds__(256) bwd_stats_kernel(const Params p)
     EpiPre none;
     none.ok = false;
     epi16_grads<IO, E>(p, b, t, d0, r, inv, none);
+}
+
+// Block-packed dW to the caller's [Tq][ldw] layout, zeros past each row's
+// packed extent: one warp per row, lanes on consecutive columns.
+__global__ void __launch_bounds__(256)
+    dw_unpack_kernel(const float *__restrict__ packed, float *__restrict__ dW, int ldw, int Tq, int Tk)
+{
+    grid_dep_wait();  // launched early (programmatic dependent launch)
+    grid_dep_launch();
+    const int t = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (t >= Tq) return;
+    const float *src = packed + dw_packed_row(t, Tk);
+    const int width = (int)dw_packed_width(t, Tk) < Tk ? (int)dw_packed_width(t, Tk) : Tk;
+    float *dst = dW + (size_t)t * ldw;
+    for (int i = lane; i < Tk; i += 32) dst[i] = i < width ? src[i] : 0.f;
 }
 
 // ------------------------------------------------------------ host side
@@ -1015,6 +1064,7 @@ static int bwd_impl(const void *Q, const void *K, const void *V, const float *w,
     p.ldw = ldw;
     p.vec_io = vec_ok<IO>(L, {Q, K, V, dZ, dQ, dK, dV});
     p.vec_w = (ldw % 8 == 0) && ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(dW)) & 31) == 0;
+    p.dw_packed = (flags & DC_AFT_DW_PACKED) ? 1 : 0;
     // dQ, g and n, then dW (which needs only g, n and the prep panels), then
     // dK and dV: a caller that splits the call can reduce dW across ranks
     // while the last contraction runs
@@ -1025,7 +1075,9 @@ static int bwd_impl(const void *Q, const void *K, const void *V, const float *w,
         // statistics kernels clear it themselves (no memset node between
         // them and the dW launch); the CUDA-core cross-check path does not
         if (!(flags & DC_AFT_ACCUMULATE)) {
-            if (flags & DC_AFT_SIMT)
+            if ((flags & DC_AFT_SIMT) && p.dw_packed)
+                DC_CUDA_TRY(cudaMemsetAsync(dW, 0, dw_packed_floats(L.Tq, L.Tk) * 4, st));
+            else if (flags & DC_AFT_SIMT)
                 DC_CUDA_TRY(cudaMemset2DAsync(dW, (size_t)ldw * 4, 0, (size_t)L.Tk * 4, L.Tq, st));
             else
                 p.zero_dw = 1;
@@ -1106,6 +1158,29 @@ int dc_aft_trace(void *device_buffer, size_t bytes, int mode_mask)
     return DC_OK;
 }
 
+int dc_aft_dw_packed_size(int Tq, int Tk, size_t *floats)
+{
+    clear_error();
+    if (!floats) return fail(DC_ERR_INVALID, "floats is NULL");
+    if (Tq < 0 || Tk < 0) return fail(DC_ERR_INVALID, "negative shape");
+    *floats = dw_packed_floats(Tq, Tk);
+    return DC_OK;
+}
+
+int dc_aft_dw_unpack(const float *packed, float *dW, int ldw, int Tq, int Tk, void *stream)
+{
+    clear_error();
+    if (Tq < 0 || Tk < 0 || ldw < Tk) return fail(DC_ERR_INVALID, "bad shape Tq=%d Tk=%d ldw=%d", Tq, Tk, ldw);
+    if ((long long)Tq * Tk == 0) return DC_OK;
+    if (!packed || !dW) return fail(DC_ERR_INVALID, "null pointer");
+    cudaStream_t st = as_stream(stream);
+    KernelTimer kt("aft_dw_unpack", st);
+    DC_CUDA_TRY(launch_pdl(dw_unpack_kernel, dim3((unsigned)((Tq + 7) / 8)), dim3(256), 0, st, 1, packed, dW,
+                           ldw, Tq, Tk));
+    DC_CUDA_TRY(cudaGetLastError());
+    return DC_OK;
+}
+
 int dc_aft_workspace_size(int B, int Tq, int Tk, int D, int dtype, int flags, size_t *bytes)
 {
     clear_error();
@@ -1170,6 +1245,8 @@ int dc_aft_bwd_strided(const void *Q, const void *K, const void *V, const float 
     if ((part1 && (!dZ || !dQ || !dW)) || (part2 && (!dK || !dV)))
         return fail(DC_ERR_INVALID, "null gradient pointer");
     if (ldi < D || ldo < D) return fail(DC_ERR_INVALID, "row strides (%d, %d) < D (%d)", ldi, ldo, D);
+    if ((flags & DC_AFT_DW_PACKED) && !(flags & DC_AFT_CAUSAL))
+        return fail(DC_ERR_INVALID, "DC_AFT_DW_PACKED needs DC_AFT_CAUSAL (the packed layout holds the causal extent)");
     cudaStream_t st = as_stream(stream);
     Layout L = make_layout(B, Tq, Tk, D, dtype, flags);
     L.ldi = ldi;

@@ -460,7 +460,7 @@ __device__ __forceinline__ void epi16_wgrad(const Params &p, int t, int i0, cons
     if (t >= p.Tq || i0 >= p.Tk || (p.causal && i0 > t)) return;
     const float m = __ldg(p.m + t);
     const float *w = p.w + (size_t)t * p.ldw;
-    float *dW = p.dW + (size_t)t * p.ldw;
+    float *dW = dw_row(p, t);
     if (p.vec_w && i0 + 16 <= p.Tk && (!p.causal || i0 + 15 <= t)) {
         float wv[16];
         ld16g(w + i0, wv);
@@ -488,6 +488,16 @@ __device__ __forceinline__ void epi16_wgrad(const Params &p, int t, int i0, cons
 // atomics (the dW launch waits for that kernel to complete).
 __device__ __forceinline__ void zero_dw(const Params &p, size_t i, size_t count)
 {
+    if (p.dw_packed) {  // one contiguous run (a multiple of 8 floats)
+        const size_t n = dw_packed_floats(p.Tq, p.Tk);
+        if (p.vec_w) {
+            for (size_t e = i; e < n / 4; e += count)
+                reinterpret_cast<float4 *>(p.dW)[e] = make_float4(0.f, 0.f, 0.f, 0.f);
+        } else {
+            for (size_t e = i; e < n; e += count) p.dW[e] = 0.f;
+        }
+        return;
+    }
     if (p.vec_w) {  // rows of whole float4s (ldw % 8 == 0, 32-byte aligned base)
         const size_t per = (size_t)(p.Tk + 3) / 4, n = per * p.Tq;
         for (size_t e = i; e < n; e += count) {

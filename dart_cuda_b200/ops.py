@@ -16,7 +16,7 @@ from ctypes import byref, c_int, c_size_t
 
 import torch
 
-from ._lib import (DC_AFT_ACCUMULATE, DC_AFT_BWD_DKDV, DC_AFT_BWD_NO_DKDV, DC_AFT_CAUSAL,
+from ._lib import (DC_AFT_ACCUMULATE, DC_AFT_BWD_DKDV, DC_AFT_BWD_NO_DKDV, DC_AFT_CAUSAL, DC_AFT_DW_PACKED,
                    DC_AFT_COMPUTE_BF16, DC_AFT_SAVE_STATS, DC_AFT_SIMT, DC_AFT_SPARE_SMS,
                    DC_AFT_WS_VALID, DC_BF16, DC_F32, DC_GEMM_ACCUMULATE, DC_GEMM_BIAS, DC_GEMM_GELU,
                    DC_GEMM_GELU_BWD, DC_GEMM_TRANS_A, DC_GEMM_TRANS_B, DcError, check, lib)
@@ -111,16 +111,37 @@ def aft_fwd(Q, K, V, w, causal=True, out=None, workspace: AftWorkspace | None = 
     return Z
 
 
+def aft_dw_packed_size(Tq: int, Tk: int) -> int:
+    """Floats of a block-packed causal dW (dw_packed=True in aft_bwd)."""
+    n = c_size_t(0)
+    check(lib().dc_aft_dw_packed_size(int(Tq), int(Tk), byref(n)), "dc_aft_dw_packed_size")
+    return int(n.value)
+
+
+def aft_dw_unpack(packed: torch.Tensor, dW: torch.Tensor) -> torch.Tensor:
+    """Expand a block-packed causal dW into dW [Tq, Tk] (row stride dW.stride(0))."""
+    if dW.dtype != torch.float32 or dW.dim() != 2 or dW.stride(1) != 1:
+        raise DcError("dW must be a 2-D float32 tensor with unit column stride")
+    Tq, Tk = dW.shape
+    if packed.numel() < aft_dw_packed_size(Tq, Tk):
+        raise DcError("packed dW is too small")
+    check(lib().dc_aft_dw_unpack(packed.data_ptr(), dW.data_ptr(), dW.stride(0), Tq, Tk, _stream()),
+          "dc_aft_dw_unpack")
+    return dW
+
+
 def aft_bwd(Q, K, V, w, dZ, causal=True, grads=None, accumulate=False,
             workspace: AftWorkspace | None = None, ws_valid=False, simt=False, compute_bf16=False,
-            part=None, spare_sms=0):
+            part=None, spare_sms=0, dw_packed=False):
     """dQ, dK, dV, dW of the AFT-full op.
 
     part=None computes all four.  part="dw" computes dQ and dW only and leaves
     g, n in `workspace`; part="dkdv" then computes dK and dV from them (same
     workspace, ws_valid=True), so a data-parallel caller can all-reduce dW
     while dK and dV run.  spare_sms leaves that many SMs free for such a
-    collective.  Entries of `grads` a part does not write may be None."""
+    collective.  Entries of `grads` a part does not write may be None.
+    dw_packed=True (causal only): dW is a 1-D float32 buffer of
+    aft_dw_packed_size(Tq, Tk) floats in the block-packed layout."""
     Q3, K3, V3, G3 = _as3d(Q), _as3d(K), _as3d(V), _as3d(dZ)
     for t, n in ((Q3, "Q"), (K3, "K"), (V3, "V"), (G3, "dZ")):
         _need(t, n)
@@ -130,16 +151,23 @@ def aft_bwd(Q, K, V, w, dZ, causal=True, grads=None, accumulate=False,
     if part not in (None, "dw", "dkdv"):
         raise DcError(f"part must be None, 'dw' or 'dkdv' (got {part!r})")
     if grads is None:
-        grads = (torch.empty_like(Q), torch.empty_like(K), torch.empty_like(V),
-                 torch.empty(w.shape[0], w.stride(0), device=w.device)[:, : w.shape[1]])
+        dW0 = (torch.empty(aft_dw_packed_size(Tq, Tk), device=w.device) if dw_packed else
+               torch.empty(w.shape[0], w.stride(0), device=w.device)[:, : w.shape[1]])
+        grads = (torch.empty_like(Q), torch.empty_like(K), torch.empty_like(V), dW0)
     dQ, dK, dV, dW = grads
-    if dW is not None and (dW.dtype != torch.float32 or dW.stride(0) != w.stride(0) or dW.stride(1) != 1):
+    if dw_packed:
+        if dW is not None and (dW.dtype != torch.float32 or not dW.is_contiguous()
+                               or dW.numel() < aft_dw_packed_size(Tq, Tk)):
+            raise DcError("packed dW must be a contiguous float32 buffer of aft_dw_packed_size floats")
+    elif dW is not None and (dW.dtype != torch.float32 or dW.stride(0) != w.stride(0) or dW.stride(1) != 1):
         raise DcError("dW must be float32 with the row stride of w")
     ws = workspace.ptr if workspace is not None else None
     nb = workspace.nbytes if workspace is not None else 0
     flags = _flags(causal, accumulate, ws_valid, simt, compute_bf16) | DC_AFT_SPARE_SMS(spare_sms)
     if workspace is not None and workspace.save_stats:
         flags |= DC_AFT_SAVE_STATS
+    if dw_packed:
+        flags |= DC_AFT_DW_PACKED
     if part == "dw":
         flags |= DC_AFT_BWD_NO_DKDV
     elif part == "dkdv":

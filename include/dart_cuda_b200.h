@@ -62,6 +62,14 @@ extern "C" {
  * and dV only (dZ, dQ, dW may be NULL). */
 #define DC_AFT_BWD_NO_DKDV 0x40
 #define DC_AFT_BWD_DKDV 0x80
+/* Causal backward only: dW is written in the block-packed layout instead of
+ * [Tq][ldw] — query rows in blocks of 256, block k holding its rows'
+ * causal extent min(Tk8, 256(k+1)) columns (Tk8 = Tk rounded up to 8) row
+ * after row; dc_aft_dw_packed_size gives its size in floats (53% of Tq*Tk at
+ * T = 4096) and dc_aft_dw_unpack expands it.  For a data-parallel caller
+ * that reduces dW across ranks: the upper triangle, zero on every rank, is
+ * not moved.  No counterpart in the reference. */
+#define DC_AFT_DW_PACKED 0x100
 /* The persistent tensor-core kernels of this call leave n SMs (0..255) free,
  * e.g. for a collective running beside them on another stream. */
 #define DC_AFT_SPARE_SMS(n) (((n)&0xff) << 16)
@@ -121,6 +129,12 @@ int dc_aft_trace(void *device_buffer, size_t bytes, int mode_mask);
  * (native/src/kernels/attention.cuh:41-128), batched over B sequences.
  */
 int dc_aft_workspace_size(int B, int Tq, int Tk, int D, int dtype, int flags, size_t *bytes);
+
+/* Size in floats of a block-packed causal dW (DC_AFT_DW_PACKED), and its
+ * expansion into dW [Tq][ldw] (zeros above each row's causal extent), on
+ * `stream`.  No counterpart in the reference. */
+int dc_aft_dw_packed_size(int Tq, int Tk, size_t *floats);
+int dc_aft_dw_unpack(const float *packed, float *dW, int ldw, int Tq, int Tk, void *stream);
 
 int dc_aft_fwd(const void *Q, const void *K, const void *V, const float *w, int ldw, void *Z,
                int B, int Tq, int Tk, int D, int dtype, int flags, void *workspace,

@@ -96,3 +96,23 @@ def test_split_backward_flags_are_validated_on_the_host():
     assert bwd(dkdv, dK=None) == _lib.DC_ERR_INVALID
     assert bwd(base | _lib.DC_AFT_BWD_NO_DKDV, dW=None) == _lib.DC_ERR_INVALID
     assert _lib.DC_AFT_SPARE_SMS(48) == 48 << 16 and _lib.DC_AFT_SPARE_SMS(300) == (300 & 0xFF) << 16
+
+
+def test_packed_dw_size():
+    """Block-packed causal dW: rows in blocks of 256, block k holding
+    min(Tk rounded up to 8, 256 (k+1)) columns per row."""
+    import ctypes
+
+    from dart_cuda_b200 import lib
+
+    def expect(T):
+        tk8 = (T + 7) // 8 * 8
+        return sum(min(tk8, 256 * (t // 256 + 1)) for t in range(T))
+
+    for T in (0, 1, 7, 256, 257, 300, 1024, 1100, 4096):
+        n = ctypes.c_size_t(0)
+        assert lib().dc_aft_dw_packed_size(T, T, ctypes.byref(n)) == 0
+        assert n.value == expect(T), T
+    n = ctypes.c_size_t(0)
+    lib().dc_aft_dw_packed_size(4096, 4096, ctypes.byref(n))
+    assert abs(n.value / 4096 ** 2 - 0.53) < 0.005

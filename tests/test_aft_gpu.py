@@ -506,3 +506,61 @@ def test_large_spreads(ops, dev, dtype, wscale, kscale):
     tol = TOL[dtype] if dtype == torch.float32 else 2e-2
     assert_errs(out_errs(f"spread w={wscale} k={kscale} {dtype}", outs, ref), tol,
                 None if dtype == torch.float32 else 2e-1)
+
+
+# ----------------------------------------------------------- block-packed dW
+@pytest.mark.parametrize("dtype,B,T,D", [(torch.bfloat16, 2, 512, 128), (torch.bfloat16, 1, 1100, 72),
+                                         (torch.float32, 2, 300, 40)])
+@pytest.mark.parametrize("save", [False, True])
+def test_packed_dw_matches_full(ops, dev, dtype, B, T, D, save):
+    """dW written in the block-packed causal layout, expanded with
+    dc_aft_dw_unpack, equals the [T, T] dW of the same backward (up to the
+    order of split-K additions), including zeros above the diagonal; the
+    other gradients are unchanged; accumulate adds into the packed buffer."""
+    Q, K, V, W, dZ = make_inputs(60, B, T, T, D)
+    tq, tk, tv, tg = to_dev(dev, dtype, Q, K, V, dZ)
+    tw = torch.from_numpy(W).to(dev)
+    ws = ops.AftWorkspace(B, T, T, D, dtype, flags=1, save_stats=save)
+    ops.aft_fwd(tq, tk, tv, tw, causal=True, workspace=ws)
+    g0 = ops.aft_bwd(tq, tk, tv, tw, tg, causal=True, workspace=ws, ws_valid=True)
+    packed = torch.full((ops.aft_dw_packed_size(T, T),), 5.0, device=dev)
+    g1 = ops.aft_bwd(tq, tk, tv, tw, tg, causal=True, workspace=ws, ws_valid=True, dw_packed=True,
+                     grads=(torch.empty_like(tq), torch.empty_like(tk), torch.empty_like(tv), packed))
+    for a, b in zip(g0[:3], g1[:3]):
+        assert torch.equal(a, b)
+    full = torch.full((T, T), 7.0, device=dev)
+    ops.aft_dw_unpack(packed, full)
+    torch.testing.assert_close(full, g0[3], rtol=1e-5, atol=1e-6)
+    assert float(torch.triu(full, 1).abs().max()) == 0.0
+    # accumulate: the packed buffer receives a second dW
+    ops.aft_bwd(tq, tk, tv, tw, tg, causal=True, workspace=ws, ws_valid=True, dw_packed=True, accumulate=True,
+                grads=(torch.zeros_like(tq), torch.zeros_like(tk), torch.zeros_like(tv), packed))
+    ops.aft_dw_unpack(packed, full)
+    torch.testing.assert_close(full, 2 * g0[3], rtol=1e-5, atol=1e-6)
+    assert ops.device_status() == 0
+
+
+def test_packed_dw_split_backward_and_rejects_noncausal(ops, dev):
+    from dart_cuda_b200 import DcError
+
+    B, T, D = 4, 1024, 128
+    Q, K, V, W, dZ = make_inputs(61, B, T, T, D)
+    tq, tk, tv, tg = to_dev(dev, torch.bfloat16, Q, K, V, dZ)
+    tw = torch.from_numpy(W).to(dev)
+    ws = ops.AftWorkspace(B, T, T, D, torch.bfloat16, flags=1, save_stats=True)
+    ops.aft_fwd(tq, tk, tv, tw, causal=True, workspace=ws)
+    g0 = ops.aft_bwd(tq, tk, tv, tw, tg, causal=True, workspace=ws, ws_valid=True)
+    packed = torch.empty(ops.aft_dw_packed_size(T, T), device=dev)
+    dQ, dK, dV = torch.empty_like(tq), torch.empty_like(tk), torch.empty_like(tv)
+    ops.aft_bwd(tq, tk, tv, tw, tg, causal=True, grads=(dQ, None, None, packed), workspace=ws, ws_valid=True,
+                part="dw", dw_packed=True)
+    ops.aft_bwd(tq, tk, tv, tw, tg, causal=True, grads=(None, dK, dV, None), workspace=ws, ws_valid=True,
+                part="dkdv", spare_sms=16)
+    full = torch.empty(T, T, device=dev)
+    ops.aft_dw_unpack(packed, full)
+    torch.testing.assert_close(full, g0[3], rtol=1e-5, atol=1e-6)
+    for a, b in zip(g0[:3], (dQ, dK, dV)):
+        assert torch.equal(a, b)
+    with pytest.raises(DcError):
+        ops.aft_bwd(tq, tk, tv, tw, tg, causal=False, dw_packed=True)
+    assert ops.device_status() == 0
