@@ -378,7 +378,10 @@ def bench_train(args, dev, rank, world, dist):
     # overlap the rest of the backward; the CUDA graph of forward + backward
     # is captured as one graph per bucket, replayed with the bucket's
     # all-reduce queued between replays
-    overlap = dist is not None and not args.no_overlap
+    # (opt-in: measured slower than one all-reduce after the backward at 2
+    # and 8 GPUs, 3.05 / 3.17 against 3.00 / 3.09 ms — the NCCL kernels beside
+    # the backward cost more than the 25.6 MB all-reduce they hide)
+    overlap = dist is not None and args.c3_overlap
     buckets = m.grad_buckets()
     comm = torch.cuda.Stream(device=dev) if overlap else None
 
@@ -680,6 +683,9 @@ def main():
                     help="N>1: SMs the dK/dV kernel leaves free for the overlapped all-reduce "
                          "(default: 32 at N=2, 48 from N=4, where NCCL's all-reduce runs more CTAs; "
                          "measured at C2: N=8 6.6x with 16-32, 7.4x with 48)")
+    ap.add_argument("--c3-overlap", action="store_true",
+                    help="c3, N>1: all-reduce the gradients bucket by bucket beside the backward "
+                         "(one CUDA graph per bucket) instead of once after it")
     ap.add_argument("--no-dw-pack", action="store_true",
                     help="N>1: all-reduce the full T x T dW instead of its block-packed causal part")
     ap.add_argument("--nccl-max-ctas", type=int, default=0,
@@ -779,14 +785,18 @@ def main():
     overlap = dist is not None and not args.no_overlap
     # N > 1: dW in the block-packed causal layout for the all-reduce (the
     # upper triangle, zero on every rank, is not moved), expanded after it
-    pack = dist is not None and not args.no_dw_pack
+    # (from T = 2048: below, the unpack costs more than the bytes it saves)
+    pack = dist is not None and not args.no_dw_pack and T >= 2048
     dWp = torch.empty(ops.aft_dw_packed_size(T, T), device=dev) if pack else None
     red = dWp if pack else dW
     if args.spare_sms < 0:
+        # measured: with the packed dW (T >= 2048) 32 free SMs beat 48 at 8
+        # GPUs (C4: 7.38x against 7.21x one GPU) and 16 at 2 (1.072 against
+        # 1.106 ms); the full 1 MiB dW of T = 512 ran best with 48 from N = 4
         if args.nccl_max_ctas > 0:
             args.spare_sms = args.nccl_max_ctas
         else:
-            args.spare_sms = 32 if world <= 2 else 48
+            args.spare_sms = 32 if world <= 2 or T >= 2048 else 48
     config["dw_allreduce"] = ("none" if dist is None else ("serial" if not overlap
                               else f"beside dK/dV ({args.spare_sms} SMs left free)")
                               + (", block-packed causal dW (53% of T^2 at T=4096), expanded after"

@@ -612,6 +612,16 @@ __global__ void __launch_bounds__(256)
     const float *src = packed + dw_packed_row(t, Tk);
     const int width = (int)dw_packed_width(t, Tk) < Tk ? (int)dw_packed_width(t, Tk) : Tk;
     float *dst = dW + (size_t)t * ldw;
+    // 16-byte accesses when the rows of dW start on 16-byte boundaries (the
+    // packed rows always do; their widths are multiples of 8 unless clipped
+    // to Tk, and Tk % 4 == 0 keeps whole float4s inside the row)
+    if ((ldw % 4) == 0 && (Tk % 4) == 0 && (reinterpret_cast<uintptr_t>(dW) & 15) == 0) {
+        const float4 *s4 = reinterpret_cast<const float4 *>(src);
+        float4 *d4 = reinterpret_cast<float4 *>(dst);
+        for (int i = lane; i < Tk / 4; i += 32)
+            d4[i] = 4 * i < width ? __ldg(s4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        return;
+    }
     for (int i = lane; i < Tk; i += 32) dst[i] = i < width ? src[i] : 0.f;
 }
 
