@@ -474,10 +474,15 @@ def bench_train(args, dev, rank, world, dist):
     dom = max(prof, key=lambda k: prof[k][0]) if prof else None
     roof = None
     if dom == "gemm_tc":
+        # the decoder's GEMMs run tf32 operands: their ceiling is the dense
+        # tf32 rate, half the bf16 rate on this part (1.1 against 2.25
+        # PFLOP/s nominal), taken as half the measured bf16 burst peak
         k = kern[dom]
-        roof = {"bound": "tensor", "achieved": k["TFLOP/s"], "peak": P["bf16_tflops"], "unit": "TFLOP/s",
-                "frac": k["tensor_frac"], "traffic": None, "kernel": dom,
-                "peak_source": P["source"] + " bf16 burst (the GEMMs run tf32: half that rate is their ceiling)"}
+        tf32 = P["bf16_tflops"] / 2
+        roof = {"bound": "tensor", "achieved": k["TFLOP/s"], "peak": tf32, "unit": "TFLOP/s",
+                "frac": k["TFLOP/s"] / tf32, "traffic": None, "kernel": dom,
+                "peak_source": P["source"] + " bf16 burst / 2 (tf32 operands)"}
+        kern[dom]["tensor_frac"] = k["TFLOP/s"] / tf32
 
     # end to end: token ids and targets from pinned host memory, the loss back
     h_idx, h_tgt = idx.cpu().pin_memory(), tgt.cpu().pin_memory()

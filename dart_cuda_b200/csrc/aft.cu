@@ -586,11 +586,6 @@ __global__ void __launch_bounds__(256) bwd_stats_kernel(const Params p)
             ld16g((const E *)p.Rb + so, r);
             ld16g((const E *)p.Ib + so, inv);
         }
-        bool bad = false;  // the forward's range guard, on 1/den' and r
-#pragma unroll
-        for (int j = 0; j < 16; ++j)
-            bad |= d0 + j < p.D && (!(inv[j] <= 0x1p100f) || !(fabsf(r[j]) <= 3.0e38f));
-        if (bad) report_range(p);
     } else {
 #pragma unroll
         for (int j = 0; j < 16; ++j) r[j] = inv[j] = 0.f;
@@ -598,6 +593,15 @@ __global__ void __launch_bounds__(256) bwd_stats_kernel(const Params p)
     EpiPre none;
     none.ok = false;
     epi16_grads<IO, E>(p, b, t, d0, r, inv, none);
+    // the forward's range guard, on 1/den' and r (after the gradient pass has
+    // issued its loads, so that it does not hold them up)
+    if (t < p.Tq) {
+        bool bad = false;
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+            bad |= d0 + j < p.D && (!(inv[j] <= 0x1p100f) || !(fabsf(r[j]) <= 3.0e38f));
+        if (bad) report_range(p);
+    }
 }
 
 // Block-packed dW to the caller's [Tq][ldw] layout, zeros past each row's

@@ -8,6 +8,7 @@
 #include <math.h>
 
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 
 #include "dc_internal.h"
@@ -442,16 +443,20 @@ __global__ void bias_bwd_vec4(const float4 *__restrict__ dy, float4 *__restrict_
     }
 }
 
-// Column sums on clusters, one launch: the kSumCluster CTAs of a cluster
-// (grid x) split the rows of one 16-column block (grid y).  A CTA's 512
-// threads are 128 row lanes x 4 float4 column lanes with four rows in flight
+// Column sums on clusters, one launch: the CL CTAs of a cluster (grid x)
+// split the rows of one block of 4*QN columns (grid y).  A CTA's 512 threads
+// are 512/QN row lanes x QN float4 column lanes with four rows in flight
 // each; lanes of a column meet by shuffles and shared memory, and rank 0 adds
 // the cluster's CTA sums, read from distributed shared memory in rank order.
 // The sums are deterministic and no partial rows go through global memory
 // (the two-pass form spent a second launch and an L2 round trip on them).
+// QN = 4 (16 columns, 64-byte row segments): 8-column blocks doubled the
+// CTAs but halved the bytes per L1 wavefront and ran at half the bandwidth.
+// 16-CTA clusters (a non-portable size) for narrow matrices, to fill the
+// SMs with 256 CTAs at [262144, 256], ran slower still; tall matrices of at
+// most 1024 columns take the row-contiguous form below instead.
 constexpr int kSumCluster = 8;
 constexpr int kSumThreads = 512;
-constexpr int kSumRowLanes = kSumThreads / 4;
 
 __device__ __forceinline__ void add4(float4 &a, const float4 &b)
 {
@@ -461,37 +466,39 @@ __device__ __forceinline__ void add4(float4 &a, const float4 &b)
     a.w += b.w;
 }
 
+template <int QN, int CL>
 __global__ void __launch_bounds__(kSumThreads)
     bias_bwd_cluster(const float4 *__restrict__ dy, float4 *__restrict__ da,
                      float *__restrict__ db, int M, int N4, int accumulate)
 {
+    constexpr int kRowLanes = kSumThreads / QN;
     grid_dep_wait();  // programmatic dependent launch: inputs are ready
     grid_dep_launch();
-    __shared__ float4 wsum[kSumThreads / 32][4];
-    __shared__ float csum[16];
-    const int q = threadIdx.x & 3, rl = threadIdx.x >> 2;
-    const int c4 = blockIdx.y * 4 + q;
-    const int rpc = (M + kSumCluster - 1) / kSumCluster;
+    __shared__ float4 wsum[kSumThreads / 32][QN];
+    __shared__ float csum[4 * QN];
+    const int q = threadIdx.x % QN, rl = threadIdx.x / QN;
+    const int c4 = blockIdx.y * QN + q;
+    const int rpc = (M + CL - 1) / CL;
     const int r0 = (int)cluster_rank() * rpc, r1 = min(M, r0 + rpc);
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     if (c4 < N4) {
         int r = r0 + rl;
-        for (; r + 3 * kSumRowLanes < r1; r += 4 * kSumRowLanes) {
+        for (; r + 3 * kRowLanes < r1; r += 4 * kRowLanes) {
             float4 g[4];
 #pragma unroll
-            for (int k = 0; k < 4; ++k) g[k] = __ldcs(dy + (size_t)(r + k * kSumRowLanes) * N4 + c4);
+            for (int k = 0; k < 4; ++k) g[k] = __ldcs(dy + (size_t)(r + k * kRowLanes) * N4 + c4);
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
                 add4(acc, g[k]);
                 if (da) {
-                    const size_t o = (size_t)(r + k * kSumRowLanes) * N4 + c4;
+                    const size_t o = (size_t)(r + k * kRowLanes) * N4 + c4;
                     float4 a = g[k];
                     if (accumulate) add4(a, da[o]);
                     da[o] = a;
                 }
             }
         }
-        for (; r < r1; r += kSumRowLanes) {
+        for (; r < r1; r += kRowLanes) {
             const size_t o = (size_t)r * N4 + c4;
             const float4 g = __ldcs(dy + o);
             add4(acc, g);
@@ -503,15 +510,15 @@ __global__ void __launch_bounds__(kSumThreads)
         }
     }
 #pragma unroll
-    for (int off = 4; off < 32; off <<= 1) {
+    for (int off = QN; off < 32; off <<= 1) {
         acc.x += __shfl_xor_sync(0xffffffffu, acc.x, off);
         acc.y += __shfl_xor_sync(0xffffffffu, acc.y, off);
         acc.z += __shfl_xor_sync(0xffffffffu, acc.z, off);
         acc.w += __shfl_xor_sync(0xffffffffu, acc.w, off);
     }
-    if ((threadIdx.x & 31) < 4) wsum[threadIdx.x >> 5][q] = acc;
+    if ((threadIdx.x & 31) < QN) wsum[threadIdx.x >> 5][q] = acc;
     __syncthreads();
-    if (threadIdx.x < 16) {
+    if (threadIdx.x < 4 * QN) {
         float v = 0.f;
 #pragma unroll
         for (int w = 0; w < kSumThreads / 32; ++w)
@@ -519,15 +526,86 @@ __global__ void __launch_bounds__(kSumThreads)
         csum[threadIdx.x] = v;
     }
     cluster_sync_all();
-    if (cluster_rank() == 0 && threadIdx.x < 16) {
-        const int j = blockIdx.y * 16 + threadIdx.x;
+    if (cluster_rank() == 0 && threadIdx.x < 4 * QN) {
+        const int j = blockIdx.y * 4 * QN + threadIdx.x;
         const uint32_t mine = (uint32_t)__cvta_generic_to_shared(&csum[threadIdx.x]);
         float v = 0.f;
 #pragma unroll
-        for (int r = 0; r < kSumCluster; ++r) v += ld_dsmem_f32(smem_in_cta(mine, r));
+        for (int r = 0; r < CL; ++r) v += ld_dsmem_f32(smem_in_cta(mine, r));
         if (j < 4 * N4) db[j] = accumulate ? db[j] + v : v;
     }
     cluster_sync_all();  // the CTA sums stay readable until rank 0 has added them
+}
+
+// Column sums of a tall matrix of at most 1024 columns, row-contiguous: CTA c
+// streams rows [c*rpc, (c+1)*rpc) whole (512 threads = 512/N4 rows x N4
+// float4 lanes, four row groups in flight; every warp reads and writes
+// contiguous bytes, as a copy does), adds its rows per column in shared
+// memory in row-lane order and writes its partial sums; the CTA that
+// finishes last (an atomic count, no CTA waits for another) adds the
+// partials in CTA order, so the sums are deterministic.  It resets the count
+// for the next call.
+__global__ void __launch_bounds__(kSumThreads)
+    bias_bwd_rows(const float4 *__restrict__ dy, float4 *__restrict__ da, float *__restrict__ db,
+                  float4 *__restrict__ part, unsigned *__restrict__ done, int M, int N4, int rpc,
+                  int accumulate)
+{
+    grid_dep_wait();  // programmatic dependent launch: inputs are ready
+    grid_dep_launch();
+    __shared__ float4 red[kSumThreads];
+    __shared__ bool last;
+    const int lanes = kSumThreads / N4;  // rows in flight per step (>= 2)
+    const int c4 = threadIdx.x % N4, rl = threadIdx.x / N4;
+    const int r0 = blockIdx.x * rpc, r1 = min(M, r0 + rpc);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (rl < lanes) {
+        int r = r0 + rl;
+        for (; r + 3 * lanes < r1; r += 4 * lanes) {
+            float4 g[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) g[k] = __ldcs(dy + (size_t)(r + k * lanes) * N4 + c4);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                add4(acc, g[k]);
+                if (da) {
+                    const size_t o = (size_t)(r + k * lanes) * N4 + c4;
+                    float4 a = g[k];
+                    if (accumulate) add4(a, da[o]);
+                    __stcs(da + o, a);
+                }
+            }
+        }
+        for (; r < r1; r += lanes) {
+            const size_t o = (size_t)r * N4 + c4;
+            const float4 g = __ldcs(dy + o);
+            add4(acc, g);
+            if (da) {
+                float4 a = g;
+                if (accumulate) add4(a, da[o]);
+                __stcs(da + o, a);
+            }
+        }
+    }
+    red[threadIdx.x] = acc;
+    __syncthreads();
+    if (threadIdx.x < N4) {
+        float4 v = red[threadIdx.x];
+        for (int k = 1; k < lanes; ++k) add4(v, red[k * N4 + threadIdx.x]);
+        part[(size_t)blockIdx.x * N4 + threadIdx.x] = v;
+    }
+    __threadfence();  // this CTA's partials are visible before it is counted
+    __syncthreads();
+    if (threadIdx.x == 0) last = atomicAdd(done, 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    for (int j = threadIdx.x; j < 4 * N4; j += blockDim.x) {
+        const float *pf = reinterpret_cast<const float *>(part);
+        float v = 0.f;
+        for (int c = 0; c < (int)gridDim.x; ++c) v += __ldcg(pf + (size_t)c * 4 * N4 + j);
+        db[j] = accumulate ? db[j] + v : v;
+    }
+    if (threadIdx.x == 0) *done = 0u;
 }
 
 // ===================================================================== CE
@@ -997,14 +1075,39 @@ int dc_bias_bwd(const float *dy, float *da, float *db, int M, int N, int accumul
     if (!dy || !db) return fail(DC_ERR_INVALID, "null pointer");
     cudaStream_t st = as_stream(stream);
     const bool vec = N % 4 == 0 && aligned16(dy) && (!da || aligned16(da));
+    // tall matrices of at most 1024 columns: the row-contiguous form (whole
+    // rows per CTA; its partial sums and the finishing count in a scratch of
+    // the stream-ordered allocator)
+    if (vec && N <= 1024 && (long long)M * N >= (1ll << 22)) {
+        const int N4 = N / 4, lanes = kSumThreads / N4;
+        const int ctas = std::max(1, std::min(2 * sm_count(), (M + 4 * lanes - 1) / (4 * lanes)));
+        const int rpc = (M + ctas - 1) / ctas;
+        const int grid = (M + rpc - 1) / rpc;
+        char *scratch = nullptr;
+        const size_t pbytes = (size_t)grid * N * sizeof(float);
+        DC_CUDA_TRY(cudaMallocAsync(&scratch, pbytes + 256, st));
+        unsigned *done = reinterpret_cast<unsigned *>(scratch + round_up((int64_t)pbytes, 256));
+        cudaError_t e = cudaMemsetAsync(done, 0, sizeof(unsigned), st);
+        if (e == cudaSuccess) {
+            KernelTimer kt("bias_bwd", st);
+            e = launch_pdl(bias_bwd_rows, dim3(grid), dim3(kSumThreads), 0, st, 1,
+                           reinterpret_cast<const float4 *>(dy), reinterpret_cast<float4 *>(da), db,
+                           reinterpret_cast<float4 *>(scratch), done, M, N4, rpc, accumulate);
+        }
+        cudaFreeAsync(scratch, st);
+        if (e != cudaSuccess) return fail(DC_ERR_CUDA, "bias bwd: %s", cudaGetErrorString(e));
+        return DC_OK;
+    }
     // one-launch cluster form when its CTAs (a cluster per 16 columns) fill
     // at least half the SMs
     const int nb16 = (N + 15) / 16;
     if (vec && 2 * nb16 * kSumCluster >= sm_count() && nb16 <= 65535) {
         KernelTimer kt("bias_bwd", st);
-        DC_CUDA_TRY(launch_pdl(bias_bwd_cluster, dim3(kSumCluster, nb16), dim3(kSumThreads), 0, st,
-                               kSumCluster, reinterpret_cast<const float4 *>(dy),
-                               reinterpret_cast<float4 *>(da), db, M, N / 4, accumulate));
+        {
+            DC_CUDA_TRY(launch_pdl(bias_bwd_cluster<4, kSumCluster>, dim3(kSumCluster, nb16),
+                                   dim3(kSumThreads), 0, st, kSumCluster, reinterpret_cast<const float4 *>(dy),
+                                   reinterpret_cast<float4 *>(da), db, M, N / 4, accumulate));
+        }
         return DC_OK;
     }
     const int cblocks = vec ? (N / 4 + 31) / 32 : (N + 31) / 32;
