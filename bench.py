@@ -1061,6 +1061,14 @@ def main():
         "roofline": roof, "kernels": kern, "gpu_launches": launches * args.steps,
         "clocks": sampler.summary(),
     }
+    rg = ROOT / "profiles" / "reference_gpu_kernels.json"
+    if rg.exists():
+        # the reference's own GPU kernels on this workload (a committed,
+        # separately measured bounded sample: profiles/reference_gpu_kernels.md)
+        ref_gpu = json.loads(rg.read_text()).get(args.config)
+        if ref_gpu:
+            line["reference_gpu_kernels"] = {"value": ref_gpu["tokens_per_s"], "unit": "tokens/s",
+                                             "sample": ref_gpu["sample"], "source": "profiles/reference_gpu_kernels.md"}
     if rank == 0 and world == 1 and not args.no_rows:
         line["row_kernels"] = row_kernels(dev, P)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -562,7 +562,7 @@ namespace aft {
 // needs no second pass of the forward contraction.  One thread per 16
 // columns of one padded row; consecutive threads walk a row.
 template <class IO, class E>
-__global__ void __launch_bounds__(256) bwd_stats_kernel(const Params p)
+__global__ void __launch_bounds__(256, 3) bwd_stats_kernel(const Params p)
 {
     grid_dep_wait();  // launched early (programmatic dependent launch)
     grid_dep_launch();

@@ -1077,8 +1077,10 @@ int dc_bias_bwd(const float *dy, float *da, float *db, int M, int N, int accumul
     const bool vec = N % 4 == 0 && aligned16(dy) && (!da || aligned16(da));
     // tall matrices of at most 1024 columns: the row-contiguous form (whole
     // rows per CTA; its partial sums and the finishing count in a scratch of
-    // the stream-ordered allocator)
-    if (vec && N <= 1024 && (long long)M * N >= (1ll << 22)) {
+    // the stream-ordered allocator).  From 131072 rows on: below, the last
+    // CTA's serial sum of the partials outweighs the streaming gain (the
+    // decoder's [16384, 256..1024] gradients ran 309 -> 516 us a step)
+    if (vec && N <= 1024 && M >= 131072) {
         const int N4 = N / 4, lanes = kSumThreads / N4;
         const int ctas = std::max(1, std::min(2 * sm_count(), (M + 4 * lanes - 1) / (4 * lanes)));
         const int rpc = (M + ctas - 1) / ctas;
