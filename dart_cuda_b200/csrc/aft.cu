@@ -433,17 +433,27 @@ __global__ void __launch_bounds__(256)
     grid_dep_wait();  // launched early (programmatic dependent launch)
     grid_dep_launch();
     __shared__ __align__(16) float cs[128];
+    __shared__ float half_mx[128];
     const int b = blockIdx.z;
     const int dblk = blockIdx.x * 128;
-    if (threadIdx.x < 128) {
-        const int d = dblk + threadIdx.x;
-        float mx = 0.f;
+    {
+        // the column maxima of this block's 128 columns from the nsplit
+        // partials: two threads a column, each over half of the partials
+        // (independent loads, unrolled), then combined in shared memory
+        const int col = threadIdx.x & 127, h = threadIdx.x >> 7;
+        const int d = dblk + col;
+        float mx = -INFINITY;
         if (d < D) {
-            mx = -INFINITY;
-            for (int s = 0; s < nsplit; ++s) mx = fmaxf(mx, cpart[((size_t)s * B + b) * dp + d]);
+#pragma unroll 4
+            for (int s = h; s < nsplit; s += 2) mx = fmaxf(mx, __ldg(cpart + ((size_t)s * B + b) * dp + d));
         }
-        cs[threadIdx.x] = mx;
-        if (blockIdx.y == 0 && d < dp) c[(size_t)b * dp + d] = mx;
+        if (h) half_mx[col] = mx;
+        __syncthreads();
+        if (!h) {
+            mx = d < D ? fmaxf(mx, half_mx[col]) : 0.f;
+            cs[col] = mx;
+            if (blockIdx.y == 0 && d < dp) c[(size_t)b * dp + d] = mx;
+        }
     }
     __syncthreads();
     const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
@@ -684,7 +694,10 @@ static Layout make_layout(int B, int Tq, int Tk, int D, int dtype, int flags)
     L.dp = D <= 64 && !use_pairs(L) ? 64 : (int)round_up(std::max(D, 1), D_ALIGN);
     const int dblocks = (D + 255) / 256;
     int want = (8 * 148 + dblocks * B - 1) / std::max(1, dblocks * B);
-    L.nsplit = std::max(1, std::min(want, (Tk + 31) / 32));
+    // (at most 32 row slices: prep_p combines the slices' partial maxima of
+    // every column before its panel rows, so more of them only lengthen
+    // that serial part; small batches asked for up to 128)
+    L.nsplit = std::max(1, std::min(std::min(want, 32), (Tk + 31) / 32));
     L.rows_per_split = (Tk + L.nsplit - 1) / L.nsplit;
     L.nsplit = std::max(1, (Tk + L.rows_per_split - 1) / L.rows_per_split);
     size_t off = 0;
