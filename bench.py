@@ -996,6 +996,7 @@ def main():
     # per kernel: the user-tensor bytes each kernel must move (intermediate
     # panels are not credited) and the FLOPs of its contraction
     user_bytes = {
+        "aft_prep": wbytes + 2 * io,          # w, K, V (one-launch prep)
         "aft_prep_w_colmax": wbytes + io,     # w, K
         "aft_prep_p": 2 * io,                 # K, V
         "aft_tc_fwd": 2 * io,                 # Q in, Z out

@@ -54,6 +54,7 @@ SIGNATURES = {
     "dc_version": (ctypes.c_char_p, []),
     "dc_device_status": (c_int, [_VP, POINTER(c_int)]),
     "dc_aft_dw_packed_size": (c_int, [c_int, c_int, POINTER(c_size_t)]),
+    "dc_aft_prep_mode": (c_int, [c_int]),
     "dc_aft_dw_unpack": (c_int, [_VP, _VP, c_int, c_int, c_int, _VP]),
     "dc_profile_enable": (c_int, [c_int]),
     "dc_profile_read": (c_int, [ctypes.c_char_p, _FP, POINTER(c_int), c_int]),

@@ -129,6 +129,10 @@ struct Params {
 static int g_test_withhold = 0;
 #endif
 
+// Test hook: the two-launch prep (prep_wc_kernel + prep_p_kernel) instead of
+// the one-launch clustered prep, to cross-check the two (dc_aft_prep_mode).
+static int g_prep_two_launch = 0;
+
 // Per-tile timeline of the tensor-core launches whose mode bit is set in
 // g_trace_modes (bit MODE); see trace_at() in aft_tc.cuh.
 static unsigned long long *g_trace_buf = nullptr;
@@ -493,6 +497,125 @@ __global__ void __launch_bounds__(256)
     }
 }
 
+// One-launch prep: clusters of kPrepCluster CTAs along x.  The first `wcl`
+// clusters build A' rows and m (8 rows a CTA, a warp a row).  Every other
+// cluster owns one (sequence b, 128-column block) of the panels: CTA `rank`
+// reads its rows [rank * rpb, ...) of K for their partial column maxima, the
+// cluster combines the kPrepCluster partials over distributed shared memory
+// (rank 0 also stores c for the backward's epilogue), and each CTA then reads
+// its rows of K again — the same 1 MB column block moments later, an L2 hit —
+// with V to write its rows of E'V and E'.  K comes from DRAM once and the
+// partial maxima never leave the cluster: prep_wc_kernel's column pass and a
+// launch boundary are gone.
+constexpr int kPrepCluster = 8;
+
+template <class IO, class E>
+__global__ void __launch_bounds__(256)
+    prep_fused_kernel(const float *__restrict__ w, int ldw, int Tq, int Tqp, int Tk, int Tkp, int causal,
+                      float *__restrict__ m, E *__restrict__ Ap, const IO *__restrict__ K,
+                      const IO *__restrict__ V, int D, int ldk, int dp, int ndb, int rpb, int vec,
+                      int wcl, float *__restrict__ c, E *__restrict__ PV, E *__restrict__ PE)
+{
+    grid_dep_wait();  // launched early (programmatic dependent launch)
+    grid_dep_launch();
+    const int cl = blockIdx.x / kPrepCluster;
+    if (cl < wcl) {  // A' rows: every CTA of these clusters, no cluster barrier
+        const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+        if (t < Tqp) prep_w_row<E>(t, threadIdx.x & 31, w, ldw, Tq, Tk, Tkp, causal, m, Ap);
+        return;
+    }
+    __shared__ float red[16][129];
+    __shared__ float cpart_s[128];
+    __shared__ float cs[128];
+    const int g = cl - wcl, b = g / ndb, dblk = (g % ndb) * 128;
+    const uint32_t rank = cluster_rank();
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    const int d0 = dblk + tx * 8;
+    const int r0 = (int)rank * rpb, r1 = min(Tkp, r0 + rpb), rk1 = min(r1, Tk);
+    const IO *Kb = K + (size_t)b * Tk * ldk;
+    const IO *Vb = V + (size_t)b * Tk * ldk;
+    // pass 1: partial column maxima of this CTA's rows
+    float mx[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) mx[k] = -INFINITY;
+    if (vec && d0 + 8 <= D) {
+        int i = r0 + ty;
+        for (; i + 16 < rk1; i += 32) {
+            float a[8], a2[8];
+            ld8(Kb + (size_t)i * ldk + d0, a);
+            ld8(Kb + (size_t)(i + 16) * ldk + d0, a2);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) mx[k] = fmaxf(mx[k], fmaxf(a[k], a2[k]));
+        }
+        for (; i < rk1; i += 16) {
+            float a[8];
+            ld8(Kb + (size_t)i * ldk + d0, a);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) mx[k] = fmaxf(mx[k], a[k]);
+        }
+    } else if (d0 < D) {
+        for (int i = r0 + ty; i < rk1; i += 16)
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+                if (d0 + k < D) mx[k] = fmaxf(mx[k], ld_io(Kb, (size_t)i * ldk + d0 + k));
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) red[ty][tx * 8 + k] = mx[k];
+    __syncthreads();
+    if (threadIdx.x < 128) {
+        float v = red[0][threadIdx.x];
+#pragma unroll
+        for (int r = 1; r < 16; ++r) v = fmaxf(v, red[r][threadIdx.x]);
+        cpart_s[threadIdx.x] = v;
+    }
+    // the cluster's partials, combined over distributed shared memory in rank order
+    cluster_sync_all();
+    if (threadIdx.x < 128) {
+        const int d = dblk + threadIdx.x;
+        const uint32_t mine = (uint32_t)__cvta_generic_to_shared(&cpart_s[threadIdx.x]);
+        float v = -INFINITY;
+#pragma unroll
+        for (int r = 0; r < kPrepCluster; ++r) v = fmaxf(v, ld_dsmem_f32(smem_in_cta(mine, r)));
+        v = d < D ? v : 0.f;
+        cs[threadIdx.x] = v;
+        if (rank == 0 && d < dp) c[(size_t)b * dp + d] = v;
+    }
+    cluster_sync_all();  // every CTA has read the partials; cs is visible in the CTA
+    // pass 2: E'V and E' of this CTA's rows (K again, from L2)
+    if (d0 >= dp) return;  // narrow panels: 64 columns
+    float cc[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) cc[k] = cs[tx * 8 + k];
+    for (int i = r0 + ty; i < r1; i += 16) {
+        float pv[8], pe[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) pv[k] = pe[k] = 0.f;
+        if (i < Tk) {
+            const size_t src = (size_t)i * ldk + d0;
+            if (vec && d0 + 8 <= D) {
+                float k8[8], v8[8];
+                ld8(Kb + src, k8);
+                ld8(Vb + src, v8);
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    pe[k] = __expf(k8[k] - cc[k]);
+                    pv[k] = pe[k] * v8[k];
+                }
+            } else {
+#pragma unroll
+                for (int k = 0; k < 8; ++k)
+                    if (d0 + k < D) {
+                        pe[k] = __expf(ld_io(Kb, src + k) - cc[k]);
+                        pv[k] = pe[k] * ld_io(Vb, src + k);
+                    }
+            }
+        }
+        const size_t dst = ((size_t)b * Tkp + i) * dp + d0;
+        st8op(PV + dst, pv);
+        st8op(PE + dst, pe);
+    }
+}
+
 // ------------------------------------------------------------ CUDA-core path
 // Same contractions on CUDA cores in fp32 (cross-check of the tensor-core
 // path and of the prep kernels; not the product's fast path).
@@ -790,6 +913,25 @@ static int run_prep(const Layout &L, const IO *K, const IO *V, const float *w, i
     // 16-byte access to K and V rows: D a multiple of 8 and aligned bases
     const int vec = (L.D % 8 == 0) && (L.ldi % 8 == 0) &&
                     ((reinterpret_cast<uintptr_t>(K) | reinterpret_cast<uintptr_t>(V)) & 15) == 0;
+    // one launch for panels of up to 16 M elements (measured: C2 31.6 -> 28.3
+    // us, the decoder's heads 306 -> 204 us of prep a step); larger ones keep
+    // the two launches, whose column pass streams K at the full rate (C4:
+    // 82 us against 92 us in one launch, whose second read of K and the A'
+    // rows' stream then compete for L2)
+    if (!g_prep_two_launch && (long long)L.B * L.Tkp * L.dp <= (16ll << 20)) {
+        // one launch: A' clusters first, then a cluster per (b, 128 columns)
+        KernelTimer kt("aft_prep", st);
+        const int ndb = (L.dp + 127) / 128;
+        const int rpb = (L.Tkp + kPrepCluster - 1) / kPrepCluster;
+        const int wcl = (L.Tqp + 8 * kPrepCluster - 1) / (8 * kPrepCluster);
+        const long long clusters = (long long)wcl + (long long)L.B * ndb;
+        if (clusters * kPrepCluster > 0x7fffffffLL) return fail(DC_ERR_INVALID, "prep grid too large");
+        DC_CUDA_TRY(launch_pdl(prep_fused_kernel<IO, E>, dim3((unsigned)(clusters * kPrepCluster)), dim3(256), 0,
+                               st, kPrepCluster, w, ldw, L.Tq, L.Tqp, L.Tk, L.Tkp, causal, m, Ap, K, V, L.D,
+                               L.ldi, L.dp, ndb, rpb, vec, wcl, c, PV, PE));
+        DC_CUDA_TRY(cudaGetLastError());
+        return DC_OK;
+    }
     {
         // A' rows and the partial column maxima of K in one launch
         KernelTimer kt("aft_prep_w_colmax", st);
@@ -1182,6 +1324,12 @@ int dc_aft_trace(void *device_buffer, size_t bytes, int mode_mask)
         return fail(DC_ERR_NOMEM, "trace buffer needs %zu bytes", need);
     g_trace_buf = static_cast<unsigned long long *>(device_buffer);
     g_trace_modes = device_buffer ? mode_mask : 0;
+    return DC_OK;
+}
+
+int dc_aft_prep_mode(int two_launch)
+{
+    g_prep_two_launch = two_launch ? 1 : 0;
     return DC_OK;
 }
 

@@ -130,6 +130,14 @@ int dc_aft_trace(void *device_buffer, size_t bytes, int mode_mask);
  */
 int dc_aft_workspace_size(int B, int Tq, int Tk, int D, int dtype, int flags, size_t *bytes);
 
+/* Operand-panel preparation of the following AFT calls in this process:
+ * 0 (default) one launch, the column maxima of K combined inside CTA
+ * clusters, for panels of up to 16 M elements (B * T * D), two launches
+ * above; 1 always the two-launch form (row/column maxima, then the panels).
+ * Both give the same panels bit for bit; the switch lets a caller or test
+ * compare them.  No counterpart in the reference. */
+int dc_aft_prep_mode(int two_launch);
+
 /* Size in floats of a block-packed causal dW (DC_AFT_DW_PACKED), and its
  * expansion into dW [Tq][ldw] (zeros above each row's causal extent), on
  * `stream`.  No counterpart in the reference. */

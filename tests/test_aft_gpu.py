@@ -567,3 +567,35 @@ def test_packed_dw_split_backward_and_rejects_noncausal(ops, dev):
     with pytest.raises(DcError):
         ops.aft_bwd(tq, tk, tv, tw, tg, causal=False, dw_packed=True)
     assert ops.device_status() == 0
+
+
+# ----------------------------------------------------------- one-launch prep
+@pytest.mark.parametrize("dtype,B,Tq,Tk,D,causal", [(torch.bfloat16, 4, 512, 512, 256, True),
+                                                    (torch.float32, 2, 300, 300, 40, True),
+                                                    (torch.bfloat16, 8, 256, 256, 64, True),
+                                                    (torch.bfloat16, 1, 1100, 1100, 136, True),
+                                                    (torch.float32, 2, 130, 70, 40, False)])
+def test_prep_one_launch_matches_two_launch(ops, dev, dtype, B, Tq, Tk, D, causal):
+    """The one-launch prep (column maxima of K combined inside CTA clusters)
+    and the two-launch prep build the same panels: every output bit for bit
+    (dW up to the order of its split-K additions)."""
+    from dart_cuda_b200 import lib
+
+    Q, K, V, W, dZ = make_inputs(70, B, Tq, Tk, D, 0.3)
+    tq, tk, tv, tg = to_dev(dev, dtype, Q, K, V, dZ)
+    tw = torch.from_numpy(W).to(dev)
+
+    def run(two):
+        lib().dc_aft_prep_mode(two)
+        try:
+            Z = ops.aft_fwd(tq, tk, tv, tw, causal=causal)
+            g = ops.aft_bwd(tq, tk, tv, tw, tg, causal=causal)
+        finally:
+            lib().dc_aft_prep_mode(0)
+        return (Z,) + tuple(g)
+
+    a, b = run(1), run(0)
+    for x, y in zip(a[:4], b[:4]):
+        assert torch.equal(x, y)
+    torch.testing.assert_close(b[4], a[4], rtol=1e-5, atol=1e-6)
+    assert ops.device_status() == 0
