@@ -602,6 +602,20 @@ def bench_decode(args, dev, rank, world, dist):
         roof = {"bound": "hbm", "achieved": k["GB/s"], "peak": P["hbm_gbs"], "unit": "GB/s",
                 "frac": k["hbm_frac"], "traffic": traffic, "kernel": "aft_decode", "peak_source": P["source"],
                 "algorithmic_bytes": algo}
+        # the whole decode step: every weight the step's GEMMs read once (fp32;
+        # the cross key/value weights are not read, the encoder row being
+        # constant) plus the decode kernel's history and activations, per
+        # generated token, against the step's measured time
+        Fd = cfg.ffn_mult * d
+        w_layer = (d * 3 * d + 3 * d) + (d * d + d) * 3 + (d * Fd + Fd) + (Fd * d + d) + 6 * d + d
+        w_bytes = 4 * (L * w_layer + d * cfg.vocab + cfg.vocab + 2 * d)
+        step_bytes = w_bytes + dec_bytes / (new - 1)
+        step_ms = dec_ms / (new - 1)
+        roof["step"] = {"bytes_per_token_step": step_bytes, "weights_bytes": w_bytes,
+                        "history_bytes_mean": dec_bytes / (new - 1), "ms_per_token_step": step_ms,
+                        "GB/s": step_bytes / (step_ms / 1e3) / 1e9,
+                        "frac": step_bytes / (step_ms / 1e3) / 1e9 / P["hbm_gbs"],
+                        "launches_per_token_step": sum(cnt for _, cnt in prof.values()) / max(new - 1, 1)}
     toks = m._dec["tokens"]
     h_prompt = prompt.cpu().pin_memory()
     h_toks = torch.empty(B, T0 + new, dtype=torch.int32).pin_memory()
