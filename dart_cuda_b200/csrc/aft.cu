@@ -723,11 +723,20 @@ __global__ void __launch_bounds__(256, 3) bwd_stats_kernel(const Params p)
 #pragma unroll
         for (int j = 0; j < 16; ++j) r[j] = inv[j] = 0.f;
     }
-    EpiPre none;
-    none.ok = false;
-    epi16_grads<IO, E>(p, b, t, d0, r, inv, none);
-    // the forward's range guard, on 1/den' and r (after the gradient pass has
-    // issued its loads, so that it does not hold them up)
+    // Q and dZ requested beside r and 1/den' (bf16 tensors, whole 16-column
+    // runs), so all four loads are in flight before the range guard below
+    // waits on the statistics
+    EpiPre pf;
+    pf.ok = false;
+    if constexpr (sizeof(IO) == 2) {
+        if (t < p.Tq && p.vec_io && d0 + 16 <= p.D) {
+            const size_t row = (size_t)b * p.Tq + t;
+            ld32B_nc((const IO *)p.Q + row * p.ldi + d0, pf.a);
+            ld32B_nc((const IO *)p.dZ + row * p.ldo + d0, pf.b);
+            pf.ok = true;
+        }
+    }
+    // the forward's range guard, on 1/den' and r
     if (t < p.Tq) {
         bool bad = false;
 #pragma unroll
@@ -735,6 +744,7 @@ __global__ void __launch_bounds__(256, 3) bwd_stats_kernel(const Params p)
             bad |= d0 + j < p.D && (!(inv[j] <= 0x1p100f) || !(fabsf(r[j]) <= 3.0e38f));
         if (bad) report_range(p);
     }
+    epi16_grads<IO, E>(p, b, t, d0, r, inv, pf);
 }
 
 // Block-packed dW to the caller's [Tq][ldw] layout, zeros past each row's
