@@ -693,8 +693,8 @@ def main():
     ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of a CUDA graph")
     ap.add_argument("--backward", default="auto", choices=["auto", "stats", "recompute"],
                     help="stats: the forward keeps r, 1/den for the backward; recompute: the backward "
-                         "repeats the forward contraction; auto: stats from T >= 1024, where the "
-                         "contraction costs more than the 16 bytes per element of saved statistics")
+                         "repeats the forward contraction; auto: stats from T >= 256, where the "
+                         "contraction costs more than the saved statistics' bytes")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-overlap", action="store_true",
                     help="N>1: all-reduce dW after the whole backward instead of beside dK/dV")
@@ -721,7 +721,7 @@ def main():
     if args.batch:
         B = args.batch
         desc = desc.replace(f"B={CONFIGS[args.config][0]}", f"B={B}")
-    stats = args.backward == "stats" or (args.backward == "auto" and T >= 1024)
+    stats = args.backward == "stats" or (args.backward == "auto" and T >= 256)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))

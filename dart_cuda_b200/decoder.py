@@ -76,6 +76,10 @@ class DecoderConfig:
 
 
 class AftDecoder:
+    # sequence length from which the AFT forward keeps r and 1/den' for the
+    # backward instead of the backward repeating the forward contraction
+    STATS_FROM_T = 256
+
     def __init__(self, cfg: DecoderConfig, device="cuda", seed=0, std=0.02):
         if cfg.d_model % cfg.n_heads:
             raise ValueError("d_model must be a multiple of n_heads")
@@ -226,8 +230,8 @@ class AftDecoder:
         b["scale"] = torch.ones(1, device=dev)
         b["loss"] = torch.zeros(1, device=dev)
         # one AFT workspace per (layer, head): the forward's panels are reused
-        # by the backward; r and 1/den are kept from T >= 1024 on
-        self._aft_flags = DC_AFT_CAUSAL | (DC_AFT_SAVE_STATS if T >= 1024 else 0)
+        # by the backward; r and 1/den are kept from T >= STATS_FROM_T on
+        self._aft_flags = DC_AFT_CAUSAL | (DC_AFT_SAVE_STATS if T >= self.STATS_FROM_T else 0)
         n = ctypes.c_size_t(0)
         check(lib().dc_aft_workspace_size(B, T, T, c.head, DC_F32, self._aft_flags, ctypes.byref(n)),
               "dc_aft_workspace_size")
