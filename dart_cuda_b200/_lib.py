@@ -74,6 +74,8 @@ SIGNATURES = {
                              c_float, _VP]),
     "dc_gemm": (c_int, [_VP, c_int, _VP, c_int, _VP, c_int, c_int, c_int, c_int, c_int, c_int, c_float,
                         _VP, _VP, c_int, _VP, c_int, _VP]),
+    "dc_gemm_gate": (c_int, [_VP, c_int, _VP, c_int, _VP, c_int, c_int, c_int, c_int, c_int, c_int,
+                             c_float, _VP, _VP, c_int, _VP, _VP]),
     "dc_aft_fwd_strided": (c_int, [_VP, _VP, _VP, _VP, c_int, _VP, c_int, c_int, c_int, c_int, c_int,
                                    c_int, c_int, c_int, _VP, c_size_t, _VP]),
     "dc_aft_bwd_strided": (c_int, [_VP, _VP, _VP, _VP, c_int, _VP, _VP, _VP, _VP, _VP, c_int, c_int,

@@ -296,6 +296,17 @@ __device__ __forceinline__ float ld_dsmem_f32(uint32_t addr)
     return v;
 }
 
+// 16-byte load from the shared memory of a CTA of the cluster (16-byte aligned).
+__device__ __forceinline__ float4 ld_dsmem_f32x4(uint32_t addr)
+{
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(addr)
+                 : "memory");
+    return v;
+}
+
 __device__ __forceinline__ void cluster_sync_all()
 {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\t"

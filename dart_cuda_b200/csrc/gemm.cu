@@ -12,10 +12,12 @@
 // (native/src/engine.cu:480-507 matmul, :352-372 row-broadcast bias,
 // native/src/kernels/elementwise.cuh:328-351 tanh GELU and its derivative,
 // residual adds): bias, GELU (keeping the pre-activation for the backward),
-// the GELU derivative, and a residual / accumulate input.
+// the GELU derivative, and a residual / accumulate input; and the decoder's
+// cross-attention gate, sigmoid(value) * v0 (dc_gate_fwd).
 //
 // One persistent CTA per SM walks 128 x BN output tiles (split along K when
-// the tiles alone cannot fill the SMs and the epilogue is linear): warp 16
+// the tiles alone cannot fill the SMs: with atomics into C for a linear
+// epilogue, else over a cluster of CTAs a tile, see below): warp 16
 // issues TMA loads into a ring of stages (six of 32 KB with BN = 128, four of
 // 48 KB with BN = 256), warp 17 owns TMEM and issues the MMAs into a
 // double-buffered accumulator, warps 0-15 drain it.  BN = 256 (one N = 256
@@ -42,6 +44,7 @@ enum : int {
     EPI_GELU_BWD = 4,  // C = value * gelu'(aux)
     EPI_RESID = 8,     // + R[m, n] before the activation (R may alias C)
     EPI_ATOMIC = 16,   // split-K: C += value with atomics (C pre-initialised)
+    EPI_GATE = 32,     // C = sigmoid(value) * gate[n] (after bias and residual)
 };
 
 template <class E, bool A_MN, bool B_MN, int TBN_ = BN>
@@ -64,6 +67,9 @@ struct Cfg {
     static constexpr uint32_t TMEM_COLS = 2 * TBN;
     static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 512;
     static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+    // cluster split-K: a CTA's partial tile, rows padded by 16 bytes, in the stages
+    static constexpr int RED_LD = TBN + 4;
+    static_assert(BM * RED_LD * 4 <= STAGES * STAGE_BYTES, "partial tile fits the stages");
 };
 
 struct Params {
@@ -78,6 +84,11 @@ struct Params {
     int tiles_m, tiles_n, splits, ksteps, n_tiles;
     int vec;
     int *status;
+    const float *gate;  // EPI_GATE: [N]
+    // cluster split-K: the `cl` splits of one tile are consecutive CTAs of
+    // one cluster and add their partial tiles over distributed shared
+    // memory before the epilogue (0: off)
+    int cl;
 };
 
 // tanh-approximated GELU and its derivative, the forms of the reference's
@@ -92,6 +103,9 @@ __device__ __forceinline__ float gelu_d(float x)
     const float t = tanhf(0.7978845608f * (x + 0.044715f * x2 * x));
     return 0.5f * (1.0f + t) + 0.5f * x * (1.0f - t * t) * 0.7978845608f * (1.0f + 3.0f * 0.044715f * x2);
 }
+
+// the sigmoid of the cross-attention gate (dc_gate_fwd's form)
+__device__ __forceinline__ float sigm_f(float x) { return 1.0f / (1.0f + __expf(-x)); }
 
 __device__ __forceinline__ void ld16f(const float *p, float (&v)[16])
 {
@@ -117,7 +131,10 @@ __device__ __forceinline__ void st16f(float *p, const float (&v)[16])
                      : "memory");
 }
 
-// 16 consecutive accumulator columns of one row.
+// 16 consecutive accumulator columns of one row.  EXT: the kernel form
+// that also has the gate (a separate instantiation: the plain GEMMs carry
+// none of its code, which measured slower even where it never ran).
+template <bool EXT>
 __device__ __forceinline__ void epilogue16(const Params &p, int r, int c0, int split,
                                            float (&v)[16])
 {
@@ -154,6 +171,10 @@ __device__ __forceinline__ void epilogue16(const Params &p, int r, int c0, int s
             ld16f(p.aux + (size_t)r * p.ldx + c0, t);
 #pragma unroll
             for (int j = 0; j < 16; ++j) v[j] *= gelu_d(t[j]);
+        } else if (EXT && (epi & EPI_GATE)) {
+            ld16f(p.gate + c0, t);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = sigm_f(v[j]) * t[j];
         }
         st16f(c, v);
         return;
@@ -175,8 +196,61 @@ __device__ __forceinline__ void epilogue16(const Params &p, int r, int c0, int s
             x = gelu_f(x);
         } else if (epi & EPI_GELU_BWD) {
             x *= gelu_d(p.aux[(size_t)r * p.ldx + c]);
+        } else if (EXT && (epi & EPI_GATE)) {
+            x = sigm_f(x) * p.gate[c];
         }
         *dst = x;
+    }
+}
+
+// Four consecutive columns of one row of a tile reduced over its cluster:
+// the whole epilogue (the bias once, no atomics).
+__device__ __forceinline__ void epilogue4(const Params &p, int r, int c0, float4 acc)
+{
+    if (r >= p.M || c0 >= p.N) return;
+    const int epi = p.epi;
+    float v[4] = {acc.x * p.alpha, acc.y * p.alpha, acc.z * p.alpha, acc.w * p.alpha};
+    if (p.vec && c0 + 4 <= p.N) {
+        if (epi & EPI_BIAS) {
+            const float4 b = *reinterpret_cast<const float4 *>(p.bias + c0);
+            v[0] += b.x; v[1] += b.y; v[2] += b.z; v[3] += b.w;
+        }
+        if (epi & EPI_RESID) {
+            const float4 t = *reinterpret_cast<const float4 *>(p.R + (size_t)r * p.ldr + c0);
+            v[0] += t.x; v[1] += t.y; v[2] += t.z; v[3] += t.w;
+        }
+        if (epi & EPI_GELU) {
+            if (p.aux)
+                *reinterpret_cast<float4 *>(p.aux + (size_t)r * p.ldx + c0) = make_float4(v[0], v[1], v[2], v[3]);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) v[j] = gelu_f(v[j]);
+        } else if (epi & EPI_GELU_BWD) {
+            const float4 t = *reinterpret_cast<const float4 *>(p.aux + (size_t)r * p.ldx + c0);
+            v[0] *= gelu_d(t.x); v[1] *= gelu_d(t.y); v[2] *= gelu_d(t.z); v[3] *= gelu_d(t.w);
+        } else if (epi & EPI_GATE) {
+            const float4 t = *reinterpret_cast<const float4 *>(p.gate + c0);
+            v[0] = sigm_f(v[0]) * t.x; v[1] = sigm_f(v[1]) * t.y;
+            v[2] = sigm_f(v[2]) * t.z; v[3] = sigm_f(v[3]) * t.w;
+        }
+        *reinterpret_cast<float4 *>(p.C + (size_t)r * p.ldc + c0) = make_float4(v[0], v[1], v[2], v[3]);
+        return;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int c = c0 + j;
+        if (c >= p.N) break;
+        float x = v[j];
+        if (epi & EPI_BIAS) x += p.bias[c];
+        if (epi & EPI_RESID) x += p.R[(size_t)r * p.ldr + c];
+        if (epi & EPI_GELU) {
+            if (p.aux) p.aux[(size_t)r * p.ldx + c] = x;
+            x = gelu_f(x);
+        } else if (epi & EPI_GELU_BWD) {
+            x *= gelu_d(p.aux[(size_t)r * p.ldx + c]);
+        } else if (epi & EPI_GATE) {
+            x = sigm_f(x) * p.gate[c];
+        }
+        p.C[(size_t)r * p.ldc + c] = x;
     }
 }
 
@@ -208,6 +282,7 @@ __device__ __forceinline__ float4 ld_shared4(uint32_t a)
 // lanes per row: every instruction then covers 8 rows x 64 contiguous bytes.
 // The streamed inputs (residual, GELU pre-activation) of all 4 passes are
 // loaded before the first store (R may alias C: same elements, read first).
+template <bool EXT>
 __device__ __forceinline__ void epilogue16_staged(const Params &p, int row0, int c0, int split,
                                                   const float (&v)[16], uint32_t sbase, int lane)
 {
@@ -221,6 +296,8 @@ __device__ __forceinline__ void epilogue16_staged(const Params &p, int row0, int
     const int gc = c0 + 4 * c;
     float4 bb = make_float4(0.f, 0.f, 0.f, 0.f);
     if ((epi & EPI_BIAS) && split == 0) bb = *reinterpret_cast<const float4 *>(p.bias + gc);
+    float4 gt = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (EXT && (epi & EPI_GATE)) gt = *reinterpret_cast<const float4 *>(p.gate + gc);
     float4 in[4];
     if (epi & (EPI_RESID | EPI_GELU_BWD)) {
         const float *src = (epi & EPI_RESID) ? p.R : p.aux;
@@ -257,19 +334,25 @@ __device__ __forceinline__ void epilogue16_staged(const Params &p, int row0, int
             x.y *= gelu_d(in[it].y);
             x.z *= gelu_d(in[it].z);
             x.w *= gelu_d(in[it].w);
+        } else if (EXT && (epi & EPI_GATE)) {
+            x = make_float4(sigm_f(x.x) * gt.x, sigm_f(x.y) * gt.y, sigm_f(x.z) * gt.z,
+                            sigm_f(x.w) * gt.w);
         }
         *reinterpret_cast<float4 *>(p.C + grow * p.ldc + gc) = x;
     }
     __syncwarp();  // the staging block is rewritten by the next pass
 }
 
-template <int TBN>
+template <int TBN, bool EXT>
 __device__ __forceinline__ Tile decode_tile(const Params &p, int idx)
 {
     Tile t;
     const int per = p.tiles_m * p.tiles_n;
-    t.split = idx / per;
-    const int rem = idx % per;
+    // split-major, except under cluster split-K, where a tile's splits are
+    // consecutive CTAs (one cluster)
+    const bool cl = EXT && p.cl;
+    t.split = cl ? idx % p.splits : idx / per;
+    const int rem = cl ? idx / p.splits : idx % per;
     t.m0 = (rem / p.tiles_n) * BM;
     t.n0 = (rem % p.tiles_n) * TBN;
     t.k0 = (int)(((long long)t.split * p.ksteps) / p.splits);
@@ -283,7 +366,7 @@ __device__ __forceinline__ int sched_tile(int j, int ntiles)
     return t < ntiles ? t : -1;
 }
 
-template <class E, bool A_MN, bool B_MN, int TBN>
+template <class E, bool A_MN, bool B_MN, int TBN, bool EXT>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtensorMap mapA,
                    const __grid_constant__ CUtensorMap mapB)
@@ -346,7 +429,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int jt = 0; !stop; ++jt) {
                 const int tile = sched_tile(jt, ntiles);
                 if (tile < 0) break;
-                const Tile tl = decode_tile<TBN>(p, tile);
+                const Tile tl = decode_tile<TBN, EXT>(p, tile);
                 for (int k = tl.k0; k < tl.k1; ++k, ++g) {
                     const int s = g % C::STAGES;
                     if (!mbar_wait(smem_u32(&empty[s]), ((g / C::STAGES) & 1) ^ 1, abort_flag,
@@ -394,7 +477,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (uint32_t j = 0; !stop; ++j) {
                 const int tile = sched_tile(j, ntiles);
                 if (tile < 0) break;
-                const Tile tl = decode_tile<TBN>(p, tile);
+                const Tile tl = decode_tile<TBN, EXT>(p, tile);
                 const uint32_t buf = j & 1, use = j >> 1;
                 if (!mbar_wait(smem_u32(&acce[buf]), (use & 1) ^ 1, abort_flag, p.status,
                                DC_DEVERR_TIMEOUT_ACC))
@@ -441,7 +524,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (uint32_t j = 0;; ++j) {
             const int tile = sched_tile(j, ntiles);
             if (tile < 0) break;
-            const Tile tl = decode_tile<TBN>(p, tile);
+            const Tile tl = decode_tile<TBN, EXT>(p, tile);
             const uint32_t buf = j & 1, use = j >> 1;
             const bool ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&accf[buf]), use & 1,
                                                               abort_flag, p.status,
@@ -451,6 +534,26 @@ __global__ void __launch_bounds__(kThreads, 1)
             // a quarter of the tile's columns per warp of a lane quadrant
             constexpr int QC = TBN / 4;
             const uint32_t lane_addr = tmem + buf * TBN + ((uint32_t)(quad * 32) << 16) + slice * QC;
+            if constexpr (EXT) {
+                if (p.cl) {
+                    // cluster split-K (one tile a CTA): the partial tile goes
+                    // to this CTA's stages, free now that its MMAs are
+                    // complete, and the cluster adds the partials below
+                    if (quad * 32 < p.M - tl.m0) {
+#pragma unroll 1
+                        for (int sb = 0; sb < QC / 16; ++sb) {
+                            float v[16];
+                            tmem_ld16(lane_addr + sb * 16, v);
+                            const uint32_t dst = stg + (uint32_t)(row * C::RED_LD + slice * QC + sb * 16) * 4u;
+#pragma unroll
+                            for (int k = 0; k < 4; ++k)
+                                st_shared4(dst + 16 * k, v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+                        }
+                    }
+                    tc_fence_before();
+                    break;
+                }
+            }
             // a CTA's last tile (under split-K its only one) goes through the
             // staged form where the warp's 32 rows and the tile's columns are
             // in bounds on the 16-byte path: its shared memory is then free (a
@@ -466,14 +569,47 @@ __global__ void __launch_bounds__(kThreads, 1)
                 float v[16];
                 tmem_ld16(lane_addr + sb * 16, v);
                 if (staged)
-                    epilogue16_staged(p, tl.m0 + quad * 32, tl.n0 + slice * QC + sb * 16, tl.split, v,
-                                      stg + warp * 2048, lane);
+                    epilogue16_staged<EXT>(p, tl.m0 + quad * 32, tl.n0 + slice * QC + sb * 16, tl.split, v,
+                                           stg + warp * 2048, lane);
                 else
-                    epilogue16(p, tl.m0 + row, tl.n0 + slice * QC + sb * 16, tl.split, v);
+                    epilogue16<EXT>(p, tl.m0 + row, tl.n0 + slice * QC + sb * 16, tl.split, v);
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(&acce[buf]));
+        }
+    }
+    if constexpr (EXT) {
+        if (p.cl) {
+            // every role of every CTA of the cluster passes both barriers
+            __syncwarp();
+            cluster_sync_all();  // the cluster's partial tiles are in shared memory
+            if (warp < kEpiWarps && !*abort_flag) {
+                // CTA `rank` finishes a 1/cl share of the tile's 16-byte
+                // cells: the partials added in rank order (the same bits on
+                // every run), then the whole epilogue
+                const Tile tl = decode_tile<TBN, EXT>(p, blockIdx.x);
+                constexpr int C4 = TBN / 4;
+                const int total = min(BM, p.M - tl.m0) * C4;
+                const int rank = (int)cluster_rank();
+                const int beg = (int)((long long)total * rank / p.cl);
+                const int end = (int)((long long)total * (rank + 1) / p.cl);
+                for (int i = beg + (int)threadIdx.x; i < end; i += kEpiWarps * 32) {
+                    const int r = i / C4, c4 = i % C4;
+                    const uint32_t a = stg + (uint32_t)(r * C::RED_LD + 4 * c4) * 4u;
+                    float4 acc = ld_dsmem_f32x4(smem_in_cta(a, 0));
+                    for (int q = 1; q < p.cl; ++q) {
+                        const float4 v = ld_dsmem_f32x4(smem_in_cta(a, (uint32_t)q));
+                        acc.x += v.x;
+                        acc.y += v.y;
+                        acc.z += v.z;
+                        acc.w += v.w;
+                    }
+                    epilogue4(p, tl.m0 + r, tl.n0 + 4 * c4, acc);
+                }
+            }
+            __syncwarp();
+            cluster_sync_all();  // no CTA leaves while another reads its partial
         }
     }
     __syncthreads();
@@ -512,10 +648,11 @@ static int map_operand(CUtensorMap *m, const void *base, int esz, int rows, int 
     return encode_tmap(m, tmap_type(esz), 2, base, dims, strides, box, sw);
 }
 
-template <class E, bool A_MN, bool B_MN, int TBN>
+template <class E, bool A_MN, bool B_MN, int TBN, bool EXT>
 static int launch(Params p, const void *A, int lda, const void *B, int ldb, cudaStream_t st)
 {
     using C = Cfg<E, A_MN, B_MN, TBN>;
+    auto kernel = gemm_tc_kernel<E, A_MN, B_MN, TBN, EXT>;
     // per instantiation and device; host threads may race to set them (the
     // attribute call is idempotent), the flags themselves are atomic
     static std::atomic<bool> attr_set[64];
@@ -523,8 +660,7 @@ static int launch(Params p, const void *A, int lda, const void *B, int ldb, cuda
     DC_CUDA_TRY(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64) return fail(DC_ERR_UNSUPPORTED, "device ordinal %d", dev);
     if (!attr_set[dev].load(std::memory_order_acquire)) {
-        DC_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel<E, A_MN, B_MN, TBN>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+        DC_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          C::SMEM_BYTES));
         attr_set[dev].store(true, std::memory_order_release);
     }
@@ -536,25 +672,65 @@ static int launch(Params p, const void *A, int lda, const void *B, int ldb, cuda
     // B: op(B) is [K,N]; stored [K,N] (MN-major) or [N,K] (K-major)
     DC_TRY(B_MN ? map_operand(&mB, B, esz, p.K, p.N, ldb, true)
                 : map_operand(&mB, B, esz, p.N, p.K, ldb, false));
-    const int grid = std::max(1, std::min(p.n_tiles, sm_count()));
+    if (EXT && p.cl) {
+        // cluster split-K: the largest cluster (at most the one asked for)
+        // of which one per tile can be resident at once (a cluster's CTAs
+        // share a GPC, one CTA fills an SM), so no tile waits for a second wave
+        static std::atomic<int> fits[64][9];
+        const int tiles = p.tiles_m * p.tiles_n;
+        int cl = p.cl;
+        for (; cl > 1; --cl) {
+            int n = fits[dev][cl].load(std::memory_order_acquire);
+            if (n == 0) {
+                cudaLaunchConfig_t cfg = {};
+                cfg.gridDim = dim3(cl * std::max(1, sm_count() / cl));
+                cfg.blockDim = dim3(kThreads);
+                cfg.dynamicSmemBytes = C::SMEM_BYTES;
+                cudaLaunchAttribute at[1];
+                at[0].id = cudaLaunchAttributeClusterDimension;
+                at[0].val.clusterDim.x = cl;
+                at[0].val.clusterDim.y = 1;
+                at[0].val.clusterDim.z = 1;
+                cfg.attrs = at;
+                cfg.numAttrs = 1;
+                DC_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, kernel, &cfg));
+                n = std::max(n, 1);
+                fits[dev][cl].store(n, std::memory_order_release);
+            }
+            if (tiles <= n) break;
+        }
+        p.cl = cl > 1 ? cl : 0;
+        p.splits = cl;
+        p.n_tiles = tiles * cl;
+    }
+    const int grid = p.cl ? p.n_tiles : std::max(1, std::min(p.n_tiles, sm_count()));
     {
         KernelTimer kt("gemm_tc", st);
-        DC_CUDA_TRY(launch_pdl(gemm_tc_kernel<E, A_MN, B_MN, TBN>, dim3(grid), dim3(kThreads),
-                               C::SMEM_BYTES, st, 1, p, mA, mB));
+        DC_CUDA_TRY(launch_pdl(kernel, dim3(grid), dim3(kThreads), C::SMEM_BYTES, st,
+                               p.cl ? p.cl : 1, p, mA, mB));
     }
     DC_CUDA_TRY(cudaGetLastError());
     return DC_OK;
 }
 
-template <class E, int TBN>
+template <class E, int TBN, bool EXT>
 static int dispatch(const Params &p, bool ta, bool tb, const void *A, int lda, const void *B,
                     int ldb, cudaStream_t st)
 {
     // op(B) = B   -> B stored [K,N] -> MN-major;  op(B) = B^T -> K-major
-    if (!ta && !tb) return launch<E, false, true, TBN>(p, A, lda, B, ldb, st);
-    if (!ta && tb) return launch<E, false, false, TBN>(p, A, lda, B, ldb, st);
-    if (ta && !tb) return launch<E, true, true, TBN>(p, A, lda, B, ldb, st);
-    return launch<E, true, false, TBN>(p, A, lda, B, ldb, st);
+    if (!ta && !tb) return launch<E, false, true, TBN, EXT>(p, A, lda, B, ldb, st);
+    if (!ta && tb) return launch<E, false, false, TBN, EXT>(p, A, lda, B, ldb, st);
+    if (ta && !tb) return launch<E, true, true, TBN, EXT>(p, A, lda, B, ldb, st);
+    return launch<E, true, false, TBN, EXT>(p, A, lda, B, ldb, st);
+}
+
+template <class E, int TBN>
+static int dispatch_ext(const Params &p, bool ta, bool tb, const void *A, int lda, const void *B,
+                        int ldb, cudaStream_t st)
+{
+    // the gate and the cluster split-K live in their own instantiations
+    if (p.cl || (p.epi & EPI_GATE)) return dispatch<E, TBN, true>(p, ta, tb, A, lda, B, ldb, st);
+    return dispatch<E, TBN, false>(p, ta, tb, A, lda, B, ldb, st);
 }
 
 static bool aligned(const void *q, int bytes)
@@ -562,17 +738,11 @@ static bool aligned(const void *q, int bytes)
     return (reinterpret_cast<uintptr_t>(q) & (uintptr_t)(bytes - 1)) == 0;
 }
 
-}  // namespace gemm
-}  // namespace dc
-
-using namespace dc;
-
-extern "C" int dc_gemm(const void *A, int lda, const void *B, int ldb, float *C, int ldc, int M,
-                       int N, int K, int dtype, int flags, float alpha, const float *bias,
-                       const float *R, int ldr, float *aux, int ldaux, void *stream)
+// dc_gemm and dc_gemm_gate: shapes and flags checked, tiles and splits chosen.
+static int gemm_impl(const void *A, int lda, const void *B, int ldb, float *C, int ldc, int M,
+                     int N, int K, int dtype, int flags, float alpha, const float *bias,
+                     const float *R, int ldr, float *aux, int ldaux, const float *gate, void *stream)
 {
-    using namespace dc::gemm;
-    clear_error();
     if (M < 0 || N < 0 || K < 0) return fail(DC_ERR_INVALID, "negative shape M=%d N=%d K=%d", M, N, K);
     if ((long long)M * N == 0) return DC_OK;
     if (K == 0) return fail(DC_ERR_INVALID, "K == 0");
@@ -585,7 +755,8 @@ extern "C" int dc_gemm(const void *A, int lda, const void *B, int ldb, float *C,
     if ((lda * esz) % 16 || (ldb * esz) % 16 || !aligned(A, 16) || !aligned(B, 16))
         return fail(DC_ERR_INVALID, "A and B need 16-byte aligned bases and row strides");
     const bool gelu = flags & DC_GEMM_GELU, gelu_bwd = flags & DC_GEMM_GELU_BWD;
-    if (gelu && gelu_bwd) return fail(DC_ERR_INVALID, "GELU and GELU_BWD are exclusive");
+    if ((int)gelu + (int)gelu_bwd + (int)(gate != nullptr) > 1)
+        return fail(DC_ERR_INVALID, "GELU, GELU_BWD and the gate are exclusive");
     if (gelu_bwd && !aux) return fail(DC_ERR_INVALID, "GELU_BWD needs the pre-activation in aux");
     if ((flags & DC_GEMM_BIAS) && !bias) return fail(DC_ERR_INVALID, "BIAS without a bias vector");
     if (flags & DC_GEMM_ACCUMULATE) {
@@ -608,34 +779,48 @@ extern "C" int dc_gemm(const void *A, int lda, const void *B, int ldb, float *C,
     p.R = R;
     p.bias = bias;
     p.aux = aux;
+    p.gate = gate;
     p.epi = ((flags & DC_GEMM_BIAS) ? EPI_BIAS : 0) | (gelu ? EPI_GELU : 0) |
-            (gelu_bwd ? EPI_GELU_BWD : 0) | (R ? EPI_RESID : 0);
+            (gelu_bwd ? EPI_GELU_BWD : 0) | (R ? EPI_RESID : 0) | (gate ? EPI_GATE : 0);
     p.tiles_m = (M + BM - 1) / BM;
     const int sms = sm_count();
+    const bool linear = !gelu && !gelu_bwd && !gate;
     // 128 x 256 tiles where they fill at least half the SMs unsplit, or
     // where K is long enough to be split into many long units (the weight
     // gradients' K = B*T): each A tile then feeds twice the outputs
     const int wide_tiles = p.tiles_m * ((N + 255) / 256);
     const int bke = 128 / esz;
     p.ksteps = (K + bke - 1) / bke;
-    const bool long_k = !gelu && !gelu_bwd && p.ksteps >= 128 && 2 * wide_tiles <= sms;
+    const bool long_k = linear && p.ksteps >= 128 && 2 * wide_tiles <= sms;
     const int tbn = N >= 256 && (2 * wide_tiles >= sms || long_k) ? 256 : BN;
     p.tiles_n = (N + tbn - 1) / tbn;
-    // split K when the tiles leave SMs idle and the epilogue is linear, down
-    // to one K step a split: the decode step's 64-row products are latency
-    // bound, and more, shorter splits measured faster (C5: 121k -> 126k
-    // tokens/s with at least 4 / 1 K steps a split)
+    // split K when the tiles leave SMs idle, down to one K step a split (the
+    // decode step's 64-row products are latency bound: more, shorter splits
+    // measured faster).  A linear epilogue adds the splits with atomics into
+    // C (initialised with the residual, or zero, unless the residual is C
+    // itself); any other splits over a cluster of up to 8 CTAs a tile that
+    // add their partial tiles over distributed shared memory before the
+    // epilogue.  Measured on the decode step's 64-row layers (graph-replayed
+    // launches): GELU 10.1 us unsplit, 6.9 us over a cluster; a linear layer
+    // 5.9 us with atomics and the initialising memset, 6.7 us over a cluster.
     const int tiles = p.tiles_m * p.tiles_n;
     int splits = 1;
-    if (!gelu && !gelu_bwd && tiles * 2 <= sms)
-        splits = std::max(1, std::min(sms / tiles, p.ksteps));
+    p.cl = 0;
+    if (tiles * 2 <= sms) {
+        const int most = std::max(1, std::min(sms / tiles, p.ksteps));
+        if (linear)
+            splits = most;
+        else if (std::min(most, 8) >= 2)
+            p.cl = splits = std::min(most, 8);
+    }
     p.splits = splits;
     p.n_tiles = tiles * splits;
     p.vec = (ldc % 8 == 0) && gemm::aligned(C, 32) && (!R || (ldr % 8 == 0 && gemm::aligned(R, 32))) &&
-            (!aux || (ldaux % 8 == 0 && gemm::aligned(aux, 32))) && (!bias || gemm::aligned(bias, 32));
+            (!aux || (ldaux % 8 == 0 && gemm::aligned(aux, 32))) && (!bias || gemm::aligned(bias, 32)) &&
+            (!gate || gemm::aligned(gate, 32));
     p.status = device_status_word();
     cudaStream_t st = as_stream(stream);
-    if (splits > 1) {
+    if (splits > 1 && !p.cl) {
         // C starts as the residual (or zero) and every split adds its part
         if (!R)
             DC_CUDA_TRY(cudaMemset2DAsync(C, (size_t)ldc * 4, 0, (size_t)N * 4, M, st));
@@ -645,9 +830,34 @@ extern "C" int dc_gemm(const void *A, int lda, const void *B, int ldb, float *C,
         p.epi = (p.epi & EPI_BIAS) | EPI_ATOMIC;
     }
     if (tbn == 256) {
-        if (dtype == DC_F32) return dispatch<float, 256>(p, ta, tb, A, lda, B, ldb, st);
-        return dispatch<__nv_bfloat16, 256>(p, ta, tb, A, lda, B, ldb, st);
+        if (dtype == DC_F32) return dispatch_ext<float, 256>(p, ta, tb, A, lda, B, ldb, st);
+        return dispatch_ext<__nv_bfloat16, 256>(p, ta, tb, A, lda, B, ldb, st);
     }
-    if (dtype == DC_F32) return dispatch<float, BN>(p, ta, tb, A, lda, B, ldb, st);
-    return dispatch<__nv_bfloat16, BN>(p, ta, tb, A, lda, B, ldb, st);
+    if (dtype == DC_F32) return dispatch_ext<float, BN>(p, ta, tb, A, lda, B, ldb, st);
+    return dispatch_ext<__nv_bfloat16, BN>(p, ta, tb, A, lda, B, ldb, st);
+}
+
+}  // namespace gemm
+}  // namespace dc
+
+using namespace dc;
+
+extern "C" int dc_gemm(const void *A, int lda, const void *B, int ldb, float *C, int ldc, int M,
+                       int N, int K, int dtype, int flags, float alpha, const float *bias,
+                       const float *R, int ldr, float *aux, int ldaux, void *stream)
+{
+    clear_error();
+    return gemm::gemm_impl(A, lda, B, ldb, C, ldc, M, N, K, dtype, flags, alpha, bias, R, ldr, aux,
+                           ldaux, nullptr, stream);
+}
+
+extern "C" int dc_gemm_gate(const void *A, int lda, const void *B, int ldb, float *C, int ldc,
+                            int M, int N, int K, int dtype, int flags, float alpha,
+                            const float *bias, const float *R, int ldr, const float *gate,
+                            void *stream)
+{
+    clear_error();
+    if (!gate) return fail(DC_ERR_INVALID, "dc_gemm_gate without a gate vector");
+    return gemm::gemm_impl(A, lda, B, ldb, C, ldc, M, N, K, dtype, flags, alpha, bias, R, ldr,
+                           nullptr, 0, gate, stream);
 }

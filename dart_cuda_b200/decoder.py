@@ -538,9 +538,10 @@ class AftDecoder:
             # residual adds in place on x (the step keeps no activations), so a
             # split-K GEMM starts from x itself rather than from a copy
             ops.gemm(s["zd"], P[f"{l}.wo"], out=x, bias=P[f"{l}.bo"], residual=x)
+            # cross-attention against the one encoder row, sigmoid(q) * v0, in
+            # the query projection's epilogue
             ops.layernorm_fwd(x, P[f"{l}.ln2g"], P[f"{l}.ln2b"], out=s["a"])
-            ops.gemm(s["a"], P[f"{l}.wcq"], out=s["qc"], bias=P[f"{l}.bcq"])
-            self._gate(s["qc"], s["v0"][l], s["cg"])
+            ops.gemm(s["a"], P[f"{l}.wcq"], out=s["cg"], bias=P[f"{l}.bcq"], gate=s["v0"][l])
             ops.gemm(s["cg"], P[f"{l}.wco"], out=x, bias=P[f"{l}.bco"], residual=x)
             ops.layernorm_fwd(x, P[f"{l}.ln3g"], P[f"{l}.ln3b"], out=s["a"])
             ops.gemm(s["a"], P[f"{l}.w1"], out=s["h"], bias=P[f"{l}.b1"], gelu=True)

@@ -268,13 +268,14 @@ def _ld(t: torch.Tensor, name: str) -> int:
 
 
 def gemm(A, B, out=None, trans_a=False, trans_b=False, bias=None, residual=None, accumulate=False,
-         gelu=False, gelu_aux=None, gelu_bwd_aux=None, alpha=1.0):
+         gelu=False, gelu_aux=None, gelu_bwd_aux=None, alpha=1.0, gate=None):
     """C = epilogue(alpha * op(A) @ op(B)) through ``dc_gemm``: A and B fp32
     (tf32 tensor-core operands) or bf16, C fp32.  ``residual`` (or C itself
     with ``accumulate``) is added after the bias; ``gelu`` applies the tanh
     GELU and stores the pre-activation in ``gelu_aux`` when given;
     ``gelu_bwd_aux`` multiplies by the GELU derivative at that
-    pre-activation."""
+    pre-activation.  ``gate`` ([N]) ends the epilogue with
+    sigmoid(value) * gate (``dc_gemm_gate``)."""
     if A.dtype != B.dtype:
         raise DcError("A and B must share a dtype")
     M = A.shape[1] if trans_a else A.shape[0]
@@ -294,9 +295,16 @@ def gemm(A, B, out=None, trans_a=False, trans_b=False, bias=None, residual=None,
         flags |= DC_GEMM_GELU_BWD
         aux, ldx = gelu_bwd_aux.data_ptr(), _ld(gelu_bwd_aux, "gelu_bwd_aux")
     R, ldr = (None, 0) if residual is None else (residual.data_ptr(), _ld(residual, "residual"))
-    check(lib().dc_gemm(A.data_ptr(), _ld(A, "A"), B.data_ptr(), _ld(B, "B"), C.data_ptr(), _ld(C, "C"),
-                        M, N, K, _dtype_code(A), flags, float(alpha), _ptr(bias), R, ldr, aux, ldx,
-                        _stream()), "dc_gemm")
+    if gate is None:
+        check(lib().dc_gemm(A.data_ptr(), _ld(A, "A"), B.data_ptr(), _ld(B, "B"), C.data_ptr(), _ld(C, "C"),
+                            M, N, K, _dtype_code(A), flags, float(alpha), _ptr(bias), R, ldr, aux, ldx,
+                            _stream()), "dc_gemm")
+        return C
+    if aux is not None:
+        raise DcError("the gate excludes GELU and GELU_BWD")
+    check(lib().dc_gemm_gate(A.data_ptr(), _ld(A, "A"), B.data_ptr(), _ld(B, "B"), C.data_ptr(), _ld(C, "C"),
+                             M, N, K, _dtype_code(A), flags, float(alpha), _ptr(bias), R, ldr, gate.data_ptr(),
+                             _stream()), "dc_gemm_gate")
     return C
 
 

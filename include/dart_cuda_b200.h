@@ -227,9 +227,12 @@ int dc_adam_step(float *p, const float *g, float *m, float *v, int64_t n, int t,
  * strides.  Epilogue, in this order: + bias[N] (DC_GEMM_BIAS); + R[M,N]
  * (ldr; or C itself under DC_GEMM_ACCUMULATE); then DC_GEMM_GELU (aux, when
  * non-NULL, receives the pre-activation; C = gelu(pre)) or DC_GEMM_GELU_BWD
- * (C = value * gelu'(aux)).  GELU is the reference's tanh form.  Linear
- * epilogues may split K across CTAs and add with atomics (the summation
- * order then varies between runs).  Replaces matmul_fwd / the matmul closure
+ * (C = value * gelu'(aux)).  GELU is the reference's tanh form.  When the
+ * output tiles leave SMs idle, K is split across CTAs: the splits of a tile
+ * form a cluster that adds its partial tiles over distributed shared memory
+ * (any epilogue, a fixed summation order), or, for a linear epilogue whose
+ * residual is C itself (or a long K with few tiles), add into C with
+ * atomics (the summation order then varies between runs).  Replaces matmul_fwd / the matmul closure
  * (native/src/engine.cu:480-507, native/src/kernels/matmul.cuh:27-131) plus
  * the bias add, GELU and residual adds of a Layer / FeedForward forward and
  * backward. */
@@ -242,6 +245,18 @@ int dc_adam_step(float *p, const float *g, float *m, float *v, int64_t n, int t,
 int dc_gemm(const void *A, int lda, const void *B, int ldb, float *C, int ldc, int M, int N,
             int K, int dtype, int flags, float alpha, const float *bias, const float *R, int ldr,
             float *aux, int ldaux, void *stream);
+
+/* dc_gemm whose epilogue ends with the decoder's cross-attention gate,
+ * C = sigmoid(value) * gate[n] (gate [N], after the bias and the residual):
+ * the query projection and dc_gate_fwd in one launch.  Replaces the
+ * cross-attention of a decoder block against the one encoder row
+ * (lib/core/transformers/aft/transformer_decoder_block.dart:63-67,
+ * native/src/kernels/attention.cuh:41-128 at TEnc = 1) after its query
+ * projection (matmul_tensors + add_tensor_row_broadcast).  Excludes GELU and
+ * GELU_BWD. */
+int dc_gemm_gate(const void *A, int lda, const void *B, int ldb, float *C, int ldc, int M, int N,
+                 int K, int dtype, int flags, float alpha, const float *bias, const float *R,
+                 int ldr, const float *gate, void *stream);
 
 /* -------------------------------------------------- decoder step kernels
  * Token + position embedding of B sequences of T ids (int32, [B*T]):

@@ -128,7 +128,8 @@ def test_skinny_split_k(ops, M, N, K):
 @pytest.mark.parametrize("M,N,K", [(64, 2048, 512), (1, 100, 40), (3, 36, 1000)])
 def test_skinny_gelu_alpha(ops, M, N, K):
     """Few rows (the decode step's layers): GELU with the pre-activation
-    kept, a bias and alpha, in one pass (GELU is never split along K)."""
+    kept, a bias and alpha (K split over a cluster of CTAs where the tiles
+    are few: the partial tiles are added before the GELU)."""
     A = torch.randn(M, K).cuda()
     B = torch.randn(K, N).cuda()
     bias = torch.randn(N).cuda()
@@ -176,4 +177,63 @@ def test_rejects_unaligned(ops):
     B = torch.randn(66, 64).cuda()
     with pytest.raises(ops.DcError):
         ops.gemm(A, B)
+    assert ops.device_status() == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(64, 512, 512), (4736, 512, 256), (300, 200, 72), (1, 100, 40)])
+def test_gate_epilogue(ops, M, N, K):
+    """C = sigmoid(A B + bias) * v0 (the decoder's cross-attention query
+    projection and gate in one launch): few tiles split K over a cluster,
+    many run unsplit, through both epilogue forms; against dc_gate_fwd on the
+    unfused product and against float64."""
+    from dart_cuda_b200._lib import check, lib
+    g = torch.Generator().manual_seed(M + N)
+    A = torch.randn(M, K, generator=g).cuda()
+    B = (torch.randn(K, N, generator=g) / K ** 0.5).cuda()
+    bias = torch.randn(N, generator=g).cuda()
+    v0 = torch.randn(N, generator=g).cuda()
+    Y = ops.gemm(A, B, bias=bias, gate=v0)
+    Y2 = ops.gemm(A, B, bias=bias, gate=v0)
+    q = ops.gemm(A, B, bias=bias)
+    G = torch.empty_like(q)
+    check(lib().dc_gate_fwd(q.data_ptr(), N, v0.data_ptr(), G.data_ptr(), N, M, N, ops._stream()),
+          "dc_gate_fwd")
+    torch.cuda.synchronize()
+    pre = A.double().cpu() @ B.double().cpu() + bias.double().cpu()
+    assert rel(Y, torch.sigmoid(pre) * v0.double().cpu()) < TOL[torch.float32]
+    assert rel(Y, G.double().cpu()) < 1e-5
+    assert torch.equal(Y, Y2)  # a cluster adds its partial tiles in a fixed order
+    assert ops.device_status() == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(64, 2048, 512), (64, 512, 512), (128, 640, 1024), (3, 36, 1000)])
+def test_cluster_split_k_gelu_residual(ops, M, N, K):
+    """GELU with a separate residual and few tiles: K split over a cluster of
+    CTAs whose partial tiles are added before the epilogue, the same bits on
+    every run."""
+    g = torch.Generator().manual_seed(N + K)
+    A = torch.randn(M, K, generator=g).cuda()
+    B = (torch.randn(K, N, generator=g) / K ** 0.5).cuda()
+    bias = torch.randn(N, generator=g).cuda()
+    R = torch.randn(M, N, generator=g).cuda()
+    aux = torch.empty(M, N, device="cuda")
+    H = ops.gemm(A, B, bias=bias, residual=R, gelu=True, gelu_aux=aux)
+    H2 = ops.gemm(A, B, bias=bias, residual=R, gelu=True)
+    torch.cuda.synchronize()
+    pre = A.double().cpu() @ B.double().cpu() + bias.double().cpu() + R.double().cpu()
+    assert rel(aux, pre) < TOL[torch.float32]
+    assert rel(H, gelu64(pre)) < TOL[torch.float32]
+    assert torch.equal(H, H2)
+
+
+def test_gate_rejects(ops):
+    A = torch.randn(64, 64).cuda()
+    B = torch.randn(64, 128).cuda()
+    v0 = torch.randn(128).cuda()
+    with pytest.raises(ops.DcError):
+        ops.gemm(A, B, gelu=True, gelu_aux=torch.empty(64, 128, device="cuda"), gate=v0)
+    from dart_cuda_b200._lib import lib
+    C = torch.empty(64, 128, device="cuda")
+    assert lib().dc_gemm_gate(A.data_ptr(), 64, B.data_ptr(), 128, C.data_ptr(), 128, 64, 128, 64, 0,
+                              0x8, 1.0, None, None, 0, v0.data_ptr(), ops._stream()) != 0
     assert ops.device_status() == 0
