@@ -708,8 +708,37 @@ __global__ void __launch_bounds__(256, 3) bwd_stats_kernel(const Params p)
     const size_t bt = idx / groups;
     const int t = (int)(bt % p.Tqp);
     const int b = (int)(bt / p.Tqp);
-    float r[16], inv[16];
+    // every load of the thread is issued before any of its data is used:
+    // the bf16 statistics and the Q and dZ runs as raw words, so the four
+    // requests are in flight together (converting the statistics as they
+    // arrived held the Q and dZ loads back by a whole memory round trip)
+    uint32_t rw[8], iw[8];
+    bool raw_stats = false;
+    EpiPre pf;
+    pf.ok = false;
     if (t < p.Tq) {
+        if constexpr (sizeof(E) == 2) {
+            if (t >= p.stat_lo) {
+                const size_t so = ((size_t)b * p.Tqp + t) * p.dp + d0;
+                ld32B_nc((const E *)p.Rb + so, rw);
+                ld32B_nc((const E *)p.Ib + so, iw);
+                raw_stats = true;
+            }
+        }
+        if constexpr (sizeof(IO) == 2) {
+            if (p.vec_io && d0 + 16 <= p.D) {
+                const size_t row = (size_t)b * p.Tq + t;
+                ld32B_nc((const IO *)p.Q + row * p.ldi + d0, pf.a);
+                ld32B_nc((const IO *)p.dZ + row * p.ldo + d0, pf.b);
+                pf.ok = true;
+            }
+        }
+    }
+    float r[16], inv[16];
+    if (raw_stats) {
+        words_to_bf16(rw, r);
+        words_to_bf16(iw, inv);
+    } else if (t < p.Tq) {
         if (t < p.stat_lo) {
             const size_t so = ((size_t)b * p.stat_lo + t) * p.dp + d0;
             ld16g(p.Rs + so, r);
@@ -722,19 +751,6 @@ __global__ void __launch_bounds__(256, 3) bwd_stats_kernel(const Params p)
     } else {
 #pragma unroll
         for (int j = 0; j < 16; ++j) r[j] = inv[j] = 0.f;
-    }
-    // Q and dZ requested beside r and 1/den' (bf16 tensors, whole 16-column
-    // runs), so all four loads are in flight before the range guard below
-    // waits on the statistics
-    EpiPre pf;
-    pf.ok = false;
-    if constexpr (sizeof(IO) == 2) {
-        if (t < p.Tq && p.vec_io && d0 + 16 <= p.D) {
-            const size_t row = (size_t)b * p.Tq + t;
-            ld32B_nc((const IO *)p.Q + row * p.ldi + d0, pf.a);
-            ld32B_nc((const IO *)p.dZ + row * p.ldo + d0, pf.b);
-            pf.ok = true;
-        }
     }
     // the forward's range guard, on 1/den' and r
     if (t < p.Tq) {
