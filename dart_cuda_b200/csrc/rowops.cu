@@ -537,17 +537,19 @@ __global__ void __launch_bounds__(kSumThreads)
     cluster_sync_all();  // the CTA sums stay readable until rank 0 has added them
 }
 
-// Column sums of a tall matrix of at most 1024 columns, row-contiguous: CTA c
-// streams rows [c*rpc, (c+1)*rpc) whole (512 threads = 512/N4 rows x N4
-// float4 lanes, four row groups in flight; every warp reads and writes
-// contiguous bytes, as a copy does), adds its rows per column in shared
-// memory in row-lane order and writes its partial sums; the CTA that
+// Column sums of a tall matrix of at most 1024 columns, whole rows: the rows
+// go in units of 512/N4 (one row per N4 float4 lanes of the 512 threads), and
+// the units round-robin over the CTAs, four in flight a thread, so the grid
+// streams one contiguous front as a copy does (whole row ranges a CTA ran at
+// 0.77 of HBM, 296 separate streams; round-robin units 0.80).  Every warp
+// reads and writes contiguous bytes.  A CTA adds its rows per column in
+// shared memory in row-lane order and writes its partial sums; the CTA that
 // finishes last (an atomic count, no CTA waits for another) adds the
 // partials in CTA order, so the sums are deterministic.  It resets the count
 // for the next call.
 __global__ void __launch_bounds__(kSumThreads)
     bias_bwd_rows(const float4 *__restrict__ dy, float4 *__restrict__ da, float *__restrict__ db,
-                  float4 *__restrict__ part, unsigned *__restrict__ done, int M, int N4, int rpc,
+                  float4 *__restrict__ part, unsigned *__restrict__ done, int M, int N4,
                   int accumulate)
 {
     grid_dep_wait();  // programmatic dependent launch: inputs are ready
@@ -556,26 +558,32 @@ __global__ void __launch_bounds__(kSumThreads)
     __shared__ bool last;
     const int lanes = kSumThreads / N4;  // rows in flight per step (>= 2)
     const int c4 = threadIdx.x % N4, rl = threadIdx.x / N4;
-    const int r0 = blockIdx.x * rpc, r1 = min(M, r0 + rpc);
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     if (rl < lanes) {
-        int r = r0 + rl;
-        for (; r + 3 * lanes < r1; r += 4 * lanes) {
+        const int units = (M + lanes - 1) / lanes, G = (int)gridDim.x;
+        int u = blockIdx.x;
+        for (; u + 3 * G < units; u += 4 * G) {
             float4 g[4];
 #pragma unroll
-            for (int k = 0; k < 4; ++k) g[k] = __ldcs(dy + (size_t)(r + k * lanes) * N4 + c4);
+            for (int k = 0; k < 4; ++k) {
+                const int r = (u + k * G) * lanes + rl;
+                g[k] = r < M ? __ldcs(dy + (size_t)r * N4 + c4) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
+                const int r = (u + k * G) * lanes + rl;
                 add4(acc, g[k]);
-                if (da) {
-                    const size_t o = (size_t)(r + k * lanes) * N4 + c4;
+                if (da && r < M) {
+                    const size_t o = (size_t)r * N4 + c4;
                     float4 a = g[k];
                     if (accumulate) add4(a, da[o]);
                     __stcs(da + o, a);
                 }
             }
         }
-        for (; r < r1; r += lanes) {
+        for (; u < units; u += G) {
+            const int r = u * lanes + rl;
+            if (r >= M) continue;
             const size_t o = (size_t)r * N4 + c4;
             const float4 g = __ldcs(dy + o);
             add4(acc, g);
@@ -1082,9 +1090,7 @@ int dc_bias_bwd(const float *dy, float *da, float *db, int M, int N, int accumul
     // decoder's [16384, 256..1024] gradients ran 309 -> 516 us a step)
     if (vec && N <= 1024 && M >= 131072) {
         const int N4 = N / 4, lanes = kSumThreads / N4;
-        const int ctas = std::max(1, std::min(2 * sm_count(), (M + 4 * lanes - 1) / (4 * lanes)));
-        const int rpc = (M + ctas - 1) / ctas;
-        const int grid = (M + rpc - 1) / rpc;
+        const int grid = std::max(1, std::min(2 * sm_count(), (M + 4 * lanes - 1) / (4 * lanes)));
         char *scratch = nullptr;
         const size_t pbytes = (size_t)grid * N * sizeof(float);
         DC_CUDA_TRY(cudaMallocAsync(&scratch, pbytes + 256, st));
@@ -1094,7 +1100,7 @@ int dc_bias_bwd(const float *dy, float *da, float *db, int M, int N, int accumul
             KernelTimer kt("bias_bwd", st);
             e = launch_pdl(bias_bwd_rows, dim3(grid), dim3(kSumThreads), 0, st, 1,
                            reinterpret_cast<const float4 *>(dy), reinterpret_cast<float4 *>(da), db,
-                           reinterpret_cast<float4 *>(scratch), done, M, N4, rpc, accumulate);
+                           reinterpret_cast<float4 *>(scratch), done, M, N4, accumulate);
         }
         cudaFreeAsync(scratch, st);
         if (e != cudaSuccess) return fail(DC_ERR_CUDA, "bias bwd: %s", cudaGetErrorString(e));

@@ -85,6 +85,25 @@ def test_bias_grad_only(ops, dev, M, N):
     assert relerr(db.cpu().numpy(), 2 * rb) < 1e-5
 
 
+@pytest.mark.parametrize("M,N", [(262144, 256), (131072, 1024), (140001, 12)])
+def test_bias_bwd_tall(ops, dev, M, N):
+    """Tall matrices take the row-contiguous form: whole rows a CTA, then the
+    last CTA adds the CTAs' partial column sums (several threads a column,
+    in a fixed order: the same bits on every call)."""
+    rng = np.random.default_rng(M + N)
+    dy = rng.standard_normal((M, N)).astype(np.float32)
+    rb = dy.astype(np.float64).sum(0)
+    tdy = T(dev, dy)
+    da, db = ops.bias_bwd(tdy)
+    assert np.array_equal(da.cpu().numpy(), dy)
+    assert relerr(db.cpu().numpy(), rb) < 1e-5
+    db2 = torch.zeros(N, device=dev)
+    ops.bias_bwd(tdy, grads=(None, db2))
+    assert torch.equal(db, db2)
+    ops.bias_bwd(tdy, grads=(None, db2), accumulate=True)
+    assert relerr(db2.cpu().numpy(), 2 * rb) < 1e-5
+
+
 @pytest.mark.parametrize("M,N,ld", [(16384, 256, 256), (300, 96, 100), (7, 6, 6)])
 def test_gate(ops, dev, M, N, ld):
     """z = sigmoid(q) * v0 and its backward (dq, dv0 accumulated) against
