@@ -482,7 +482,7 @@ class AftDecoder:
         z = lambda *s: torch.zeros(*s, device=dev)
         s = {"B": B}
         s["cache"] = [z(Tm, B * d * 2) for _ in range(c.n_layers)]
-        s["x"], s["a"], s["zd"], s["qc"], s["cg"] = (z(B, d) for _ in range(5))
+        s["x"], s["a"], s["zd"], s["cg"] = (z(B, d) for _ in range(4))
         s["qkv"], s["h"] = z(B, 3 * d), z(B, F)
         s["logits"] = z(B, c.vocab)
         s["v0"] = [self.P[f"{l}.bcv"] for l in range(c.n_layers)]
