@@ -586,7 +586,47 @@ __global__ void __launch_bounds__(256)
     float cc[8];
 #pragma unroll
     for (int k = 0; k < 8; ++k) cc[k] = cs[tx * 8 + k];
-    for (int i = r0 + ty; i < r1; i += 16) {
+    int i0 = r0 + ty;
+    if constexpr (sizeof(IO) == 2) {
+        if (vec && d0 + 8 <= D) {
+            // two rows a step, their four 16-byte loads issued before any of
+            // them is converted (a conversion waits for its load)
+            for (; i0 + 16 < r1; i0 += 32) {
+                const int ia = i0, ib = i0 + 16;
+                uint4 ka = make_uint4(0u, 0u, 0u, 0u), va = ka, kb = ka, vb = ka;
+                if (ia < Tk) {
+                    ka = __ldg(reinterpret_cast<const uint4 *>(Kb + (size_t)ia * ldk + d0));
+                    va = __ldg(reinterpret_cast<const uint4 *>(Vb + (size_t)ia * ldk + d0));
+                }
+                if (ib < Tk) {
+                    kb = __ldg(reinterpret_cast<const uint4 *>(Kb + (size_t)ib * ldk + d0));
+                    vb = __ldg(reinterpret_cast<const uint4 *>(Vb + (size_t)ib * ldk + d0));
+                }
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int i = h ? ib : ia;
+                    const uint4 kw = h ? kb : ka, vw = h ? vb : va;
+                    const uint32_t kx[4] = {kw.x, kw.y, kw.z, kw.w}, vx[4] = {vw.x, vw.y, vw.z, vw.w};
+                    float pv[8], pe[8];
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+#pragma unroll
+                        for (int u = 0; u < 2; ++u) {
+                            const float kv = __uint_as_float(u ? (kx[q] & 0xFFFF0000u) : (kx[q] << 16));
+                            const float vv = __uint_as_float(u ? (vx[q] & 0xFFFF0000u) : (vx[q] << 16));
+                            const int k = 2 * q + u;
+                            pe[k] = i < Tk ? __expf(kv - cc[k]) : 0.f;
+                            pv[k] = pe[k] * vv;
+                        }
+                    }
+                    const size_t dst = ((size_t)b * Tkp + i) * dp + d0;
+                    st8op(PV + dst, pv);
+                    st8op(PE + dst, pe);
+                }
+            }
+        }
+    }
+    for (int i = i0; i < r1; i += 16) {
         float pv[8], pe[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k) pv[k] = pe[k] = 0.f;
