@@ -421,6 +421,47 @@ __global__ void __launch_bounds__(256)
                           rows_per_split, vec, cpart);
 }
 
+// E'V and E' (eight columns from d0, bf16 K and V) of rows ia and ib of one
+// sequence: the four 16-byte loads are issued before any is converted (a
+// conversion waits for its load); rows at or past Tk are written as zeros.
+template <class E>
+__device__ __forceinline__ void panel_rows2(const __nv_bfloat16 *__restrict__ Kb,
+                                            const __nv_bfloat16 *__restrict__ Vb, int ldk, int Tk,
+                                            int ia, int ib, int d0, const float (&cc)[8],
+                                            E *__restrict__ PVa, E *__restrict__ PEa,
+                                            E *__restrict__ PVb, E *__restrict__ PEb)
+{
+    uint4 ka = make_uint4(0u, 0u, 0u, 0u), va = ka, kb = ka, vb = ka;
+    if (ia < Tk) {
+        ka = __ldg(reinterpret_cast<const uint4 *>(Kb + (size_t)ia * ldk + d0));
+        va = __ldg(reinterpret_cast<const uint4 *>(Vb + (size_t)ia * ldk + d0));
+    }
+    if (ib < Tk) {
+        kb = __ldg(reinterpret_cast<const uint4 *>(Kb + (size_t)ib * ldk + d0));
+        vb = __ldg(reinterpret_cast<const uint4 *>(Vb + (size_t)ib * ldk + d0));
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const bool in = (h ? ib : ia) < Tk;
+        const uint4 kw = h ? kb : ka, vw = h ? vb : va;
+        const uint32_t kx[4] = {kw.x, kw.y, kw.z, kw.w}, vx[4] = {vw.x, vw.y, vw.z, vw.w};
+        float pv[8], pe[8];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const float kv = __uint_as_float(u ? (kx[q] & 0xFFFF0000u) : (kx[q] << 16));
+                const float vv = __uint_as_float(u ? (vx[q] & 0xFFFF0000u) : (vx[q] << 16));
+                const int k = 2 * q + u;
+                pe[k] = in ? __expf(kv - cc[k]) : 0.f;
+                pv[k] = pe[k] * vv;
+            }
+        }
+        st8op(h ? PVb : PVa, pv);
+        st8op(h ? PEb : PEa, pe);
+    }
+}
+
 // PV = exp(K - c) * V and PE = exp(K - c) over the padded [B, Tkp, dp] space,
 // eight consecutive d per thread (16-byte loads and stores when `vec`).
 
@@ -467,6 +508,8 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
     for (int k = 0; k < 8; ++k) cc[k] = cs[tx * 8 + k];
     const int r0 = blockIdx.y * rows_per_block, r1 = min(Tkp, r0 + rows_per_block);
+    // one row a step: two rows a step with all four loads ahead (panel_rows2,
+    // as the clustered prep does) measured slower at T = 4096 (48-53 -> 60 us)
     for (int i = r0 + ty; i < r1; i += 16) {
         float pv[8], pe[8];
 #pragma unroll
@@ -589,40 +632,9 @@ __global__ void __launch_bounds__(256)
     int i0 = r0 + ty;
     if constexpr (sizeof(IO) == 2) {
         if (vec && d0 + 8 <= D) {
-            // two rows a step, their four 16-byte loads issued before any of
-            // them is converted (a conversion waits for its load)
             for (; i0 + 16 < r1; i0 += 32) {
-                const int ia = i0, ib = i0 + 16;
-                uint4 ka = make_uint4(0u, 0u, 0u, 0u), va = ka, kb = ka, vb = ka;
-                if (ia < Tk) {
-                    ka = __ldg(reinterpret_cast<const uint4 *>(Kb + (size_t)ia * ldk + d0));
-                    va = __ldg(reinterpret_cast<const uint4 *>(Vb + (size_t)ia * ldk + d0));
-                }
-                if (ib < Tk) {
-                    kb = __ldg(reinterpret_cast<const uint4 *>(Kb + (size_t)ib * ldk + d0));
-                    vb = __ldg(reinterpret_cast<const uint4 *>(Vb + (size_t)ib * ldk + d0));
-                }
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int i = h ? ib : ia;
-                    const uint4 kw = h ? kb : ka, vw = h ? vb : va;
-                    const uint32_t kx[4] = {kw.x, kw.y, kw.z, kw.w}, vx[4] = {vw.x, vw.y, vw.z, vw.w};
-                    float pv[8], pe[8];
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-#pragma unroll
-                        for (int u = 0; u < 2; ++u) {
-                            const float kv = __uint_as_float(u ? (kx[q] & 0xFFFF0000u) : (kx[q] << 16));
-                            const float vv = __uint_as_float(u ? (vx[q] & 0xFFFF0000u) : (vx[q] << 16));
-                            const int k = 2 * q + u;
-                            pe[k] = i < Tk ? __expf(kv - cc[k]) : 0.f;
-                            pv[k] = pe[k] * vv;
-                        }
-                    }
-                    const size_t dst = ((size_t)b * Tkp + i) * dp + d0;
-                    st8op(PV + dst, pv);
-                    st8op(PE + dst, pe);
-                }
+                const size_t da = ((size_t)b * Tkp + i0) * dp + d0, db = da + (size_t)16 * dp;
+                panel_rows2<E>(Kb, Vb, ldk, Tk, i0, i0 + 16, d0, cc, PV + da, PE + da, PV + db, PE + db);
             }
         }
     }
