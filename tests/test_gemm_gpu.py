@@ -181,15 +181,18 @@ def test_rejects_unaligned(ops):
 
 
 @pytest.mark.parametrize("M,N,K", [(64, 512, 512), (4736, 512, 256), (300, 200, 72), (1, 100, 40)])
-def test_gate_epilogue(ops, M, N, K):
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_gate_epilogue(ops, M, N, K, dtype):
     """C = sigmoid(A B + bias) * v0 (the decoder's cross-attention query
     projection and gate in one launch): few tiles split K over a cluster,
     many run unsplit, through both epilogue forms; against dc_gate_fwd on the
     unfused product and against float64."""
     from dart_cuda_b200._lib import check, lib
     g = torch.Generator().manual_seed(M + N)
-    A = torch.randn(M, K, generator=g).cuda()
-    B = (torch.randn(K, N, generator=g) / K ** 0.5).cuda()
+    if dtype == torch.bfloat16 and (K % 8 or N % 8):
+        pytest.skip("bf16 rows must be 16-byte multiples")
+    A = torch.randn(M, K, generator=g).to(dtype).cuda()
+    B = (torch.randn(K, N, generator=g) / K ** 0.5).to(dtype).cuda()
     bias = torch.randn(N, generator=g).cuda()
     v0 = torch.randn(N, generator=g).cuda()
     Y = ops.gemm(A, B, bias=bias, gate=v0)
@@ -206,14 +209,15 @@ def test_gate_epilogue(ops, M, N, K):
     assert ops.device_status() == 0
 
 
-@pytest.mark.parametrize("M,N,K", [(64, 2048, 512), (64, 512, 512), (128, 640, 1024), (3, 36, 1000)])
-def test_cluster_split_k_gelu_residual(ops, M, N, K):
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("M,N,K", [(64, 2048, 512), (64, 512, 512), (128, 640, 1024), (3, 40, 1000)])
+def test_cluster_split_k_gelu_residual(ops, M, N, K, dtype):
     """GELU with a separate residual and few tiles: K split over a cluster of
     CTAs whose partial tiles are added before the epilogue, the same bits on
-    every run."""
+    every run (tf32 and bf16 operands)."""
     g = torch.Generator().manual_seed(N + K)
-    A = torch.randn(M, K, generator=g).cuda()
-    B = (torch.randn(K, N, generator=g) / K ** 0.5).cuda()
+    A = torch.randn(M, K, generator=g).to(dtype).cuda()
+    B = (torch.randn(K, N, generator=g) / K ** 0.5).to(dtype).cuda()
     bias = torch.randn(N, generator=g).cuda()
     R = torch.randn(M, N, generator=g).cuda()
     aux = torch.empty(M, N, device="cuda")
